@@ -1,0 +1,113 @@
+/*
+ * inzg.h -- C ABI of the B200 (sm_100a) implementation of inferenZ's mixture-of-experts layer.
+ *
+ * Drop-in for the routed part of the reference's `moe_block` (src/model_fwd.c:992-1140): the F16 router with softmax
+ * and top-k, the dispatch of tokens to experts, the gate|up -> SiLU*up -> down products over Q4L / Q8G expert blobs,
+ * and the routing-weighted rank-order combine. The expert cache's blob pointers (ec_try_acquire / ec_acquire /
+ * ec_release, src/expert_cache.h:55-71) are replaced by an HBM-resident pool filled once per layer from the
+ * `blk.%d.experts` tensor (src/engine.c:336-400). Plain C types only; no CUDA or torch types in the signatures.
+ *
+ * Threading: one context per engine, called from the engine thread (the reference's control flow is
+ * single-threaded, src/threadpool.c:221-247); not re-entrant. Host pointers are borrowed for the duration of a call;
+ * weights are copied into the context. Errors are status codes (the reference exits through inz_die,
+ * src/util.c:22-30; a host shim maps a non-OK status onto it).
+ */
+#ifndef INZG_H
+#define INZG_H
+
+#if defined(__GNUC__)
+#define INZG_EXPORT __attribute__((visibility("default")))
+#else
+#define INZG_EXPORT
+#endif
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* tensor type ids, as in the reference's GGUF (src/quant.h:25-37) */
+#define INZG_T_F16 1
+#define INZG_T_Q4L 102
+#define INZG_T_Q8G 103
+
+typedef enum {
+    INZG_OK = 0,
+    INZG_BAD_ARG = 1,        /* a size, pointer or layer index out of range */
+    INZG_CORRUPT_BLOB = 2,   /* bad INZQ magic or rows/cols mismatch, as src/model_fwd.c:854-855 / 958-960 */
+    INZG_OOM = 3,            /* device allocation failed */
+    INZG_CUDA = 4,           /* a CUDA call failed; inzg_last_error has the text */
+    INZG_NCCL = 5,           /* a collective failed (expert-parallel mode) */
+    INZG_TIMEOUT = 6,        /* a bounded device-side wait ran out */
+    INZG_DEVICE_CHECK = 7,   /* a kernel's own bounds check fired (expert id, slot, capacity) */
+    INZG_UNSUPPORTED = 8,    /* a shape or format this build does not implement */
+    INZG_NOT_READY = 9       /* layer has no router or no experts yet */
+} inzg_status;
+
+typedef struct inzg_ctx inzg_ctx;
+
+typedef struct {
+    int hidden;       /* H: 2048 (benchmark configurations) or 2560 (the reference model, src/model.h:11) */
+    int ff;           /* expert FFN width, 640 (src/model.h:53) */
+    int n_expert;     /* 512 (src/model.h:51) */
+    int topk;         /* 10 (src/model.h:52) */
+    int max_tokens;   /* largest n of one forward call (the reference's Q_MAX_T is 512, src/engine_internal.h:82) */
+    int n_layers;     /* layer slots: 49 = 48 layers + the MTP layer (src/model_fwd.c:1435) */
+    int device;       /* CUDA device ordinal */
+} inzg_config;
+
+#define INZG_IO_DEVICE 1u   /* xin, y, logit_bias and logits_override are device pointers; the call is stream-ordered */
+#define INZG_DUMP_ROUTE 2u  /* keep the routing products of this call for inzg_moe_route_dump */
+
+typedef struct {
+    unsigned flags;
+    const float *logit_bias;       /* optional [n_expert], added to the router logits before the softmax (test hook,
+                                      no counterpart in the reference) */
+    const float *logits_override;  /* optional [n][n_expert], replaces the router logits (test hook) */
+    void *stream;                  /* cudaStream_t to run on; NULL = the context's own stream */
+} inzg_moe_opts;
+
+typedef struct {
+    uint64_t calls, tokens;
+    uint64_t units, dec_units, gemm_units;   /* of the last call with INZG_DUMP_ROUTE */
+    uint64_t pool_bytes;
+    int last_launches;                       /* kernels launched by the last forward call */
+} inzg_stats;
+
+/* Context on one device; replaces the engine's expert-cache set-up (src/engine.c:336-400 -> ec_open). */
+INZG_EXPORT inzg_ctx *inzg_create(const inzg_config *cfg, inzg_status *status);
+INZG_EXPORT void inzg_destroy(inzg_ctx *ctx);
+INZG_EXPORT const char *inzg_last_error(const inzg_ctx *ctx);
+INZG_EXPORT const char *inzg_status_str(inzg_status st);
+
+/* Router of one layer: F16 [rows = n_expert][cols = hidden], as bound by q_bind_lin (src/model_fwd.c:87-96) and
+ * multiplied by inz_matvec_f16_rows / inz_matmul_f16_rows (src/quant.c:1290-1366). Copied and re-laid out. */
+INZG_EXPORT inzg_status inzg_set_router(inzg_ctx *ctx, int layer, const uint16_t *w_f16, int rows, int cols);
+
+/* Experts of one layer: the GGUF tensor `blk.%d.experts` (n_expert blobs of blob_bytes, gate|up then down,
+ * src/convert.c:565-584), replacing ec_preload of the layer (src/engine.c:389-397) and the per-expert
+ * q_bind_lin views (src/model_fwd.c:853-855, 958-960). Blobs are validated (magic, type, rows, cols), copied to HBM
+ * and re-laid out for the kernels. */
+INZG_EXPORT inzg_status inzg_pool_add_layer(inzg_ctx *ctx, int layer, int expert_type, const void *blobs, uint64_t blob_bytes,
+                                int n_expert);
+
+/* The routed MoE layer: y[n][hidden] = sum over the top-k experts of w_k * down(silu(gate x) * up x), in rank order,
+ * OVERWRITING y (src/model_fwd.c:1033, 1134-1140). xin [n][hidden] fp32. Same per-expert numeric path as the
+ * reference: experts with fewer than 12 tokens (or every expert when n <= 8) use the decode numerics
+ * (src/quant.c:611-671, 767-953), the others the prefill GEMM numerics (src/quant.c:1407-1668). */
+INZG_EXPORT inzg_status inzg_moe_forward(inzg_ctx *ctx, int layer, int n, const float *xin, float *y, const inzg_moe_opts *opt);
+
+/* Routing products of the last forward call made with INZG_DUMP_ROUTE (host pointers, each optional):
+ * sel [n][topk], w [n][topk] (renormalised), logits [n][n_expert] (after the test hook), probs [n][n_expert],
+ * unit_expert [n_units] in the reference's first-touch order (src/model_fwd.c:1020-1022), *n_units. */
+INZG_EXPORT inzg_status inzg_moe_route_dump(inzg_ctx *ctx, int n, int32_t *sel, float *w, float *logits, float *probs,
+                                int32_t *unit_expert, int *n_units);
+
+INZG_EXPORT inzg_status inzg_get_stats(const inzg_ctx *ctx, inzg_stats *out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

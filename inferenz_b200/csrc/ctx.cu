@@ -1,0 +1,458 @@
+// ctx.cu -- the C ABI of libinzg (include/inzg.h): context, HBM expert pool, and the routed MoE forward.
+//
+// One forward call (all on one stream, no host synchronisation until the result is copied back):
+//   router logits (bit-exact F16 GEMV)  ->  softmax + top-k + renormalised weights  ->  activation quantization of
+//   the inputs (both numeric paths)  ->  dispatch lists  ->  gate|up (decode GEMV / prefill GEMM)  ->  SiLU*up +
+//   quantization  ->  down (GEMV / GEMM) writing w * y into the token's slot  ->  rank-order combine.
+// Reference: moe_block, src/model_fwd.c:992-1140; the expert cache (src/expert_cache.c) is replaced by the pool.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/inzg.h"
+#include "host/inzg_host.h"
+#include "inzg_internal.h"
+#include "k_launch.h"
+
+using namespace inzg;
+
+namespace {
+
+constexpr uint32_t kMagic = 0x515A4E49u;  // "INZQ"
+
+struct QHeader {  // src/quant.h:40-50
+    uint32_t magic;
+    uint16_t type, rot_block;
+    uint32_t rows, cols, rot_seed;
+    uint8_t bits, pad[3];
+    uint8_t lut[32];
+    uint8_t pad2[8];
+};
+static_assert(sizeof(QHeader) == 64, "header is 64 bytes");
+
+struct LayerSlot {
+    bool has_router = false, has_experts = false;
+    uint4 *router = nullptr;
+    uint8_t *pool = nullptr;
+    uint8_t *luts = nullptr;
+    LayerDev dev{};
+};
+
+template <class T>
+T *dalloc(size_t count, bool &ok) {
+    void *p = nullptr;
+    if (count == 0) count = 1;
+    if (cudaMalloc(&p, sizeof(T) * count) != cudaSuccess) {
+        ok = false;
+        cudaGetLastError();
+        return nullptr;
+    }
+    return static_cast<T *>(p);
+}
+
+MatLayout make_layout(int type, int rows, int cols) {
+    MatLayout m{};
+    m.rows = rows;
+    m.cols = cols;
+    m.ng = cols / kGroup;
+    m.wb = type == INZG_T_Q8G ? 8 : 4;
+    m.gc = pick_gc(m.ng, m.wb);
+    m.nch = m.ng / m.gc;
+    return m;
+}
+
+uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+struct inzg_ctx {
+    inzg_config cfg{};
+    int num_sms = 0;
+    cudaStream_t stream = nullptr;
+    std::vector<LayerSlot> layers;
+    std::string err;
+    inzg_stats stats{};
+    // scratch
+    float *xin = nullptr, *y = nullptr, *logits = nullptr, *probs = nullptr, *bias = nullptr;
+    int32_t *sel = nullptr;
+    float *w = nullptr;
+    int8_t *xq64 = nullptr, *xq256 = nullptr;
+    float *xs64 = nullptr, *xb64 = nullptr, *xs256 = nullptr;
+    int32_t *cnt = nullptr, *off = nullptr, *first = nullptr, *etok = nullptr, *eslot = nullptr, *ccnt = nullptr;
+    int32_t *units = nullptr, *meta = nullptr, *dec_units = nullptr, *gemm_units = nullptr, *gemm_tiles = nullptr;
+    int32_t *upath = nullptr, *eexp = nullptr;
+    float *ew = nullptr, *GU = nullptr, *mo = nullptr;
+    int8_t *dq64 = nullptr, *dq256 = nullptr;
+    float *ds64 = nullptr, *db64 = nullptr, *ds256 = nullptr;
+    int last_n = 0;
+    bool last_dump = false;
+};
+
+static inzg_status fail(inzg_ctx *c, inzg_status st, const std::string &msg) {
+    if (c) c->err = msg;
+    return st;
+}
+
+static inzg_status cuda_fail(inzg_ctx *c, cudaError_t e, const char *what) {
+    return fail(c, INZG_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+extern "C" {
+
+const char *inzg_status_str(inzg_status st) {
+    switch (st) {
+    case INZG_OK: return "ok";
+    case INZG_BAD_ARG: return "bad argument";
+    case INZG_CORRUPT_BLOB: return "corrupt expert blob";
+    case INZG_OOM: return "out of device memory";
+    case INZG_CUDA: return "CUDA error";
+    case INZG_NCCL: return "NCCL error";
+    case INZG_TIMEOUT: return "device wait timed out";
+    case INZG_DEVICE_CHECK: return "device-side check failed";
+    case INZG_UNSUPPORTED: return "unsupported shape or format";
+    case INZG_NOT_READY: return "layer not loaded";
+    }
+    return "unknown status";
+}
+
+const char *inzg_last_error(const inzg_ctx *c) { return c ? c->err.c_str() : "no context"; }
+
+static void free_scratch(inzg_ctx *c) {
+    void *ptrs[] = {c->xin, c->y, c->logits, c->probs, c->bias, c->sel, c->w, c->xq64, c->xq256, c->xs64, c->xb64,
+                    c->xs256, c->cnt, c->off, c->first, c->etok, c->eslot, c->ccnt, c->units, c->meta, c->dec_units,
+                    c->gemm_units, c->gemm_tiles, c->upath, c->eexp, c->ew, c->GU, c->mo, c->dq64, c->dq256, c->ds64,
+                    c->db64, c->ds256};
+    for (void *p : ptrs)
+        if (p) cudaFree(p);
+}
+
+inzg_ctx *inzg_create(const inzg_config *cfg, inzg_status *status) {
+    inzg_status dummy;
+    inzg_status &st = status ? *status : dummy;
+    if (!cfg || cfg->hidden <= 0 || cfg->hidden % 256 || cfg->ff <= 0 || cfg->ff % kGroup || cfg->n_expert <= 0 ||
+        cfg->n_expert % 32 || cfg->n_expert > 1024 || cfg->topk <= 0 || cfg->topk > kMaxTopK ||
+        cfg->topk > cfg->n_expert || cfg->max_tokens <= 0 || cfg->n_layers <= 0) {
+        st = INZG_BAD_ARG;
+        return nullptr;
+    }
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || cfg->device < 0 || cfg->device >= ndev) {
+        cudaGetLastError();
+        st = INZG_CUDA;
+        return nullptr;
+    }
+    if (cudaSetDevice(cfg->device) != cudaSuccess) {
+        st = INZG_CUDA;
+        return nullptr;
+    }
+    inzg_ctx *c = new inzg_ctx();
+    c->cfg = *cfg;
+    c->layers.resize(cfg->n_layers);
+    cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, cfg->device);
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        delete c;
+        st = INZG_CUDA;
+        return nullptr;
+    }
+    const size_t T = cfg->max_tokens, H = cfg->hidden, E = cfg->n_expert, K = cfg->topk, FF = cfg->ff;
+    const size_t NE = T * K, nkbH = (H + kKB - 1) / kKB, nkbF = (FF + kKB - 1) / kKB;
+    const size_t nchunk = (T + 31) / 32;
+    bool ok = true;
+    c->xin = dalloc<float>(T * H, ok);
+    c->y = dalloc<float>(T * H, ok);
+    c->logits = dalloc<float>(T * E, ok);
+    c->probs = dalloc<float>(T * E, ok);
+    c->bias = dalloc<float>(E, ok);
+    c->sel = dalloc<int32_t>(NE, ok);
+    c->w = dalloc<float>(NE, ok);
+    c->xq64 = dalloc<int8_t>(T * H, ok);
+    c->xq256 = dalloc<int8_t>(T * H, ok);
+    c->xs64 = dalloc<float>(T * H / kGroup, ok);
+    c->xb64 = dalloc<float>(T * H / kGroup, ok);
+    c->xs256 = dalloc<float>(T * nkbH, ok);
+    c->cnt = dalloc<int32_t>(E, ok);
+    c->off = dalloc<int32_t>(E + 1, ok);
+    c->first = dalloc<int32_t>(E, ok);
+    c->etok = dalloc<int32_t>(NE, ok);
+    c->eslot = dalloc<int32_t>(NE, ok);
+    c->eexp = dalloc<int32_t>(NE, ok);
+    c->ew = dalloc<float>(NE, ok);
+    c->ccnt = dalloc<int32_t>(nchunk * E, ok);
+    c->units = dalloc<int32_t>(E, ok);
+    c->meta = dalloc<int32_t>(16, ok);
+    c->dec_units = dalloc<int32_t>(E, ok);
+    c->gemm_units = dalloc<int32_t>(E, ok);
+    c->gemm_tiles = dalloc<int32_t>(NE / 16 + E, ok);
+    c->upath = dalloc<int32_t>(E, ok);
+    c->GU = dalloc<float>(NE * 2 * FF, ok);
+    c->mo = dalloc<float>(NE * H, ok);
+    c->dq64 = dalloc<int8_t>(NE * FF, ok);
+    c->dq256 = dalloc<int8_t>(NE * FF, ok);
+    c->ds64 = dalloc<float>(NE * FF / kGroup, ok);
+    c->db64 = dalloc<float>(NE * FF / kGroup, ok);
+    c->ds256 = dalloc<float>(NE * nkbF, ok);
+    if (!ok) {
+        free_scratch(c);
+        cudaStreamDestroy(c->stream);
+        delete c;
+        st = INZG_OOM;
+        return nullptr;
+    }
+    router_set_attributes(cfg->hidden);
+    st = INZG_OK;
+    return c;
+}
+
+void inzg_destroy(inzg_ctx *c) {
+    if (!c) return;
+    cudaSetDevice(c->cfg.device);
+    cudaStreamSynchronize(c->stream);
+    for (auto &L : c->layers) {
+        if (L.router) cudaFree(L.router);
+        if (L.pool) cudaFree(L.pool);
+        if (L.luts) cudaFree(L.luts);
+    }
+    free_scratch(c);
+    cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+inzg_status inzg_set_router(inzg_ctx *c, int layer, const uint16_t *w, int rows, int cols) {
+    if (!c) return INZG_BAD_ARG;
+    if (layer < 0 || layer >= c->cfg.n_layers || !w) return fail(c, INZG_BAD_ARG, "set_router: bad layer or pointer");
+    if (rows != c->cfg.n_expert || cols != c->cfg.hidden)
+        return fail(c, INZG_BAD_ARG, "set_router: router must be n_expert x hidden");
+    cudaSetDevice(c->cfg.device);
+    LayerSlot &L = c->layers[layer];
+    const size_t bytes = (size_t)rows * cols * 2;
+    uint16_t *tmp = nullptr;
+    cudaError_t e = cudaMalloc(&tmp, bytes);
+    if (e != cudaSuccess) return fail(c, INZG_OOM, "set_router: staging buffer");
+    if (!L.router && cudaMalloc(&L.router, bytes) != cudaSuccess) {
+        cudaFree(tmp);
+        return fail(c, INZG_OOM, "set_router: router buffer");
+    }
+    e = cudaMemcpyAsync(tmp, w, bytes, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) {
+        launch_router_repack(tmp, L.router, rows, cols, c->stream);
+        e = cudaStreamSynchronize(c->stream);
+    }
+    cudaFree(tmp);
+    if (e != cudaSuccess) return cuda_fail(c, e, "set_router");
+    L.has_router = true;
+    L.dev.router = L.router;
+    return INZG_OK;
+}
+
+inzg_status inzg_pool_add_layer(inzg_ctx *c, int layer, int type, const void *blobs, uint64_t blob_bytes, int n_expert) {
+    if (!c) return INZG_BAD_ARG;
+    const inzg_config &cf = c->cfg;
+    if (layer < 0 || layer >= cf.n_layers || !blobs) return fail(c, INZG_BAD_ARG, "pool_add_layer: bad layer or pointer");
+    if (n_expert != cf.n_expert) return fail(c, INZG_BAD_ARG, "pool_add_layer: n_expert differs from the context");
+    if (type != INZG_T_Q4L && type != INZG_T_Q8G)
+        return fail(c, INZG_UNSUPPORTED, "pool_add_layer: expert type must be Q4L or Q8G");
+    const int H = cf.hidden, FF = cf.ff, E = cf.n_expert;
+    const uint64_t gu_bytes = inzg_qmat_bytes(type, 2 * FF, H), dn_bytes = inzg_qmat_bytes(type, H, FF);
+    if (blob_bytes < gu_bytes + dn_bytes) return fail(c, INZG_BAD_ARG, "pool_add_layer: blob smaller than its matrices");
+    // validate every blob the way q_bind_lin does (src/model_fwd.c:87-96, 853-855): magic, type, rows, cols
+    const uint8_t *b = static_cast<const uint8_t *>(blobs);
+    QHeader h0g, h0d;
+    memcpy(&h0g, b, 64);
+    memcpy(&h0d, b + gu_bytes, 64);
+    for (int e = 0; e < E; e++) {
+        QHeader hg, hd;
+        memcpy(&hg, b + (size_t)e * blob_bytes, 64);
+        memcpy(&hd, b + (size_t)e * blob_bytes + gu_bytes, 64);
+        if (hg.magic != kMagic || hd.magic != kMagic || hg.type != type || hd.type != type || hg.rows != (uint32_t)(2 * FF) ||
+            hg.cols != (uint32_t)H || hd.rows != (uint32_t)H || hd.cols != (uint32_t)FF) {
+            char msg[128];
+            snprintf(msg, sizeof(msg), "expert blob is corrupt (expert %d)", e);
+            return fail(c, INZG_CORRUPT_BLOB, msg);
+        }
+        // one activation quantization per layer input needs one rotation for all experts' gate|up (and down)
+        if (hg.rot_block != h0g.rot_block || hg.rot_seed != h0g.rot_seed || hd.rot_block != h0d.rot_block ||
+            hd.rot_seed != h0d.rot_seed)
+            return fail(c, INZG_UNSUPPORTED, "pool_add_layer: experts of one layer must share their rotations");
+    }
+    if ((h0g.rot_block > 1 && H % h0g.rot_block) || (h0d.rot_block > 1 && FF % h0d.rot_block))
+        return fail(c, INZG_CORRUPT_BLOB, "pool_add_layer: rotation block does not divide the matrix width");
+    cudaSetDevice(cf.device);
+    LayerSlot &L = c->layers[layer];
+    LayerDev &D = L.dev;
+    D.type = type;
+    D.H = H;
+    D.FF = FF;
+    D.E = E;
+    D.gu = make_layout(type, 2 * FF, H);
+    D.dn = make_layout(type, H, FF);
+    const uint64_t gb = type == INZG_T_Q8G ? 64 : 32;
+    D.gu.q_off = 0;
+    D.gu.d_off = align_up(D.gu.q_off + (uint64_t)D.gu.rows * D.gu.ng * gb, 256);
+    D.dn.q_off = align_up(D.gu.d_off + (uint64_t)D.gu.rows * D.gu.ng * 2, 256);
+    D.dn.d_off = align_up(D.dn.q_off + (uint64_t)D.dn.rows * D.dn.ng * gb, 256);
+    D.slab_bytes = align_up(D.dn.d_off + (uint64_t)D.dn.rows * D.dn.ng * 2, 256);
+    D.gu_rot = h0g.rot_block;
+    D.gu_seed = h0g.rot_seed;
+    D.dn_rot = h0d.rot_block;
+    D.dn_seed = h0d.rot_seed;
+    if (L.pool) { cudaFree(L.pool); L.pool = nullptr; }
+    if (L.luts) { cudaFree(L.luts); L.luts = nullptr; }
+    L.has_experts = false;
+    if (cudaMalloc(&L.pool, D.slab_bytes * E) != cudaSuccess || cudaMalloc(&L.luts, (size_t)E * 32) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(c, INZG_OOM, "pool_add_layer: pool allocation");
+    }
+    D.pool = L.pool;
+    D.luts = L.luts;
+    // stage blobs through a device buffer in chunks of experts and re-lay them out on the device
+    const int chunk = std::min(E, 32);
+    uint8_t *stage = nullptr;
+    if (cudaMalloc(&stage, blob_bytes * chunk) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(c, INZG_OOM, "pool_add_layer: staging buffer");
+    }
+    cudaError_t err = cudaSuccess;
+    for (int e0 = 0; e0 < E && err == cudaSuccess; e0 += chunk) {
+        const int ne = std::min(chunk, E - e0);
+        err = cudaMemcpyAsync(stage, b + (size_t)e0 * blob_bytes, blob_bytes * ne, cudaMemcpyHostToDevice, c->stream);
+        if (err == cudaSuccess) launch_pool_repack(stage, blob_bytes, gu_bytes, e0, ne, D, L.pool, L.luts, c->stream);
+        if (err == cudaSuccess) err = cudaStreamSynchronize(c->stream);
+    }
+    cudaFree(stage);
+    if (err != cudaSuccess) return cuda_fail(c, err, "pool_add_layer");
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return cuda_fail(c, err, "pool_add_layer repack");
+    L.has_experts = true;
+    c->stats.pool_bytes = 0;
+    for (auto &S : c->layers)
+        if (S.has_experts) c->stats.pool_bytes += S.dev.slab_bytes * S.dev.E;
+    return INZG_OK;
+}
+
+inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, float *y, const inzg_moe_opts *opt) {
+    if (!c) return INZG_BAD_ARG;
+    const inzg_config &cf = c->cfg;
+    if (layer < 0 || layer >= cf.n_layers) return fail(c, INZG_BAD_ARG, "moe_forward: bad layer");
+    if (n <= 0 || n > cf.max_tokens || !xin || !y) return fail(c, INZG_BAD_ARG, "moe_forward: bad n or pointer");
+    LayerSlot &L = c->layers[layer];
+    const unsigned flags = opt ? opt->flags : 0;
+    const bool dev_io = flags & INZG_IO_DEVICE;
+    const float *ovr = opt ? opt->logits_override : nullptr;
+    const float *bias = opt ? opt->logit_bias : nullptr;
+    if (!L.has_experts || (!L.has_router && !ovr)) return fail(c, INZG_NOT_READY, "moe_forward: layer not loaded");
+    cudaSetDevice(cf.device);
+    cudaStream_t st = opt && opt->stream ? static_cast<cudaStream_t>(opt->stream) : c->stream;
+    const int H = cf.hidden, E = cf.n_expert, K = cf.topk, FF = cf.ff;
+    const int NE = n * K;
+    const LayerDev &D = L.dev;
+    int launches = 0;
+    cudaError_t e = cudaSuccess;
+    const float *X = xin;
+    if (!dev_io) {
+        e = cudaMemcpyAsync(c->xin, xin, sizeof(float) * (size_t)n * H, cudaMemcpyHostToDevice, st);
+        X = c->xin;
+        if (e == cudaSuccess && bias) {
+            e = cudaMemcpyAsync(c->bias, bias, sizeof(float) * E, cudaMemcpyHostToDevice, st);
+            bias = c->bias;
+        }
+    }
+    if (e != cudaSuccess) return cuda_fail(c, e, "moe_forward: input copy");
+    // 1-2. router, softmax, top-k
+    const float *lg = c->logits;
+    if (ovr) {
+        e = cudaMemcpyAsync(c->logits, ovr, sizeof(float) * (size_t)n * E,
+                            dev_io ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st);
+        if (e != cudaSuccess) return cuda_fail(c, e, "moe_forward: logits override copy");
+    } else {
+        launches += launch_router_logits(L.router, X, n, H, E, bias, c->logits, st);
+    }
+    const bool dump = flags & INZG_DUMP_ROUTE;
+    launches += launch_softmax_topk(lg, n, E, K, c->sel, c->w, dump ? c->probs : nullptr, st);
+    // 3. the inputs, quantized for both numeric paths with the gate|up rotation
+    const bool any_gemm = n > 8 && (int64_t)n * K >= kGemmMinT;
+    launches += launch_act_quant_x(X, n, H, D.gu_rot, D.gu_seed, c->xq64, c->xs64, c->xb64, any_gemm ? c->xq256 : nullptr,
+                                   c->xs256, st);
+    // 4. dispatch lists
+    RouteDev R{};
+    R.n = n; R.topk = K; R.E = E;
+    R.sel = c->sel; R.w = c->w; R.cnt = c->cnt; R.off = c->off; R.first = c->first; R.etok = c->etok; R.eslot = c->eslot;
+    R.ew = c->ew; R.ccnt = c->ccnt; R.units = c->units; R.meta = c->meta; R.dec_units = c->dec_units;
+    R.gemm_units = c->gemm_units; R.gemm_tiles = c->gemm_tiles;
+    const int nchunk = (n + 31) / 32;
+    launches += launch_route(R, nchunk, D.gu.rows / 32, D.dn.rows / 32, gemm_token_tile(), c->upath, c->eexp, st);
+    // 5-7. experts
+    const int grid = c->num_sms * 4;
+    int r1 = launch_gemv_decode(D, 0, R, c->xq64, c->xs64, c->xb64, c->GU, 2 * FF, grid, st);
+    if (r1 < 0) return fail(c, INZG_UNSUPPORTED, "moe_forward: no decode kernel for this geometry");
+    launches += r1;
+    if (any_gemm) launches += launch_gemm_v1(D, 0, R, c->xq256, c->xs256, c->GU, 2 * FF, grid, st);
+    launches += launch_swiglu_quant(c->GU, FF, NE, c->eexp, c->upath, D.dn_rot, D.dn_seed, c->dq64, c->ds64, c->db64,
+                                    c->dq256, c->ds256, st);
+    launches += launch_gemv_decode(D, 1, R, c->dq64, c->ds64, c->db64, c->mo, H, grid, st);
+    if (any_gemm) launches += launch_gemm_v1(D, 1, R, c->dq256, c->ds256, c->mo, H, grid, st);
+    // 8. combine
+    float *yd = dev_io ? y : c->y;
+    launches += launch_combine(c->mo, n, H, K, yd, c->num_sms, st);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(c, e, "moe_forward: kernel launch");
+    c->stats.calls++;
+    c->stats.tokens += n;
+    c->stats.last_launches = launches;
+    c->last_n = n;
+    c->last_dump = dump;
+    if (!dev_io) {
+        e = cudaMemcpyAsync(y, c->y, sizeof(float) * (size_t)n * H, cudaMemcpyDeviceToHost, st);
+        int32_t meta[16];
+        if (e == cudaSuccess) e = cudaMemcpyAsync(meta, c->meta, sizeof(meta), cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) return cuda_fail(c, e, "moe_forward");
+        if (meta[kMetaError] != kErrNone) {
+            char msg[96];
+            snprintf(msg, sizeof(msg), "moe_forward: device check failed (code %d)", meta[kMetaError]);
+            return fail(c, INZG_DEVICE_CHECK, msg);
+        }
+    }
+    return INZG_OK;
+}
+
+inzg_status inzg_moe_route_dump(inzg_ctx *c, int n, int32_t *sel, float *w, float *logits, float *probs,
+                                int32_t *unit_expert, int *n_units) {
+    if (!c) return INZG_BAD_ARG;
+    if (!c->last_dump || n != c->last_n) return fail(c, INZG_BAD_ARG, "route_dump: no dumped call with this n");
+    cudaSetDevice(c->cfg.device);
+    const int E = c->cfg.n_expert, K = c->cfg.topk;
+    cudaError_t e = cudaStreamSynchronize(c->stream);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess && sel) e = cudaMemcpy(sel, c->sel, sizeof(int32_t) * (size_t)n * K, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && w) e = cudaMemcpy(w, c->w, sizeof(float) * (size_t)n * K, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && logits) e = cudaMemcpy(logits, c->logits, sizeof(float) * (size_t)n * E, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && probs) e = cudaMemcpy(probs, c->probs, sizeof(float) * (size_t)n * E, cudaMemcpyDeviceToHost);
+    int32_t meta[16] = {0};
+    if (e == cudaSuccess) e = cudaMemcpy(meta, c->meta, sizeof(meta), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(c, e, "route_dump");
+    const int nu = meta[kMetaNUnits];
+    std::vector<int32_t> units(nu), first(E);
+    if (nu > 0) e = cudaMemcpy(units.data(), c->units, sizeof(int32_t) * nu, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(first.data(), c->first, sizeof(int32_t) * E, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(c, e, "route_dump");
+    // first-touch order of the reference's units: ascending first slot t*topk+k
+    std::sort(units.begin(), units.end(), [&](int a, int b) { return first[a] < first[b]; });
+    if (unit_expert) std::copy(units.begin(), units.end(), unit_expert);
+    if (n_units) *n_units = nu;
+    c->stats.units = nu;
+    c->stats.dec_units = meta[kMetaNDec];
+    c->stats.gemm_units = meta[kMetaNGemm];
+    return INZG_OK;
+}
+
+inzg_status inzg_get_stats(const inzg_ctx *c, inzg_stats *out) {
+    if (!c || !out) return INZG_BAD_ARG;
+    *out = c->stats;
+    return INZG_OK;
+}
+
+}  // extern "C"

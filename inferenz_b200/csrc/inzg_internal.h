@@ -1,0 +1,107 @@
+// inzg_internal.h -- shared definitions of the libinzg CUDA implementation (device layouts, work lists, helpers).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/inzg.h"
+
+namespace inzg {
+
+constexpr int kGroup = 64;     // weights per quantization group (src/quant.h:21)
+constexpr int kLutBias = 64;   // LUT levels are stored biased by 64 (src/quant.h:22)
+constexpr int kKB = 256;       // prefill activation block (src/quant.h:152)
+constexpr int kGemmMinT = 12;  // experts with >= 12 tokens use the prefill numerics (src/model_fwd.c:126)
+constexpr int kMaxTopK = 16;
+
+// ---------------------------------------------------------------------------------------------------------------
+// Decode layout of one expert matrix (M rows x K cols, ng = K/64 groups).
+// A warp computes 4 rows x 8 "lanes"; lane l of a group owns the weights {4l..4l+3} and {32+4l..32+4l+3}, which is
+// exactly lane l of the reference's 8-wide VPDPBUSD accumulators (src/quant.c:767-875), so a thread reproduces the
+// reference's per-lane float accumulation. Per (row quad, chunk of gc groups): 4 rows x 8 lanes x gc x wb bytes,
+// wb = 4 (Q4L: 8 nibbles) or 8 (Q8G: 8 bytes); each thread loads its gc*wb bytes with one vector load and the warp's
+// load is one contiguous 128*gc*wb/4-byte segment. Scales: per (row quad, chunk): 4 rows x gc fp16.
+// Q4L words are re-packed so that bits 0-15 hold the 4 nibbles of weights 4l..4l+3 and bits 16-31 those of
+// 32+4l..32+4l+3 (one PRMT selector each).
+// ---------------------------------------------------------------------------------------------------------------
+struct MatLayout {
+    int rows, cols, ng, gc, wb, nch;  // nch = ng / gc chunks
+    uint64_t q_off, d_off;            // byte offsets of the weight and scale regions inside the expert's slab
+};
+
+__host__ __device__ inline int pick_gc(int ng, int wb) {
+    for (int gc = 16 / wb; gc > 1; gc >>= 1)
+        if (ng % gc == 0) return gc;
+    return 1;
+}
+
+// Per-layer, per-matrix metadata shared by all experts of the layer (rotation) plus per-expert LUTs.
+struct LayerDev {
+    int type;                 // INZG_T_Q4L / INZG_T_Q8G
+    int H, FF, E;
+    MatLayout gu, dn;         // identical geometry for every expert
+    uint64_t slab_bytes;      // bytes per expert in the pool (gu region + dn region)
+    int gu_rot, dn_rot;
+    uint32_t gu_seed, dn_seed;
+    const uint8_t *pool;      // [E][slab_bytes]
+    const uint8_t *luts;      // [E][2][16]: biased levels of gate|up, down
+    const uint4 *router;      // repacked F16 router, see router layout in k_router.cu
+};
+
+// Routing products of one forward call (device).
+struct RouteDev {
+    int n, topk, E;
+    int32_t *sel;        // [n][topk]
+    float *w;            // [n][topk]  renormalised
+    int32_t *cnt;        // [E] tokens per expert
+    int32_t *off;        // [E+1] exclusive prefix of cnt (entries sorted by expert, then token)
+    int32_t *first;      // [E] first slot t*topk+k that chose the expert (first-touch order key)
+    int32_t *etok;       // [n*topk] token of each entry
+    int32_t *eslot;      // [n*topk] slot t*topk+k of each entry
+    float *ew;           // [n*topk] weight of each entry
+    int32_t *ccnt;       // [nchunk][E] per-32-token-chunk counts, then their exclusive prefix per expert
+    int32_t *units;      // [E] experts with cnt > 0, ascending
+    int32_t *meta;       // [16] counters: 0 nunits, 1 n_dec_units, 2 n_gemm_units, 3 n_dec_items_gu, 4 n_dec_items_dn,
+                         //      5 n_gemm_tiles_gu, 6 n_gemm_tiles_dn, 7 device error code
+    int32_t *dec_units;  // [E] decode-path experts
+    int32_t *gemm_units; // [E] prefill-path experts
+    int32_t *gemm_tiles; // [E * tiles] (unit index << 16 | token tile) for the GEMM path
+};
+
+constexpr int kMetaNUnits = 0, kMetaNDec = 1, kMetaNGemm = 2, kMetaDecItemsGU = 3, kMetaDecItemsDN = 4,
+              kMetaGemmTilesGU = 5, kMetaGemmTilesDN = 6, kMetaError = 7;
+
+// device error codes (sticky, first one wins)
+constexpr int kErrNone = 0, kErrBadExpert = 1, kErrBadSlot = 2, kErrOverflow = 3;
+
+// ---------------------------------------------------------------------------------------------------------------
+// IEEE helpers with explicit rounding (no contraction, no fast math)
+// ---------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ float hsum8_tree(const float a[8]) {
+    float b0 = __fadd_rn(a[0], a[4]), b1 = __fadd_rn(a[1], a[5]), b2 = __fadd_rn(a[2], a[6]), b3 = __fadd_rn(a[3], a[7]);
+    return __fadd_rn(__fadd_rn(b0, b2), __fadd_rn(b1, b3));
+}
+
+// The reference's hsum8 over 8 consecutive lanes of a warp (lane & 7 = accumulator lane): result valid in all 8.
+__device__ __forceinline__ float hsum8_lanes(float v) {
+    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));  // (a0+a4) (a1+a5) (a2+a6) (a3+a7)
+    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));  // ((a0+a4)+(a2+a6)) ((a1+a5)+(a3+a7))
+    return __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+}
+
+__device__ __forceinline__ uint32_t rot_sign_bit(uint32_t seed, uint32_t i) {
+    uint32_t h = (i + 1) * 0x9E3779B1u ^ seed;
+    h ^= h >> 15; h *= 0x2C1B3C6Du; h ^= h >> 12; h *= 0x297A2D39u; h ^= h >> 15;
+    return h & 1u;
+}
+
+__device__ __forceinline__ int dp4a_ss(int a, int b, int c) { return __dp4a(a, b, c); }
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+__device__ __forceinline__ void set_error(int32_t *meta, int code) { atomicCAS(&meta[kMetaError], 0, code); }
+
+}  // namespace inzg

@@ -1,0 +1,34 @@
+// k_launch.h -- host launchers of the libinzg kernels (each returns the number of kernels it launched, -1 = no
+// instantiation for the geometry).
+#pragma once
+
+#include "inzg_internal.h"
+
+namespace inzg {
+
+void router_set_attributes(int H);
+void launch_router_repack(const uint16_t *W, uint4 *Wr, int E, int H, cudaStream_t st);
+int launch_router_logits(const uint4 *Wr, const float *X, int n, int H, int E, const float *bias, float *logits,
+                         cudaStream_t st);
+int launch_softmax_topk(const float *logits, int n, int E, int topk, int32_t *sel, float *w, float *probs,
+                        cudaStream_t st);
+
+int launch_route(const RouteDev &R, int nchunk, int gu_items_per_unit, int dn_items_per_unit, int gemm_tn,
+                 int32_t *upath, int32_t *eexp, cudaStream_t st);
+
+int launch_act_quant_x(const float *X, int n, int H, int rot, uint32_t seed, int8_t *q64, float *s64, float *b64,
+                       int8_t *q256, float *s256, cudaStream_t st);
+int launch_swiglu_quant(const float *GU, int FF, int n_entries, const int32_t *eexp, const int32_t *upath, int rot,
+                        uint32_t seed, int8_t *q64, float *s64, float *b64, int8_t *q256, float *s256, cudaStream_t st);
+int launch_combine(const float *mo, int n, int H, int topk, float *y, int num_sms, cudaStream_t st);
+
+int launch_gemv_decode(const LayerDev &L, int kind, const RouteDev &R, const int8_t *aq, const float *as,
+                       const float *ab, float *out, int out_ld, int grid, cudaStream_t st);
+int launch_gemm_v1(const LayerDev &L, int kind, const RouteDev &R, const int8_t *aq, const float *as, float *out,
+                   int out_ld, int grid, cudaStream_t st);
+int gemm_token_tile();
+
+void launch_pool_repack(const uint8_t *blobs, uint64_t blob_bytes, uint64_t gu_bytes, int e0, int ne,
+                        const LayerDev &L, uint8_t *pool, uint8_t *luts, cudaStream_t st);
+
+}  // namespace inzg

@@ -1,0 +1,218 @@
+// k_router.cu -- F16 router, softmax and top-k on sm_100a, bit-exact with the reference CPU path.
+//
+// Logits: the reference's inz_matvec_f16_rows (src/quant.c:1290-1304) keeps 8 fp32 accumulators per (row, token):
+// lane l accumulates f16(W[e][8j+l]) * x[8j+l] over j = 0, 1, ... with one FMA each, then hsum8
+// ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7)) (src/quant.c:705-711). Here one thread owns one (expert, lane) chain and
+// runs the same FMAs in the same order; the 8 threads of an expert finish with the same add tree over shuffles.
+// The router is re-laid out at upload so that a warp (4 experts x 8 lanes) reads one contiguous 512-byte segment per
+// 8 chain steps: Wr[eq][jc][e%4][l][8 halves], eq = e/4, jc = j/8.
+#include "inzg_internal.h"
+#include "k_launch.h"
+
+#include <cuda_fp16.h>
+
+namespace inzg {
+
+// W [E][H] f16 -> Wr (see above). One thread per output uint4.
+__global__ void router_repack_kernel(const uint16_t *__restrict__ W, uint4 *__restrict__ Wr, int E, int H) {
+    const int S = H / 8, SC = S / 8;  // chain steps per lane, 8-step chunks
+    const int64_t total = (int64_t)(E / 4) * SC * 32;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int l = (int)(i % 8), e4 = (int)((i / 8) % 4), jc = (int)((i / 32) % SC), eq = (int)(i / (32 * SC));
+        const int e = eq * 4 + e4;
+        uint16_t h[8];
+        for (int s = 0; s < 8; s++) h[s] = W[(size_t)e * H + 8 * (jc * 8 + s) + l];
+        uint4 v;
+        v.x = h[0] | ((uint32_t)h[1] << 16);
+        v.y = h[2] | ((uint32_t)h[3] << 16);
+        v.z = h[4] | ((uint32_t)h[5] << 16);
+        v.w = h[6] | ((uint32_t)h[7] << 16);
+        Wr[i] = v;
+    }
+}
+
+__device__ __forceinline__ float h2f(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)bits16)); }
+
+// logits[t][e] (+ bias[e]) for a tile of TT tokens per block.y and 4*warps experts per block.x.
+// Shared: x of the tile transposed to [tt][l][S + 4] so a thread reads its lane's chain steps contiguously (the pad
+// of 4 floats puts the 8 lanes of an expert on distinct banks).
+template <int TT>
+__global__ void __launch_bounds__(256) router_logits_kernel(const uint4 *__restrict__ Wr, const float *__restrict__ X,
+                                                             int n, int H, int E, const float *__restrict__ bias,
+                                                             float *__restrict__ logits) {
+    extern __shared__ float xs[];  // [TT][8][S + 4]
+    const int S = H / 8, SC = S / 8, SP = S + 4;
+    const int t0 = blockIdx.y * TT;
+    const int nt = min(TT, n - t0);
+    for (int i = threadIdx.x; i < TT * H; i += blockDim.x) {
+        const int tt = i / H, k = i % H;
+        const float v = tt < nt ? X[(size_t)(t0 + tt) * H + k] : 0.0f;
+        xs[(size_t)tt * 8 * SP + (k & 7) * SP + (k >> 3)] = v;
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int eq = blockIdx.x * (blockDim.x >> 5) + warp;  // expert quad of this warp
+    const int e = eq * 4 + (lane >> 3), l = lane & 7;
+    if (eq * 4 >= E) return;
+    float acc[TT];
+#pragma unroll
+    for (int tt = 0; tt < TT; tt++) acc[tt] = 0.0f;
+    const uint4 *wp = Wr + (size_t)eq * SC * 32 + lane;
+    for (int jc = 0; jc < SC; jc++) {
+        const uint4 v = __ldg(wp + (size_t)jc * 32);
+        float w[8];
+        w[0] = h2f(v.x & 0xFFFF); w[1] = h2f(v.x >> 16); w[2] = h2f(v.y & 0xFFFF); w[3] = h2f(v.y >> 16);
+        w[4] = h2f(v.z & 0xFFFF); w[5] = h2f(v.z >> 16); w[6] = h2f(v.w & 0xFFFF); w[7] = h2f(v.w >> 16);
+#pragma unroll
+        for (int tt = 0; tt < TT; tt++) {
+            const float4 *xp = reinterpret_cast<const float4 *>(xs + (size_t)tt * 8 * SP + l * SP + jc * 8);
+            const float4 a = xp[0], b = xp[1];
+            float r = acc[tt];
+            r = __fmaf_rn(w[0], a.x, r); r = __fmaf_rn(w[1], a.y, r); r = __fmaf_rn(w[2], a.z, r); r = __fmaf_rn(w[3], a.w, r);
+            r = __fmaf_rn(w[4], b.x, r); r = __fmaf_rn(w[5], b.y, r); r = __fmaf_rn(w[6], b.z, r); r = __fmaf_rn(w[7], b.w, r);
+            acc[tt] = r;
+        }
+    }
+#pragma unroll
+    for (int tt = 0; tt < TT; tt++) {
+        float s = hsum8_lanes(acc[tt]);
+        if (l == 0 && tt < nt && e < E) {
+            if (bias) s = __fadd_rn(s, bias[e]);  // test hook: logits[x] += bias[x] before the softmax
+            logits[(size_t)(t0 + tt) * E + e] = s;
+        }
+    }
+}
+
+// exp256_ps (Cephes), src/vmath.h:9-25, one lane
+__device__ __forceinline__ float cephes_exp(float x) {
+    x = fminf(fmaxf(x, -87.3f), 88.3f);
+    const float fx = rintf(__fmul_rn(x, 1.44269504088896341f));
+    x = __fmaf_rn(-fx, 0.693359375f, x);
+    x = __fmaf_rn(-fx, -2.12194440e-4f, x);
+    const float z = __fmul_rn(x, x);
+    float y = 1.9875691500e-4f;
+    y = __fmaf_rn(y, x, 1.3981999507e-3f);
+    y = __fmaf_rn(y, x, 8.3334519073e-3f);
+    y = __fmaf_rn(y, x, 4.1665795894e-2f);
+    y = __fmaf_rn(y, x, 1.6666665459e-1f);
+    y = __fmaf_rn(y, x, 5.0000001201e-1f);
+    y = __fadd_rn(__fmaf_rn(y, z, x), 1.0f);
+    return __fmul_rn(y, __int_as_float(((int)fx + 127) << 23));
+}
+
+// One warp per token: softmax_inplace (src/vmath.h:42-60), topk_f32 (src/sampler.c:95-127: order value desc,
+// index asc), and the renormalised weights of moe_block (src/model_fwd.c:1006-1011, 1028: sum left to right,
+// w_k = p_k / sum). E % 32 == 0, E <= 1024. Lane j holds elements j + 32 m.
+constexpr int kMaxPerLane = 32;
+__global__ void __launch_bounds__(256) softmax_topk_kernel(const float *__restrict__ logits, int n, int E, int topk,
+                                                            int32_t *__restrict__ sel, float *__restrict__ wsel,
+                                                            float *__restrict__ probs_out) {
+    __shared__ float ex[8][1024];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (t >= n) return;
+    const int per = E / 32;
+    const float *lg = logits + (size_t)t * E;
+    float v[kMaxPerLane];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int m = 0; m < kMaxPerLane; m++)
+        if (m < per) {
+            v[m] = lg[lane + 32 * m];
+            mx = v[m] > mx ? v[m] : mx;
+        }
+    for (int o = 16; o; o >>= 1) {
+        const float q = __shfl_xor_sync(0xffffffffu, mx, o);
+        mx = q > mx ? q : mx;
+    }
+#pragma unroll
+    for (int m = 0; m < kMaxPerLane; m++)
+        if (m < per) {
+            v[m] = cephes_exp(__fsub_rn(v[m], mx));
+            ex[warp][lane + 32 * m] = v[m];
+        }
+    __syncwarp();
+    // 8 lane sums: accumulator l adds elements l, l+8, l+16, ... in order (the reference's 8-wide running sum)
+    float part = 0.0f;
+    if (lane < 8)
+        for (int i = lane; i < E; i += 8) part = __fadd_rn(part, ex[warp][i]);
+    const float sum = __shfl_sync(0xffffffffu, hsum8_lanes(part), 0);
+    const float inv = __fdiv_rn(1.0f, sum);
+#pragma unroll
+    for (int m = 0; m < kMaxPerLane; m++)
+        if (m < per) {
+            v[m] = __fmul_rn(v[m], inv);
+            if (probs_out) probs_out[(size_t)t * E + lane + 32 * m] = v[m];
+        }
+    // top-k: k rounds of a warp arg-max under (value desc, index asc); the winner is removed by its owner
+    unsigned taken = 0;  // bit m: element lane + 32 m already selected
+    float wk[kMaxTopK];
+    int ik[kMaxTopK];
+    for (int k = 0; k < topk; k++) {
+        float bv = -INFINITY;
+        int bi = 0x7FFFFFFF;
+#pragma unroll
+        for (int m = 0; m < kMaxPerLane; m++)
+            if (m < per && !((taken >> m) & 1u)) {
+                const int i = lane + 32 * m;
+                if (v[m] > bv || (v[m] == bv && i < bi)) { bv = v[m]; bi = i; }
+            }
+        for (int o = 16; o; o >>= 1) {
+            const float qv = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int qi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (qv > bv || (qv == bv && qi < bi)) { bv = qv; bi = qi; }
+        }
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+        wk[k] = bv;
+        ik[k] = bi;
+    }
+    if (lane == 0) {
+        float s = 0.0f;
+        for (int k = 0; k < topk; k++) s = __fadd_rn(s, wk[k]);
+        for (int k = 0; k < topk; k++) {
+            sel[(size_t)t * topk + k] = ik[k];
+            wsel[(size_t)t * topk + k] = __fdiv_rn(wk[k], s);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+void launch_router_repack(const uint16_t *W, uint4 *Wr, int E, int H, cudaStream_t st) {
+    const int64_t total = (int64_t)(E / 4) * (H / 64) * 32;
+    const int blocks = (int)((total + 255) / 256);
+    router_repack_kernel<<<blocks, 256, 0, st>>>(W, Wr, E, H);
+}
+
+static size_t router_smem(int TT, int H) { return (size_t)TT * 8 * (H / 8 + 4) * sizeof(float); }
+
+void router_set_attributes(int H) {
+    cudaFuncSetAttribute(router_logits_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_smem(16, H));
+    cudaFuncSetAttribute(router_logits_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_smem(4, H));
+}
+
+int launch_router_logits(const uint4 *Wr, const float *X, int n, int H, int E, const float *bias, float *logits,
+                         cudaStream_t st) {
+    // few tokens: spread the 2 MB router over many SMs (one warp = 4 experts per block); many tokens: 16 tokens
+    // per thread so each weight load feeds 16 FMA chains
+    if (n <= 4) {
+        dim3 grid(E / 4, n);
+        router_logits_kernel<1><<<grid, 32, router_smem(1, H), st>>>(Wr, X, n, H, E, bias, logits);
+        return 1;
+    }
+    if (n <= 64) {
+        dim3 grid(E / 16, (n + 3) / 4);
+        router_logits_kernel<4><<<grid, 128, router_smem(4, H), st>>>(Wr, X, n, H, E, bias, logits);
+        return 1;
+    }
+    dim3 grid(E / 32, (n + 15) / 16);
+    router_logits_kernel<16><<<grid, 256, router_smem(16, H), st>>>(Wr, X, n, H, E, bias, logits);
+    return 1;
+}
+
+int launch_softmax_topk(const float *logits, int n, int E, int topk, int32_t *sel, float *w, float *probs,
+                        cudaStream_t st) {
+    softmax_topk_kernel<<<(n + 7) / 8, 256, 0, st>>>(logits, n, E, topk, sel, w, probs);
+    return 1;
+}
+
+}  // namespace inzg

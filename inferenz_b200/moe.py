@@ -1,0 +1,101 @@
+"""Host-side mirror of the reference's MoE operator over the libinzg C ABI.
+
+The reference engine calls ``moe_block(e, L, l, n, xin, y)`` (src/model_fwd.c:992) with the layer's router and the
+expert cache behind it. :class:`MoePool` holds the same inputs on the device -- one router per layer
+(``inzg_set_router``) and one HBM pool of expert blobs per layer (``inzg_pool_add_layer``, replacing the expert
+cache) -- and :meth:`MoePool.moe_block` runs the routed layer, overwriting ``y`` like the reference (:1033).
+Errors raise :class:`InzgError` carrying the C status (the reference exits through ``inz_die``).
+"""
+import ctypes
+
+import numpy as np
+
+from ._lib import (DUMP_ROUTE, IO_DEVICE, Config, InzgError, MoeOpts, Stats, T_Q4L, T_Q8G, lib)
+
+
+def _ptr(a):
+    return None if a is None else ctypes.c_void_p(a.ctypes.data)
+
+
+class MoePool:
+    def __init__(self, hidden=2048, ff=640, n_expert=512, topk=10, max_tokens=512, n_layers=1, device=0):
+        cfg = Config(hidden, ff, n_expert, topk, max_tokens, n_layers, device)
+        st = ctypes.c_int(0)
+        self._ctx = lib.inzg_create(ctypes.byref(cfg), ctypes.byref(st))
+        if not self._ctx:
+            raise InzgError(st.value, "inzg_create failed")
+        self.hidden, self.ff, self.n_expert, self.topk = hidden, ff, n_expert, topk
+        self.max_tokens, self.n_layers, self.device = max_tokens, n_layers, device
+
+    # -- lifetime --
+    def close(self):
+        if self._ctx:
+            lib.inzg_destroy(self._ctx)
+            self._ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def _check(self, status, what):
+        if status != 0:
+            raise InzgError(status, f"{what}: {lib.inzg_last_error(self._ctx).decode()}")
+
+    # -- weights --
+    def set_router(self, layer, w_f16):
+        w = np.ascontiguousarray(w_f16, dtype=np.uint16)
+        assert w.shape == (self.n_expert, self.hidden)
+        self._check(lib.inzg_set_router(self._ctx, layer, _ptr(w), w.shape[0], w.shape[1]), "set_router")
+
+    def add_layer(self, layer, expert_type, blobs, blob_bytes):
+        b = np.ascontiguousarray(blobs, dtype=np.uint8)
+        assert b.size >= blob_bytes * self.n_expert
+        self._check(lib.inzg_pool_add_layer(self._ctx, layer, expert_type, _ptr(b), blob_bytes, self.n_expert),
+                    "pool_add_layer")
+
+    # -- forward --
+    def moe_block(self, layer, xin, bias=None, logits_override=None, dump=False):
+        """y [n][H] = routed MoE layer of xin [n][H] (host arrays; copies in and out inside the call)."""
+        x = np.ascontiguousarray(xin, dtype=np.float32)
+        n = x.shape[0]
+        y = np.empty_like(x)
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        o = None if logits_override is None else np.ascontiguousarray(logits_override, dtype=np.float32)
+        opts = MoeOpts(DUMP_ROUTE if dump else 0, None if b is None else b.ctypes.data,
+                       None if o is None else o.ctypes.data, None)
+        self._check(lib.inzg_moe_forward(self._ctx, layer, n, _ptr(x), _ptr(y), ctypes.byref(opts)), "moe_forward")
+        return y
+
+    def moe_block_device(self, layer, n, x_ptr, y_ptr, bias_ptr=None, override_ptr=None, stream=None, dump=False):
+        """Stream-ordered call on device pointers (ints); returns immediately."""
+        opts = MoeOpts(IO_DEVICE | (DUMP_ROUTE if dump else 0), bias_ptr, override_ptr, stream)
+        self._check(lib.inzg_moe_forward(self._ctx, layer, n, ctypes.c_void_p(x_ptr), ctypes.c_void_p(y_ptr),
+                                         ctypes.byref(opts)), "moe_forward")
+
+    def route_dump(self, n):
+        K, E = self.topk, self.n_expert
+        sel = np.zeros((n, K), np.int32)
+        w = np.zeros((n, K), np.float32)
+        logits = np.zeros((n, E), np.float32)
+        probs = np.zeros((n, E), np.float32)
+        units = np.zeros(E, np.int32)
+        nu = ctypes.c_int(0)
+        self._check(lib.inzg_moe_route_dump(self._ctx, n, _ptr(sel), _ptr(w), _ptr(logits), _ptr(probs), _ptr(units),
+                                            ctypes.byref(nu)), "route_dump")
+        return {"sel": sel, "w": w, "logits": logits, "probs": probs, "units": units[:nu.value]}
+
+    def stats(self):
+        s = Stats()
+        self._check(lib.inzg_get_stats(self._ctx, ctypes.byref(s)), "get_stats")
+        return {f: getattr(s, f) for f, _ in Stats._fields_}
+
+
+__all__ = ["MoePool", "InzgError", "T_Q4L", "T_Q8G"]
