@@ -1,0 +1,383 @@
+"""MoE-layer benchmark (the metric of BASELINE.json) on B200.
+
+Workload (headline, N=1): BASELINE configs[1] -- one MoE layer, d=2048, 512 experts, top-10, FF 640, Q4L experts
+(synthetic, seeded, quantized with the engine's own quantizer), F16 router, decode batch of 32 tokens with a
+per-expert N(0,1) logit bias. Sub-results under "extra": configs[0] shape (1 token) and configs[2] (4096-token
+prefill, Zipf(1.1) bias).
+
+value  = tokens/s with inputs resident in HBM; each timed step is one layer call timed with CUDA events on the
+         launching stream; the L2 is flushed (512 MB write) before every step, outside the timed events.
+e2e    = the same through the public host API (MoePool.moe_block on pinned host buffers): H2D of the step's input and
+         D2H of its output inside the timed region (host wall clock around the synchronous call).
+--impl reference: the reference's own CPU implementation of the layer (oracle/_ref, all host cores).
+Multi-GPU (--gpus N, one process per GPU): N independent replicas (the expert-parallel path is not built yet).
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MoE-layer tokens/s at 1/32/4096 tok; % of HBM or tensor roofline, 1–8 GPU"
+H, FF, E, K = 2048, 640, 512, 10
+GU_PAYLOAD = 2 * FF * (H // 64) * 34        # gate|up indices + fp16 scales, Q4L (header excluded)
+DN_PAYLOAD = H * (FF // 64) * 34
+EXPERT_BYTES_Q4L = 2089088                   # both matrices incl. their 64-byte headers (inz_qmat_bytes)
+ROUTER_BYTES = E * H * 2
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        p = json.load(open(path))
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampler over the timed region (SM clock, throttle reasons)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"], stdout=subprocess.PIPE,
+                                      stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.p:
+            time.sleep(0.25)
+            self.p.terminate()
+            try:
+                out, _ = self.p.communicate(timeout=5)
+                self.lines = [l for l in out.splitlines() if l.strip()]
+            except Exception:
+                self.p.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_inputs(cfg, n):
+    from inferenz_b200 import synth
+    x = synth.hidden(n, H)
+    bias = override = None
+    if cfg == "decode32":
+        bias = synth.normal_bias(E)
+    elif cfg == "prefill4096":
+        bias = synth.zipf_bias(E)
+    return x, bias, override
+
+
+def time_device(pool, torch, x, bias, steps, warmup, flush, layer=0):
+    """Per-step CUDA-event time (ms) of the layer on HBM-resident inputs."""
+    n = x.shape[0]
+    dev = torch.device("cuda", pool.device)
+    xd = torch.from_numpy(x).to(dev)
+    yd = torch.empty_like(xd)
+    bd = None if bias is None else torch.from_numpy(bias).to(dev)
+    # a dedicated (non-default) stream: the flush, the events and the layer all run on it
+    stream = torch.cuda.Stream(dev)
+    sh = stream.cuda_stream
+    assert sh != 0
+
+    def call():
+        pool.moe_block_device(layer, n, xd.data_ptr(), yd.data_ptr(), None if bd is None else bd.data_ptr(),
+                              stream=sh)
+
+    torch.cuda.synchronize(dev)
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            flush.zero_()
+            call()
+        stream.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for a, b in evs:
+            flush.zero_()
+            a.record(stream)
+            call()
+            b.record(stream)
+    torch.cuda.synchronize(dev)
+    return [a.elapsed_time(b) for a, b in evs], yd
+
+
+def profile_stages(pool, torch, x, bias, reps, flush, layer=0):
+    n = x.shape[0]
+    dev = torch.device("cuda", pool.device)
+    xd = torch.from_numpy(x).to(dev)
+    yd = torch.empty_like(xd)
+    bd = None if bias is None else torch.from_numpy(bias).to(dev)
+    stream = torch.cuda.Stream(dev)
+    sh = stream.cuda_stream
+    torch.cuda.synchronize(dev)
+    pool.stage_times(reset=True)
+    with torch.cuda.stream(stream):
+        for _ in range(reps):
+            flush.zero_()
+            pool.moe_block_device(layer, n, xd.data_ptr(), yd.data_ptr(), None if bd is None else bd.data_ptr(),
+                                  stream=sh, profile=True)
+    torch.cuda.synchronize(dev)
+    st, calls = pool.stage_times(reset=True)
+    # routing summary of this input (one dumped call)
+    pool.moe_block(layer, x, bias=bias, dump=True)
+    pool.route_dump(n)
+    s = pool.stats()
+    return {k: v / max(calls, 1) for k, v in st.items()}, s
+
+
+def time_e2e(pool, torch, x, bias, steps, warmup, flush):
+    n = x.shape[0]
+    xp = torch.from_numpy(x).pin_memory().numpy()
+    yp = torch.empty(x.shape, dtype=torch.float32).pin_memory().numpy()
+    bp = None if bias is None else torch.from_numpy(bias).pin_memory().numpy()
+    for _ in range(warmup):
+        pool.moe_block(0, xp, bias=bp, y=yp)
+    ts = []
+    for _ in range(steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        pool.moe_block(0, xp, bias=bp, y=yp)
+        ts.append((time.perf_counter() - t0) * 1e3)
+    h2d = x.nbytes + (0 if bias is None else bias.nbytes)
+    d2h = x.nbytes + 64
+    return ts, h2d, d2h, yp
+
+
+def stage_roofline(stage_ms, stats, n, hbm):
+    """Algorithmic bytes per launch of each stage; the dominant stage's achieved GB/s."""
+    dec, gemm = stats["dec_units"], stats["gemm_units"]
+    algo = {
+        "router_logits": ROUTER_BYTES + n * H * 4 + n * E * 4,
+        "gate_up_gemv": dec * GU_PAYLOAD,
+        "down_gemv": dec * DN_PAYLOAD,
+        "gate_up_gemm": gemm * GU_PAYLOAD,
+        "down_gemm": gemm * DN_PAYLOAD,
+    }
+    dom = max(stage_ms, key=lambda k: stage_ms[k])
+    total = sum(stage_ms.values())
+    share = {k: round(v / total, 4) for k, v in stage_ms.items() if v > 0}
+    out = {"dominant": dom, "stage_ms": {k: round(v, 5) for k, v in stage_ms.items()}, "share": share}
+    if dom in algo and stage_ms[dom] > 0:
+        ach = algo[dom] / (stage_ms[dom] * 1e-3) / 1e9
+        out["roofline"] = {"bound": "hbm", "kernel": dom, "algorithmic_bytes": algo[dom], "achieved": round(ach, 1),
+                           "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4)}
+    return out
+
+
+def run_mine(args):
+    import torch
+
+    from inferenz_b200 import MoePool, synth
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    dev = torch.device("cuda", local)
+    hbm, bf16, peak_kind = peaks()
+    t0 = time.time()
+    blobs, bb = synth.layer_blobs(0, synth.T_Q4L, H, FF, E)
+    gen_s = time.time() - t0
+    R = synth.router(0, E, H)
+    pool = MoePool(H, FF, E, K, max_tokens=4096, n_layers=1, device=local)
+    pool.set_router(0, R)
+    pool.add_layer(0, synth.T_Q4L, blobs, bb)
+    flush = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    results = {}
+    plan = [("decode32", 32, args.steps, args.warmup)]
+    if not args.headline_only:
+        plan += [("decode1", 1, max(args.steps // 2, 10), args.warmup), ("prefill4096", 4096, max(args.steps // 50, 5), 3)]
+    clocks_summary = None
+    for name, n, steps, warm in plan:
+        x, bias, _ = make_inputs(name, n)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        if name == "decode32":
+            with Clocks(local) as ck:
+                ts, yd = time_device(pool, torch, x, bias, steps, warm, flush)
+            clocks_summary = ck.summary()
+        else:
+            ts, yd = time_device(pool, torch, x, bias, steps, warm, flush)
+        torch.cuda.synchronize(dev)
+        if dist:
+            dist.barrier()
+        total_ms = sum(ts)
+        if dist:
+            tt = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            total_ms = float(tt.item())
+        stage_ms, stats = profile_stages(pool, torch, x, bias, max(3, min(20, steps)), flush)
+        roof = stage_roofline(stage_ms, stats, n, hbm)
+        U = stats["units"]
+        layer_bytes = ROUTER_BYTES + U * EXPERT_BYTES_Q4L + 2 * n * H * 4
+        ms_step = total_ms / steps
+        results[name] = {
+            "n_tokens": n, "steps": steps, "ms_per_step": round(ms_step, 5),
+            "tokens_per_s": round(n * steps * world / (total_ms * 1e-3), 1),
+            "units": U, "decode_units": stats["dec_units"], "gemm_units": stats["gemm_units"],
+            "launches_per_step": stats["last_launches"],
+            "layer_roofline": {"bound": "hbm", "algorithmic_bytes": layer_bytes,
+                               "achieved": round(layer_bytes / (ms_step * 1e-3) / 1e9, 1), "peak": hbm,
+                               "unit": "GB/s", "frac": round(layer_bytes / (ms_step * 1e-3) / 1e9 / hbm, 4)},
+            "stages": roof,
+        }
+        if name == "decode32":
+            e2e_ts, h2d, d2h, _ = time_e2e(pool, torch, x, bias, max(steps // 4, 5), 3, flush)
+            results[name]["e2e"] = {"value": round(n * len(e2e_ts) / (sum(e2e_ts) * 1e-3), 1), "unit": "tokens/s",
+                                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                                    "ms_per_step": round(sum(e2e_ts) / len(e2e_ts), 5)}
+    head = results["decode32"]
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_reference("decode32", 32, budget_s=args.cpu_seconds, blobs=blobs, bb=bb, R=R)
+    if rank == 0:
+        traffic = None
+        tp = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(tp):
+            try:
+                traffic = json.load(open(tp)).get(head["stages"].get("dominant"))
+            except Exception:
+                traffic = None
+        roof = head["stages"].get("roofline", {})
+        if roof:
+            roof = dict(roof)
+            roof["peak_kind"] = peak_kind + " (MEASURED_PEAKS.json hbm_gbs, copy burst)"
+            roof["traffic"] = traffic
+        line = {
+            "metric": METRIC, "value": head["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 x Q4L (fp32 accumulate)", "data": "synthetic (seeded; no dataset)",
+            "config": {"workload": "BASELINE configs[1]: MoE layer, decode batch of 32 tokens, d=2048, 512 experts, "
+                                   "top-10, FF 640, Q4L experts, F16 router, N(0,1) per-expert logit bias",
+                       "global_batch": 32 * world, "seq_len": 1,
+                       "parallelism": "replicas" if world > 1 else "single GPU",
+                       "l2": "flushed (512 MB write) before every timed step"},
+            "roofline": roof or None,
+            "layer_roofline": head["layer_roofline"],
+            "cpu_baseline": cpu,
+            "e2e": head.get("e2e"),
+            "clocks": clocks_summary,
+            "gpu_launches": head["launches_per_step"] * args.steps,
+            "extra": {k: v for k, v in results.items() if k != "decode32"},
+            "detail": {"decode32": head, "layer_gen_s": round(gen_s, 1)},
+        }
+        print(json.dumps(line))
+    pool.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_reference(cfg, n, budget_s=12.0, blobs=None, bb=None, R=None, steps=None, warmup=1):
+    """The reference's own CPU layer (oracle/_ref, all host threads) on a bounded sample of the workload."""
+    import oracle
+    from inferenz_b200 import synth
+    if blobs is None:
+        blobs, bb = synth.layer_blobs(0, synth.T_Q4L, H, FF, E)
+        R = synth.router(0, E, H)
+    x, bias, _ = make_inputs(cfg, n)
+    try:
+        ref = oracle.Ref(H, threads=0)
+        kind, cores, call = "reference", ref.threads, (lambda: ref.moe_routed(R, blobs, bb, x, bias=bias, dumps=False))
+        isa = ref.isa
+    except (FileNotFoundError, OSError):
+        orc = oracle.Oracle()
+        gu_bytes = int(synth.lib.inzg_qmat_bytes(synth.T_Q4L, 2 * FF, H))
+        kind, cores, isa = "port", 1, "scalar C restatement"
+        call = (lambda: orc.moe_routed(R, blobs, bb, gu_bytes, x, bias=bias, dumps=False))
+    for _ in range(warmup):
+        call()
+    ts = []
+    t_start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        call()
+        ts.append(time.perf_counter() - t0)
+        if steps is not None and len(ts) >= steps:
+            break
+        if steps is None and (time.perf_counter() - t_start > budget_s or len(ts) >= 2000):
+            break
+    med = statistics.median(ts)
+    return {"value": round(n / med, 1), "unit": "tokens/s", "cores": cores, "kind": kind,
+            "sample": f"{len(ts)} calls of the {n}-token layer (median {med * 1e3:.3f} ms), {isa}",
+            "ms_median": round(med * 1e3, 4)}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cpu = cpu_reference("decode32", 32, steps=args.steps, warmup=max(args.warmup, 1))
+    line = {"metric": METRIC, "value": cpu["value"], "unit": "tokens/s", "impl": "reference",
+            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": cpu["ms_median"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 x Q4L (fp32 accumulate)", "data": "synthetic (seeded; no dataset)",
+            "config": {"workload": "BASELINE configs[1]: MoE layer, decode batch of 32 tokens, d=2048, 512 experts, "
+                                   "top-10, FF 640, Q4L experts, F16 router, N(0,1) per-expert logit bias",
+                       "global_batch": 32, "seq_len": 1, "parallelism": "CPU threads (reference thread pool)"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": cpu["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
+    ap.add_argument("--headline-only", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_mine(args)
+
+
+if __name__ == "__main__":
+    main()
