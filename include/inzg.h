@@ -60,6 +60,11 @@ typedef struct {
 
 #define INZG_IO_DEVICE 1u   /* xin, y, logit_bias and logits_override are device pointers; the call is stream-ordered */
 #define INZG_DUMP_ROUTE 2u  /* keep the routing products of this call for inzg_moe_route_dump */
+#define INZG_PROFILE 4u     /* time every stage with CUDA events on the call's stream; the call then synchronises */
+#define INZG_NO_GRAPH 8u    /* launch the kernels one by one instead of replaying the cached CUDA graph */
+
+/* stages timed under INZG_PROFILE (the reference's diag stages are coarser: DG_ROUTER, DG_EXPERT_*) */
+#define INZG_N_STAGES 10
 
 typedef struct {
     unsigned flags;
@@ -106,6 +111,12 @@ INZG_EXPORT inzg_status inzg_moe_route_dump(inzg_ctx *ctx, int n, int32_t *sel, 
                                 int32_t *unit_expert, int *n_units);
 
 INZG_EXPORT inzg_status inzg_get_stats(const inzg_ctx *ctx, inzg_stats *out);
+
+/* Per-stage device time (ms, summed over the calls made with INZG_PROFILE) and the number of such calls; reset != 0
+ * clears them after reading. Stage i is named by inzg_stage_name(i), i < INZG_N_STAGES. The per-stage counterpart of
+ * the reference's diag_add accounting (src/diag.c:67-83). */
+INZG_EXPORT inzg_status inzg_stage_times(inzg_ctx *ctx, double *ms, uint64_t *calls, int reset);
+INZG_EXPORT const char *inzg_stage_name(int stage);
 
 #ifdef __cplusplus
 }

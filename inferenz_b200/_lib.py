@@ -10,7 +10,8 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libinzg.so")
 
 T_F16, T_Q4L, T_Q8G = 1, 102, 103
-IO_DEVICE, DUMP_ROUTE = 1, 2
+IO_DEVICE, DUMP_ROUTE, PROFILE, NO_GRAPH = 1, 2, 4, 8
+N_STAGES = 10
 
 STATUS = {0: "INZG_OK", 1: "INZG_BAD_ARG", 2: "INZG_CORRUPT_BLOB", 3: "INZG_OOM", 4: "INZG_CUDA", 5: "INZG_NCCL",
           6: "INZG_TIMEOUT", 7: "INZG_DEVICE_CHECK", 8: "INZG_UNSUPPORTED", 9: "INZG_NOT_READY"}
@@ -47,6 +48,8 @@ SIGNATURES = {
     "inzg_moe_forward": (I, [P, I, I, P, P, ctypes.POINTER(MoeOpts)]),
     "inzg_moe_route_dump": (I, [P, I, P, P, P, P, P, P]),
     "inzg_get_stats": (I, [P, ctypes.POINTER(Stats)]),
+    "inzg_stage_times": (I, [P, P, P, I]),
+    "inzg_stage_name": (ctypes.c_char_p, [I]),
     # inzg_tools.h
     "inzg_synth_jump": (U64, [U64, U64]),
     "inzg_synth_randn": (U64, [U64, I64, F, P]),

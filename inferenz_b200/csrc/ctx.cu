@@ -90,7 +90,39 @@ struct inzg_ctx {
     float *ds64 = nullptr, *db64 = nullptr, *ds256 = nullptr;
     int last_n = 0;
     bool last_dump = false;
+    // per-stage profile
+    double stage_ms[INZG_N_STAGES] = {0};
+    uint64_t profiled_calls = 0;
+    cudaEvent_t ev[INZG_N_STAGES + 1] = {};
+    // CUDA graphs of the forward, keyed by everything a replay bakes in
+    struct GraphKey {
+        int layer, n;
+        const void *x, *y, *bias, *ovr;
+        unsigned flags;
+        bool operator==(const GraphKey &o) const {
+            return layer == o.layer && n == o.n && x == o.x && y == o.y && bias == o.bias && ovr == o.ovr &&
+                   flags == o.flags;
+        }
+    };
+    struct GraphEntry {
+        GraphKey key;
+        cudaGraphExec_t exec;
+        int launches;
+        uint64_t last_use;
+    };
+    std::vector<GraphEntry> graphs;
+    uint64_t use_clock = 0;
+    cudaStream_t capture_stream = nullptr;
 };
+
+static const char *kStageNames[INZG_N_STAGES] = {"router_logits", "softmax_topk", "act_quant", "route",
+                                                 "gate_up_gemv", "gate_up_gemm", "swiglu_quant", "down_gemv",
+                                                 "down_gemm", "combine"};
+
+static void drop_graphs(inzg_ctx *c) {
+    for (auto &g : c->graphs) cudaGraphExecDestroy(g.exec);
+    c->graphs.clear();
+}
 
 static inzg_status fail(inzg_ctx *c, inzg_status st, const std::string &msg) {
     if (c) c->err = msg;
@@ -203,6 +235,9 @@ inzg_ctx *inzg_create(const inzg_config *cfg, inzg_status *status) {
         return nullptr;
     }
     router_set_attributes(cfg->hidden);
+    gemv_set_attributes();
+    for (int i = 0; i <= INZG_N_STAGES; i++) cudaEventCreate(&c->ev[i]);
+    cudaStreamCreateWithFlags(&c->capture_stream, cudaStreamNonBlocking);
     st = INZG_OK;
     return c;
 }
@@ -216,6 +251,10 @@ void inzg_destroy(inzg_ctx *c) {
         if (L.pool) cudaFree(L.pool);
         if (L.luts) cudaFree(L.luts);
     }
+    drop_graphs(c);
+    for (int i = 0; i <= INZG_N_STAGES; i++)
+        if (c->ev[i]) cudaEventDestroy(c->ev[i]);
+    if (c->capture_stream) cudaStreamDestroy(c->capture_stream);
     free_scratch(c);
     cudaStreamDestroy(c->stream);
     delete c;
@@ -227,6 +266,7 @@ inzg_status inzg_set_router(inzg_ctx *c, int layer, const uint16_t *w, int rows,
     if (rows != c->cfg.n_expert || cols != c->cfg.hidden)
         return fail(c, INZG_BAD_ARG, "set_router: router must be n_expert x hidden");
     cudaSetDevice(c->cfg.device);
+    drop_graphs(c);
     LayerSlot &L = c->layers[layer];
     const size_t bytes = (size_t)rows * cols * 2;
     uint16_t *tmp = nullptr;
@@ -281,6 +321,7 @@ inzg_status inzg_pool_add_layer(inzg_ctx *c, int layer, int type, const void *bl
     if ((h0g.rot_block > 1 && H % h0g.rot_block) || (h0d.rot_block > 1 && FF % h0d.rot_block))
         return fail(c, INZG_CORRUPT_BLOB, "pool_add_layer: rotation block does not divide the matrix width");
     cudaSetDevice(cf.device);
+    drop_graphs(c);
     LayerSlot &L = c->layers[layer];
     LayerDev &D = L.dev;
     D.type = type;
@@ -333,50 +374,31 @@ inzg_status inzg_pool_add_layer(inzg_ctx *c, int layer, int type, const void *bl
     return INZG_OK;
 }
 
-inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, float *y, const inzg_moe_opts *opt) {
-    if (!c) return INZG_BAD_ARG;
+// Enqueue the whole layer on `st`. ev != nullptr: record ev[i] before stage i and ev[N] at the end.
+static int enqueue_forward(inzg_ctx *c, const LayerSlot &L, int n, const float *X, float *yd, const float *bias,
+                           const float *ovr, bool ovr_on_device, bool dump, cudaEvent_t *ev, cudaStream_t st) {
     const inzg_config &cf = c->cfg;
-    if (layer < 0 || layer >= cf.n_layers) return fail(c, INZG_BAD_ARG, "moe_forward: bad layer");
-    if (n <= 0 || n > cf.max_tokens || !xin || !y) return fail(c, INZG_BAD_ARG, "moe_forward: bad n or pointer");
-    LayerSlot &L = c->layers[layer];
-    const unsigned flags = opt ? opt->flags : 0;
-    const bool dev_io = flags & INZG_IO_DEVICE;
-    const float *ovr = opt ? opt->logits_override : nullptr;
-    const float *bias = opt ? opt->logit_bias : nullptr;
-    if (!L.has_experts || (!L.has_router && !ovr)) return fail(c, INZG_NOT_READY, "moe_forward: layer not loaded");
-    cudaSetDevice(cf.device);
-    cudaStream_t st = opt && opt->stream ? static_cast<cudaStream_t>(opt->stream) : c->stream;
     const int H = cf.hidden, E = cf.n_expert, K = cf.topk, FF = cf.ff;
     const int NE = n * K;
     const LayerDev &D = L.dev;
     int launches = 0;
-    cudaError_t e = cudaSuccess;
-    const float *X = xin;
-    if (!dev_io) {
-        e = cudaMemcpyAsync(c->xin, xin, sizeof(float) * (size_t)n * H, cudaMemcpyHostToDevice, st);
-        X = c->xin;
-        if (e == cudaSuccess && bias) {
-            e = cudaMemcpyAsync(c->bias, bias, sizeof(float) * E, cudaMemcpyHostToDevice, st);
-            bias = c->bias;
-        }
-    }
-    if (e != cudaSuccess) return cuda_fail(c, e, "moe_forward: input copy");
-    // 1-2. router, softmax, top-k
-    const float *lg = c->logits;
+    auto mark = [&](int i) {
+        if (ev) cudaEventRecord(ev[i], st);
+    };
+    mark(0);
     if (ovr) {
-        e = cudaMemcpyAsync(c->logits, ovr, sizeof(float) * (size_t)n * E,
-                            dev_io ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st);
-        if (e != cudaSuccess) return cuda_fail(c, e, "moe_forward: logits override copy");
+        if (ovr_on_device)
+            cudaMemcpyAsync(c->logits, ovr, sizeof(float) * (size_t)n * E, cudaMemcpyDeviceToDevice, st);
     } else {
         launches += launch_router_logits(L.router, X, n, H, E, bias, c->logits, st);
     }
-    const bool dump = flags & INZG_DUMP_ROUTE;
-    launches += launch_softmax_topk(lg, n, E, K, c->sel, c->w, dump ? c->probs : nullptr, st);
-    // 3. the inputs, quantized for both numeric paths with the gate|up rotation
+    mark(1);
+    launches += launch_softmax_topk(c->logits, n, E, K, c->sel, c->w, dump ? c->probs : nullptr, st);
+    mark(2);
     const bool any_gemm = n > 8 && (int64_t)n * K >= kGemmMinT;
     launches += launch_act_quant_x(X, n, H, D.gu_rot, D.gu_seed, c->xq64, c->xs64, c->xb64, any_gemm ? c->xq256 : nullptr,
                                    c->xs256, st);
-    // 4. dispatch lists
+    mark(3);
     RouteDev R{};
     R.n = n; R.topk = K; R.E = E;
     R.sel = c->sel; R.w = c->w; R.cnt = c->cnt; R.off = c->off; R.first = c->first; R.etok = c->etok; R.eslot = c->eslot;
@@ -384,19 +406,98 @@ inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, fl
     R.gemm_units = c->gemm_units; R.gemm_tiles = c->gemm_tiles;
     const int nchunk = (n + 31) / 32;
     launches += launch_route(R, nchunk, D.gu.rows / 32, D.dn.rows / 32, gemm_token_tile(), c->upath, c->eexp, st);
-    // 5-7. experts
+    mark(4);
     const int grid = c->num_sms * 4;
-    int r1 = launch_gemv_decode(D, 0, R, c->xq64, c->xs64, c->xb64, c->GU, 2 * FF, grid, st);
-    if (r1 < 0) return fail(c, INZG_UNSUPPORTED, "moe_forward: no decode kernel for this geometry");
+    const int r1 = launch_gemv_decode(D, 0, R, c->xq64, c->xs64, c->xb64, c->GU, 2 * FF, grid, st);
+    if (r1 < 0) return -1;
     launches += r1;
+    mark(5);
     if (any_gemm) launches += launch_gemm_v1(D, 0, R, c->xq256, c->xs256, c->GU, 2 * FF, grid, st);
+    mark(6);
     launches += launch_swiglu_quant(c->GU, FF, NE, c->eexp, c->upath, D.dn_rot, D.dn_seed, c->dq64, c->ds64, c->db64,
                                     c->dq256, c->ds256, st);
+    mark(7);
     launches += launch_gemv_decode(D, 1, R, c->dq64, c->ds64, c->db64, c->mo, H, grid, st);
+    mark(8);
     if (any_gemm) launches += launch_gemm_v1(D, 1, R, c->dq256, c->ds256, c->mo, H, grid, st);
-    // 8. combine
-    float *yd = dev_io ? y : c->y;
+    mark(9);
     launches += launch_combine(c->mo, n, H, K, yd, c->num_sms, st);
+    mark(10);
+    return launches;
+}
+
+inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, float *y, const inzg_moe_opts *opt) {
+    if (!c) return INZG_BAD_ARG;
+    const inzg_config &cf = c->cfg;
+    if (layer < 0 || layer >= cf.n_layers) return fail(c, INZG_BAD_ARG, "moe_forward: bad layer");
+    if (n <= 0 || n > cf.max_tokens || !xin || !y) return fail(c, INZG_BAD_ARG, "moe_forward: bad n or pointer");
+    LayerSlot &L = c->layers[layer];
+    const unsigned flags = opt ? opt->flags : 0;
+    const bool dev_io = flags & INZG_IO_DEVICE, dump = flags & INZG_DUMP_ROUTE, profile = flags & INZG_PROFILE;
+    const float *ovr = opt ? opt->logits_override : nullptr;
+    const float *bias = opt ? opt->logit_bias : nullptr;
+    if (!L.has_experts || (!L.has_router && !ovr)) return fail(c, INZG_NOT_READY, "moe_forward: layer not loaded");
+    cudaSetDevice(cf.device);
+    cudaStream_t st = opt && opt->stream ? static_cast<cudaStream_t>(opt->stream) : c->stream;
+    const int H = cf.hidden, E = cf.n_expert;
+    const LayerDev &D = L.dev;
+    if (launch_gemv_decode(D, -1, RouteDev{}, nullptr, nullptr, nullptr, nullptr, 0, 0, st) < 0)
+        return fail(c, INZG_UNSUPPORTED, "moe_forward: no decode kernel for this geometry");
+    cudaError_t e = cudaSuccess;
+    const float *X = xin;
+    if (!dev_io) {  // host buffers: stage into the context's device buffers (outside any graph)
+        e = cudaMemcpyAsync(c->xin, xin, sizeof(float) * (size_t)n * H, cudaMemcpyHostToDevice, st);
+        X = c->xin;
+        if (e == cudaSuccess && bias) {
+            e = cudaMemcpyAsync(c->bias, bias, sizeof(float) * E, cudaMemcpyHostToDevice, st);
+            bias = c->bias;
+        }
+        if (e == cudaSuccess && ovr)
+            e = cudaMemcpyAsync(c->logits, ovr, sizeof(float) * (size_t)n * E, cudaMemcpyHostToDevice, st);
+        if (e != cudaSuccess) return cuda_fail(c, e, "moe_forward: input copy");
+    }
+    float *yd = dev_io ? y : c->y;
+    int launches = 0;
+    if (profile || (flags & INZG_NO_GRAPH)) {
+        launches = enqueue_forward(c, L, n, X, yd, bias, ovr, dev_io, dump, profile ? c->ev : nullptr, st);
+    } else {
+        inzg_ctx::GraphKey key{layer, n, X, yd, bias, ovr, flags & (INZG_IO_DEVICE | INZG_DUMP_ROUTE)};
+        inzg_ctx::GraphEntry *g = nullptr;
+        for (auto &ge : c->graphs)
+            if (ge.key == key) g = &ge;
+        if (!g) {
+            cudaStream_t cs = c->capture_stream;
+            e = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
+            if (e != cudaSuccess) return cuda_fail(c, e, "moe_forward: begin capture");
+            const int nl = enqueue_forward(c, L, n, X, yd, bias, ovr, dev_io, dump, nullptr, cs);
+            cudaGraph_t graph = nullptr;
+            e = cudaStreamEndCapture(cs, &graph);
+            if (e != cudaSuccess || nl < 0) {
+                if (graph) cudaGraphDestroy(graph);
+                return e != cudaSuccess ? cuda_fail(c, e, "moe_forward: capture")
+                                        : fail(c, INZG_UNSUPPORTED, "moe_forward: capture");
+            }
+            cudaGraphExec_t exec = nullptr;
+            e = cudaGraphInstantiate(&exec, graph, 0);
+            cudaGraphDestroy(graph);
+            if (e != cudaSuccess) return cuda_fail(c, e, "moe_forward: graph instantiate");
+            if (c->graphs.size() >= 64) {  // evict the least recently used
+                auto it = std::min_element(c->graphs.begin(), c->graphs.end(),
+                                           [](const inzg_ctx::GraphEntry &a, const inzg_ctx::GraphEntry &b) {
+                                               return a.last_use < b.last_use;
+                                           });
+                cudaGraphExecDestroy(it->exec);
+                c->graphs.erase(it);
+            }
+            c->graphs.push_back({key, exec, nl, 0});
+            g = &c->graphs.back();
+        }
+        g->last_use = ++c->use_clock;
+        launches = g->launches;
+        e = cudaGraphLaunch(g->exec, st);
+        if (e != cudaSuccess) return cuda_fail(c, e, "moe_forward: graph launch");
+    }
+    if (launches < 0) return fail(c, INZG_UNSUPPORTED, "moe_forward: no kernel for this geometry");
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(c, e, "moe_forward: kernel launch");
     c->stats.calls++;
@@ -404,6 +505,16 @@ inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, fl
     c->stats.last_launches = launches;
     c->last_n = n;
     c->last_dump = dump;
+    if (profile) {
+        e = cudaEventSynchronize(c->ev[INZG_N_STAGES]);
+        if (e != cudaSuccess) return cuda_fail(c, e, "moe_forward: profile");
+        for (int i = 0; i < INZG_N_STAGES; i++) {
+            float ms = 0;
+            cudaEventElapsedTime(&ms, c->ev[i], c->ev[i + 1]);
+            c->stage_ms[i] += ms;
+        }
+        c->profiled_calls++;
+    }
     if (!dev_io) {
         e = cudaMemcpyAsync(y, c->y, sizeof(float) * (size_t)n * H, cudaMemcpyDeviceToHost, st);
         int32_t meta[16];
@@ -418,6 +529,20 @@ inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, fl
     }
     return INZG_OK;
 }
+
+inzg_status inzg_stage_times(inzg_ctx *c, double *ms, uint64_t *calls, int reset) {
+    if (!c) return INZG_BAD_ARG;
+    if (ms)
+        for (int i = 0; i < INZG_N_STAGES; i++) ms[i] = c->stage_ms[i];
+    if (calls) *calls = c->profiled_calls;
+    if (reset) {
+        for (int i = 0; i < INZG_N_STAGES; i++) c->stage_ms[i] = 0;
+        c->profiled_calls = 0;
+    }
+    return INZG_OK;
+}
+
+const char *inzg_stage_name(int stage) { return stage >= 0 && stage < INZG_N_STAGES ? kStageNames[stage] : nullptr; }
 
 inzg_status inzg_moe_route_dump(inzg_ctx *c, int n, int32_t *sel, float *w, float *logits, float *probs,
                                 int32_t *unit_expert, int *n_units) {

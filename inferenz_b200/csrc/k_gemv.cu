@@ -150,18 +150,23 @@ static void launch_one(const LayerDev &L, const MatLayout &M, const RouteDev &R,
                        const float *ab, float *out, int out_ld, int meta_items, int grid, cudaStream_t st) {
     const size_t smem = (size_t)kMaxDecTok * M.cols + (size_t)2 * kMaxDecTok * M.ng * sizeof(float);
     auto k = gemv_decode_kernel<Q8, NCH, GC, KIND>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     k<<<grid, 256, smem, st>>>(L.pool, L.slab_bytes, M, L.luts, KIND == 0 ? 0 : 16, R, aq, as, ab, out, out_ld, meta_items);
 }
 
 // Returns the number of kernels launched, or -1 if the geometry has no instantiation.
 int launch_gemv_decode(const LayerDev &L, int kind, const RouteDev &R, const int8_t *aq, const float *as,
                        const float *ab, float *out, int out_ld, int grid, cudaStream_t st) {
+    if (kind < 0)  // geometry probe: both matrices must have an instantiation
+        return launch_gemv_decode(L, 2, R, aq, as, ab, out, out_ld, grid, st) < 0 ||
+                       launch_gemv_decode(L, 3, R, aq, as, ab, out, out_ld, grid, st) < 0 ? -1 : 0;
+    const bool probe = kind >= 2;
+    if (probe) kind -= 2;
     const MatLayout &M = kind == 0 ? L.gu : L.dn;
     const int mi = kind == 0 ? kMetaDecItemsGU : kMetaDecItemsDN;
     const bool q8 = L.type == INZG_T_Q8G;
 #define INZG_GEMV_CASE(Q, N, G)                                                                                  \
     if (q8 == Q && M.nch == N && M.gc == G) {                                                                    \
+        if (probe) return 0;                                                                                     \
         if (kind == 0) launch_one<Q, N, G, 0>(L, M, R, aq, as, ab, out, out_ld, mi, grid, st);                  \
         else launch_one<Q, N, G, 1>(L, M, R, aq, as, ab, out, out_ld, mi, grid, st);                            \
         return 1;                                                                                                \
@@ -174,6 +179,20 @@ int launch_gemv_decode(const LayerDev &L, int kind, const RouteDev &R, const int
     INZG_GEMV_CASE(true, 5, 2)     // Q8G K = 640
 #undef INZG_GEMV_CASE
     return -1;
+}
+
+// The dynamic shared memory of every instantiation stays below 48 KB except at H = 4096+; set the opt-in anyway.
+void gemv_set_attributes() {
+#define INZG_GEMV_ATTR(Q, N, G)                                                                                  \
+    cudaFuncSetAttribute(gemv_decode_kernel<Q, N, G, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024); \
+    cudaFuncSetAttribute(gemv_decode_kernel<Q, N, G, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    INZG_GEMV_ATTR(false, 8, 4)
+    INZG_GEMV_ATTR(false, 10, 4)
+    INZG_GEMV_ATTR(false, 5, 2)
+    INZG_GEMV_ATTR(true, 16, 2)
+    INZG_GEMV_ATTR(true, 20, 2)
+    INZG_GEMV_ATTR(true, 5, 2)
+#undef INZG_GEMV_ATTR
 }
 
 }  // namespace inzg

@@ -22,6 +22,7 @@ int launch_swiglu_quant(const float *GU, int FF, int n_entries, const int32_t *e
                         uint32_t seed, int8_t *q64, float *s64, float *b64, int8_t *q256, float *s256, cudaStream_t st);
 int launch_combine(const float *mo, int n, int H, int topk, float *y, int num_sms, cudaStream_t st);
 
+void gemv_set_attributes();
 int launch_gemv_decode(const LayerDev &L, int kind, const RouteDev &R, const int8_t *aq, const float *as,
                        const float *ab, float *out, int out_ld, int grid, cudaStream_t st);
 int launch_gemm_v1(const LayerDev &L, int kind, const RouteDev &R, const int8_t *aq, const float *as, float *out,

@@ -10,7 +10,8 @@ import ctypes
 
 import numpy as np
 
-from ._lib import (DUMP_ROUTE, IO_DEVICE, Config, InzgError, MoeOpts, Stats, T_Q4L, T_Q8G, lib)
+from ._lib import (DUMP_ROUTE, IO_DEVICE, N_STAGES, NO_GRAPH, PROFILE, Config, InzgError, MoeOpts, Stats, T_Q4L,
+                   T_Q8G, lib)
 
 
 def _ptr(a):
@@ -62,21 +63,23 @@ class MoePool:
                     "pool_add_layer")
 
     # -- forward --
-    def moe_block(self, layer, xin, bias=None, logits_override=None, dump=False):
+    def moe_block(self, layer, xin, bias=None, logits_override=None, dump=False, y=None, graph=True):
         """y [n][H] = routed MoE layer of xin [n][H] (host arrays; copies in and out inside the call)."""
         x = np.ascontiguousarray(xin, dtype=np.float32)
         n = x.shape[0]
-        y = np.empty_like(x)
+        y = np.empty_like(x) if y is None else y
         b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
         o = None if logits_override is None else np.ascontiguousarray(logits_override, dtype=np.float32)
-        opts = MoeOpts(DUMP_ROUTE if dump else 0, None if b is None else b.ctypes.data,
+        opts = MoeOpts((DUMP_ROUTE if dump else 0) | (0 if graph else NO_GRAPH), None if b is None else b.ctypes.data,
                        None if o is None else o.ctypes.data, None)
         self._check(lib.inzg_moe_forward(self._ctx, layer, n, _ptr(x), _ptr(y), ctypes.byref(opts)), "moe_forward")
         return y
 
-    def moe_block_device(self, layer, n, x_ptr, y_ptr, bias_ptr=None, override_ptr=None, stream=None, dump=False):
-        """Stream-ordered call on device pointers (ints); returns immediately."""
-        opts = MoeOpts(IO_DEVICE | (DUMP_ROUTE if dump else 0), bias_ptr, override_ptr, stream)
+    def moe_block_device(self, layer, n, x_ptr, y_ptr, bias_ptr=None, override_ptr=None, stream=None, dump=False,
+                         profile=False, graph=True):
+        """Stream-ordered call on device pointers (ints); returns immediately (profile=True: after the call)."""
+        flags = IO_DEVICE | (DUMP_ROUTE if dump else 0) | (PROFILE if profile else 0) | (0 if graph else NO_GRAPH)
+        opts = MoeOpts(flags, bias_ptr, override_ptr, stream)
         self._check(lib.inzg_moe_forward(self._ctx, layer, n, ctypes.c_void_p(x_ptr), ctypes.c_void_p(y_ptr),
                                          ctypes.byref(opts)), "moe_forward")
 
@@ -91,6 +94,13 @@ class MoePool:
         self._check(lib.inzg_moe_route_dump(self._ctx, n, _ptr(sel), _ptr(w), _ptr(logits), _ptr(probs), _ptr(units),
                                             ctypes.byref(nu)), "route_dump")
         return {"sel": sel, "w": w, "logits": logits, "probs": probs, "units": units[:nu.value]}
+
+    def stage_times(self, reset=True):
+        """{stage name: ms summed over profiled calls}, number of profiled calls"""
+        ms = (ctypes.c_double * N_STAGES)()
+        calls = ctypes.c_uint64(0)
+        self._check(lib.inzg_stage_times(self._ctx, ms, ctypes.byref(calls), 1 if reset else 0), "stage_times")
+        return {lib.inzg_stage_name(i).decode(): ms[i] for i in range(N_STAGES)}, calls.value
 
     def stats(self):
         s = Stats()

@@ -28,6 +28,9 @@
 #define Q_MAX_T REF_MAX_T
 #include "model_fwd.c"
 
+#include <pthread.h>
+#include <sched.h>
+
 #define API __attribute__((visibility("default")))
 
 /* ---- expert cache stubs: every expert resident (the engine's all-resident mode, src/engine.c:370-399) ---- */
@@ -49,6 +52,9 @@ typedef struct {
     inz_engine *e;
     float *logits;
     int max_tokens;
+    cpu_set_t caller_cpus;   /* tp_create pins the calling thread to its first CPU (src/threadpool.c:200); the
+                                caller's mask is restored by ref_ctx_destroy */
+    int have_cpus;
 } ref_ctx;
 
 API int ref_hidden(void) { return Q_H; }
@@ -64,6 +70,7 @@ API void *ref_ctx_create(int threads, int expert_type) {
     inz_engine *e = calloc(1, sizeof(*e));
     c->e = e;
     c->max_tokens = Q_MAX_T;
+    c->have_cpus = pthread_getaffinity_np(pthread_self(), sizeof(c->caller_cpus), &c->caller_cpus) == 0;
     e->tp = tp_create(threads, NULL);
     const size_t T = Q_MAX_T;
     const int nthr = tp_size(e->tp);
@@ -114,6 +121,7 @@ API void ref_ctx_destroy(void *ctx) {
     tp_destroy(e->tp);
     free(e);
     free(c->logits);
+    if (c->have_cpus) pthread_setaffinity_np(pthread_self(), sizeof(c->caller_cpus), &c->caller_cpus);
     free(c);
 }
 
