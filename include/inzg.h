@@ -118,6 +118,20 @@ INZG_EXPORT inzg_status inzg_get_stats(const inzg_ctx *ctx, inzg_stats *out);
 INZG_EXPORT inzg_status inzg_stage_times(inzg_ctx *ctx, double *ms, uint64_t *calls, int reset);
 INZG_EXPORT const char *inzg_stage_name(int stage);
 
+/* Allocation-free routing: no counterpart in the reference. For callers that cannot allocate device memory on the
+ * call path -- an engine whose device-memory plan is fixed at start-up, or a latency-critical decode loop in which a
+ * cudaMalloc/cudaFree would synchronise the device -- this runs the router, softmax and top-k of one layer (the
+ * routing stage of inzg_moe_forward, same results bit for bit) with its intermediate logits in a static device array
+ * of the library instead of allocated scratch. x_dev [n][hidden], logit_bias_dev [n_expert] (optional), sel_dev
+ * [n][topk] and w_dev [n][topk] are device pointers; the call is ordered on `stream` (NULL = the legacy default
+ * stream) and returns without synchronising. Limits: n <= 64 and n_expert <= 512 (the array is 64 x 512 fp32 =
+ * 128 KiB, held by every GPU that loads the library until exit); larger calls return INZG_BAD_ARG. The first call on
+ * a device looks up the array's device address (cudaGetSymbolAddress) and should come before any stream capture.
+ * All calls share the array: calls that overlap on the GPU race. */
+INZG_EXPORT inzg_status inzg_route_topk_noalloc(inzg_ctx *ctx, int layer, int n, const float *x_dev,
+                                                const float *logit_bias_dev, int32_t *sel_dev, float *w_dev,
+                                                void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -50,6 +50,7 @@ SIGNATURES = {
     "inzg_get_stats": (I, [P, ctypes.POINTER(Stats)]),
     "inzg_stage_times": (I, [P, P, P, I]),
     "inzg_stage_name": (ctypes.c_char_p, [I]),
+    "inzg_route_topk_noalloc": (I, [P, I, I, P, P, P, P, P]),
     # inzg_tools.h
     "inzg_synth_jump": (U64, [U64, U64]),
     "inzg_synth_randn": (U64, [U64, I64, F, P]),

@@ -542,6 +542,22 @@ inzg_status inzg_stage_times(inzg_ctx *c, double *ms, uint64_t *calls, int reset
     return INZG_OK;
 }
 
+// internal helpers for noalloc.cu (hidden: not part of the exported ABI)
+int inzg__router_view(const inzg_ctx *c, int layer, const void **router, int *device, int *hidden, int *n_expert,
+                      int *topk) {
+    if (!c || layer < 0 || layer >= c->cfg.n_layers || !c->layers[layer].has_router) return 0;
+    *router = c->layers[layer].router;
+    *device = c->cfg.device;
+    *hidden = c->cfg.hidden;
+    *n_expert = c->cfg.n_expert;
+    *topk = c->cfg.topk;
+    return 1;
+}
+
+void inzg__set_error(inzg_ctx *c, const char *msg) {
+    if (c) c->err = msg;
+}
+
 const char *inzg_stage_name(int stage) { return stage >= 0 && stage < INZG_N_STAGES ? kStageNames[stage] : nullptr; }
 
 inzg_status inzg_moe_route_dump(inzg_ctx *c, int n, int32_t *sel, float *w, float *logits, float *probs,
