@@ -81,13 +81,15 @@ struct inzg_ctx {
     int32_t *sel = nullptr;
     float *w = nullptr;
     int8_t *xq64 = nullptr, *xq256 = nullptr;
-    float *xs64 = nullptr, *xb64 = nullptr, *xs256 = nullptr;
+    float2 *xsb64 = nullptr;
+    float *xs256 = nullptr;
     int32_t *cnt = nullptr, *off = nullptr, *first = nullptr, *etok = nullptr, *eslot = nullptr, *ccnt = nullptr;
     int32_t *units = nullptr, *meta = nullptr, *dec_units = nullptr, *gemm_units = nullptr, *gemm_tiles = nullptr;
     int32_t *upath = nullptr, *eexp = nullptr;
     float *ew = nullptr, *GU = nullptr, *mo = nullptr;
     int8_t *dq64 = nullptr, *dq256 = nullptr;
-    float *ds64 = nullptr, *db64 = nullptr, *ds256 = nullptr;
+    float2 *dsb64 = nullptr;
+    float *ds256 = nullptr;
     int last_n = 0;
     bool last_dump = false;
     // per-stage profile
@@ -154,10 +156,10 @@ const char *inzg_status_str(inzg_status st) {
 const char *inzg_last_error(const inzg_ctx *c) { return c ? c->err.c_str() : "no context"; }
 
 static void free_scratch(inzg_ctx *c) {
-    void *ptrs[] = {c->xin, c->y, c->logits, c->probs, c->bias, c->sel, c->w, c->xq64, c->xq256, c->xs64, c->xb64,
+    void *ptrs[] = {c->xin, c->y, c->logits, c->probs, c->bias, c->sel, c->w, c->xq64, c->xq256, c->xsb64,
                     c->xs256, c->cnt, c->off, c->first, c->etok, c->eslot, c->ccnt, c->units, c->meta, c->dec_units,
-                    c->gemm_units, c->gemm_tiles, c->upath, c->eexp, c->ew, c->GU, c->mo, c->dq64, c->dq256, c->ds64,
-                    c->db64, c->ds256};
+                    c->gemm_units, c->gemm_tiles, c->upath, c->eexp, c->ew, c->GU, c->mo, c->dq64, c->dq256, c->dsb64,
+                    c->ds256};
     for (void *p : ptrs)
         if (p) cudaFree(p);
 }
@@ -203,8 +205,7 @@ inzg_ctx *inzg_create(const inzg_config *cfg, inzg_status *status) {
     c->w = dalloc<float>(NE, ok);
     c->xq64 = dalloc<int8_t>(T * H, ok);
     c->xq256 = dalloc<int8_t>(T * H, ok);
-    c->xs64 = dalloc<float>(T * H / kGroup, ok);
-    c->xb64 = dalloc<float>(T * H / kGroup, ok);
+    c->xsb64 = dalloc<float2>(T * H / kGroup, ok);
     c->xs256 = dalloc<float>(T * nkbH, ok);
     c->cnt = dalloc<int32_t>(E, ok);
     c->off = dalloc<int32_t>(E + 1, ok);
@@ -224,8 +225,7 @@ inzg_ctx *inzg_create(const inzg_config *cfg, inzg_status *status) {
     c->mo = dalloc<float>(NE * H, ok);
     c->dq64 = dalloc<int8_t>(NE * FF, ok);
     c->dq256 = dalloc<int8_t>(NE * FF, ok);
-    c->ds64 = dalloc<float>(NE * FF / kGroup, ok);
-    c->db64 = dalloc<float>(NE * FF / kGroup, ok);
+    c->dsb64 = dalloc<float2>(NE * FF / kGroup, ok);
     c->ds256 = dalloc<float>(NE * nkbF, ok);
     if (!ok) {
         free_scratch(c);
@@ -396,7 +396,7 @@ static int enqueue_forward(inzg_ctx *c, const LayerSlot &L, int n, const float *
     launches += launch_softmax_topk(c->logits, n, E, K, c->sel, c->w, dump ? c->probs : nullptr, st);
     mark(2);
     const bool any_gemm = n > 8 && (int64_t)n * K >= kGemmMinT;
-    launches += launch_act_quant_x(X, n, H, D.gu_rot, D.gu_seed, c->xq64, c->xs64, c->xb64, any_gemm ? c->xq256 : nullptr,
+    launches += launch_act_quant_x(X, n, H, D.gu_rot, D.gu_seed, c->xq64, c->xsb64, any_gemm ? c->xq256 : nullptr,
                                    c->xs256, st);
     mark(3);
     RouteDev R{};
@@ -408,16 +408,17 @@ static int enqueue_forward(inzg_ctx *c, const LayerSlot &L, int n, const float *
     launches += launch_route(R, nchunk, D.gu.rows / 32, D.dn.rows / 32, gemm_token_tile(), c->upath, c->eexp, st);
     mark(4);
     const int grid = c->num_sms * 4;
-    const int r1 = launch_gemv_decode(D, 0, R, c->xq64, c->xs64, c->xb64, c->GU, 2 * FF, grid, st);
+    const int maxt = n == 1 ? 1 : n <= 8 ? 8 : kGemmMinT - 1;
+    const int r1 = launch_gemv_decode(D, 0, R, c->xq64, c->xsb64, c->GU, 2 * FF, maxt, grid, st);
     if (r1 < 0) return -1;
     launches += r1;
     mark(5);
     if (any_gemm) launches += launch_gemm_v1(D, 0, R, c->xq256, c->xs256, c->GU, 2 * FF, grid, st);
     mark(6);
-    launches += launch_swiglu_quant(c->GU, FF, NE, c->eexp, c->upath, D.dn_rot, D.dn_seed, c->dq64, c->ds64, c->db64,
-                                    c->dq256, c->ds256, st);
+    launches += launch_swiglu_quant(c->GU, FF, NE, c->eexp, c->upath, D.dn_rot, D.dn_seed, c->dq64, c->dsb64, c->dq256,
+                                    c->ds256, st);
     mark(7);
-    launches += launch_gemv_decode(D, 1, R, c->dq64, c->ds64, c->db64, c->mo, H, grid, st);
+    launches += launch_gemv_decode(D, 1, R, c->dq64, c->dsb64, c->mo, H, maxt, grid, st);
     mark(8);
     if (any_gemm) launches += launch_gemm_v1(D, 1, R, c->dq256, c->ds256, c->mo, H, grid, st);
     mark(9);
@@ -441,7 +442,7 @@ inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, fl
     cudaStream_t st = opt && opt->stream ? static_cast<cudaStream_t>(opt->stream) : c->stream;
     const int H = cf.hidden, E = cf.n_expert;
     const LayerDev &D = L.dev;
-    if (launch_gemv_decode(D, -1, RouteDev{}, nullptr, nullptr, nullptr, nullptr, 0, 0, st) < 0)
+    if (launch_gemv_decode(D, -1, RouteDev{}, nullptr, nullptr, nullptr, 0, 0, 0, st) < 0)
         return fail(c, INZG_UNSUPPORTED, "moe_forward: no decode kernel for this geometry");
     cudaError_t e = cudaSuccess;
     const float *X = xin;

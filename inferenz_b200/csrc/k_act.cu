@@ -34,8 +34,9 @@ __device__ void rotate_smem(float *v, int n, int block, uint32_t seed, float nor
     __syncthreads();
 }
 
-// quantize v[0..n) (shared) by warps: 64-groups into q64 (lane-pair order), s64, b64; and/or 256-blocks into q256, s256
-__device__ void quantize_smem(const float *v, int n, int8_t *q64, float *s64, float *b64, int8_t *q256, float *s256) {
+// quantize v[0..n) (shared) by warps: 64-groups into q64 (lane-pair order) and sb64 = (scale, bias sum); and/or
+// 256-blocks into q256, s256
+__device__ void quantize_smem(const float *v, int n, int8_t *q64, float2 *sb64, int8_t *q256, float *s256) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     if (q64)
         for (int g = warp; g < n / kGroup; g += nw) {
@@ -49,10 +50,7 @@ __device__ void quantize_smem(const float *v, int n, int8_t *q64, float *s64, fl
             for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
             q64[g * kGroup + lane_pair_pos(lane)] = (int8_t)a;
             q64[g * kGroup + lane_pair_pos(32 + lane)] = (int8_t)b;
-            if (lane == 0) {
-                s64[g] = s;
-                b64[g] = __fmul_rn(s, (float)sum);
-            }
+            if (lane == 0) sb64[g] = make_float2(s, __fmul_rn(s, (float)sum));
         }
     if (q256) {
         const int nkb = (n + kKB - 1) / kKB;
@@ -71,17 +69,16 @@ __device__ void quantize_smem(const float *v, int n, int8_t *q64, float *s64, fl
 
 // one block per token: x [n][H] -> decode activations (q64, s64, b64) and prefill activations (q256, s256)
 __global__ void __launch_bounds__(256) act_quant_x_kernel(const float *__restrict__ X, int n, int H, int rot, uint32_t seed,
-                                                          float norm, int8_t *__restrict__ q64, float *__restrict__ s64,
-                                                          float *__restrict__ b64, int8_t *__restrict__ q256,
-                                                          float *__restrict__ s256) {
+                                                          float norm, int8_t *__restrict__ q64, float2 *__restrict__ sb64,
+                                                          int8_t *__restrict__ q256, float *__restrict__ s256) {
     extern __shared__ float v[];
     const int t = blockIdx.x;
     for (int i = threadIdx.x; i < H; i += blockDim.x) v[i] = X[(size_t)t * H + i];
     __syncthreads();
     if (rot > 1) rotate_smem(v, H, rot, seed, norm);
     const int ng = H / kGroup, nkb = (H + kKB - 1) / kKB;
-    quantize_smem(v, H, q64 + (size_t)t * H, s64 + (size_t)t * ng, b64 + (size_t)t * ng,
-                  q256 ? q256 + (size_t)t * H : nullptr, q256 ? s256 + (size_t)t * nkb : nullptr);
+    quantize_smem(v, H, q64 + (size_t)t * H, sb64 + (size_t)t * ng, q256 ? q256 + (size_t)t * H : nullptr,
+                  q256 ? s256 + (size_t)t * nkb : nullptr);
 }
 
 // The expert's input to its down matrix, one block per entry: h = silu(g) * u (src/model_fwd.c:43, 859-862, 925,
@@ -91,8 +88,8 @@ __global__ void __launch_bounds__(256) act_quant_x_kernel(const float *__restric
 __global__ void __launch_bounds__(128) swiglu_quant_kernel(const float *__restrict__ GU, int FF, int n_entries,
                                                            const int32_t *__restrict__ eexp, const int32_t *__restrict__ upath,
                                                            int rot, uint32_t seed, float norm, int8_t *__restrict__ q64,
-                                                           float *__restrict__ s64, float *__restrict__ b64,
-                                                           int8_t *__restrict__ q256, float *__restrict__ s256) {
+                                                           float2 *__restrict__ sb64, int8_t *__restrict__ q256,
+                                                           float *__restrict__ s256) {
     extern __shared__ float v[];
     const int pos = blockIdx.x;
     if (pos >= n_entries) return;
@@ -106,8 +103,8 @@ __global__ void __launch_bounds__(128) swiglu_quant_kernel(const float *__restri
     if (rot > 1) rotate_smem(v, FF, rot, seed, norm);
     const int ng = FF / kGroup, nkb = (FF + kKB - 1) / kKB;
     const bool gemm = upath[eexp[pos]] != 0;
-    if (gemm) quantize_smem(v, FF, nullptr, nullptr, nullptr, q256 + (size_t)pos * FF, s256 + (size_t)pos * nkb);
-    else quantize_smem(v, FF, q64 + (size_t)pos * FF, s64 + (size_t)pos * ng, b64 + (size_t)pos * ng, nullptr, nullptr);
+    if (gemm) quantize_smem(v, FF, nullptr, nullptr, q256 + (size_t)pos * FF, s256 + (size_t)pos * nkb);
+    else quantize_smem(v, FF, q64 + (size_t)pos * FF, sb64 + (size_t)pos * ng, nullptr, nullptr);
 }
 
 // y[t][c] = (((0 + o[t,0][c]) + o[t,1][c]) + ...) in rank order (src/model_fwd.c:1033, 1134-1140)
@@ -125,18 +122,18 @@ __global__ void combine_kernel(const float *__restrict__ mo, int n, int H, int t
     }
 }
 
-int launch_act_quant_x(const float *X, int n, int H, int rot, uint32_t seed, int8_t *q64, float *s64, float *b64,
-                       int8_t *q256, float *s256, cudaStream_t st) {
+int launch_act_quant_x(const float *X, int n, int H, int rot, uint32_t seed, int8_t *q64, float2 *sb64, int8_t *q256,
+                       float *s256, cudaStream_t st) {
     const float norm = rot > 1 ? 1.0f / sqrtf((float)rot) : 1.0f;
-    act_quant_x_kernel<<<n, 256, H * sizeof(float), st>>>(X, n, H, rot, seed, norm, q64, s64, b64, q256, s256);
+    act_quant_x_kernel<<<n, 256, H * sizeof(float), st>>>(X, n, H, rot, seed, norm, q64, sb64, q256, s256);
     return 1;
 }
 
 int launch_swiglu_quant(const float *GU, int FF, int n_entries, const int32_t *eexp, const int32_t *upath, int rot,
-                        uint32_t seed, int8_t *q64, float *s64, float *b64, int8_t *q256, float *s256, cudaStream_t st) {
+                        uint32_t seed, int8_t *q64, float2 *sb64, int8_t *q256, float *s256, cudaStream_t st) {
     const float norm = rot > 1 ? 1.0f / sqrtf((float)rot) : 1.0f;
     swiglu_quant_kernel<<<n_entries, 128, FF * sizeof(float), st>>>(GU, FF, n_entries, eexp, upath, rot, seed, norm, q64,
-                                                                     s64, b64, q256, s256);
+                                                                     sb64, q256, s256);
     return 1;
 }
 

@@ -125,9 +125,84 @@ __global__ void __launch_bounds__(128) route_scatter_kernel(const int32_t *__res
     }
 }
 
+// Small calls (n <= 64): the whole dispatch in one block of E threads, thread e = expert e. Counting, the
+// first-touch key and the token-ordered scatter read the call's n * topk selections from shared memory.
+constexpr int kSmallRouteMax = 64;
+__global__ void __launch_bounds__(1024) route_small_kernel(const int32_t *__restrict__ sel, const float *__restrict__ w,
+                                                           int n, int topk, int E, int gu_items_per_unit,
+                                                           int dn_items_per_unit, int gemm_tn, RouteDev R,
+                                                           int32_t *__restrict__ upath, int32_t *__restrict__ eexp) {
+    __shared__ int32_t ss[kSmallRouteMax * kMaxTopK];
+    __shared__ int32_t sc[1024], su[1024], sd[1024], sg[1024], st[1024];
+    const int e = threadIdx.x, nk = n * topk;
+    for (int i = e; i < nk; i += blockDim.x) ss[i] = sel[i];
+    if (e == 0) R.meta[kMetaError] = kErrNone;  // this call's sticky error code starts clear
+    __syncthreads();
+    int c = 0, first = 0x7F7F7F7F;
+    if (e < E)
+        for (int i = 0; i < nk; i++)
+            if (ss[i] == e) { c++; first = min(first, i); }
+    if (e == 0)
+        for (int i = 0; i < nk; i++)
+            if (ss[i] < 0 || ss[i] >= E) set_error(R.meta, kErrBadExpert);
+    const int is_unit = c > 0;
+    const int is_dec = is_unit && (n <= 8 || c < kGemmMinT);
+    const int is_gemm = is_unit && !is_dec;
+    const int tiles = is_gemm ? (c + gemm_tn - 1) / gemm_tn : 0;
+    sc[e] = c; su[e] = is_unit; sd[e] = is_dec; sg[e] = is_gemm; st[e] = tiles;
+    __syncthreads();
+    for (int o = 1; o < blockDim.x; o <<= 1) {
+        int a = 0, b = 0, d = 0, g = 0, h = 0;
+        if (e >= o) { a = sc[e - o]; b = su[e - o]; d = sd[e - o]; g = sg[e - o]; h = st[e - o]; }
+        __syncthreads();
+        if (e >= o) { sc[e] += a; su[e] += b; sd[e] += d; sg[e] += g; st[e] += h; }
+        __syncthreads();
+    }
+    if (e < E) {
+        const int off = sc[e] - c;
+        R.cnt[e] = c;
+        R.off[e] = off;
+        R.first[e] = first;
+        if (e == E - 1) R.off[E] = sc[e];
+        upath[e] = is_gemm;
+        if (is_unit) R.units[su[e] - 1] = e;
+        if (is_dec) R.dec_units[sd[e] - 1] = e;
+        if (is_gemm) {
+            R.gemm_units[sg[e] - 1] = e;
+            const int base = st[e] - tiles;
+            for (int i = 0; i < tiles; i++) R.gemm_tiles[base + i] = ((sg[e] - 1) << 16) | i;
+        }
+        int pos = off;  // scan in (token, k) order: tokens ascending inside the expert's list
+        for (int i = 0; i < nk && pos < off + c; i++)
+            if (ss[i] == e) {
+                R.etok[pos] = i / topk;
+                R.eslot[pos] = i;
+                R.ew[pos] = w[i];
+                eexp[pos] = e;
+                pos++;
+            }
+    }
+    if (e == blockDim.x - 1) {
+        R.meta[kMetaNUnits] = su[e];
+        R.meta[kMetaNDec] = sd[e];
+        R.meta[kMetaNGemm] = sg[e];
+        R.meta[kMetaDecItemsGU] = sd[e] * gu_items_per_unit;
+        R.meta[kMetaDecItemsDN] = sd[e] * dn_items_per_unit;
+        R.meta[kMetaGemmTilesGU] = st[e];
+        R.meta[kMetaGemmTilesDN] = st[e];
+        if (sc[e] != nk) set_error(R.meta, kErrOverflow);
+    }
+}
+
 int launch_route(const RouteDev &R, int nchunk, int gu_items_per_unit, int dn_items_per_unit, int gemm_tn,
                  int32_t *upath, int32_t *eexp, cudaStream_t st) {
     const int n = R.n, topk = R.topk, E = R.E;
+    if (n <= kSmallRouteMax) {
+        const int threads = (E + 31) / 32 * 32;
+        route_small_kernel<<<1, threads, 0, st>>>(R.sel, R.w, n, topk, E, gu_items_per_unit, dn_items_per_unit, gemm_tn,
+                                                  R, upath, eexp);
+        return 1;
+    }
     cudaMemsetAsync(R.ccnt, 0, sizeof(int32_t) * (size_t)nchunk * E, st);
     cudaMemsetAsync(R.first, 0x7F, sizeof(int32_t) * (size_t)E, st);
     cudaMemsetAsync(R.meta, 0, sizeof(int32_t) * 16, st);

@@ -33,53 +33,143 @@ __global__ void router_repack_kernel(const uint16_t *__restrict__ W, uint4 *__re
 
 __device__ __forceinline__ float h2f(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)bits16)); }
 
-// logits[t][e] (+ bias[e]) for a tile of TT tokens per block.y and 4*warps experts per block.x.
-// Shared: x of the tile transposed to [tt][l][S + 4] so a thread reads its lane's chain steps contiguously (the pad
-// of 4 floats puts the 8 lanes of an expert on distinct banks).
+// x tile of TT tokens -> shared [tt][l][S + 4] (lane-major: a thread reads its chain steps contiguously; the pad of 4
+// floats puts the 8 lanes of an expert on distinct banks). float4 global loads, all in flight together.
 template <int TT>
-__global__ void __launch_bounds__(256) router_logits_kernel(const uint4 *__restrict__ Wr, const float *__restrict__ X,
-                                                             int n, int H, int E, const float *__restrict__ bias,
-                                                             float *__restrict__ logits) {
-    extern __shared__ float xs[];  // [TT][8][S + 4]
-    const int S = H / 8, SC = S / 8, SP = S + 4;
-    const int t0 = blockIdx.y * TT;
-    const int nt = min(TT, n - t0);
-    for (int i = threadIdx.x; i < TT * H; i += blockDim.x) {
-        const int tt = i / H, k = i % H;
-        const float v = tt < nt ? X[(size_t)(t0 + tt) * H + k] : 0.0f;
-        xs[(size_t)tt * 8 * SP + (k & 7) * SP + (k >> 3)] = v;
+__device__ __forceinline__ void stage_x(float *xs, const float *__restrict__ X, int t0, int nt, int H) {
+    const int S = H / 8, SP = S + 4, H4 = H / 4;
+    for (int i = threadIdx.x; i < TT * H4; i += blockDim.x) {
+        const int tt = i / H4, k4 = i % H4;
+        const float4 v = tt < nt ? reinterpret_cast<const float4 *>(X + (size_t)(t0 + tt) * H)[k4]
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+        const int k = 4 * k4;  // k, k+1, k+2, k+3: lanes (k&7)..(k&7)+3 of step k>>3
+        float *d = xs + (size_t)tt * 8 * SP + (k & 7) * SP + (k >> 3);
+        d[0] = v.x; d[SP] = v.y; d[2 * SP] = v.z; d[3 * SP] = v.w;
     }
-    __syncthreads();
+}
+
+__device__ __forceinline__ void h8(const uint4 &v, float w[8]) {
+    w[0] = h2f(v.x & 0xFFFF); w[1] = h2f(v.x >> 16); w[2] = h2f(v.y & 0xFFFF); w[3] = h2f(v.y >> 16);
+    w[4] = h2f(v.z & 0xFFFF); w[5] = h2f(v.z >> 16); w[6] = h2f(v.w & 0xFFFF); w[7] = h2f(v.w >> 16);
+}
+
+// 8 chain steps of one (expert, lane) for one token: r = fma(w[s], x[s], r), s = 0..7 in order
+__device__ __forceinline__ float chain8(float r, const float w[8], const float *xp) {
+    const float4 a = reinterpret_cast<const float4 *>(xp)[0], b = reinterpret_cast<const float4 *>(xp)[1];
+    r = __fmaf_rn(w[0], a.x, r); r = __fmaf_rn(w[1], a.y, r); r = __fmaf_rn(w[2], a.z, r); r = __fmaf_rn(w[3], a.w, r);
+    r = __fmaf_rn(w[4], b.x, r); r = __fmaf_rn(w[5], b.y, r); r = __fmaf_rn(w[6], b.z, r); r = __fmaf_rn(w[7], b.w, r);
+    return r;
+}
+
+__device__ __forceinline__ void write_logit(float acc, int l, int tt, int nt, int t0, int e, int E,
+                                            const float *__restrict__ bias, float *__restrict__ logits) {
+    float s = hsum8_lanes(acc);
+    if (l == 0 && tt < nt && e < E) {
+        if (bias) s = __fadd_rn(s, bias[e]);  // test hook: logits[x] += bias[x] before the softmax
+        logits[(size_t)(t0 + tt) * E + e] = s;
+    }
+}
+
+// Few tokens: one thread per (expert, lane) and TT tokens, 4 experts per warp, warps per block = blockDim/32.
+// Latency-bound (2 MB of weights, chains of H/8 dependent FMAs): the weights of the next 8 chunks are loaded while
+// the current 8 are used.
+template <int TT>
+__global__ void __launch_bounds__(128) router_small_kernel(const uint4 *__restrict__ Wr, const float *__restrict__ X,
+                                                            int n, int H, int E, const float *__restrict__ bias,
+                                                            float *__restrict__ logits) {
+    extern __shared__ __align__(16) float xs[];
+    const int S = H / 8, SC = S / 8, SP = S + 4;
+    const int t0 = blockIdx.y * TT, nt = min(TT, n - t0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int eq = blockIdx.x * (blockDim.x >> 5) + warp;  // expert quad of this warp
+    const int eq = blockIdx.x * (blockDim.x >> 5) + warp;
     const int e = eq * 4 + (lane >> 3), l = lane & 7;
-    if (eq * 4 >= E) return;
+    const uint4 *wp = Wr + (size_t)eq * SC * 32 + lane;
+    uint4 cur[8], nxt[8];
+    const bool live = eq * 4 < E;
+#pragma unroll
+    for (int j = 0; j < 8; j++) cur[j] = live && j < SC ? __ldg(wp + (size_t)j * 32) : make_uint4(0, 0, 0, 0);
+    stage_x<TT>(xs, X, t0, nt, H);
+    __syncthreads();
+    if (!live) return;
     float acc[TT];
 #pragma unroll
     for (int tt = 0; tt < TT; tt++) acc[tt] = 0.0f;
-    const uint4 *wp = Wr + (size_t)eq * SC * 32 + lane;
-    for (int jc = 0; jc < SC; jc++) {
-        const uint4 v = __ldg(wp + (size_t)jc * 32);
-        float w[8];
-        w[0] = h2f(v.x & 0xFFFF); w[1] = h2f(v.x >> 16); w[2] = h2f(v.y & 0xFFFF); w[3] = h2f(v.y >> 16);
-        w[4] = h2f(v.z & 0xFFFF); w[5] = h2f(v.z >> 16); w[6] = h2f(v.w & 0xFFFF); w[7] = h2f(v.w >> 16);
+    for (int g0 = 0; g0 < SC; g0 += 8) {
 #pragma unroll
-        for (int tt = 0; tt < TT; tt++) {
-            const float4 *xp = reinterpret_cast<const float4 *>(xs + (size_t)tt * 8 * SP + l * SP + jc * 8);
-            const float4 a = xp[0], b = xp[1];
-            float r = acc[tt];
-            r = __fmaf_rn(w[0], a.x, r); r = __fmaf_rn(w[1], a.y, r); r = __fmaf_rn(w[2], a.z, r); r = __fmaf_rn(w[3], a.w, r);
-            r = __fmaf_rn(w[4], b.x, r); r = __fmaf_rn(w[5], b.y, r); r = __fmaf_rn(w[6], b.z, r); r = __fmaf_rn(w[7], b.w, r);
-            acc[tt] = r;
+        for (int j = 0; j < 8; j++)
+            nxt[j] = g0 + 8 + j < SC ? __ldg(wp + (size_t)(g0 + 8 + j) * 32) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            if (g0 + j < SC) {
+                float w[8];
+                h8(cur[j], w);
+#pragma unroll
+                for (int tt = 0; tt < TT; tt++)
+                    acc[tt] = chain8(acc[tt], w, xs + (size_t)tt * 8 * SP + l * SP + (g0 + j) * 8);
+            }
         }
+#pragma unroll
+        for (int j = 0; j < 8; j++) cur[j] = nxt[j];
     }
 #pragma unroll
-    for (int tt = 0; tt < TT; tt++) {
-        float s = hsum8_lanes(acc[tt]);
-        if (l == 0 && tt < nt && e < E) {
-            if (bias) s = __fadd_rn(s, bias[e]);  // test hook: logits[x] += bias[x] before the softmax
-            logits[(size_t)(t0 + tt) * E + e] = s;
+    for (int tt = 0; tt < TT; tt++) write_logit(acc[tt], l, tt, nt, t0, e, E, bias, logits);
+}
+
+// Many tokens: FMA-bound (4.3 G FMA at 4096 tokens). Thread = (lane l, 2 experts from two quads, 8 tokens): each
+// 16-byte shared load of x (4 chain steps of one token) feeds 8 FMAs; the next chunk's weights load during the FMAs.
+// Block = 8 warps = 16 expert quads = 64 experts; grid = (E / 64, n / 8).
+constexpr int kLT = 8;
+__global__ void __launch_bounds__(256) router_large_kernel(const uint4 *__restrict__ Wr, const float *__restrict__ X,
+                                                           int n, int H, int E, const float *__restrict__ bias,
+                                                           float *__restrict__ logits) {
+    extern __shared__ __align__(16) float xs[];
+    const int S = H / 8, SC = S / 8, SP = S + 4;
+    const int t0 = blockIdx.y * kLT, nt = min(kLT, n - t0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, l = lane & 7;
+    const int qa = blockIdx.x * 16 + warp * 2, qb = qa + 1;  // the warp's two expert quads
+    const int ea = qa * 4 + (lane >> 3), eb = qb * 4 + (lane >> 3);
+    const bool live = qb * 4 < E + 4 && qa * 4 < E;
+    const uint4 *wa = Wr + (size_t)qa * SC * 32 + lane, *wb = Wr + (size_t)qb * SC * 32 + lane;
+    const bool hasb = qb * 4 < E;
+    uint4 ca = live ? __ldg(wa) : make_uint4(0, 0, 0, 0), cb = hasb ? __ldg(wb) : make_uint4(0, 0, 0, 0);
+    stage_x<kLT>(xs, X, t0, nt, H);
+    __syncthreads();
+    if (!live) return;
+    float A[kLT], B[kLT];
+#pragma unroll
+    for (int tt = 0; tt < kLT; tt++) { A[tt] = 0.0f; B[tt] = 0.0f; }
+    for (int jc = 0; jc < SC; jc++) {
+        uint4 na = make_uint4(0, 0, 0, 0), nb = make_uint4(0, 0, 0, 0);
+        if (jc + 1 < SC) {
+            na = __ldg(wa + (size_t)(jc + 1) * 32);
+            if (hasb) nb = __ldg(wb + (size_t)(jc + 1) * 32);
         }
+        float w1[8], w2[8];
+        h8(ca, w1);
+        h8(cb, w2);
+#pragma unroll
+        for (int tt = 0; tt < kLT; tt++) {
+            const float *xp = xs + (size_t)tt * 8 * SP + l * SP + jc * 8;
+            const float4 a = reinterpret_cast<const float4 *>(xp)[0], b = reinterpret_cast<const float4 *>(xp)[1];
+            float r = A[tt], q = B[tt];
+            r = __fmaf_rn(w1[0], a.x, r); q = __fmaf_rn(w2[0], a.x, q);
+            r = __fmaf_rn(w1[1], a.y, r); q = __fmaf_rn(w2[1], a.y, q);
+            r = __fmaf_rn(w1[2], a.z, r); q = __fmaf_rn(w2[2], a.z, q);
+            r = __fmaf_rn(w1[3], a.w, r); q = __fmaf_rn(w2[3], a.w, q);
+            r = __fmaf_rn(w1[4], b.x, r); q = __fmaf_rn(w2[4], b.x, q);
+            r = __fmaf_rn(w1[5], b.y, r); q = __fmaf_rn(w2[5], b.y, q);
+            r = __fmaf_rn(w1[6], b.z, r); q = __fmaf_rn(w2[6], b.z, q);
+            r = __fmaf_rn(w1[7], b.w, r); q = __fmaf_rn(w2[7], b.w, q);
+            A[tt] = r;
+            B[tt] = q;
+        }
+        ca = na;
+        cb = nb;
+    }
+#pragma unroll
+    for (int tt = 0; tt < kLT; tt++) {
+        write_logit(A[tt], l, tt, nt, t0, ea, E, bias, logits);
+        if (hasb) write_logit(B[tt], l, tt, nt, t0, eb, E, bias, logits);
     }
 }
 
@@ -186,26 +276,28 @@ void launch_router_repack(const uint16_t *W, uint4 *Wr, int E, int H, cudaStream
 static size_t router_smem(int TT, int H) { return (size_t)TT * 8 * (H / 8 + 4) * sizeof(float); }
 
 void router_set_attributes(int H) {
-    cudaFuncSetAttribute(router_logits_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_smem(16, H));
-    cudaFuncSetAttribute(router_logits_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_smem(4, H));
+    cudaFuncSetAttribute(router_large_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_smem(kLT, H));
+    cudaFuncSetAttribute(router_small_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_smem(4, H));
+    cudaFuncSetAttribute(router_small_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_smem(2, H));
 }
 
 int launch_router_logits(const uint4 *Wr, const float *X, int n, int H, int E, const float *bias, float *logits,
                          cudaStream_t st) {
-    // few tokens: spread the 2 MB router over many SMs (one warp = 4 experts per block); many tokens: 16 tokens
-    // per thread so each weight load feeds 16 FMA chains
-    if (n <= 4) {
+    // few tokens: one warp (4 experts) per block so the 2 MB router spreads over every SM; many tokens: 64 experts
+    // x 8 tokens per block, FMA-bound
+    if (n <= 2) {
         dim3 grid(E / 4, n);
-        router_logits_kernel<1><<<grid, 32, router_smem(1, H), st>>>(Wr, X, n, H, E, bias, logits);
-        return 1;
+        router_small_kernel<1><<<grid, 32, router_smem(1, H), st>>>(Wr, X, n, H, E, bias, logits);
+    } else if (n <= 8) {
+        dim3 grid(E / 4, (n + 1) / 2);
+        router_small_kernel<2><<<grid, 32, router_smem(2, H), st>>>(Wr, X, n, H, E, bias, logits);
+    } else if (n <= 64) {
+        dim3 grid(E / 8, (n + 3) / 4);
+        router_small_kernel<4><<<grid, 64, router_smem(4, H), st>>>(Wr, X, n, H, E, bias, logits);
+    } else {
+        dim3 grid((E + 63) / 64, (n + kLT - 1) / kLT);
+        router_large_kernel<<<grid, 256, router_smem(kLT, H), st>>>(Wr, X, n, H, E, bias, logits);
     }
-    if (n <= 64) {
-        dim3 grid(E / 16, (n + 3) / 4);
-        router_logits_kernel<4><<<grid, 128, router_smem(4, H), st>>>(Wr, X, n, H, E, bias, logits);
-        return 1;
-    }
-    dim3 grid(E / 32, (n + 15) / 16);
-    router_logits_kernel<16><<<grid, 256, router_smem(16, H), st>>>(Wr, X, n, H, E, bias, logits);
     return 1;
 }
 
