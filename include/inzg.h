@@ -62,6 +62,7 @@ typedef struct {
 #define INZG_DUMP_ROUTE 2u  /* keep the routing products of this call for inzg_moe_route_dump */
 #define INZG_PROFILE 4u     /* time every stage with CUDA events on the call's stream; the call then synchronises */
 #define INZG_NO_GRAPH 8u    /* launch the kernels one by one instead of replaying the cached CUDA graph */
+#define INZG_GEMM_SIMT 16u  /* prefill-path experts on the CUDA-core int8 GEMM instead of tcgen05 (cross-check) */
 
 /* stages timed under INZG_PROFILE (the reference's diag stages are coarser: DG_ROUTER, DG_EXPERT_*) */
 #define INZG_N_STAGES 10

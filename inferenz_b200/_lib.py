@@ -10,7 +10,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libinzg.so")
 
 T_F16, T_Q4L, T_Q8G = 1, 102, 103
-IO_DEVICE, DUMP_ROUTE, PROFILE, NO_GRAPH = 1, 2, 4, 8
+IO_DEVICE, DUMP_ROUTE, PROFILE, NO_GRAPH, GEMM_SIMT = 1, 2, 4, 8, 16
 N_STAGES = 10
 
 STATUS = {0: "INZG_OK", 1: "INZG_BAD_ARG", 2: "INZG_CORRUPT_BLOB", 3: "INZG_OOM", 4: "INZG_CUDA", 5: "INZG_NCCL",

@@ -34,11 +34,18 @@ struct QHeader {  // src/quant.h:40-50
 };
 static_assert(sizeof(QHeader) == 64, "header is 64 bytes");
 
+struct TmaMap {
+    alignas(64) unsigned char bytes[128];  // a CUtensorMap, opaque here
+};
+
 struct LayerSlot {
     bool has_router = false, has_experts = false;
+    bool has_maps = false;
+    TmaMap map_gu, map_dn;      // TMA maps over the prefill-path int8 weights
     uint4 *router = nullptr;
     uint8_t *pool = nullptr;
     uint8_t *luts = nullptr;
+    uint8_t *gemm_w = nullptr;  // one allocation: w8_gu | w8_dn | ws_gu | ws_dn
     LayerDev dev{};
 };
 
@@ -59,9 +66,8 @@ MatLayout make_layout(int type, int rows, int cols) {
     m.rows = rows;
     m.cols = cols;
     m.ng = cols / kGroup;
-    m.wb = type == INZG_T_Q8G ? 8 : 4;
-    m.gc = pick_gc(m.ng, m.wb);
-    m.nch = m.ng / m.gc;
+    m.gd = (m.ng + 3) / 4;
+    m.wb = type == INZG_T_Q8G ? 32 : 16;
     return m;
 }
 
@@ -81,15 +87,19 @@ struct inzg_ctx {
     int32_t *sel = nullptr;
     float *w = nullptr;
     int8_t *xq64 = nullptr, *xq256 = nullptr;
-    float2 *xsb64 = nullptr;
+    int2 *xsb64 = nullptr;
     float *xs256 = nullptr;
     int32_t *cnt = nullptr, *off = nullptr, *first = nullptr, *etok = nullptr, *eslot = nullptr, *ccnt = nullptr;
     int32_t *units = nullptr, *meta = nullptr, *dec_units = nullptr, *gemm_units = nullptr, *gemm_tiles = nullptr;
     int32_t *upath = nullptr, *eexp = nullptr;
     float *ew = nullptr, *GU = nullptr, *mo = nullptr;
     int8_t *dq64 = nullptr, *dq256 = nullptr;
-    float2 *dsb64 = nullptr;
+    int2 *dsb64 = nullptr;
     float *ds256 = nullptr;
+    int8_t *xqe = nullptr;      // prefill-path token activations in entry order [n*topk][H]
+    float *xse = nullptr;       // their block scales [n*topk][H/256]
+    TmaMap map_xqe, map_dq;     // TMA maps over xqe and dq256
+    bool have_tc = false;
     int last_n = 0;
     bool last_dump = false;
     // per-stage profile
@@ -159,7 +169,7 @@ static void free_scratch(inzg_ctx *c) {
     void *ptrs[] = {c->xin, c->y, c->logits, c->probs, c->bias, c->sel, c->w, c->xq64, c->xq256, c->xsb64,
                     c->xs256, c->cnt, c->off, c->first, c->etok, c->eslot, c->ccnt, c->units, c->meta, c->dec_units,
                     c->gemm_units, c->gemm_tiles, c->upath, c->eexp, c->ew, c->GU, c->mo, c->dq64, c->dq256, c->dsb64,
-                    c->ds256};
+                    c->ds256, c->xqe, c->xse};
     for (void *p : ptrs)
         if (p) cudaFree(p);
 }
@@ -205,7 +215,7 @@ inzg_ctx *inzg_create(const inzg_config *cfg, inzg_status *status) {
     c->w = dalloc<float>(NE, ok);
     c->xq64 = dalloc<int8_t>(T * H, ok);
     c->xq256 = dalloc<int8_t>(T * H, ok);
-    c->xsb64 = dalloc<float2>(T * H / kGroup, ok);
+    c->xsb64 = dalloc<int2>(T * H / kGroup, ok);
     c->xs256 = dalloc<float>(T * nkbH, ok);
     c->cnt = dalloc<int32_t>(E, ok);
     c->off = dalloc<int32_t>(E + 1, ok);
@@ -225,8 +235,10 @@ inzg_ctx *inzg_create(const inzg_config *cfg, inzg_status *status) {
     c->mo = dalloc<float>(NE * H, ok);
     c->dq64 = dalloc<int8_t>(NE * FF, ok);
     c->dq256 = dalloc<int8_t>(NE * FF, ok);
-    c->dsb64 = dalloc<float2>(NE * FF / kGroup, ok);
+    c->dsb64 = dalloc<int2>(NE * FF / kGroup, ok);
     c->ds256 = dalloc<float>(NE * nkbF, ok);
+    c->xqe = dalloc<int8_t>(NE * H, ok);
+    c->xse = dalloc<float>(NE * nkbH, ok);
     if (!ok) {
         free_scratch(c);
         cudaStreamDestroy(c->stream);
@@ -236,6 +248,8 @@ inzg_ctx *inzg_create(const inzg_config *cfg, inzg_status *status) {
     }
     router_set_attributes(cfg->hidden);
     gemv_set_attributes();
+    gemm_tc_set_attributes();
+    c->have_tc = make_tma_map_i8(c->map_xqe.bytes, c->xqe, NE, H, 128) && make_tma_map_i8(c->map_dq.bytes, c->dq256, NE, FF, 128);
     for (int i = 0; i <= INZG_N_STAGES; i++) cudaEventCreate(&c->ev[i]);
     cudaStreamCreateWithFlags(&c->capture_stream, cudaStreamNonBlocking);
     st = INZG_OK;
@@ -330,18 +344,21 @@ inzg_status inzg_pool_add_layer(inzg_ctx *c, int layer, int type, const void *bl
     D.E = E;
     D.gu = make_layout(type, 2 * FF, H);
     D.dn = make_layout(type, H, FF);
+    if (D.gu.rows % 16 || D.dn.rows % 16)
+        return fail(c, INZG_UNSUPPORTED, "pool_add_layer: matrix rows must be a multiple of 16");
     const uint64_t gb = type == INZG_T_Q8G ? 64 : 32;
     D.gu.q_off = 0;
     D.gu.d_off = align_up(D.gu.q_off + (uint64_t)D.gu.rows * D.gu.ng * gb, 256);
-    D.dn.q_off = align_up(D.gu.d_off + (uint64_t)D.gu.rows * D.gu.ng * 2, 256);
+    D.dn.q_off = align_up(D.gu.d_off + (uint64_t)D.gu.rows * D.gu.gd * 4 * 2, 256);
     D.dn.d_off = align_up(D.dn.q_off + (uint64_t)D.dn.rows * D.dn.ng * gb, 256);
-    D.slab_bytes = align_up(D.dn.d_off + (uint64_t)D.dn.rows * D.dn.ng * 2, 256);
+    D.slab_bytes = align_up(D.dn.d_off + (uint64_t)D.dn.rows * D.dn.gd * 4 * 2, 256);
     D.gu_rot = h0g.rot_block;
     D.gu_seed = h0g.rot_seed;
     D.dn_rot = h0d.rot_block;
     D.dn_seed = h0d.rot_seed;
     if (L.pool) { cudaFree(L.pool); L.pool = nullptr; }
     if (L.luts) { cudaFree(L.luts); L.luts = nullptr; }
+    if (L.gemm_w) { cudaFree(L.gemm_w); L.gemm_w = nullptr; }
     L.has_experts = false;
     if (cudaMalloc(&L.pool, D.slab_bytes * E) != cudaSuccess || cudaMalloc(&L.luts, (size_t)E * 32) != cudaSuccess) {
         cudaGetLastError();
@@ -349,6 +366,20 @@ inzg_status inzg_pool_add_layer(inzg_ctx *c, int layer, int type, const void *bl
     }
     D.pool = L.pool;
     D.luts = L.luts;
+    {   // prefill-path copy: int8 weights + block scales
+        const uint64_t ngu = (uint64_t)E * 2 * FF * H, ndn = (uint64_t)E * H * FF;
+        const uint64_t sgu = (uint64_t)E * 2 * FF * ((H + kKB - 1) / kKB), sdn = (uint64_t)E * H * ((FF + kKB - 1) / kKB);
+        const uint64_t o_dn = align_up(ngu, 256), o_sgu = align_up(o_dn + ndn, 256), o_sdn = align_up(o_sgu + 4 * sgu, 256);
+        if (cudaMalloc(&L.gemm_w, o_sdn + 4 * sdn) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(c, INZG_OOM, "pool_add_layer: prefill weight allocation");
+        }
+        D.w8_gu = reinterpret_cast<int8_t *>(L.gemm_w);
+        D.w8_dn = reinterpret_cast<int8_t *>(L.gemm_w + o_dn);
+        D.ws_gu = reinterpret_cast<float *>(L.gemm_w + o_sgu);
+        D.ws_dn = reinterpret_cast<float *>(L.gemm_w + o_sdn);
+    }
+    cudaMemsetAsync(L.pool, 0, D.slab_bytes * E, c->stream);  // scale padding past ng stays zero
     // stage blobs through a device buffer in chunks of experts and re-lay them out on the device
     const int chunk = std::min(E, 32);
     uint8_t *stage = nullptr;
@@ -360,11 +391,16 @@ inzg_status inzg_pool_add_layer(inzg_ctx *c, int layer, int type, const void *bl
     for (int e0 = 0; e0 < E && err == cudaSuccess; e0 += chunk) {
         const int ne = std::min(chunk, E - e0);
         err = cudaMemcpyAsync(stage, b + (size_t)e0 * blob_bytes, blob_bytes * ne, cudaMemcpyHostToDevice, c->stream);
-        if (err == cudaSuccess) launch_pool_repack(stage, blob_bytes, gu_bytes, e0, ne, D, L.pool, L.luts, c->stream);
+        if (err == cudaSuccess) {
+            launch_pool_repack(stage, blob_bytes, gu_bytes, e0, ne, D, L.pool, L.luts, c->stream);
+            launch_pool_requant(stage, blob_bytes, gu_bytes, e0, ne, D, c->stream);
+        }
         if (err == cudaSuccess) err = cudaStreamSynchronize(c->stream);
     }
     cudaFree(stage);
     if (err != cudaSuccess) return cuda_fail(c, err, "pool_add_layer");
+    L.has_maps = make_tma_map_i8(L.map_gu.bytes, D.w8_gu, (uint64_t)E * 2 * FF, H, 128) &&
+                 make_tma_map_i8(L.map_dn.bytes, D.w8_dn, (uint64_t)E * H, FF, 128);
     err = cudaGetLastError();
     if (err != cudaSuccess) return cuda_fail(c, err, "pool_add_layer repack");
     L.has_experts = true;
@@ -376,7 +412,8 @@ inzg_status inzg_pool_add_layer(inzg_ctx *c, int layer, int type, const void *bl
 
 // Enqueue the whole layer on `st`. ev != nullptr: record ev[i] before stage i and ev[N] at the end.
 static int enqueue_forward(inzg_ctx *c, const LayerSlot &L, int n, const float *X, float *yd, const float *bias,
-                           const float *ovr, bool ovr_on_device, bool dump, cudaEvent_t *ev, cudaStream_t st) {
+                           const float *ovr, bool ovr_on_device, bool dump, bool simt_gemm, cudaEvent_t *ev,
+                           cudaStream_t st) {
     const inzg_config &cf = c->cfg;
     const int H = cf.hidden, E = cf.n_expert, K = cf.topk, FF = cf.ff;
     const int NE = n * K;
@@ -405,7 +442,10 @@ static int enqueue_forward(inzg_ctx *c, const LayerSlot &L, int n, const float *
     R.ew = c->ew; R.ccnt = c->ccnt; R.units = c->units; R.meta = c->meta; R.dec_units = c->dec_units;
     R.gemm_units = c->gemm_units; R.gemm_tiles = c->gemm_tiles;
     const int nchunk = (n + 31) / 32;
-    launches += launch_route(R, nchunk, D.gu.rows / 32, D.dn.rows / 32, gemm_token_tile(), c->upath, c->eexp, st);
+    const bool tc = !simt_gemm && c->have_tc && L.has_maps;
+    launches += launch_route(R, nchunk, D.gu.rows / 16, D.dn.rows / 16, gemm_token_tile(), c->upath, c->eexp, st);
+    const int nkbH = (H + kKB - 1) / kKB;
+    const int max_tiles = (NE + gemm_token_tile() - 1) / gemm_token_tile() + std::min(E, NE / kGemmMinT) + 1;
     mark(4);
     const int grid = c->num_sms * 4;
     const int maxt = n == 1 ? 1 : n <= 8 ? 8 : kGemmMinT - 1;
@@ -413,14 +453,27 @@ static int enqueue_forward(inzg_ctx *c, const LayerSlot &L, int n, const float *
     if (r1 < 0) return -1;
     launches += r1;
     mark(5);
-    if (any_gemm) launches += launch_gemm_v1(D, 0, R, c->xq256, c->xs256, c->GU, 2 * FF, grid, st);
+    if (any_gemm) {
+        if (tc) {
+            launches += launch_gather_gemm_rows(c->xq256, c->xs256, H, nkbH, c->etok, c->eexp, c->upath, NE, c->xqe,
+                                                c->xse, st);
+            launches += launch_gemm_tc(0, L.map_gu.bytes, c->map_xqe.bytes, D.ws_gu, 2 * FF, H, R, c->xse, c->GU,
+                                       2 * FF, max_tiles, st);
+        } else {
+            launches += launch_gemm_v1(D, 0, R, c->xq256, c->xs256, c->GU, 2 * FF, grid, st);
+        }
+    }
     mark(6);
     launches += launch_swiglu_quant(c->GU, FF, NE, c->eexp, c->upath, D.dn_rot, D.dn_seed, c->dq64, c->dsb64, c->dq256,
                                     c->ds256, st);
     mark(7);
     launches += launch_gemv_decode(D, 1, R, c->dq64, c->dsb64, c->mo, H, maxt, grid, st);
     mark(8);
-    if (any_gemm) launches += launch_gemm_v1(D, 1, R, c->dq256, c->ds256, c->mo, H, grid, st);
+    if (any_gemm) {
+        if (tc) launches += launch_gemm_tc(1, L.map_dn.bytes, c->map_dq.bytes, D.ws_dn, H, FF, R, c->ds256, c->mo, H,
+                                           max_tiles, st);
+        else launches += launch_gemm_v1(D, 1, R, c->dq256, c->ds256, c->mo, H, grid, st);
+    }
     mark(9);
     launches += launch_combine(c->mo, n, H, K, yd, c->num_sms, st);
     mark(10);
@@ -460,9 +513,10 @@ inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, fl
     float *yd = dev_io ? y : c->y;
     int launches = 0;
     if (profile || (flags & INZG_NO_GRAPH)) {
-        launches = enqueue_forward(c, L, n, X, yd, bias, ovr, dev_io, dump, profile ? c->ev : nullptr, st);
+        launches = enqueue_forward(c, L, n, X, yd, bias, ovr, dev_io, dump, flags & INZG_GEMM_SIMT,
+                                   profile ? c->ev : nullptr, st);
     } else {
-        inzg_ctx::GraphKey key{layer, n, X, yd, bias, ovr, flags & (INZG_IO_DEVICE | INZG_DUMP_ROUTE)};
+        inzg_ctx::GraphKey key{layer, n, X, yd, bias, ovr, flags & (INZG_IO_DEVICE | INZG_DUMP_ROUTE | INZG_GEMM_SIMT)};
         inzg_ctx::GraphEntry *g = nullptr;
         for (auto &ge : c->graphs)
             if (ge.key == key) g = &ge;
@@ -470,7 +524,7 @@ inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, fl
             cudaStream_t cs = c->capture_stream;
             e = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
             if (e != cudaSuccess) return cuda_fail(c, e, "moe_forward: begin capture");
-            const int nl = enqueue_forward(c, L, n, X, yd, bias, ovr, dev_io, dump, nullptr, cs);
+            const int nl = enqueue_forward(c, L, n, X, yd, bias, ovr, dev_io, dump, flags & INZG_GEMM_SIMT, nullptr, cs);
             cudaGraph_t graph = nullptr;
             e = cudaStreamEndCapture(cs, &graph);
             if (e != cudaSuccess || nl < 0) {
@@ -525,7 +579,7 @@ inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, fl
         if (meta[kMetaError] != kErrNone) {
             char msg[96];
             snprintf(msg, sizeof(msg), "moe_forward: device check failed (code %d)", meta[kMetaError]);
-            return fail(c, INZG_DEVICE_CHECK, msg);
+            return fail(c, meta[kMetaError] == kErrTimeout ? INZG_TIMEOUT : INZG_DEVICE_CHECK, msg);
         }
     }
     return INZG_OK;

@@ -15,25 +15,19 @@ constexpr int kGemmMinT = 12;  // experts with >= 12 tokens use the prefill nume
 constexpr int kMaxTopK = 16;
 
 // ---------------------------------------------------------------------------------------------------------------
-// Decode layout of one expert matrix (M rows x K cols, ng = K/64 groups).
-// A warp computes 4 rows x 8 "lanes"; lane l of a group owns the weights {4l..4l+3} and {32+4l..32+4l+3}, which is
-// exactly lane l of the reference's 8-wide VPDPBUSD accumulators (src/quant.c:767-875), so a thread reproduces the
-// reference's per-lane float accumulation. Per (row quad, chunk of gc groups): 4 rows x 8 lanes x gc x wb bytes,
-// wb = 4 (Q4L: 8 nibbles) or 8 (Q8G: 8 bytes); each thread loads its gc*wb bytes with one vector load and the warp's
-// load is one contiguous 128*gc*wb/4-byte segment. Scales: per (row quad, chunk): 4 rows x gc fp16.
-// Q4L words are re-packed so that bits 0-15 hold the 4 nibbles of weights 4l..4l+3 and bits 16-31 those of
-// 32+4l..32+4l+3 (one PRMT selector each).
+// Tile layout of one expert matrix (M rows x K cols, ng = K/64 groups), matched to the int8 MMA fragments
+// (mma.m16n8k32: thread (r = lane/4, t = lane%4) holds A[r][4t..4t+3], A[r+8][4t..], A[r][16+4t..], A[r+8][16+4t..]).
+// Weights: [M/16 row tiles][ng][32 lanes][wb bytes]. Q4L (wb = 16): lane (r, t) holds 4 words -- (row r, word t),
+//   (row r, word t+4), (row r+8, word t), (row r+8, word t+4) -- where word l of a row and group carries the nibbles
+//   of weights 4l..4l+3 in bits 0-15 and of 32+4l..32+4l+3 in bits 16-31 (one PRMT selector each). Q8G (wb = 32):
+//   lane (r, t) holds the byte quads c = t, t+4, t+8, t+12 of row r, then of row r+8.
+// Scales: [M/16][gd = ceil(ng/4)][8 rows r][4 groups][2] fp16 -- (d[r][g], d[r+8][g]) pairs, zero past ng.
+// A warp reads one 16-row x 64-column tile with one 512-byte (Q4L) or 1024-byte (Q8G) coalesced load.
 // ---------------------------------------------------------------------------------------------------------------
 struct MatLayout {
-    int rows, cols, ng, gc, wb, nch;  // nch = ng / gc chunks
-    uint64_t q_off, d_off;            // byte offsets of the weight and scale regions inside the expert's slab
+    int rows, cols, ng, gd, wb;
+    uint64_t q_off, d_off;  // byte offsets of the weight and scale regions inside the expert's slab
 };
-
-__host__ __device__ inline int pick_gc(int ng, int wb) {
-    for (int gc = 16 / wb; gc > 1; gc >>= 1)
-        if (ng % gc == 0) return gc;
-    return 1;
-}
 
 // Per-layer, per-matrix metadata shared by all experts of the layer (rotation) plus per-expert LUTs.
 struct LayerDev {
@@ -46,6 +40,9 @@ struct LayerDev {
     const uint8_t *pool;      // [E][slab_bytes]
     const uint8_t *luts;      // [E][2][16]: biased levels of gate|up, down
     const uint4 *router;      // repacked F16 router, see router layout in k_router.cu
+    // prefill path: requantized int8 weights (K-major rows) and per-(row, 256-block) scales
+    int8_t *w8_gu, *w8_dn;    // [E][2FF][H], [E][H][FF]
+    float *ws_gu, *ws_dn;     // [E][2FF][H/256], [E][H][ceil(FF/256)]
 };
 
 // Routing products of one forward call (device).
@@ -72,7 +69,7 @@ constexpr int kMetaNUnits = 0, kMetaNDec = 1, kMetaNGemm = 2, kMetaDecItemsGU = 
               kMetaGemmTilesGU = 5, kMetaGemmTilesDN = 6, kMetaError = 7;
 
 // device error codes (sticky, first one wins)
-constexpr int kErrNone = 0, kErrBadExpert = 1, kErrBadSlot = 2, kErrOverflow = 3;
+constexpr int kErrNone = 0, kErrBadExpert = 1, kErrBadSlot = 2, kErrOverflow = 3, kErrTimeout = 4;
 
 // ---------------------------------------------------------------------------------------------------------------
 // IEEE helpers with explicit rounding (no contraction, no fast math)

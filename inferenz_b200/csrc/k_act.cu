@@ -3,16 +3,17 @@
 // Rotation: signs x_i * rot_sign(seed, i), then the unnormalised Walsh-Hadamard butterflies a+b / a-b with
 // len = 1, 2, 4, ... inside each block, then * 1/sqrt(block) (src/quant.c:118-154). The butterfly network is the
 // reference's, stage by stage, so every element sees the same sequence of IEEE adds.
-// Decode numerics (src/quant.c:611-637): per 64-group s = amax/127, q = rne(x * (1/s)), bsum = s * sum(q). The
-// quantized bytes are stored in the "lane-pair" order the GEMV reads: inside a group, lane l's 8 bytes are
-// q[4l..4l+3] then q[32+4l..32+4l+3].
+// Decode numerics (src/quant.c:611-637): per 64-group s = amax/127, q = rne(x * (1/s)), and the group's sum of q
+// (the reference keeps bsum = s * sum(q); the GEMV removes the LUT bias with the exact integer sum instead). The
+// quantized bytes are stored in MMA B-fragment order: inside a group, thread t of a quad reads 16 bytes,
+// q[4t..4t+3], q[16+4t..], q[32+4t..], q[48+4t..].
 // Prefill numerics (src/quant.c:1407-1429): per 256-block (the last one partial) s = amax/127, q = lrint(x * (1/s)).
 #include "inzg_internal.h"
 #include "k_launch.h"
 
 namespace inzg {
 
-__device__ __forceinline__ int lane_pair_pos(int j) { return ((j & 31) >> 2) * 8 + (j >> 5) * 4 + (j & 3); }
+__device__ __forceinline__ int bfrag_pos(int j) { return ((j >> 2) & 3) * 16 + (j >> 4) * 4 + (j & 3); }
 
 // in-place rotation of v[0..n) in shared memory by the whole block; n % block == 0
 __device__ void rotate_smem(float *v, int n, int block, uint32_t seed, float norm) {
@@ -34,9 +35,9 @@ __device__ void rotate_smem(float *v, int n, int block, uint32_t seed, float nor
     __syncthreads();
 }
 
-// quantize v[0..n) (shared) by warps: 64-groups into q64 (lane-pair order) and sb64 = (scale, bias sum); and/or
-// 256-blocks into q256, s256
-__device__ void quantize_smem(const float *v, int n, int8_t *q64, float2 *sb64, int8_t *q256, float *s256) {
+// quantize v[0..n) (shared) by warps: 64-groups into q64 (B-fragment order) and sb64 = (scale bits, sum of q);
+// and/or 256-blocks into q256, s256
+__device__ void quantize_smem(const float *v, int n, int8_t *q64, int2 *sb64, int8_t *q256, float *s256) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     if (q64)
         for (int g = warp; g < n / kGroup; g += nw) {
@@ -48,9 +49,9 @@ __device__ void quantize_smem(const float *v, int n, int8_t *q64, float2 *sb64, 
             const int a = __float2int_rn(__fmul_rn(x0, inv)), b = __float2int_rn(__fmul_rn(x1, inv));
             int sum = a + b;
             for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            q64[g * kGroup + lane_pair_pos(lane)] = (int8_t)a;
-            q64[g * kGroup + lane_pair_pos(32 + lane)] = (int8_t)b;
-            if (lane == 0) sb64[g] = make_float2(s, __fmul_rn(s, (float)sum));
+            q64[g * kGroup + bfrag_pos(lane)] = (int8_t)a;
+            q64[g * kGroup + bfrag_pos(32 + lane)] = (int8_t)b;
+            if (lane == 0) sb64[g] = make_int2(__float_as_int(s), sum);
         }
     if (q256) {
         const int nkb = (n + kKB - 1) / kKB;
@@ -69,7 +70,7 @@ __device__ void quantize_smem(const float *v, int n, int8_t *q64, float2 *sb64, 
 
 // one block per token: x [n][H] -> decode activations (q64, s64, b64) and prefill activations (q256, s256)
 __global__ void __launch_bounds__(256) act_quant_x_kernel(const float *__restrict__ X, int n, int H, int rot, uint32_t seed,
-                                                          float norm, int8_t *__restrict__ q64, float2 *__restrict__ sb64,
+                                                          float norm, int8_t *__restrict__ q64, int2 *__restrict__ sb64,
                                                           int8_t *__restrict__ q256, float *__restrict__ s256) {
     extern __shared__ float v[];
     const int t = blockIdx.x;
@@ -88,7 +89,7 @@ __global__ void __launch_bounds__(256) act_quant_x_kernel(const float *__restric
 __global__ void __launch_bounds__(128) swiglu_quant_kernel(const float *__restrict__ GU, int FF, int n_entries,
                                                            const int32_t *__restrict__ eexp, const int32_t *__restrict__ upath,
                                                            int rot, uint32_t seed, float norm, int8_t *__restrict__ q64,
-                                                           float2 *__restrict__ sb64, int8_t *__restrict__ q256,
+                                                           int2 *__restrict__ sb64, int8_t *__restrict__ q256,
                                                            float *__restrict__ s256) {
     extern __shared__ float v[];
     const int pos = blockIdx.x;
@@ -122,7 +123,31 @@ __global__ void combine_kernel(const float *__restrict__ mo, int n, int H, int t
     }
 }
 
-int launch_act_quant_x(const float *X, int n, int H, int rot, uint32_t seed, int8_t *q64, float2 *sb64, int8_t *q256,
+// Prefill-path token activations in entry order (entries sorted by expert, then token), so a GEMM tile's tokens are
+// consecutive rows for TMA: qe[pos] = q[etok[pos]], se[pos] = s[etok[pos]] for entries of prefill-path experts.
+__global__ void gather_gemm_rows_kernel(const int8_t *__restrict__ q, const float *__restrict__ s, int K, int nkb,
+                                        const int32_t *__restrict__ etok, const int32_t *__restrict__ eexp,
+                                        const int32_t *__restrict__ upath, int n_entries, int8_t *__restrict__ qe,
+                                        float *__restrict__ se) {
+    const int K16 = K / 16;
+    for (int pos = blockIdx.x; pos < n_entries; pos += gridDim.x) {
+        if (!upath[eexp[pos]]) continue;  // uniform over the block
+        const int t = etok[pos];
+        const uint4 *src = reinterpret_cast<const uint4 *>(q + (size_t)t * K);
+        uint4 *dst = reinterpret_cast<uint4 *>(qe + (size_t)pos * K);
+        for (int i = threadIdx.x; i < K16; i += blockDim.x) dst[i] = src[i];
+        if (threadIdx.x < nkb) se[(size_t)pos * nkb + threadIdx.x] = s[(size_t)t * nkb + threadIdx.x];
+    }
+}
+
+int launch_gather_gemm_rows(const int8_t *q, const float *s, int K, int nkb, const int32_t *etok, const int32_t *eexp,
+                            const int32_t *upath, int n_entries, int8_t *qe, float *se, cudaStream_t st) {
+    const int blocks = n_entries < 4096 ? n_entries : 4096;
+    gather_gemm_rows_kernel<<<blocks, 128, 0, st>>>(q, s, K, nkb, etok, eexp, upath, n_entries, qe, se);
+    return 1;
+}
+
+int launch_act_quant_x(const float *X, int n, int H, int rot, uint32_t seed, int8_t *q64, int2 *sb64, int8_t *q256,
                        float *s256, cudaStream_t st) {
     const float norm = rot > 1 ? 1.0f / sqrtf((float)rot) : 1.0f;
     act_quant_x_kernel<<<n, 256, H * sizeof(float), st>>>(X, n, H, rot, seed, norm, q64, sb64, q256, s256);
@@ -130,7 +155,7 @@ int launch_act_quant_x(const float *X, int n, int H, int rot, uint32_t seed, int
 }
 
 int launch_swiglu_quant(const float *GU, int FF, int n_entries, const int32_t *eexp, const int32_t *upath, int rot,
-                        uint32_t seed, int8_t *q64, float2 *sb64, int8_t *q256, float *s256, cudaStream_t st) {
+                        uint32_t seed, int8_t *q64, int2 *sb64, int8_t *q256, float *s256, cudaStream_t st) {
     const float norm = rot > 1 ? 1.0f / sqrtf((float)rot) : 1.0f;
     swiglu_quant_kernel<<<n_entries, 128, FF * sizeof(float), st>>>(GU, FF, n_entries, eexp, upath, rot, seed, norm, q64,
                                                                      sb64, q256, s256);

@@ -1,0 +1,298 @@
+// k_gemm_tc.cu -- prefill-path grouped GEMM on the 5th-generation tensor cores (tcgen05.mma kind::i8), sm_100a.
+//
+// Numerics: the reference's prefill GEMM (inz_gemm_rows, src/quant.c:1615-1668). Per (row, 256-block) the weights are
+// the reference's requantized int8 (materialised once per layer at upload, k_pool.cu) with block scale ws; the token
+// is int8 per 256-block with scale xs (src/quant.c:1407-1429). The integer dot of one block is exact in int32 (the
+// tensor core accumulates s8 x s8 in s32), and the output is f = fma((float)dot_b, ws_b * xs_b, f) over the blocks
+// in order -- the reference's own float sequence, so a GEMM-path expert output is the reference's bits.
+//
+// Tile: 128 weight rows x 128 tokens of one expert per CTA; K in 128-byte halves (two per 256-block).
+//   warp 0      TMA producer: A (weights, [E*rows][K] int8) and B (tokens, [entries][K] int8) boxes of 128 x 128 bytes,
+//               128-byte swizzle, into a 4-stage ring (no multicast)
+//   warp 1      allocates 256 TMEM columns (two 128-column int32 accumulators), one lane issues 4 MMAs (K = 32) per
+//               half; tcgen05.commit frees the smem stage and, after a block's 8 MMAs, hands the accumulator over
+//   warps 2-5   epilogue: thread = weight row = TMEM lane; per block tcgen05.ld of its 128 int32 dots, the per-block
+//               FMA into 128 fp32 registers, then the accumulator is released; at the end the tile is written
+// Every mbarrier wait is bounded; on expiry the CTA records an error (INZG_TIMEOUT to the host), drains what it
+// issued, frees its TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "inzg_internal.h"
+#include "k_launch.h"
+
+namespace inzg {
+
+constexpr int TBM = 128, TBN = 128, TBK = 128, TSTAGES = 4;
+constexpr int kStageBytes = (TBM + TBN) * TBK;  // 32 KiB
+constexpr uint32_t kWaitLimit = 1u << 20;       // try_wait rounds before a wait is declared stuck
+
+struct TcShared {
+    uint64_t full[TSTAGES], empty[TSTAGES], acc_full[2], acc_empty[2], drain;
+    uint32_t tmem_base;
+    int abort;
+    float xs[TBN * 8];  // token block scales, [n][block] (K <= 2048: at most 8 blocks)
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+// bounded wait for the phase with parity `par` to complete; false if it did not within the limit (or aborted)
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t par, volatile int *abort) {
+    for (uint32_t i = 0; i < kWaitLimit; i++) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(b)), "r"(par)
+            : "memory");
+        if (ok) return true;
+        if ((i & 255) == 255 && *abort) return false;
+    }
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// K-major operand in shared memory, 128-byte swizzle: 8-row atoms of 1024 bytes, SBO = 1024 B, LBO unused (1)
+__device__ __forceinline__ uint64_t umma_desc(const void *smem) {
+    const uint64_t a = smem_u32(smem);
+    return ((a & 0x3FFFFull) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, int (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// instruction descriptor: s32 accumulate, s8 x s8, both K-major, N = TBN, M = TBM
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TBN >> 3) << 17) | ((uint32_t)(TBM >> 4) << 24);
+
+// KIND 0: gate|up, out = GU[entry][row]; KIND 1: down, out = moe_out[slot][row] = w * f.
+template <int KIND>
+__global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA,
+                                                         const __grid_constant__ CUtensorMap mapB,
+                                                         const float *__restrict__ wsc, int rows, int K,
+                                                         RouteDev R, const float *__restrict__ xs_e,
+                                                         float *__restrict__ out, int out_ld, int meta_tiles) {
+    extern __shared__ __align__(1024) uint8_t dyn[];
+    const int nrb = rows / TBM;
+    const int tile = blockIdx.x / nrb, rb = blockIdx.x % nrb;
+    if (tile >= R.meta[meta_tiles]) return;  // uniform over the CTA: nothing allocated yet
+    const int tv = R.gemm_tiles[tile];
+    const int e = R.gemm_units[tv >> 16], tt = tv & 0xFFFF;
+    const int base = R.off[e], ntok = R.cnt[e];
+    const int t0 = tt * TBN, nt = min(TBN, ntok - t0);
+    const int nkh = K / TBK, nkb = (K + kKB - 1) / kKB;
+    uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dyn) + 1023) & ~uintptr_t(1023));
+    TcShared &S = *reinterpret_cast<TcShared *>(ring + TSTAGES * kStageBytes);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    volatile int *abort = &S.abort;
+    __shared__ int never;  // drains ignore the abort flag: what was issued must land before the CTA leaves
+    if (threadIdx.x == 0) never = 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < TSTAGES; s++) {
+            mbar_init(&S.full[s], 1);
+            mbar_init(&S.empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&S.acc_full[b], 1);
+            mbar_init(&S.acc_empty[b], 128);
+        }
+        mbar_init(&S.drain, 1);
+        S.abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(&S.tmem_base)));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    if (warp >= 2) {  // token scales of the tile's tokens (zero past the expert's tokens)
+        for (int i = threadIdx.x - 64; i < TBN * nkb; i += 128) {
+            const int n = i / nkb, b = i % nkb;
+            S.xs[n * 8 + b] = n < nt ? xs_e[(size_t)(base + t0 + n) * nkb + b] : 0.0f;
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = S.tmem_base;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        int issued = 0;
+        if (lane == 0) {
+            const int arow = e * rows + rb * TBM, brow = base + t0;
+            for (int kh = 0; kh < nkh; kh++) {
+                const int s = kh % TSTAGES;
+                if (kh >= TSTAGES && !mbar_wait(&S.empty[s], ((kh / TSTAGES) - 1) & 1, abort)) {
+                    S.abort = 1;
+                    break;
+                }
+                uint8_t *stage = ring + s * kStageBytes;
+                mbar_expect_tx(&S.full[s], kStageBytes);
+                tma_load_2d(stage, &mapA, kh * TBK, arow, &S.full[s]);
+                tma_load_2d(stage + TBM * TBK, &mapB, kh * TBK, brow, &S.full[s]);
+                issued = kh + 1;
+            }
+            // drain: every issued copy has landed before the CTA may leave (bounded)
+            for (int kh = max(0, issued - TSTAGES); kh < issued; kh++)
+                mbar_wait(&S.full[kh % TSTAGES], (kh / TSTAGES) & 1, &never);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            bool ok = true;
+            for (int kh = 0; kh < nkh && ok; kh++) {
+                const int s = kh % TSTAGES, b = kh / 2, buf = b & 1;
+                const bool first_half = (kh & 1) == 0;
+                if (first_half && b >= 2 && !mbar_wait(&S.acc_empty[buf], ((b / 2) - 1) & 1, abort)) { ok = false; break; }
+                if (!mbar_wait(&S.full[s], (kh / TSTAGES) & 1, abort)) { ok = false; break; }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint8_t *stage = ring + s * kStageBytes;
+                const uint64_t da = umma_desc(stage), db = umma_desc(stage + TBM * TBK);
+                const uint32_t d = tmem + buf * TBN;
+#pragma unroll
+                for (int k = 0; k < TBK / 32; k++)  // 4 MMAs of K = 32 bytes; the descriptor start moves 32 B
+                    mma_i8(d, da + (uint64_t)(k * 2), db + (uint64_t)(k * 2), kIdesc, (first_half && k == 0) ? 0u : 1u);
+                mma_commit(&S.empty[s]);                                  // stage reusable once these MMAs finish
+                if (!first_half || kh == nkh - 1) mma_commit(&S.acc_full[buf]);  // block b's dot products are done
+            }
+            if (!ok) S.abort = 1;
+            // every MMA issued by this CTA has completed before TMEM and shared memory are released (bounded)
+            mma_commit(&S.drain);
+            mbar_wait(&S.drain, 0, &never);
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue: thread = weight row ----------------
+        const int sub = warp & 3;  // TMEM lanes 32*sub .. 32*sub+31
+        const int r = sub * 32 + lane, row = rb * TBM + r;
+        const float *wsr = wsc + ((size_t)e * rows + row) * nkb;
+        float f[TBN];
+#pragma unroll
+        for (int n = 0; n < TBN; n++) f[n] = 0.0f;
+        bool ok = true;
+        for (int b = 0; b < nkb && ok; b++) {
+            const int buf = b & 1;
+            if (!mbar_wait(&S.acc_full[buf], (b / 2) & 1, abort)) { ok = false; break; }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const float wsb = wsr[b];
+#pragma unroll
+            for (int c = 0; c < TBN / 32; c++) {
+                int v[32];
+                tmem_ld32(tmem + ((uint32_t)(sub * 32) << 16) + buf * TBN + c * 32, v);
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    const int n = c * 32 + j;
+                    f[n] = __fmaf_rn((float)v[j], __fmul_rn(wsb, S.xs[n * 8 + b]), f[n]);
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            mbar_arrive(&S.acc_empty[buf]);
+        }
+        if (!ok) S.abort = 1;
+        if (ok) {
+#pragma unroll
+            for (int n = 0; n < TBN; n++) {
+                if (n < nt) {
+                    const int pos = base + t0 + n;
+                    if (KIND == 0) out[(size_t)pos * out_ld + row] = f[n];
+                    else out[(size_t)R.eslot[pos] * out_ld + row] = __fmul_rn(R.ew[pos], f[n]);
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (S.abort && threadIdx.x == 0) atomicCAS(&R.meta[kMetaError], 0, kErrTimeout);
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void *p = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 2-D int8 map over [rows][cols] (row pitch = cols bytes) with 128 x 128-byte boxes and 128-byte swizzle
+bool make_tma_map_i8(void *map_out, const void *base, uint64_t rows, uint64_t cols, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn || cols % 16 || reinterpret_cast<uintptr_t>(base) % 16) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols};
+    const cuuint32_t box[2] = {(cuuint32_t)TBK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(reinterpret_cast<CUtensorMap *>(map_out), CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims,
+              strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+size_t gemm_tc_smem() { return (size_t)TSTAGES * kStageBytes + sizeof(TcShared) + 1024; }
+
+void gemm_tc_set_attributes() {
+    cudaFuncSetAttribute(gemm_tc_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_tc_smem());
+    cudaFuncSetAttribute(gemm_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_tc_smem());
+}
+
+// grid: an upper bound on (token tiles x row tiles); CTAs past the device-built tile count return at once
+int launch_gemm_tc(int kind, const void *mapA, const void *mapB, const float *wsc, int rows, int K, const RouteDev &R,
+                   const float *xs_e, float *out, int out_ld, int max_tiles, cudaStream_t st) {
+    if (rows % TBM || K % TBK || K > 8 * kKB) return -1;
+    const int mt = kind == 0 ? kMetaGemmTilesGU : kMetaGemmTilesDN;
+    const int grid = max_tiles * (rows / TBM);
+    const CUtensorMap &a = *reinterpret_cast<const CUtensorMap *>(mapA);
+    const CUtensorMap &b = *reinterpret_cast<const CUtensorMap *>(mapB);
+    if (kind == 0) gemm_tc_kernel<0><<<grid, 192, gemm_tc_smem(), st>>>(a, b, wsc, rows, K, R, xs_e, out, out_ld, mt);
+    else gemm_tc_kernel<1><<<grid, 192, gemm_tc_smem(), st>>>(a, b, wsc, rows, K, R, xs_e, out, out_ld, mt);
+    return 1;
+}
+
+int gemm_tc_token_tile() { return TBN; }
+
+}  // namespace inzg

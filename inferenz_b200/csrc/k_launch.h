@@ -16,19 +16,29 @@ int launch_softmax_topk(const float *logits, int n, int E, int topk, int32_t *se
 int launch_route(const RouteDev &R, int nchunk, int gu_items_per_unit, int dn_items_per_unit, int gemm_tn,
                  int32_t *upath, int32_t *eexp, cudaStream_t st);
 
-int launch_act_quant_x(const float *X, int n, int H, int rot, uint32_t seed, int8_t *q64, float2 *sb64, int8_t *q256,
+int launch_act_quant_x(const float *X, int n, int H, int rot, uint32_t seed, int8_t *q64, int2 *sb64, int8_t *q256,
                        float *s256, cudaStream_t st);
 int launch_swiglu_quant(const float *GU, int FF, int n_entries, const int32_t *eexp, const int32_t *upath, int rot,
-                        uint32_t seed, int8_t *q64, float2 *sb64, int8_t *q256, float *s256, cudaStream_t st);
+                        uint32_t seed, int8_t *q64, int2 *sb64, int8_t *q256, float *s256, cudaStream_t st);
 int launch_combine(const float *mo, int n, int H, int topk, float *y, int num_sms, cudaStream_t st);
 
 void gemv_set_attributes();
-int launch_gemv_decode(const LayerDev &L, int kind, const RouteDev &R, const int8_t *aq, const float2 *asb, float *out,
+int launch_gemv_decode(const LayerDev &L, int kind, const RouteDev &R, const int8_t *aq, const int2 *asb, float *out,
                        int out_ld, int maxt, int grid, cudaStream_t st);
 int launch_gemm_v1(const LayerDev &L, int kind, const RouteDev &R, const int8_t *aq, const float *as, float *out,
                    int out_ld, int grid, cudaStream_t st);
 int gemm_token_tile();
+bool make_tma_map_i8(void *map_out, const void *base, uint64_t rows, uint64_t cols, int box_rows);
+size_t gemm_tc_smem();
+void gemm_tc_set_attributes();
+int launch_gemm_tc(int kind, const void *mapA, const void *mapB, const float *wsc, int rows, int K, const RouteDev &R,
+                   const float *xs_e, float *out, int out_ld, int max_tiles, cudaStream_t st);
+int gemm_tc_token_tile();
+int launch_gather_gemm_rows(const int8_t *q, const float *s, int K, int nkb, const int32_t *etok, const int32_t *eexp,
+                            const int32_t *upath, int n_entries, int8_t *qe, float *se, cudaStream_t st);
 
+void launch_pool_requant(const uint8_t *blobs, uint64_t blob_bytes, uint64_t gu_bytes, int e0, int ne, const LayerDev &L,
+                         cudaStream_t st);
 void launch_pool_repack(const uint8_t *blobs, uint64_t blob_bytes, uint64_t gu_bytes, int e0, int ne,
                         const LayerDev &L, uint8_t *pool, uint8_t *luts, cudaStream_t st);
 

@@ -10,7 +10,7 @@ import ctypes
 
 import numpy as np
 
-from ._lib import (DUMP_ROUTE, IO_DEVICE, N_STAGES, NO_GRAPH, PROFILE, Config, InzgError, MoeOpts, Stats, T_Q4L,
+from ._lib import (DUMP_ROUTE, GEMM_SIMT, IO_DEVICE, N_STAGES, NO_GRAPH, PROFILE, Config, InzgError, MoeOpts, Stats, T_Q4L,
                    T_Q8G, lib)
 
 
@@ -63,14 +63,15 @@ class MoePool:
                     "pool_add_layer")
 
     # -- forward --
-    def moe_block(self, layer, xin, bias=None, logits_override=None, dump=False, y=None, graph=True):
+    def moe_block(self, layer, xin, bias=None, logits_override=None, dump=False, y=None, graph=True, simt_gemm=False):
         """y [n][H] = routed MoE layer of xin [n][H] (host arrays; copies in and out inside the call)."""
         x = np.ascontiguousarray(xin, dtype=np.float32)
         n = x.shape[0]
         y = np.empty_like(x) if y is None else y
         b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
         o = None if logits_override is None else np.ascontiguousarray(logits_override, dtype=np.float32)
-        opts = MoeOpts((DUMP_ROUTE if dump else 0) | (0 if graph else NO_GRAPH), None if b is None else b.ctypes.data,
+        flags = (DUMP_ROUTE if dump else 0) | (0 if graph else NO_GRAPH) | (GEMM_SIMT if simt_gemm else 0)
+        opts = MoeOpts(flags, None if b is None else b.ctypes.data,
                        None if o is None else o.ctypes.data, None)
         self._check(lib.inzg_moe_forward(self._ctx, layer, n, _ptr(x), _ptr(y), ctypes.byref(opts)), "moe_forward")
         return y
