@@ -187,8 +187,10 @@ def stage_roofline(stage_ms, stats, n, hbm):
         "gate_up_gemm": gemm * GU_PAYLOAD,
         "down_gemm": gemm * DN_PAYLOAD,
     }
-    dom = max(stage_ms, key=lambda k: stage_ms[k])
     total = sum(stage_ms.values())
+    if total <= 0:
+        return {"dominant": None, "stage_ms": {}, "share": {}}
+    dom = max(stage_ms, key=lambda k: stage_ms[k])
     share = {k: round(v / total, 4) for k, v in stage_ms.items() if v > 0}
     out = {"dominant": dom, "stage_ms": {k: round(v, 5) for k, v in stage_ms.items()}, "share": share}
     if dom in algo and stage_ms[dom] > 0:
@@ -227,6 +229,8 @@ def run_mine(args):
     plan = [("decode32", 32, args.steps, args.warmup)]
     if not args.headline_only:
         plan += [("decode1", 1, max(args.steps // 2, 10), args.warmup), ("prefill4096", 4096, max(args.steps // 50, 5), 3)]
+    if args.only:
+        plan = [p for p in plan if p[0] == args.only] or [(args.only, {"decode1": 1, "decode32": 32, "prefill4096": 4096}[args.only], args.steps, args.warmup)]
     clocks_summary = None
     for name, n, steps, warm in plan:
         x, bias, _ = make_inputs(name, n)
@@ -247,7 +251,7 @@ def run_mine(args):
             tt = torch.tensor([total_ms], dtype=torch.float64, device=dev)
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             total_ms = float(tt.item())
-        stage_ms, stats = profile_stages(pool, torch, x, bias, max(3, min(20, steps)), flush)
+        stage_ms, stats = profile_stages(pool, torch, x, bias, 0 if args.only else max(3, min(20, steps)), flush)
         roof = stage_roofline(stage_ms, stats, n, hbm)
         U = stats["units"]
         layer_bytes = ROUTER_BYTES + U * EXPERT_BYTES_Q4L + 2 * n * H * 4
@@ -262,12 +266,12 @@ def run_mine(args):
                                "unit": "GB/s", "frac": round(layer_bytes / (ms_step * 1e-3) / 1e9 / hbm, 4)},
             "stages": roof,
         }
-        if name == "decode32":
+        if name == "decode32" and not args.only:
             e2e_ts, h2d, d2h, _ = time_e2e(pool, torch, x, bias, max(steps // 4, 5), 3, flush)
             results[name]["e2e"] = {"value": round(n * len(e2e_ts) / (sum(e2e_ts) * 1e-3), 1), "unit": "tokens/s",
                                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                                     "ms_per_step": round(sum(e2e_ts) / len(e2e_ts), 5)}
-    head = results["decode32"]
+    head = results.get("decode32") or next(iter(results.values()))
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_reference("decode32", 32, budget_s=args.cpu_seconds, blobs=blobs, bb=bb, R=R)
@@ -370,6 +374,8 @@ def main():
     ap.add_argument("--headline-only", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--only", choices=["decode1", "decode32", "prefill4096"], default=None,
+                    help="time a single workload (profiling runs); the JSON line then reports that workload")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

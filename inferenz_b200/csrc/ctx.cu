@@ -87,14 +87,14 @@ struct inzg_ctx {
     int32_t *sel = nullptr;
     float *w = nullptr;
     int8_t *xq64 = nullptr, *xq256 = nullptr;
-    int2 *xsb64 = nullptr;
+    float2 *xsb64 = nullptr;
     float *xs256 = nullptr;
     int32_t *cnt = nullptr, *off = nullptr, *first = nullptr, *etok = nullptr, *eslot = nullptr, *ccnt = nullptr;
     int32_t *units = nullptr, *meta = nullptr, *dec_units = nullptr, *gemm_units = nullptr, *gemm_tiles = nullptr;
     int32_t *upath = nullptr, *eexp = nullptr;
     float *ew = nullptr, *GU = nullptr, *mo = nullptr;
     int8_t *dq64 = nullptr, *dq256 = nullptr;
-    int2 *dsb64 = nullptr;
+    float2 *dsb64 = nullptr;
     float *ds256 = nullptr;
     int8_t *xqe = nullptr;      // prefill-path token activations in entry order [n*topk][H]
     float *xse = nullptr;       // their block scales [n*topk][H/256]
@@ -125,9 +125,11 @@ struct inzg_ctx {
     std::vector<GraphEntry> graphs;
     uint64_t use_clock = 0;
     cudaStream_t capture_stream = nullptr;
+    cudaStream_t side = nullptr;            // branch for the input quantization, joined before the experts
+    cudaEvent_t fork = nullptr, join = nullptr;
 };
 
-static const char *kStageNames[INZG_N_STAGES] = {"router_logits", "softmax_topk", "act_quant", "route",
+static const char *kStageNames[INZG_N_STAGES] = {"router_logits", "softmax_topk_route", "act_quant", "route",
                                                  "gate_up_gemv", "gate_up_gemm", "swiglu_quant", "down_gemv",
                                                  "down_gemm", "combine"};
 
@@ -215,7 +217,7 @@ inzg_ctx *inzg_create(const inzg_config *cfg, inzg_status *status) {
     c->w = dalloc<float>(NE, ok);
     c->xq64 = dalloc<int8_t>(T * H, ok);
     c->xq256 = dalloc<int8_t>(T * H, ok);
-    c->xsb64 = dalloc<int2>(T * H / kGroup, ok);
+    c->xsb64 = dalloc<float2>(T * H / kGroup, ok);
     c->xs256 = dalloc<float>(T * nkbH, ok);
     c->cnt = dalloc<int32_t>(E, ok);
     c->off = dalloc<int32_t>(E + 1, ok);
@@ -235,7 +237,7 @@ inzg_ctx *inzg_create(const inzg_config *cfg, inzg_status *status) {
     c->mo = dalloc<float>(NE * H, ok);
     c->dq64 = dalloc<int8_t>(NE * FF, ok);
     c->dq256 = dalloc<int8_t>(NE * FF, ok);
-    c->dsb64 = dalloc<int2>(NE * FF / kGroup, ok);
+    c->dsb64 = dalloc<float2>(NE * FF / kGroup, ok);
     c->ds256 = dalloc<float>(NE * nkbF, ok);
     c->xqe = dalloc<int8_t>(NE * H, ok);
     c->xse = dalloc<float>(NE * nkbH, ok);
@@ -252,6 +254,10 @@ inzg_ctx *inzg_create(const inzg_config *cfg, inzg_status *status) {
     c->have_tc = make_tma_map_i8(c->map_xqe.bytes, c->xqe, NE, H, 128) && make_tma_map_i8(c->map_dq.bytes, c->dq256, NE, FF, 128);
     for (int i = 0; i <= INZG_N_STAGES; i++) cudaEventCreate(&c->ev[i]);
     cudaStreamCreateWithFlags(&c->capture_stream, cudaStreamNonBlocking);
+    cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking);
+    cudaEventCreateWithFlags(&c->fork, cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&c->join, cudaEventDisableTiming);
+    route_set_attributes(cfg->n_expert);
     st = INZG_OK;
     return c;
 }
@@ -269,6 +275,9 @@ void inzg_destroy(inzg_ctx *c) {
     for (int i = 0; i <= INZG_N_STAGES; i++)
         if (c->ev[i]) cudaEventDestroy(c->ev[i]);
     if (c->capture_stream) cudaStreamDestroy(c->capture_stream);
+    if (c->side) cudaStreamDestroy(c->side);
+    if (c->fork) cudaEventDestroy(c->fork);
+    if (c->join) cudaEventDestroy(c->join);
     free_scratch(c);
     cudaStreamDestroy(c->stream);
     delete c;
@@ -422,6 +431,16 @@ static int enqueue_forward(inzg_ctx *c, const LayerSlot &L, int n, const float *
     auto mark = [&](int i) {
         if (ev) cudaEventRecord(ev[i], st);
     };
+    const bool any_gemm = n > 8 && (int64_t)n * K >= kGemmMinT;
+    // the inputs' quantization (both numeric paths) depends on x only: a side branch when not profiling
+    const bool branch = ev == nullptr;
+    if (branch) {
+        cudaEventRecord(c->fork, st);
+        cudaStreamWaitEvent(c->side, c->fork, 0);
+        launches += launch_act_quant_x(X, n, H, D.gu_rot, D.gu_seed, c->xq64, c->xsb64, any_gemm ? c->xq256 : nullptr,
+                                       c->xs256, c->side);
+        cudaEventRecord(c->join, c->side);
+    }
     mark(0);
     if (ovr) {
         if (ovr_on_device)
@@ -430,26 +449,33 @@ static int enqueue_forward(inzg_ctx *c, const LayerSlot &L, int n, const float *
         launches += launch_router_logits(L.router, X, n, H, E, bias, c->logits, st);
     }
     mark(1);
-    launches += launch_softmax_topk(c->logits, n, E, K, c->sel, c->w, dump ? c->probs : nullptr, st);
-    mark(2);
-    const bool any_gemm = n > 8 && (int64_t)n * K >= kGemmMinT;
-    launches += launch_act_quant_x(X, n, H, D.gu_rot, D.gu_seed, c->xq64, c->xsb64, any_gemm ? c->xq256 : nullptr,
-                                   c->xs256, st);
-    mark(3);
     RouteDev R{};
     R.n = n; R.topk = K; R.E = E;
     R.sel = c->sel; R.w = c->w; R.cnt = c->cnt; R.off = c->off; R.first = c->first; R.etok = c->etok; R.eslot = c->eslot;
     R.ew = c->ew; R.ccnt = c->ccnt; R.units = c->units; R.meta = c->meta; R.dec_units = c->dec_units;
     R.gemm_units = c->gemm_units; R.gemm_tiles = c->gemm_tiles;
-    const int nchunk = (n + 31) / 32;
     const bool tc = !simt_gemm && c->have_tc && L.has_maps;
-    launches += launch_route(R, nchunk, D.gu.rows / 16, D.dn.rows / 16, gemm_token_tile(), c->upath, c->eexp, st);
+    const int fused = launch_route_fused(R, c->logits, dump ? c->probs : nullptr, gemv_items_per_unit(D, 0), gemv_items_per_unit(D, 1),
+                                         gemm_token_tile(), c->upath, c->eexp, st);
+    if (fused > 0) {
+        launches += fused;
+        mark(2);
+    } else {
+        launches += launch_softmax_topk(c->logits, n, E, K, c->sel, c->w, dump ? c->probs : nullptr, st);
+        mark(2);
+    }
+    if (!branch)
+        launches += launch_act_quant_x(X, n, H, D.gu_rot, D.gu_seed, c->xq64, c->xsb64, any_gemm ? c->xq256 : nullptr,
+                                       c->xs256, st);
+    mark(3);
+    const int nchunk = (n + 31) / 32;
+    if (fused <= 0) launches += launch_route(R, nchunk, gemv_items_per_unit(D, 0), gemv_items_per_unit(D, 1), gemm_token_tile(), c->upath, c->eexp, st);
     const int nkbH = (H + kKB - 1) / kKB;
     const int max_tiles = (NE + gemm_token_tile() - 1) / gemm_token_tile() + std::min(E, NE / kGemmMinT) + 1;
+    if (branch) cudaStreamWaitEvent(st, c->join, 0);
     mark(4);
     const int grid = c->num_sms * 4;
-    const int maxt = n == 1 ? 1 : n <= 8 ? 8 : kGemmMinT - 1;
-    const int r1 = launch_gemv_decode(D, 0, R, c->xq64, c->xsb64, c->GU, 2 * FF, maxt, grid, st);
+    const int r1 = launch_gemv_decode(D, 0, R, c->xq64, c->xsb64, c->GU, 2 * FF, c->num_sms, st);
     if (r1 < 0) return -1;
     launches += r1;
     mark(5);
@@ -467,7 +493,7 @@ static int enqueue_forward(inzg_ctx *c, const LayerSlot &L, int n, const float *
     launches += launch_swiglu_quant(c->GU, FF, NE, c->eexp, c->upath, D.dn_rot, D.dn_seed, c->dq64, c->dsb64, c->dq256,
                                     c->ds256, st);
     mark(7);
-    launches += launch_gemv_decode(D, 1, R, c->dq64, c->dsb64, c->mo, H, maxt, grid, st);
+    launches += launch_gemv_decode(D, 1, R, c->dq64, c->dsb64, c->mo, H, c->num_sms, st);
     mark(8);
     if (any_gemm) {
         if (tc) launches += launch_gemm_tc(1, L.map_dn.bytes, c->map_dq.bytes, D.ws_dn, H, FF, R, c->ds256, c->mo, H,
@@ -495,7 +521,7 @@ inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, fl
     cudaStream_t st = opt && opt->stream ? static_cast<cudaStream_t>(opt->stream) : c->stream;
     const int H = cf.hidden, E = cf.n_expert;
     const LayerDev &D = L.dev;
-    if (launch_gemv_decode(D, -1, RouteDev{}, nullptr, nullptr, nullptr, 0, 0, 0, st) < 0)
+    if (launch_gemv_decode(D, -1, RouteDev{}, nullptr, nullptr, nullptr, 0, 0, st) < 0)
         return fail(c, INZG_UNSUPPORTED, "moe_forward: no decode kernel for this geometry");
     cudaError_t e = cudaSuccess;
     const float *X = xin;

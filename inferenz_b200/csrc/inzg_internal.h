@@ -15,14 +15,17 @@ constexpr int kGemmMinT = 12;  // experts with >= 12 tokens use the prefill nume
 constexpr int kMaxTopK = 16;
 
 // ---------------------------------------------------------------------------------------------------------------
-// Tile layout of one expert matrix (M rows x K cols, ng = K/64 groups), matched to the int8 MMA fragments
+// Tile layout of one expert matrix (M rows x K cols, ng = K/64 groups), matched to the fragments of the int8 MMA
 // (mma.m16n8k32: thread (r = lane/4, t = lane%4) holds A[r][4t..4t+3], A[r+8][4t..], A[r][16+4t..], A[r+8][16+4t..]).
-// Weights: [M/16 row tiles][ng][32 lanes][wb bytes]. Q4L (wb = 16): lane (r, t) holds 4 words -- (row r, word t),
-//   (row r, word t+4), (row r+8, word t), (row r+8, word t+4) -- where word l of a row and group carries the nibbles
-//   of weights 4l..4l+3 in bits 0-15 and of 32+4l..32+4l+3 in bits 16-31 (one PRMT selector each). Q8G (wb = 32):
-//   lane (r, t) holds the byte quads c = t, t+4, t+8, t+12 of row r, then of row r+8.
+// The decode GEMV runs two MMAs per group whose K = 32 holds 4 of the reference's 8 VNNI lanes each (lane l covers
+// weights 4l..4l+3 and 32+4l..32+4l+3), so thread (r, t) of MMA h needs lane 4h + t/2 (registers a0, a1) and lane
+// 4h + 2 + t/2 (a2, a3), part t%2 of each (part 0: weights 4l.., part 1: weights 32+4l..).
+// Weights: [M/16 row tiles][ng][32 lanes][wb bytes].
+//   Q4L (wb = 16): 4 words per lane, word 2h + s (s = 0: row r, 1: row r+8): bits 0-15 the 4 nibble selectors of
+//   registers a0/a1 of MMA h, bits 16-31 those of a2/a3.
+//   Q8G (wb = 32): [h][32 lanes][4 words a0 a1 a2 a3], each word 4 raw bytes.
 // Scales: [M/16][gd = ceil(ng/4)][8 rows r][4 groups][2] fp16 -- (d[r][g], d[r+8][g]) pairs, zero past ng.
-// A warp reads one 16-row x 64-column tile with one 512-byte (Q4L) or 1024-byte (Q8G) coalesced load.
+// A warp reads one 16-row x 64-column tile with one 512-byte (Q4L) or two (Q8G) conflict-free shared-memory loads.
 // ---------------------------------------------------------------------------------------------------------------
 struct MatLayout {
     int rows, cols, ng, gd, wb;
@@ -59,14 +62,15 @@ struct RouteDev {
     int32_t *ccnt;       // [nchunk][E] per-32-token-chunk counts, then their exclusive prefix per expert
     int32_t *units;      // [E] experts with cnt > 0, ascending
     int32_t *meta;       // [16] counters: 0 nunits, 1 n_dec_units, 2 n_gemm_units, 3 n_dec_items_gu, 4 n_dec_items_dn,
-                         //      5 n_gemm_tiles_gu, 6 n_gemm_tiles_dn, 7 device error code
-    int32_t *dec_units;  // [E] decode-path experts
+                         //      5 n_gemm_tiles_gu, 6 n_gemm_tiles_dn, 7 device error code, 8/9 decode GEMV work
+                         //      queues (gate|up, down)
+    int32_t *dec_units;  // [E] decode-path experts, most tokens first
     int32_t *gemm_units; // [E] prefill-path experts
     int32_t *gemm_tiles; // [E * tiles] (unit index << 16 | token tile) for the GEMM path
 };
 
 constexpr int kMetaNUnits = 0, kMetaNDec = 1, kMetaNGemm = 2, kMetaDecItemsGU = 3, kMetaDecItemsDN = 4,
-              kMetaGemmTilesGU = 5, kMetaGemmTilesDN = 6, kMetaError = 7;
+              kMetaGemmTilesGU = 5, kMetaGemmTilesDN = 6, kMetaError = 7, kMetaWorkGU = 8, kMetaWorkDN = 9;
 
 // device error codes (sticky, first one wins)
 constexpr int kErrNone = 0, kErrBadExpert = 1, kErrBadSlot = 2, kErrOverflow = 3, kErrTimeout = 4;

@@ -3,17 +3,13 @@
 // Rotation: signs x_i * rot_sign(seed, i), then the unnormalised Walsh-Hadamard butterflies a+b / a-b with
 // len = 1, 2, 4, ... inside each block, then * 1/sqrt(block) (src/quant.c:118-154). The butterfly network is the
 // reference's, stage by stage, so every element sees the same sequence of IEEE adds.
-// Decode numerics (src/quant.c:611-637): per 64-group s = amax/127, q = rne(x * (1/s)), and the group's sum of q
-// (the reference keeps bsum = s * sum(q); the GEMV removes the LUT bias with the exact integer sum instead). The
-// quantized bytes are stored in MMA B-fragment order: inside a group, thread t of a quad reads 16 bytes,
-// q[4t..4t+3], q[16+4t..], q[32+4t..], q[48+4t..].
+// Decode numerics (src/quant.c:611-637): per 64-group s = amax/127, q = rne(x * (1/s)), bsum = s * sum(q); the
+// bytes stay in natural order and each group's (s, bsum) is one float2.
 // Prefill numerics (src/quant.c:1407-1429): per 256-block (the last one partial) s = amax/127, q = lrint(x * (1/s)).
 #include "inzg_internal.h"
 #include "k_launch.h"
 
 namespace inzg {
-
-__device__ __forceinline__ int bfrag_pos(int j) { return ((j >> 2) & 3) * 16 + (j >> 4) * 4 + (j & 3); }
 
 // in-place rotation of v[0..n) in shared memory by the whole block; n % block == 0
 __device__ void rotate_smem(float *v, int n, int block, uint32_t seed, float norm) {
@@ -35,9 +31,8 @@ __device__ void rotate_smem(float *v, int n, int block, uint32_t seed, float nor
     __syncthreads();
 }
 
-// quantize v[0..n) (shared) by warps: 64-groups into q64 (B-fragment order) and sb64 = (scale bits, sum of q);
-// and/or 256-blocks into q256, s256
-__device__ void quantize_smem(const float *v, int n, int8_t *q64, int2 *sb64, int8_t *q256, float *s256) {
+// quantize v[0..n) (shared) by warps: 64-groups into q64 and sb64 = (s, bsum); and/or 256-blocks into q256, s256
+__device__ void quantize_smem(const float *v, int n, int8_t *q64, float2 *sb64, int8_t *q256, float *s256) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     if (q64)
         for (int g = warp; g < n / kGroup; g += nw) {
@@ -49,9 +44,9 @@ __device__ void quantize_smem(const float *v, int n, int8_t *q64, int2 *sb64, in
             const int a = __float2int_rn(__fmul_rn(x0, inv)), b = __float2int_rn(__fmul_rn(x1, inv));
             int sum = a + b;
             for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            q64[g * kGroup + bfrag_pos(lane)] = (int8_t)a;
-            q64[g * kGroup + bfrag_pos(32 + lane)] = (int8_t)b;
-            if (lane == 0) sb64[g] = make_int2(__float_as_int(s), sum);
+            q64[g * kGroup + lane] = (int8_t)a;
+            q64[g * kGroup + 32 + lane] = (int8_t)b;
+            if (lane == 0) sb64[g] = make_float2(s, __fmul_rn(s, (float)sum));
         }
     if (q256) {
         const int nkb = (n + kKB - 1) / kKB;
@@ -70,7 +65,7 @@ __device__ void quantize_smem(const float *v, int n, int8_t *q64, int2 *sb64, in
 
 // one block per token: x [n][H] -> decode activations (q64, s64, b64) and prefill activations (q256, s256)
 __global__ void __launch_bounds__(256) act_quant_x_kernel(const float *__restrict__ X, int n, int H, int rot, uint32_t seed,
-                                                          float norm, int8_t *__restrict__ q64, int2 *__restrict__ sb64,
+                                                          float norm, int8_t *__restrict__ q64, float2 *__restrict__ sb64,
                                                           int8_t *__restrict__ q256, float *__restrict__ s256) {
     extern __shared__ float v[];
     const int t = blockIdx.x;
@@ -84,12 +79,13 @@ __global__ void __launch_bounds__(256) act_quant_x_kernel(const float *__restric
 
 // The expert's input to its down matrix, one block per entry: h = silu(g) * u (src/model_fwd.c:43, 859-862, 925,
 // siluf = x / (1 + expf(-x))), rotated with the down matrix's rotation, then quantized with the numerics of the
-// expert's path. exp is evaluated in double and rounded once (glibc's expf agrees with that on all but ~1e-4 of
-// inputs, by at most one ulp).
+// expert's path. exp is evaluated in double and rounded once: glibc's expf gives the same float on all but ~1e-4 of
+// inputs (by one ulp), where CUDA's expf (2 ulp) differs far more often -- every SiLU ulp can flip an int8 rounding
+// of the down projection's input.
 __global__ void __launch_bounds__(128) swiglu_quant_kernel(const float *__restrict__ GU, int FF, int n_entries,
                                                            const int32_t *__restrict__ eexp, const int32_t *__restrict__ upath,
                                                            int rot, uint32_t seed, float norm, int8_t *__restrict__ q64,
-                                                           int2 *__restrict__ sb64, int8_t *__restrict__ q256,
+                                                           float2 *__restrict__ sb64, int8_t *__restrict__ q256,
                                                            float *__restrict__ s256) {
     extern __shared__ float v[];
     const int pos = blockIdx.x;
@@ -97,8 +93,7 @@ __global__ void __launch_bounds__(128) swiglu_quant_kernel(const float *__restri
     const float *g = GU + (size_t)pos * 2 * FF;
     for (int c = threadIdx.x; c < FF; c += blockDim.x) {
         const float x = g[c];
-        const float ex = (float)exp(-(double)x);
-        v[c] = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, ex)), g[FF + c]);
+        v[c] = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, (float)exp(-(double)x))), g[FF + c]);
     }
     __syncthreads();
     if (rot > 1) rotate_smem(v, FF, rot, seed, norm);
@@ -147,16 +142,187 @@ int launch_gather_gemm_rows(const int8_t *q, const float *s, int K, int nkb, con
     return 1;
 }
 
-int launch_act_quant_x(const float *X, int n, int H, int rot, uint32_t seed, int8_t *q64, int2 *sb64, int8_t *q256,
+// ---------------------------------------------------------------------------------------------------------------
+// Warp-level versions (no block barriers): one warp per row of NB rotation blocks of B = 32 * VPL elements; lane L
+// holds elements b*B + L*VPL + r. Butterfly stage len pairs (i, i+len): inside a lane when len < VPL, else with lane
+// L ^ (len / VPL) through a shuffle; the lower element gets a + b, the upper a - b, exactly as the reference.
+template <int NB, int VPL>
+__device__ __forceinline__ void warp_rotate(float (&v)[NB][VPL], uint32_t seed, float norm, int lane) {
+    constexpr int B = 32 * VPL;
+#pragma unroll
+    for (int b = 0; b < NB; b++)
+#pragma unroll
+        for (int r = 0; r < VPL; r++)
+            if (rot_sign_bit(seed, (uint32_t)(b * B + lane * VPL + r))) v[b][r] = -v[b][r];
+#pragma unroll
+    for (int len = 1; len < B; len <<= 1) {
+        if (len < VPL) {
+#pragma unroll
+            for (int b = 0; b < NB; b++)
+#pragma unroll
+                for (int r = 0; r < VPL; r++)
+                    if (!(r & len)) {
+                        const float a = v[b][r], c = v[b][r + len];
+                        v[b][r] = __fadd_rn(a, c);
+                        v[b][r + len] = __fsub_rn(a, c);
+                    }
+        } else {
+            const int lm = len / VPL;
+            const bool upper = lane & lm;
+#pragma unroll
+            for (int b = 0; b < NB; b++)
+#pragma unroll
+                for (int r = 0; r < VPL; r++) {
+                    const float o = __shfl_xor_sync(0xffffffffu, v[b][r], lm);
+                    v[b][r] = upper ? __fsub_rn(o, v[b][r]) : __fadd_rn(v[b][r], o);
+                }
+        }
+    }
+#pragma unroll
+    for (int b = 0; b < NB; b++)
+#pragma unroll
+        for (int r = 0; r < VPL; r++) v[b][r] = __fmul_rn(v[b][r], norm);
+}
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+    return (uint32_t)(a & 255) | ((uint32_t)(b & 255) << 8) | ((uint32_t)(c & 255) << 16) | ((uint32_t)(d & 255) << 24);
+}
+
+// decode numerics of a row held as v[NB][VPL] (64-groups span 64/VPL lanes): q64, sb = (s, bsum); prefill numerics
+// (256-blocks, the last one partial): q256, s256
+template <int NB, int VPL>
+__device__ __forceinline__ void warp_quantize(const float (&v)[NB][VPL], int n, int lane, int8_t *q64, float2 *sb64,
+                                              int8_t *q256, float *s256) {
+    constexpr int B = 32 * VPL, LPG = kGroup / VPL;  // lanes per 64-group
+    if (q64) {
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            float amax = 0.0f;
+#pragma unroll
+            for (int r = 0; r < VPL; r++) amax = fmaxf(amax, fabsf(v[b][r]));
+#pragma unroll
+            for (int o = 1; o < LPG; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const float s = __fdiv_rn(amax, 127.0f);
+            const float inv = s > 0 ? __fdiv_rn(1.0f, s) : 0.0f;
+            int q[VPL], sum = 0;
+#pragma unroll
+            for (int r = 0; r < VPL; r++) {
+                q[r] = __float2int_rn(__fmul_rn(v[b][r], inv));
+                sum += q[r];
+            }
+#pragma unroll
+            for (int o = 1; o < LPG; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            const int j0 = b * B + lane * VPL, g = j0 / kGroup;
+#pragma unroll
+            for (int r = 0; r < VPL; r += 4)
+                *reinterpret_cast<uint32_t *>(q64 + j0 + r) = pack4(q[r], q[r + 1], q[r + 2], q[r + 3]);
+            if ((lane % LPG) == 0) sb64[g] = make_float2(s, __fmul_rn(s, (float)sum));
+        }
+    }
+    if (q256) {
+        constexpr int BPK = kKB / B;  // rotation blocks per 256-block
+#pragma unroll
+        for (int kb = 0; kb < (NB + BPK - 1) / BPK; kb++) {
+            float amax = 0.0f;
+#pragma unroll
+            for (int b = kb * BPK; b < kb * BPK + BPK && b < NB; b++)
+#pragma unroll
+                for (int r = 0; r < VPL; r++) amax = fmaxf(amax, fabsf(v[b][r]));
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const float s = __fdiv_rn(amax, 127.0f);
+            const float inv = s > 0 ? __fdiv_rn(1.0f, s) : 0.0f;
+#pragma unroll
+            for (int b = kb * BPK; b < kb * BPK + BPK && b < NB; b++)
+#pragma unroll
+                for (int r = 0; r < VPL; r += 4) {
+                    int q[4];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) q[i] = __float2int_rn(__fmul_rn(v[b][r + i], inv));
+                    *reinterpret_cast<uint32_t *>(q256 + b * B + lane * VPL + r) = pack4(q[0], q[1], q[2], q[3]);
+                }
+            if (lane == 0) s256[kb] = s;
+        }
+    }
+    (void)n;
+}
+
+// one warp per token: x [n][H] (H = NB * 256), rotation block 256
+template <int NB>
+__global__ void __launch_bounds__(128) act_quant_x_warp_kernel(const float *__restrict__ X, int n, uint32_t seed,
+                                                               float norm, int8_t *__restrict__ q64,
+                                                               float2 *__restrict__ sb64, int8_t *__restrict__ q256,
+                                                               float *__restrict__ s256) {
+    constexpr int VPL = 8, H = NB * 256;
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= n) return;
+    float v[NB][VPL];
+    const float *x = X + (size_t)t * H;
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+        const float4 a = reinterpret_cast<const float4 *>(x + b * 256 + lane * 8)[0];
+        const float4 c = reinterpret_cast<const float4 *>(x + b * 256 + lane * 8)[1];
+        v[b][0] = a.x; v[b][1] = a.y; v[b][2] = a.z; v[b][3] = a.w;
+        v[b][4] = c.x; v[b][5] = c.y; v[b][6] = c.z; v[b][7] = c.w;
+    }
+    warp_rotate<NB, VPL>(v, seed, norm, lane);
+    warp_quantize<NB, VPL>(v, H, lane, q64 + (size_t)t * H, sb64 + (size_t)t * (H / kGroup),
+                           q256 ? q256 + (size_t)t * H : nullptr, q256 ? s256 + (size_t)t * (H / kKB) : nullptr);
+}
+
+// one warp per entry: h = silu(g) * u over FF = NB * 128 values, rotation block 128, quantized for the expert's path
+template <int NB>
+__global__ void __launch_bounds__(128) swiglu_quant_warp_kernel(const float *__restrict__ GU, int n_entries,
+                                                                const int32_t *__restrict__ eexp,
+                                                                const int32_t *__restrict__ upath, uint32_t seed,
+                                                                float norm, int8_t *__restrict__ q64,
+                                                                float2 *__restrict__ sb64, int8_t *__restrict__ q256,
+                                                                float *__restrict__ s256) {
+    constexpr int VPL = 4, FF = NB * 128;
+    const int lane = threadIdx.x & 31;
+    const int pos = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (pos >= n_entries) return;
+    const float *g = GU + (size_t)pos * 2 * FF;
+    float v[NB][VPL];
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+        const float4 a = reinterpret_cast<const float4 *>(g + b * 128 + lane * 4)[0];
+        const float4 u = reinterpret_cast<const float4 *>(g + FF + b * 128 + lane * 4)[0];
+        const float av[4] = {a.x, a.y, a.z, a.w}, uv[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int r = 0; r < 4; r++)  // siluf (src/model_fwd.c:43): x / (1 + expf(-x)), then * up
+            v[b][r] = __fmul_rn(__fdiv_rn(av[r], __fadd_rn(1.0f, (float)exp(-(double)av[r]))), uv[r]);
+    }
+    warp_rotate<NB, VPL>(v, seed, norm, lane);
+    const bool gemm = upath[eexp[pos]] != 0;
+    constexpr int nkb = (FF + kKB - 1) / kKB;
+    if (gemm) warp_quantize<NB, VPL>(v, FF, lane, nullptr, nullptr, q256 + (size_t)pos * FF, s256 + (size_t)pos * nkb);
+    else warp_quantize<NB, VPL>(v, FF, lane, q64 + (size_t)pos * FF, sb64 + (size_t)pos * (FF / kGroup), nullptr, nullptr);
+}
+
+int launch_act_quant_x(const float *X, int n, int H, int rot, uint32_t seed, int8_t *q64, float2 *sb64, int8_t *q256,
                        float *s256, cudaStream_t st) {
     const float norm = rot > 1 ? 1.0f / sqrtf((float)rot) : 1.0f;
-    act_quant_x_kernel<<<n, 256, H * sizeof(float), st>>>(X, n, H, rot, seed, norm, q64, sb64, q256, s256);
+    const int blocks = (n + 3) / 4;
+    if (rot == 256 && H == 2048) {
+        act_quant_x_warp_kernel<8><<<blocks, 128, 0, st>>>(X, n, seed, norm, q64, sb64, q256, s256);
+    } else if (rot == 256 && H == 2560) {
+        act_quant_x_warp_kernel<10><<<blocks, 128, 0, st>>>(X, n, seed, norm, q64, sb64, q256, s256);
+    } else {
+        act_quant_x_kernel<<<n, 256, H * sizeof(float), st>>>(X, n, H, rot, seed, norm, q64, sb64, q256, s256);
+    }
     return 1;
 }
 
 int launch_swiglu_quant(const float *GU, int FF, int n_entries, const int32_t *eexp, const int32_t *upath, int rot,
-                        uint32_t seed, int8_t *q64, int2 *sb64, int8_t *q256, float *s256, cudaStream_t st) {
+                        uint32_t seed, int8_t *q64, float2 *sb64, int8_t *q256, float *s256, cudaStream_t st) {
     const float norm = rot > 1 ? 1.0f / sqrtf((float)rot) : 1.0f;
+    if (rot == 128 && FF == 640) {
+        swiglu_quant_warp_kernel<5><<<(n_entries + 3) / 4, 128, 0, st>>>(GU, n_entries, eexp, upath, seed, norm, q64,
+                                                                          sb64, q256, s256);
+        return 1;
+    }
     swiglu_quant_kernel<<<n_entries, 128, FF * sizeof(float), st>>>(GU, FF, n_entries, eexp, upath, rot, seed, norm, q64,
                                                                      sb64, q256, s256);
     return 1;

@@ -20,12 +20,12 @@
 
 #include "inzg_internal.h"
 #include "k_launch.h"
+#include "k_async.cuh"
 
 namespace inzg {
 
 constexpr int TBM = 128, TBN = 128, TBK = 128, TSTAGES = 4;
 constexpr int kStageBytes = (TBM + TBN) * TBK;  // 32 KiB
-constexpr uint32_t kWaitLimit = 1u << 20;       // try_wait rounds before a wait is declared stuck
 
 struct TcShared {
     uint64_t full[TSTAGES], empty[TSTAGES], acc_full[2], acc_empty[2], drain;
@@ -34,33 +34,6 @@ struct TcShared {
     float xs[TBN * 8];  // token block scales, [n][block] (K <= 2048: at most 8 blocks)
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
-}
-// bounded wait for the phase with parity `par` to complete; false if it did not within the limit (or aborted)
-__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t par, volatile int *abort) {
-    for (uint32_t i = 0; i < kWaitLimit; i++) {
-        uint32_t ok;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(ok)
-            : "r"(smem_u32(b)), "r"(par)
-            : "memory");
-        if (ok) return true;
-        if ((i & 255) == 255 && *abort) return false;
-    }
-    return false;
-}
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(

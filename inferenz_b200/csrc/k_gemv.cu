@@ -1,24 +1,36 @@
 // k_gemv.cu -- decode-path grouped GEMV over the routed experts (Q4L / Q8G), sm_100a.
 //
-// Experts with fewer than 12 tokens (every expert when n <= 8) take the reference's decode numerics
-// (src/quant.c:611-671, 767-953): int8 activations per 64-group (scale s_g), weights = LUT level (Q4L, biased by 64)
-// or byte (Q8G, biased by 128) with an fp16 scale d_g per 64-group, and per row and token
-//     y = sum_g d_g * s_g * (sum_j u_j q_j - bias * sum_j q_j).
-// The integer group dots are exact; they run on the int8 tensor pipe (mma.m16n8k32, u8 weights x s8 activations,
-// s32 accumulate -- one 16-row x 8-token tile per warp and 64-column group), the bias is removed with the group's
-// exact integer sum of q, and each group is folded into fp32 with one fma per element. The reference keeps 8
-// accumulation lanes per row and adds the bias in float; the values are the same integers and the same scales,
-// summed in another order, so results agree to about 1e-7 relative (tests/test_gpu_parity.py).
+// Numerics: the reference's decode matvec, bit for bit (mv_q4l / mm_q4l: src/quant.c:767-875, 1179-1225; mv_q8g /
+// mm_q8g: src/quant.c:881-953, VNNI form). Per row and token the reference keeps 8 fp32 accumulators; accumulator l
+// takes, for every 64-group g in order,
+//     acc_l = fma((float)I_lg, d_g * s_g, acc_l),   I_lg = sum_{i<4} u[4l+i] x[4l+i] + u[32+4l+i] x[32+4l+i]
+// (I_lg is the 32-bit lane l of two VPDPBUSD over the group's two 32-byte halves; u = biased LUT level or raw byte),
+// then y = hsum8(acc) - bias * b, where b is the fma chain of d_g * bsum_g: Q4L keeps 8 chains (g % 8) over the
+// first ng & ~7 groups, reduces them with hsum8 and continues with the remaining groups in order; Q8G keeps one chain.
 //
-// Work: items = (decode expert, 16-row tile); one warp per item, warps run free and load the next 4 groups' weights
-// while the current 4 compute. Activations of the (<= 11) tokens come from L1.
+// Tensor pipe: the lane partials I_lg come straight out of the int8 MMA (mma.m16n8k32, u8 x s8 -> s32). The K = 32 of
+// one MMA holds 4 lanes x 8 elements (element i < 4: x[4l+i], else x[32+4l+i-4]); the activation operand is
+// block-diagonal -- column n carries lane n's 8 activations in lane n's rows and zeros elsewhere -- so D[row][n] is
+// exactly I_n. Two MMAs (lanes 0-3, lanes 4-7) give all 8 partials of a 16-row tile for one token. Thread (r, t) of the
+// MMA holds lanes 2t, 2t+1 of rows r and r+8, folds them into its accumulators with the reference's fma, and hsum8
+// becomes two quad shuffles that pair the lanes as the reference does: ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7)).
+//
+// Pipeline (one CTA per SM, persistent): an item is 128 rows (8 row tiles) of one decode expert's matrix. A producer
+// warp takes items from the call's work queue (experts with the most tokens first), brings the item's token
+// activations, their (s, bsum) and the 8 row tiles' scales into a double-buffered item buffer, and streams the
+// weights in stages of 8 (Q4L) or 4 (Q8G) 64-groups through a 4-deep ring -- all with bulk copies (cp.async.bulk on the
+// TMA engine, completion counted on mbarriers). 8 consumer warps each own one 16-row tile of the item: per group, the
+// LUT decode of the weight fragment, then two MMAs and the reference's fma per token. The bias chains need only the
+// scales and bsum, so they run once per item in the epilogue. Every wait is bounded; a CTA that gives up records
+// INZG_TIMEOUT and drains its copies before it leaves.
 #include "inzg_internal.h"
+#include "k_async.cuh"
 #include "k_launch.h"
 
 #include <cuda_fp16.h>
+#include <string.h>
 
 namespace inzg {
-
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t d;
@@ -26,168 +38,398 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t c) {
     return d;
 }
 
-// 4 nibble selectors (bits 0..15 of w) -> 4 LUT bytes. Levels are <= 127, so a selector with bit 3 set makes PRMT
-// replicate a zero sign bit: each half-table lookup yields 0 where the other half applies.
-__device__ __forceinline__ uint32_t lut16(uint32_t w, uint4 T) {
-    return prmt(T.x, T.y, w) | prmt(T.z, T.w, w ^ 0x88888888u);
+// Pipe balancing: `one` is a kernel argument equal to 1 that the compiler cannot fold, so the integer multiply-adds
+// below stay IMADs (FMA pipe) instead of becoming adds, shifts or selects on the ALU pipe, which the PRMT-based LUT
+// decode already fills.
+// 4 nibble selectors (bits 0..15 of w; wx = w ^ 0x8888) -> 4 LUT bytes. Levels are <= 127, so a selector with bit 3
+// set makes PRMT replicate a zero sign bit: each half-table lookup yields 0 where the other half applies, and the two
+// halves are added (disjoint bytes, so the sum is the byte-wise merge).
+__device__ __forceinline__ uint32_t lut16(uint32_t w, uint32_t wx, uint4 T, uint32_t one) {
+    return prmt(T.x, T.y, w) * one + prmt(T.z, T.w, wx);
+}
+
+// the high 16 bits of w (bits 16..31 -> 0..15): w * 2^16 >> 32 on the integer multiplier (k16 = one << 16)
+__device__ __forceinline__ uint32_t hi16(uint32_t w, uint32_t k16) { return __umulhi(w, k16); }
+
+__device__ __forceinline__ float2 h2f16x2(uint32_t bits) {
+    __half2 h;
+    memcpy(&h, &bits, 4);
+    return __half22float2(h);
 }
 
 __device__ __forceinline__ float h2f16(uint32_t bits) { return __half2float(__ushort_as_half((unsigned short)bits)); }
 
-
 __device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                          uint32_t b1) {
-    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
                  : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+// D = A * B + c (the same c in all four accumulator slots)
+__device__ __forceinline__ void mma_u8s8_c(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                           uint32_t b1, int c) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c));
+}
 
-// KIND 0: gate|up, activation row = token, output GU[entry][row]. KIND 1: down, activation row = entry, output
-// moe_out[slot][row] = w * y. NT: token tiles of 8 (1, or 2 when an expert can hold up to 11 tokens).
-template <bool Q8, int NG, int KIND, int NT>
-__global__ void __launch_bounds__(128) gemv_mma_kernel(const uint8_t *__restrict__ pool, uint64_t slab_bytes,
-                                                       MatLayout M, const uint8_t *__restrict__ luts, int lut_off,
-                                                       RouteDev R, const int8_t *__restrict__ aq,
-                                                       const int2 *__restrict__ asq, float *__restrict__ out,
-                                                       int out_ld, int meta_items) {
-    constexpr int K = NG * kGroup, GD = (NG + 3) / 4, WV = Q8 ? 2 : 1;  // uint4 per lane per group
-    constexpr int BIAS = Q8 ? 128 : kLutBias;
-    const int nitems = R.meta[meta_items];
-    const int per = M.rows / 16;
-    const int lane = threadIdx.x & 31, gr = lane >> 2, t = lane & 3;
-    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), nw = gridDim.x * (blockDim.x >> 5);
-    for (int item = gw; item < nitems; item += nw) {
-        const int u = item / per, rt = item % per;
-        const int e = R.dec_units[u];
-        const int base = R.off[e], ntok = min(R.cnt[e], 8 * NT);
-        const uint8_t *slab = pool + (size_t)e * slab_bytes;
-        const uint4 *aw = reinterpret_cast<const uint4 *>(slab + M.q_off) + (size_t)rt * NG * 32 * WV + lane * WV;
-        const uint4 *ad = reinterpret_cast<const uint4 *>(slab + M.d_off) + (size_t)rt * GD * 8 + gr;
-        uint4 T = make_uint4(0, 0, 0, 0);
-        if (!Q8) T = __ldg(reinterpret_cast<const uint4 *>(luts + (size_t)e * 32 + lut_off));
-        // B operand: token gr (+8 per tile); C columns: tokens 2t, 2t+1 (+8 per tile)
-        int brow[NT], crow[NT][2];
-        bool bok[NT], cok[NT][2];
+template <bool Q8, int NG, int KIND>
+struct DecGeo {
+    static constexpr int WARPS = 8;                  // consumer warps; one 16-row tile each -> 128 rows per item
+    static constexpr int STAGES = 4;
+    static constexpr int KC = Q8 ? 4 : 8;            // 64-groups per stage
+    static constexpr int NCH = (NG + KC - 1) / KC;   // stages per item
+    static constexpr int NG8 = NG & ~7;
+    static constexpr int WB = Q8 ? 32 : 16;          // weight bytes per lane per group
+    static constexpr int GD = (NG + 3) / 4;
+    static constexpr int WQ = KC * 32 * WB;          // weight bytes of one row tile in one stage
+    static constexpr int STAGE = WARPS * WQ;
+    static constexpr int K = NG * kGroup;
+    static constexpr int MT = 12;                    // most tokens of a decode expert: 11 (8 when n <= 8)
+    // item buffer: token activations [MT][K], their (s, bsum) [MT][NG], the 8 row tiles' scales [8][GD][8][4][2]
+    static constexpr int IB_SB = MT * K, IB_D = IB_SB + MT * NG * 8;
+    static constexpr int IBUF = ((IB_D + WARPS * GD * 128) + 127) / 128 * 128;
+    static constexpr int HDR = 1024;
+    static constexpr int SMEM = HDR + STAGES * STAGE + 2 * IBUF;
+    static constexpr int THREADS = (WARPS + 1) * 32;
+};
+
+// Item descriptor written by the producer warp, read by the consumers after the item's buffer has landed
+// (e == kDecEnd: the work queue is empty).
+constexpr int kDecEnd = -3;
+struct DecItem {
+    int e, base, ntok, rb;
+    uint4 lut;
+    int oslot[16];
+    float ow[16];
+};
+
+struct DecShared {
+    uint64_t full[4], empty[4], afull[2], aempty[2];
+    int abort, never;  // never: drains ignore the abort flag
+    DecItem item[2];
+};
+
+// Consumer: the item's TC >= ntok tokens on this warp's 16-row tile. q: running stage counter (advanced by NCH).
+template <bool Q8, int NG, int KIND, int TC>
+__device__ __forceinline__ bool dec_item(DecShared &S, const uint8_t *stages, const uint8_t *ib, const DecItem &it,
+                                         int &q, float *__restrict__ out, int out_ld, uint32_t one) {
+    using G = DecGeo<Q8, NG, KIND>;
+    volatile int *abort = &S.abort;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gr = lane >> 2, t = lane & 3;
+    // block-diagonal activation operand: thread (n = gr, t) supplies lane n's activations x[32 (t&1) + 4n .. +3]
+    // when (n & 1) == (t >> 1), in MMA n >> 2, register (n >> 1) & 1
+    // (0/1 factors: the operand is selected with an integer multiply, which issues on the FMA pipe)
+    const bool act_on = (gr & 1) == (t >> 1);
+    const uint32_t m00 = act_on && gr < 4 && !((gr >> 1) & 1) ? one : 0u, m01 = act_on && gr < 4 && ((gr >> 1) & 1) ? one : 0u;
+    const uint32_t m10 = act_on && gr >= 4 && !((gr >> 1) & 1) ? one : 0u, m11 = act_on && gr >= 4 && ((gr >> 1) & 1) ? one : 0u;
+    const uint32_t k16 = one << 16;
+    const uint8_t *xq = ib + 32 * (t & 1) + 4 * gr;
+    const float2 *xsb = reinterpret_cast<const float2 *>(ib + G::IB_SB);
+    // scale pairs (d[r][g], d[r+8][g]) of this warp's row tile: word (g / 4) * 32 + gr * 4 + g % 4
+    const uint32_t *wd = reinterpret_cast<const uint32_t *>(ib + G::IB_D + (size_t)warp * G::GD * 128) + gr * 4;
+    const uint4 T = it.lut;
+    const bool valid = it.e >= 0;
+    const int ntok = it.ntok;
+
+    float acc[TC][4];  // [token][row r lane 2t, row r lane 2t+1, row r+8 lane 2t, row r+8 lane 2t+1]
 #pragma unroll
-        for (int nt = 0; nt < NT; nt++) {
-            const int bt = nt * 8 + gr, c0 = nt * 8 + 2 * t;
-            bok[nt] = bt < ntok;
-            brow[nt] = bok[nt] ? (KIND == 0 ? R.etok[base + bt] : base + bt) : 0;
+    for (int j = 0; j < TC; j++)
 #pragma unroll
-            for (int j = 0; j < 2; j++) {
-                cok[nt][j] = c0 + j < ntok;
-                crow[nt][j] = cok[nt][j] ? (KIND == 0 ? R.etok[base + c0 + j] : base + c0 + j) : 0;
+        for (int i = 0; i < 4; i++) acc[j][i] = 0.0f;
+
+    // one 64-group: g global index, i index inside the stage
+    auto group = [&](const uint8_t *wq, int g, int i) {
+        uint32_t A0[4], A1[4];  // MMA h = 0 (lanes 0-3) and h = 1 (lanes 4-7)
+        if (Q8) {
+            const uint4 w0 = *reinterpret_cast<const uint4 *>(wq + (size_t)i * 1024);
+            const uint4 w1 = *reinterpret_cast<const uint4 *>(wq + (size_t)i * 1024 + 512);
+            A0[0] = w0.x; A0[1] = w0.y; A0[2] = w0.z; A0[3] = w0.w;
+            A1[0] = w1.x; A1[1] = w1.y; A1[2] = w1.z; A1[3] = w1.w;
+        } else {
+            const uint4 w = *reinterpret_cast<const uint4 *>(wq + (size_t)i * 512);
+            const uint4 x = make_uint4(w.x ^ 0x88888888u, w.y ^ 0x88888888u, w.z ^ 0x88888888u, w.w ^ 0x88888888u);
+            A0[0] = lut16(w.x, x.x, T, one); A0[1] = lut16(w.y, x.y, T, one);
+            A0[2] = lut16(hi16(w.x, k16), hi16(x.x, k16), T, one); A0[3] = lut16(hi16(w.y, k16), hi16(x.y, k16), T, one);
+            A1[0] = lut16(w.z, x.z, T, one); A1[1] = lut16(w.w, x.w, T, one);
+            A1[2] = lut16(hi16(w.z, k16), hi16(x.z, k16), T, one); A1[3] = lut16(hi16(w.w, k16), hi16(x.w, k16), T, one);
+        }
+        const float2 dd = h2f16x2(wd[(g >> 2) * 32 + (g & 3)]);
+        const float d0 = dd.x, d8 = dd.y;
+#pragma unroll
+        for (int j = 0; j < TC; j++) {
+            if (j >= ntok) continue;
+            const uint32_t xv = *reinterpret_cast<const uint32_t *>(xq + (size_t)j * G::K + g * kGroup);
+            const float sx = xsb[j * NG + g].x;
+            // the accumulator starts at the bits of 1.5 * 2^23: D then holds 12582912 + I as a float (|I| < 2^22)
+            int D[4];
+            mma_u8s8_c(D, A0[0], A0[1], A0[2], A0[3], xv * m00, xv * m01, 0x4B400000);
+            mma_u8s8(D, A1[0], A1[1], A1[2], A1[3], xv * m10, xv * m11);
+            const float ds0 = __fmul_rn(d0, sx), ds8 = __fmul_rn(d8, sx);
+            acc[j][0] = __fmaf_rn(__fadd_rn(__int_as_float(D[0]), -12582912.0f), ds0, acc[j][0]);
+            acc[j][1] = __fmaf_rn(__fadd_rn(__int_as_float(D[1]), -12582912.0f), ds0, acc[j][1]);
+            acc[j][2] = __fmaf_rn(__fadd_rn(__int_as_float(D[2]), -12582912.0f), ds8, acc[j][2]);
+            acc[j][3] = __fmaf_rn(__fadd_rn(__int_as_float(D[3]), -12582912.0f), ds8, acc[j][3]);
+        }
+    };
+
+#pragma unroll 1
+    for (int c = 0; c < G::NCH; c++, q++) {
+        const int s = q % G::STAGES;
+        if (!mbar_wait(&S.full[s], (q / G::STAGES) & 1, abort)) return false;
+        if (valid) {
+            const uint8_t *wq = stages + (size_t)s * G::STAGE + (size_t)warp * G::WQ + lane * 16;
+            const int g0 = c * G::KC;
+            if (g0 + G::KC <= NG) {
+#pragma unroll 4
+                for (int i = 0; i < G::KC; i++) group(wq, g0 + i, i);
+            } else {
+                for (int i = 0; i < NG - g0; i++) group(wq, g0 + i, i);
             }
         }
-        const bool tile2 = NT == 2 && ntok > 8;
-        float acc[NT][4];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.empty[s]);
+    }
+    if (!valid) return true;
+
 #pragma unroll
-        for (int nt = 0; nt < NT; nt++)
+    for (int j = 0; j < TC; j++) {
+        if (j >= ntok) continue;
+        float a[4];
 #pragma unroll
-            for (int i = 0; i < 4; i++) acc[nt][i] = 0.0f;
-        uint4 wcur[4][WV], wnxt[4][WV];
+        for (int i = 0; i < 4; i++) a[i] = __fadd_rn(acc[j][i], __shfl_xor_sync(0xffffffffu, acc[j][i], 2));
 #pragma unroll
-        for (int j = 0; j < 4; j++)
-#pragma unroll
-            for (int v = 0; v < WV; v++) wcur[j][v] = j < NG ? __ldg(aw + (size_t)j * 32 * WV + v) : make_uint4(0, 0, 0, 0);
-        for (int g4 = 0; g4 < GD; g4++) {
-#pragma unroll
-            for (int j = 0; j < 4; j++)
-#pragma unroll
-                for (int v = 0; v < WV; v++) {
-                    const int g = (g4 + 1) * 4 + j;
-                    wnxt[j][v] = g < NG ? __ldg(aw + (size_t)g * 32 * WV + v) : make_uint4(0, 0, 0, 0);
+        for (int i = 0; i < 4; i++) a[i] = __fadd_rn(a[i], __shfl_xor_sync(0xffffffffu, a[i], 1));
+        // bias chains: b = fma chain of d_g * bsum_g (Q8G: one per row, in order; Q4L: 8 chains g % 8 over the first
+        // ng & ~7 groups, hsum8, then the remaining groups in order). Thread t keeps Q4L chains 2t, 2t+1 of both rows.
+        const float2 *sb = xsb + j * NG;
+        float b[2];  // row r, row r + 8
+        if (Q8) {
+#pragma unroll 4
+            for (int h = 0; h < 2; h++) {
+                float c = 0.0f;
+                for (int g = 0; g < NG; g++) {
+                    const uint32_t dv = wd[(g >> 2) * 32 + (g & 3)];
+                    c = __fmaf_rn(h2f16(h ? dv >> 16 : dv & 0xFFFFu), sb[g].y, c);
                 }
-            const uint4 dq = __ldg(ad + (size_t)g4 * 8);  // (d[r][g], d[r+8][g]) for the 4 groups
-            const uint32_t dw[4] = {dq.x, dq.y, dq.z, dq.w};
+                b[h] = c;
+            }
+        } else {
+            float ch[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // row r chain 2t, 2t+1, row r+8 chain 2t, 2t+1
+#pragma unroll 2
+            for (int g8 = 0; g8 < G::NG8; g8 += 8) {
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int g = g4 * 4 + j;
-                if (g < NG) {
-                    uint32_t A1[4], A2[4];
-                    if (Q8) {
-                        const uint4 w0 = wcur[j][0], w1 = wcur[j][1];
-                        A1[0] = w0.x; A1[1] = w1.x; A1[2] = w0.y; A1[3] = w1.y;
-                        A2[0] = w0.z; A2[1] = w1.z; A2[2] = w0.w; A2[3] = w1.w;
-                    } else {
-                        const uint4 w = wcur[j][0];
-                        A1[0] = lut16(w.x, T); A1[1] = lut16(w.z, T); A1[2] = lut16(w.y, T); A1[3] = lut16(w.w, T);
-                        A2[0] = lut16(w.x >> 16, T); A2[1] = lut16(w.z >> 16, T);
-                        A2[2] = lut16(w.y >> 16, T); A2[3] = lut16(w.w >> 16, T);
-                    }
-                    const float d0 = h2f16(dw[j] & 0xFFFFu), d8 = h2f16(dw[j] >> 16);
-#pragma unroll
-                    for (int nt = 0; nt < NT; nt++) {
-                        if (nt == 1 && !tile2) continue;
-                        const uint4 b = bok[nt] ? __ldg(reinterpret_cast<const uint4 *>(aq + (size_t)brow[nt] * K + g * kGroup) + t)
-                                                : make_uint4(0, 0, 0, 0);
-                        int D[4] = {0, 0, 0, 0};
-                        mma_u8s8(D, A1[0], A1[1], A1[2], A1[3], b.x, b.y);
-                        mma_u8s8(D, A2[0], A2[1], A2[2], A2[3], b.z, b.w);
-                        const int2 q0 = __ldg(asq + (size_t)crow[nt][0] * NG + g);
-                        const int2 q1 = __ldg(asq + (size_t)crow[nt][1] * NG + g);
-                        const float sc0 = __int_as_float(q0.x), sc1 = __int_as_float(q1.x);
-                        const int s0 = q0.y * BIAS, s1 = q1.y * BIAS;
-                        acc[nt][0] = __fmaf_rn((float)(D[0] - s0), __fmul_rn(d0, sc0), acc[nt][0]);
-                        acc[nt][1] = __fmaf_rn((float)(D[1] - s1), __fmul_rn(d0, sc1), acc[nt][1]);
-                        acc[nt][2] = __fmaf_rn((float)(D[2] - s0), __fmul_rn(d8, sc0), acc[nt][2]);
-                        acc[nt][3] = __fmaf_rn((float)(D[3] - s1), __fmul_rn(d8, sc1), acc[nt][3]);
-                    }
+                for (int e = 0; e < 2; e++) {
+                    const int g = g8 + 2 * t + e;
+                    const uint32_t dv = wd[(g >> 2) * 32 + (g & 3)];
+                    const float bs = sb[g].y;
+                    ch[e] = __fmaf_rn(h2f16(dv & 0xFFFFu), bs, ch[e]);
+                    ch[2 + e] = __fmaf_rn(h2f16(dv >> 16), bs, ch[2 + e]);
                 }
             }
 #pragma unroll
-            for (int j = 0; j < 4; j++)
+            for (int i = 0; i < 4; i++) ch[i] = __fadd_rn(ch[i], __shfl_xor_sync(0xffffffffu, ch[i], 2));
 #pragma unroll
-                for (int v = 0; v < WV; v++) wcur[j][v] = wnxt[j][v];
+            for (int i = 0; i < 4; i++) ch[i] = __fadd_rn(ch[i], __shfl_xor_sync(0xffffffffu, ch[i], 1));
+            b[0] = __fadd_rn(ch[0], ch[1]);
+            b[1] = __fadd_rn(ch[2], ch[3]);
+#pragma unroll
+            for (int g = G::NG8; g < NG; g++) {
+                const uint32_t dv = wd[(g >> 2) * 32 + (g & 3)];
+                b[0] = __fmaf_rn(h2f16(dv & 0xFFFFu), sb[g].y, b[0]);
+                b[1] = __fmaf_rn(h2f16(dv >> 16), sb[g].y, b[1]);
+            }
         }
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++) {
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const int tok = nt * 8 + 2 * t + (i & 1);
-                const int row = rt * 16 + gr + (i >> 1) * 8;
-                if (tok < ntok) {
-                    const int pos = base + tok;
-                    if (KIND == 0) out[(size_t)pos * out_ld + row] = acc[nt][i];
-                    else out[(size_t)R.eslot[pos] * out_ld + row] = __fmul_rn(R.ew[pos], acc[nt][i]);
-                }
-            }
+        if (t < 2) {
+            const float s8 = __fadd_rn(a[2 * t], a[2 * t + 1]);
+            const float y = __fsub_rn(s8, __fmul_rn(Q8 ? 128.0f : (float)kLutBias, t ? b[1] : b[0]));
+            const int row = (it.rb * G::WARPS + warp) * 16 + gr + 8 * t;
+            if (KIND == 0) out[(size_t)(it.base + j) * out_ld + row] = y;
+            else out[(size_t)it.oslot[j] * out_ld + row] = __fmul_rn(it.ow[j], y);
         }
     }
+    return true;
+}
+
+template <bool Q8, int NG, int KIND>
+__global__ void __launch_bounds__(DecGeo<Q8, NG, KIND>::THREADS, 1)
+    gemv_decode_kernel(const uint8_t *__restrict__ pool, uint64_t slab_bytes, MatLayout M, const uint8_t *__restrict__ luts,
+                       int lut_off, int E, RouteDev R, const int8_t *__restrict__ aq, const float2 *__restrict__ asb,
+                       float *__restrict__ out, int out_ld, int meta_items, int meta_work, uint32_t one) {
+    using G = DecGeo<Q8, NG, KIND>;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    DecShared &S = *reinterpret_cast<DecShared *>(smem);
+    uint8_t *stages = smem + G::HDR;
+    uint8_t *ibufs = stages + (size_t)G::STAGES * G::STAGE;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nitems = R.meta[meta_items];
+    const int per = M.rows / (16 * G::WARPS);
+    if ((int)blockIdx.x >= nitems) return;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < G::STAGES; i++) { mbar_init(&S.full[i], 1); mbar_init(&S.empty[i], G::WARPS); }
+        for (int i = 0; i < 2; i++) { mbar_init(&S.afull[i], 1); mbar_init(&S.aempty[i], G::WARPS); }
+        S.abort = 0;
+        S.never = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    volatile int *abort = &S.abort;
+
+    if (warp == G::WARPS) {
+        // ---------------- producer warp ----------------
+        // items come from the call's work queue (the route kernel lists experts heaviest first and clears the counter)
+        int q = 0, li = 0, na = 0;  // stages issued, items begun, items whose buffers were issued
+        bool ok = true;
+        for (;; li++) {
+            const int ab = li & 1;
+            if (li >= 2 && !mbar_wait(&S.aempty[ab], ((li >> 1) + 1) & 1, abort)) { ok = false; break; }
+            DecItem &D = S.item[ab];
+            int item = 0;
+            if (lane == 0) item = atomicAdd(R.meta + meta_work, 1);
+            item = __shfl_sync(0xffffffffu, item, 0);
+            if (item >= nitems) {
+                if (lane == 0) {
+                    D.e = kDecEnd;
+                    mbar_arrive(&S.afull[ab]);
+                }
+                break;
+            }
+            int e = 0, base = 0, ntok = 0;
+            if (lane == 0) {
+                e = __ldg(R.dec_units + item / per);
+                if (e < 0 || e >= E) { set_error(R.meta, kErrBadExpert); e = -1; }
+                else {
+                    base = __ldg(R.off + e);
+                    ntok = __ldg(R.cnt + e);
+                    if (ntok > G::MT) { set_error(R.meta, kErrOverflow); ntok = G::MT; }
+                }
+            }
+            e = __shfl_sync(0xffffffffu, e, 0);
+            base = __shfl_sync(0xffffffffu, base, 0);
+            ntok = __shfl_sync(0xffffffffu, ntok, 0);
+            int row = 0;
+            if (lane < ntok) {
+                row = KIND == 0 ? __ldg(R.etok + base + lane) : base + lane;
+                if (KIND == 1) { D.oslot[lane] = __ldg(R.eslot + base + lane); D.ow[lane] = __ldg(R.ew + base + lane); }
+            }
+            const int rt0 = (item % per) * G::WARPS;
+            const uint8_t *slab = pool + (size_t)(e < 0 ? 0 : e) * slab_bytes;
+            if (lane == 0) {
+                D.e = e; D.base = base; D.ntok = ntok; D.rb = item % per;
+                D.lut = (!Q8 && e >= 0) ? __ldg(reinterpret_cast<const uint4 *>(luts + (size_t)e * 32 + lut_off))
+                                        : make_uint4(0, 0, 0, 0);
+            }
+            __syncwarp();
+            uint8_t *ib = ibufs + (size_t)ab * G::IBUF;
+            const uint32_t dbytes = e >= 0 ? (uint32_t)(G::WARPS * G::GD * 128) : 0u;
+            if (lane == 0) mbar_expect_tx(&S.afull[ab], (uint32_t)(ntok * (G::K + NG * 8)) + dbytes);
+            __syncwarp();
+            if (KIND == 0) {
+                if (lane < ntok) {
+                    bulk_g2s(ib + (size_t)lane * G::K, aq + (size_t)row * G::K, G::K, &S.afull[ab]);
+                    bulk_g2s(ib + G::IB_SB + (size_t)lane * NG * 8, asb + (size_t)row * NG, NG * 8, &S.afull[ab]);
+                }
+            } else if (lane == 0 && ntok > 0) {
+                bulk_g2s(ib, aq + (size_t)base * G::K, ntok * G::K, &S.afull[ab]);
+                bulk_g2s(ib + G::IB_SB, asb + (size_t)base * NG, ntok * NG * 8, &S.afull[ab]);
+            }
+            if (lane == 31 && e >= 0)
+                bulk_g2s(ib + G::IB_D, slab + M.d_off + (size_t)rt0 * G::GD * 128, dbytes, &S.afull[ab]);
+            na++;
+            // weights of the item's 8 row tiles, one stage per KC groups
+            for (int c = 0; c < G::NCH; c++, q++) {
+                const int s = q % G::STAGES;
+                if (q >= G::STAGES && !mbar_wait(&S.empty[s], ((q / G::STAGES) + 1) & 1, abort)) { ok = false; break; }
+                const int g0 = c * G::KC, kc = NG - g0 < G::KC ? NG - g0 : G::KC;
+                const uint32_t wbytes = (uint32_t)(kc * 32 * G::WB);
+                if (lane == 0) {
+                    if (e >= 0) mbar_expect_tx(&S.full[s], G::WARPS * wbytes);
+                    else mbar_arrive(&S.full[s]);
+                }
+                __syncwarp();
+                if (e >= 0 && lane < G::WARPS)
+                    bulk_g2s(stages + (size_t)s * G::STAGE + (size_t)lane * G::WQ,
+                             slab + M.q_off + ((size_t)(rt0 + lane) * NG + g0) * 32 * G::WB, wbytes, &S.full[s]);
+            }
+            if (!ok) break;
+        }
+        // Normal end: the consumers wait for every issued copy before they see the end marker, so nothing is in
+        // flight when the CTA leaves. After an abort the producer drains what it issued (bounded): the last use of
+        // each stage slot and of each item buffer (no end marker was published, so each is the barrier's latest phase).
+        if (!ok) {
+            if (lane == 0) set_error(R.meta, kErrTimeout);
+            *abort = 1;
+            volatile int *never = &S.never;
+            for (int k = (q > G::STAGES ? q - G::STAGES : 0); k < q; k++)
+                mbar_wait(&S.full[k % G::STAGES], (k / G::STAGES) & 1, never);
+            for (int k = (na > 2 ? na - 2 : 0); k < na; k++) mbar_wait(&S.afull[k & 1], (k >> 1) & 1, never);
+        }
+        return;
+    }
+
+    // ---------------- consumer warps ----------------
+    int q = 0;
+    for (int li = 0;; li++) {
+        const int ab = li & 1;
+        if (!mbar_wait(&S.afull[ab], (li >> 1) & 1, abort)) break;
+        const DecItem &it = S.item[ab];
+        if (it.e == kDecEnd) return;
+        const uint8_t *ib = ibufs + (size_t)ab * G::IBUF;
+        const int nt = it.ntok;
+        bool ok;
+        if (nt <= 1) ok = dec_item<Q8, NG, KIND, 1>(S, stages, ib, it, q, out, out_ld, one);
+        else if (nt <= 2) ok = dec_item<Q8, NG, KIND, 2>(S, stages, ib, it, q, out, out_ld, one);
+        else if (nt <= 3) ok = dec_item<Q8, NG, KIND, 3>(S, stages, ib, it, q, out, out_ld, one);
+        else if (nt <= 4) ok = dec_item<Q8, NG, KIND, 4>(S, stages, ib, it, q, out, out_ld, one);
+        else if (nt <= 6) ok = dec_item<Q8, NG, KIND, 6>(S, stages, ib, it, q, out, out_ld, one);
+        else if (nt <= 8) ok = dec_item<Q8, NG, KIND, 8>(S, stages, ib, it, q, out, out_ld, one);
+        else ok = dec_item<Q8, NG, KIND, 12>(S, stages, ib, it, q, out, out_ld, one);
+        if (!ok) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.aempty[ab]);
+    }
+    if (lane == 0) set_error(R.meta, kErrTimeout);
+    *abort = 1;
 }
 
 // ---------------------------------------------------------------------------------------------------------------
 template <bool Q8, int NG, int KIND>
-static void launch_one(const LayerDev &L, const MatLayout &M, const RouteDev &R, const int8_t *aq, const int2 *asq,
-                       float *out, int out_ld, int meta_items, int maxt, int grid, cudaStream_t st) {
-    const int lo = KIND == 0 ? 0 : 16;
-    if (maxt <= 8)
-        gemv_mma_kernel<Q8, NG, KIND, 1><<<grid, 128, 0, st>>>(L.pool, L.slab_bytes, M, L.luts, lo, R, aq, asq, out,
-                                                               out_ld, meta_items);
-    else
-        gemv_mma_kernel<Q8, NG, KIND, 2><<<grid, 128, 0, st>>>(L.pool, L.slab_bytes, M, L.luts, lo, R, aq, asq, out,
-                                                               out_ld, meta_items);
+static void launch_one(const LayerDev &L, const MatLayout &M, const RouteDev &R, const int8_t *aq, const float2 *asb,
+                       float *out, int out_ld, int meta_items, int num_sms, cudaStream_t st) {
+    using G = DecGeo<Q8, NG, KIND>;
+    static_assert(G::SMEM <= 227 * 1024, "decode GEMV shared memory");
+    static_assert(sizeof(DecShared) <= G::HDR, "decode GEMV header");
+    cudaFuncSetAttribute(gemv_decode_kernel<Q8, NG, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
+    gemv_decode_kernel<Q8, NG, KIND><<<num_sms, G::THREADS, G::SMEM, st>>>(
+        L.pool, L.slab_bytes, M, L.luts, KIND == 0 ? 0 : 16, L.E, R, aq, asb, out, out_ld, meta_items,
+        KIND == 0 ? kMetaWorkGU : kMetaWorkDN, 1u);
+}
+
+constexpr int kRowsPerItem = 128;  // 8 consumer warps x 16 rows
+
+int gemv_items_per_unit(const LayerDev &L, int kind) {
+    const MatLayout &M = kind == 0 ? L.gu : L.dn;
+    return M.rows / kRowsPerItem;
 }
 
 // Returns the number of kernels launched, 0 for a geometry probe (kind 2/3), or -1 if the geometry has no
-// instantiation. asq: per activation row and group, (scale as int bits, sum of q). maxt: most tokens an expert on
-// this path can have in the call (8 when n <= 8, else 11).
-int launch_gemv_decode(const LayerDev &L, int kind, const RouteDev &R, const int8_t *aq, const int2 *asq, float *out,
-                       int out_ld, int maxt, int grid, cudaStream_t st) {
+// instantiation. asb: per activation row and 64-group, (scale, scale * sum of q) as the reference keeps them.
+int launch_gemv_decode(const LayerDev &L, int kind, const RouteDev &R, const int8_t *aq, const float2 *asb, float *out,
+                       int out_ld, int num_sms, cudaStream_t st) {
     if (kind < 0)  // geometry probe: both matrices must have an instantiation
-        return launch_gemv_decode(L, 2, R, aq, asq, out, out_ld, maxt, grid, st) < 0 ||
-                       launch_gemv_decode(L, 3, R, aq, asq, out, out_ld, maxt, grid, st) < 0 ? -1 : 0;
+        return launch_gemv_decode(L, 2, R, aq, asb, out, out_ld, num_sms, st) < 0 ||
+                       launch_gemv_decode(L, 3, R, aq, asb, out, out_ld, num_sms, st) < 0 ? -1 : 0;
     const bool probe = kind >= 2;
     if (probe) kind -= 2;
     const MatLayout &M = kind == 0 ? L.gu : L.dn;
     const int mi = kind == 0 ? kMetaDecItemsGU : kMetaDecItemsDN;
     const bool q8 = L.type == INZG_T_Q8G;
-    if (M.rows % 16) return -1;
+    if (M.rows % kRowsPerItem) return -1;
 #define INZG_GEMV_CASE(Q, N)                                                                                     \
     if (q8 == Q && M.ng == N) {                                                                                  \
         if (probe) return 0;                                                                                     \
-        if (kind == 0) launch_one<Q, N, 0>(L, M, R, aq, asq, out, out_ld, mi, maxt, grid, st);                  \
-        else launch_one<Q, N, 1>(L, M, R, aq, asq, out, out_ld, mi, maxt, grid, st);                            \
+        if (kind == 0) launch_one<Q, N, 0>(L, M, R, aq, asb, out, out_ld, mi, num_sms, st);                     \
+        else launch_one<Q, N, 1>(L, M, R, aq, asb, out, out_ld, mi, num_sms, st);                               \
         return 1;                                                                                                \
     }
     INZG_GEMV_CASE(false, 32)   // Q4L K = 2048

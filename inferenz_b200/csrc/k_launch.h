@@ -13,18 +13,22 @@ int launch_router_logits(const uint4 *Wr, const float *X, int n, int H, int E, c
 int launch_softmax_topk(const float *logits, int n, int E, int topk, int32_t *sel, float *w, float *probs,
                         cudaStream_t st);
 
+int launch_route_fused(const RouteDev &R, const float *logits, float *probs, int gu_items_per_unit,
+                       int dn_items_per_unit, int gemm_tn, int32_t *upath, int32_t *eexp, cudaStream_t st);
+void route_set_attributes(int E);
 int launch_route(const RouteDev &R, int nchunk, int gu_items_per_unit, int dn_items_per_unit, int gemm_tn,
                  int32_t *upath, int32_t *eexp, cudaStream_t st);
 
-int launch_act_quant_x(const float *X, int n, int H, int rot, uint32_t seed, int8_t *q64, int2 *sb64, int8_t *q256,
+int launch_act_quant_x(const float *X, int n, int H, int rot, uint32_t seed, int8_t *q64, float2 *sb64, int8_t *q256,
                        float *s256, cudaStream_t st);
 int launch_swiglu_quant(const float *GU, int FF, int n_entries, const int32_t *eexp, const int32_t *upath, int rot,
-                        uint32_t seed, int8_t *q64, int2 *sb64, int8_t *q256, float *s256, cudaStream_t st);
+                        uint32_t seed, int8_t *q64, float2 *sb64, int8_t *q256, float *s256, cudaStream_t st);
 int launch_combine(const float *mo, int n, int H, int topk, float *y, int num_sms, cudaStream_t st);
 
 void gemv_set_attributes();
-int launch_gemv_decode(const LayerDev &L, int kind, const RouteDev &R, const int8_t *aq, const int2 *asb, float *out,
-                       int out_ld, int maxt, int grid, cudaStream_t st);
+int launch_gemv_decode(const LayerDev &L, int kind, const RouteDev &R, const int8_t *aq, const float2 *asb, float *out,
+                       int out_ld, int num_sms, cudaStream_t st);
+int gemv_items_per_unit(const LayerDev &L, int kind);
 int launch_gemm_v1(const LayerDev &L, int kind, const RouteDev &R, const int8_t *aq, const float *as, float *out,
                    int out_ld, int grid, cudaStream_t st);
 int gemm_token_tile();

@@ -30,21 +30,26 @@ __global__ void pool_repack_kernel(const uint8_t *__restrict__ blobs, uint64_t b
         uint8_t *slab = pool + (size_t)(e0 + el) * L.slab_bytes;
         const int rt = r >> 4, rr = r & 7, hi = (r >> 3) & 1;  // row tile, row within the 8-row half, half
         uint8_t *tile = slab + M.q_off + ((size_t)rt * M.ng + g) * 32 * M.wb;
-        if (q8) {
-            for (int c = 0; c < 16; c++) {  // byte quad c of the row's 64-byte group
-                uint8_t *dst = tile + (size_t)(rr * 4 + (c & 3)) * M.wb + ((c >> 2) + 4 * hi) * 4;
-                for (int j = 0; j < 4; j++) dst[j] = sq[4 * c + j];
-            }
-        } else {
-            for (int l = 0; l < 8; l++) {
-                uint32_t w = 0;
-                for (int j = 0; j < 4; j++) {
-                    const uint32_t b = sq[4 * l + j];
-                    w |= (b & 15u) << (4 * j);          // weight 4l+j      -> selector nibble j of the low half
-                    w |= (b >> 4) << (16 + 4 * j);      // weight 32+4l+j   -> selector nibble j of the high half
+        // lane (rr, t) of MMA h: fragment registers a0/a1 carry lane l = 4h + t/2, a2/a3 lane l + 2, of part t % 2
+        // (part 0: weights 4l..4l+3, part 1: weights 32+4l..32+4l+3); hi selects a0/a2 (row rr) or a1/a3 (row rr + 8)
+        for (int t = 0; t < 4; t++) {
+            const int lane = rr * 4 + t, p = t & 1;
+            for (int h = 0; h < 2; h++) {
+                const int l0 = 4 * h + (t >> 1), l1 = l0 + 2;
+                if (q8) {
+                    uint8_t *dst = tile + (size_t)h * 512 + (size_t)lane * 16;
+                    for (int j = 0; j < 4; j++) {
+                        dst[hi * 4 + j] = sq[32 * p + 4 * l0 + j];      // a0 (row rr) / a1 (row rr + 8)
+                        dst[8 + hi * 4 + j] = sq[32 * p + 4 * l1 + j];  // a2 / a3
+                    }
+                } else {
+                    uint32_t w = 0;
+                    for (int j = 0; j < 4; j++) {
+                        w |= (uint32_t)((sq[4 * l0 + j] >> (4 * p)) & 15) << (4 * j);
+                        w |= (uint32_t)((sq[4 * l1 + j] >> (4 * p)) & 15) << (16 + 4 * j);
+                    }
+                    *reinterpret_cast<uint32_t *>(tile + (size_t)lane * 16 + (2 * h + hi) * 4) = w;
                 }
-                uint8_t *dst = tile + (size_t)(rr * 4 + (l & 3)) * M.wb + ((l >> 2) + 2 * hi) * 4;
-                *reinterpret_cast<uint32_t *>(dst) = w;
             }
         }
         uint16_t *dd = reinterpret_cast<uint16_t *>(slab + M.d_off);

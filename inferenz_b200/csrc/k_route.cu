@@ -9,12 +9,39 @@
 //                 path (decode numerics when n <= 8 or the expert has < GEMM_MIN_T tokens, src/model_fwd.c:229-249,
 //                 1070), work counts for the expert kernels
 //   route_scatter per chunk: entry position = off[e] + chunk prefix + rank
+// The decode-path expert list is the one list in scheduling order: heaviest experts (most tokens) first, so the
+// decode GEMV's work queue ends on light items. Every output position is fixed by the entry lists, so that order
+// (which is not deterministic within one token count) never changes a result.
 #include "inzg_internal.h"
 #include "k_launch.h"
+#include "k_softmax.cuh"
 
 namespace inzg {
 
 constexpr int kChunk = 32;
+
+// Decode experts in descending token count (bins by count, positions inside a bin by shared atomics); every thread
+// of the block calls it. bins: 32 ints of shared scratch. Also clears the decode GEMV work-queue counters.
+__device__ void order_dec_units(int is_dec, int c, int e, int32_t *__restrict__ dec_units, int32_t *__restrict__ meta,
+                                int32_t *bins) {
+    if (threadIdx.x < 32) bins[threadIdx.x] = 0;
+    __syncthreads();
+    const int b = c < 15 ? c : 15;
+    if (is_dec) atomicAdd(&bins[b], 1);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int run = 0;
+        for (int k = 15; k >= 0; k--) {
+            const int v = bins[k];
+            bins[16 + k] = run;
+            run += v;
+        }
+        meta[kMetaWorkGU] = 0;
+        meta[kMetaWorkDN] = 0;
+    }
+    __syncthreads();
+    if (is_dec) dec_units[atomicAdd(&bins[16 + b], 1)] = e;
+}
 
 // rank of (lane's token, k) among the earlier tokens of the chunk that selected the same expert
 __device__ __forceinline__ int chunk_rank(const int32_t (*s)[kMaxTopK], int topk, int t, int e) {
@@ -52,7 +79,7 @@ __global__ void __launch_bounds__(1024) route_scan_kernel(int n, int topk, int E
                                                           int32_t *__restrict__ dec_units, int32_t *__restrict__ gemm_units,
                                                           int32_t *__restrict__ gemm_tiles, int32_t *__restrict__ upath,
                                                           int32_t *__restrict__ meta) {
-    __shared__ int32_t sc[1024], su[1024], sd[1024], sg[1024], st[1024];
+    __shared__ int32_t sc[1024], su[1024], sd[1024], sg[1024], st[1024], bins[32];
     const int e = threadIdx.x;
     int run = 0;
     if (e < E)
@@ -82,13 +109,13 @@ __global__ void __launch_bounds__(1024) route_scan_kernel(int n, int topk, int E
         if (e == E - 1) off[E] = sc[e];
         upath[e] = is_gemm;
         if (is_unit) units[su[e] - 1] = e;
-        if (is_dec) dec_units[sd[e] - 1] = e;
         if (is_gemm) {
             gemm_units[sg[e] - 1] = e;
             const int base = st[e] - tiles;
             for (int i = 0; i < tiles; i++) gemm_tiles[base + i] = ((sg[e] - 1) << 16) | i;
         }
     }
+    order_dec_units(is_dec, c, e, dec_units, meta, bins);
     if (e == blockDim.x - 1) {
         meta[kMetaNUnits] = su[e];
         meta[kMetaNDec] = sd[e];
@@ -133,7 +160,7 @@ __global__ void __launch_bounds__(1024) route_small_kernel(const int32_t *__rest
                                                            int dn_items_per_unit, int gemm_tn, RouteDev R,
                                                            int32_t *__restrict__ upath, int32_t *__restrict__ eexp) {
     __shared__ int32_t ss[kSmallRouteMax * kMaxTopK];
-    __shared__ int32_t sc[1024], su[1024], sd[1024], sg[1024], st[1024];
+    __shared__ int32_t sc[1024], su[1024], sd[1024], sg[1024], st[1024], bins[32];
     const int e = threadIdx.x, nk = n * topk;
     for (int i = e; i < nk; i += blockDim.x) ss[i] = sel[i];
     if (e == 0) R.meta[kMetaError] = kErrNone;  // this call's sticky error code starts clear
@@ -166,7 +193,6 @@ __global__ void __launch_bounds__(1024) route_small_kernel(const int32_t *__rest
         if (e == E - 1) R.off[E] = sc[e];
         upath[e] = is_gemm;
         if (is_unit) R.units[su[e] - 1] = e;
-        if (is_dec) R.dec_units[sd[e] - 1] = e;
         if (is_gemm) {
             R.gemm_units[sg[e] - 1] = e;
             const int base = st[e] - tiles;
@@ -182,6 +208,7 @@ __global__ void __launch_bounds__(1024) route_small_kernel(const int32_t *__rest
                 pos++;
             }
     }
+    order_dec_units(is_dec, c, e, R.dec_units, R.meta, bins);
     if (e == blockDim.x - 1) {
         R.meta[kMetaNUnits] = su[e];
         R.meta[kMetaNDec] = sd[e];
@@ -192,6 +219,119 @@ __global__ void __launch_bounds__(1024) route_small_kernel(const int32_t *__rest
         R.meta[kMetaGemmTilesDN] = st[e];
         if (sc[e] != nk) set_error(R.meta, kErrOverflow);
     }
+}
+
+// inclusive scan of v over the block (blockDim.x <= 1024); ws: 32 ints of shared scratch
+__device__ __forceinline__ int block_scan_incl(int v, int *ws) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+    }
+    if (lane == 31) ws[w] = v;
+    __syncthreads();
+    if (w == 0) {
+        int s = lane < nw ? ws[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += t;
+        }
+        ws[lane] = s;
+    }
+    __syncthreads();
+    if (w > 0) v += ws[w - 1];
+    __syncthreads();
+    return v;
+}
+
+// Small calls (n <= 64) in one block of 1024 threads: softmax + top-k per token (warp per token), then the dispatch
+// lists: per entry its expert's count, first-touch key and its rank among the earlier entries of the same expert
+// (entries in (token, k) order, so ranks follow the reference's token order), the per-expert scans, and the scatter.
+constexpr int kFusedMax = 64;
+__global__ void __launch_bounds__(1024) route_fused_kernel(const float *__restrict__ logits, int n, int E, int topk,
+                                                           float *__restrict__ probs_out, int gu_items_per_unit,
+                                                           int dn_items_per_unit, int gemm_tn, RouteDev R,
+                                                           int32_t *__restrict__ upath, int32_t *__restrict__ eexp) {
+    extern __shared__ __align__(16) float ex[];  // [32][E] softmax scratch
+    __shared__ int32_t ss[kFusedMax * kMaxTopK], scnt[1024], sfirst[1024], soff[1024], ws[32], bins[32];
+    __shared__ float sw[kFusedMax * kMaxTopK];
+    const int tid = threadIdx.x, warp = tid >> 5, nk = n * topk;
+    if (tid == 0) R.meta[kMetaError] = kErrNone;
+    for (int e = tid; e < E; e += blockDim.x) { scnt[e] = 0; sfirst[e] = 0x7F7F7F7F; }
+    for (int t = warp; t < n; t += blockDim.x >> 5)
+        softmax_topk_warp(logits + (size_t)t * E, E, topk, ex + (size_t)warp * E,
+                          probs_out ? probs_out + (size_t)t * E : nullptr, ss + t * topk, sw + t * topk);
+    __syncthreads();
+    int rank = 0, e_i = -1;
+    if (tid < nk) {
+        e_i = ss[tid];
+        R.sel[tid] = e_i;
+        R.w[tid] = sw[tid];
+        if (e_i < 0 || e_i >= E) { set_error(R.meta, kErrBadExpert); e_i = -1; }
+        else {
+            atomicAdd(&scnt[e_i], 1);
+            atomicMin(&sfirst[e_i], tid);
+            for (int j = 0; j < tid; j++) rank += ss[j] == e_i;
+        }
+    }
+    __syncthreads();
+    const int e = tid;
+    const int c = e < E ? scnt[e] : 0;
+    const int is_unit = c > 0, is_dec = is_unit && (n <= 8 || c < kGemmMinT), is_gemm = is_unit && !is_dec;
+    const int tiles = is_gemm ? (c + gemm_tn - 1) / gemm_tn : 0;
+    // two scans: counts | tiles (11 bits each), units | decode | prefill counts (10 bits each)
+    const int sa = block_scan_incl(c | (tiles << 11), ws);
+    const int sb = block_scan_incl(is_unit | (is_dec << 10) | (is_gemm << 20), ws);
+    const int c_incl = sa & 2047, t_incl = sa >> 11;
+    const int u_incl = sb & 1023, d_incl = (sb >> 10) & 1023, g_incl = sb >> 20;
+    if (e < E) {
+        const int off = c_incl - c;
+        soff[e] = off;
+        R.cnt[e] = c;
+        R.off[e] = off;
+        R.first[e] = sfirst[e];
+        if (e == E - 1) R.off[E] = c_incl;
+        upath[e] = is_gemm;
+        if (is_unit) R.units[u_incl - 1] = e;
+        if (is_gemm) {
+            R.gemm_units[g_incl - 1] = e;
+            for (int i = 0; i < tiles; i++) R.gemm_tiles[t_incl - tiles + i] = ((g_incl - 1) << 16) | i;
+        }
+    }
+    order_dec_units(is_dec, c, e, R.dec_units, R.meta, bins);
+    if (tid == blockDim.x - 1) {
+        R.meta[kMetaNUnits] = u_incl;
+        R.meta[kMetaNDec] = d_incl;
+        R.meta[kMetaNGemm] = g_incl;
+        R.meta[kMetaDecItemsGU] = d_incl * gu_items_per_unit;
+        R.meta[kMetaDecItemsDN] = d_incl * dn_items_per_unit;
+        R.meta[kMetaGemmTilesGU] = t_incl;
+        R.meta[kMetaGemmTilesDN] = t_incl;
+        if (c_incl != nk) set_error(R.meta, kErrOverflow);
+    }
+    __syncthreads();
+    if (tid < nk && e_i >= 0) {
+        const int pos = soff[e_i] + rank;
+        R.etok[pos] = tid / topk;
+        R.eslot[pos] = tid;
+        R.ew[pos] = sw[tid];
+        eexp[pos] = e_i;
+    }
+}
+
+int launch_route_fused(const RouteDev &R, const float *logits, float *probs, int gu_items_per_unit,
+                       int dn_items_per_unit, int gemm_tn, int32_t *upath, int32_t *eexp, cudaStream_t st) {
+    if (R.n > kFusedMax || R.E > 1024 || R.n * R.topk > kFusedMax * kMaxTopK) return -1;
+    const size_t smem = (size_t)32 * R.E * sizeof(float);
+    route_fused_kernel<<<1, 1024, smem, st>>>(logits, R.n, R.E, R.topk, probs, gu_items_per_unit, dn_items_per_unit,
+                                              gemm_tn, R, upath, eexp);
+    return 1;
+}
+
+void route_set_attributes(int E) {
+    cudaFuncSetAttribute(route_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 32 * E * (int)sizeof(float));
 }
 
 int launch_route(const RouteDev &R, int nchunk, int gu_items_per_unit, int dn_items_per_unit, int gemm_tn,

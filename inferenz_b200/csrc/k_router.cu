@@ -8,6 +8,7 @@
 // 8 chain steps: Wr[eq][jc][e%4][l][8 halves], eq = e/4, jc = j/8.
 #include "inzg_internal.h"
 #include "k_launch.h"
+#include "k_softmax.cuh"
 
 #include <cuda_fp16.h>
 
@@ -173,97 +174,16 @@ __global__ void __launch_bounds__(256) router_large_kernel(const uint4 *__restri
     }
 }
 
-// exp256_ps (Cephes), src/vmath.h:9-25, one lane
-__device__ __forceinline__ float cephes_exp(float x) {
-    x = fminf(fmaxf(x, -87.3f), 88.3f);
-    const float fx = rintf(__fmul_rn(x, 1.44269504088896341f));
-    x = __fmaf_rn(-fx, 0.693359375f, x);
-    x = __fmaf_rn(-fx, -2.12194440e-4f, x);
-    const float z = __fmul_rn(x, x);
-    float y = 1.9875691500e-4f;
-    y = __fmaf_rn(y, x, 1.3981999507e-3f);
-    y = __fmaf_rn(y, x, 8.3334519073e-3f);
-    y = __fmaf_rn(y, x, 4.1665795894e-2f);
-    y = __fmaf_rn(y, x, 1.6666665459e-1f);
-    y = __fmaf_rn(y, x, 5.0000001201e-1f);
-    y = __fadd_rn(__fmaf_rn(y, z, x), 1.0f);
-    return __fmul_rn(y, __int_as_float(((int)fx + 127) << 23));
-}
-
-// One warp per token: softmax_inplace (src/vmath.h:42-60), topk_f32 (src/sampler.c:95-127: order value desc,
-// index asc), and the renormalised weights of moe_block (src/model_fwd.c:1006-1011, 1028: sum left to right,
-// w_k = p_k / sum). E % 32 == 0, E <= 1024. Lane j holds elements j + 32 m.
-constexpr int kMaxPerLane = 32;
+// One warp per token: the routing weights of every token (see k_softmax.cuh).
 __global__ void __launch_bounds__(256) softmax_topk_kernel(const float *__restrict__ logits, int n, int E, int topk,
                                                             int32_t *__restrict__ sel, float *__restrict__ wsel,
                                                             float *__restrict__ probs_out) {
     __shared__ float ex[8][1024];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
     const int t = blockIdx.x * (blockDim.x >> 5) + warp;
     if (t >= n) return;
-    const int per = E / 32;
-    const float *lg = logits + (size_t)t * E;
-    float v[kMaxPerLane];
-    float mx = -INFINITY;
-#pragma unroll
-    for (int m = 0; m < kMaxPerLane; m++)
-        if (m < per) {
-            v[m] = lg[lane + 32 * m];
-            mx = v[m] > mx ? v[m] : mx;
-        }
-    for (int o = 16; o; o >>= 1) {
-        const float q = __shfl_xor_sync(0xffffffffu, mx, o);
-        mx = q > mx ? q : mx;
-    }
-#pragma unroll
-    for (int m = 0; m < kMaxPerLane; m++)
-        if (m < per) {
-            v[m] = cephes_exp(__fsub_rn(v[m], mx));
-            ex[warp][lane + 32 * m] = v[m];
-        }
-    __syncwarp();
-    // 8 lane sums: accumulator l adds elements l, l+8, l+16, ... in order (the reference's 8-wide running sum)
-    float part = 0.0f;
-    if (lane < 8)
-        for (int i = lane; i < E; i += 8) part = __fadd_rn(part, ex[warp][i]);
-    const float sum = __shfl_sync(0xffffffffu, hsum8_lanes(part), 0);
-    const float inv = __fdiv_rn(1.0f, sum);
-#pragma unroll
-    for (int m = 0; m < kMaxPerLane; m++)
-        if (m < per) {
-            v[m] = __fmul_rn(v[m], inv);
-            if (probs_out) probs_out[(size_t)t * E + lane + 32 * m] = v[m];
-        }
-    // top-k: k rounds of a warp arg-max under (value desc, index asc); the winner is removed by its owner
-    unsigned taken = 0;  // bit m: element lane + 32 m already selected
-    float wk[kMaxTopK];
-    int ik[kMaxTopK];
-    for (int k = 0; k < topk; k++) {
-        float bv = -INFINITY;
-        int bi = 0x7FFFFFFF;
-#pragma unroll
-        for (int m = 0; m < kMaxPerLane; m++)
-            if (m < per && !((taken >> m) & 1u)) {
-                const int i = lane + 32 * m;
-                if (v[m] > bv || (v[m] == bv && i < bi)) { bv = v[m]; bi = i; }
-            }
-        for (int o = 16; o; o >>= 1) {
-            const float qv = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int qi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (qv > bv || (qv == bv && qi < bi)) { bv = qv; bi = qi; }
-        }
-        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-        wk[k] = bv;
-        ik[k] = bi;
-    }
-    if (lane == 0) {
-        float s = 0.0f;
-        for (int k = 0; k < topk; k++) s = __fadd_rn(s, wk[k]);
-        for (int k = 0; k < topk; k++) {
-            sel[(size_t)t * topk + k] = ik[k];
-            wsel[(size_t)t * topk + k] = __fdiv_rn(wk[k], s);
-        }
-    }
+    softmax_topk_warp(logits + (size_t)t * E, E, topk, ex[warp], probs_out ? probs_out + (size_t)t * E : nullptr,
+                      sel + (size_t)t * topk, wsel + (size_t)t * topk);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
