@@ -58,7 +58,8 @@ typedef struct {
     int device;       /* CUDA device ordinal */
 } inzg_config;
 
-#define INZG_IO_DEVICE 1u   /* xin, y, logit_bias and logits_override are device pointers; the call is stream-ordered */
+#define INZG_IO_DEVICE 1u   /* xin, y, logit_bias and logits_override are device pointers (xin, y, logits_override
+                             * 16-byte aligned, else INZG_BAD_ARG); the call is stream-ordered */
 #define INZG_DUMP_ROUTE 2u  /* keep the routing products of this call for inzg_moe_route_dump */
 #define INZG_PROFILE 4u     /* time every stage with CUDA events on the call's stream; the call then synchronises */
 #define INZG_NO_GRAPH 8u    /* launch the kernels one by one instead of replaying the cached CUDA graph */
@@ -123,8 +124,8 @@ INZG_EXPORT const char *inzg_stage_name(int stage);
  * call path -- an engine whose device-memory plan is fixed at start-up, or a latency-critical decode loop in which a
  * cudaMalloc/cudaFree would synchronise the device -- this runs the router, softmax and top-k of one layer (the
  * routing stage of inzg_moe_forward, same results bit for bit) with its intermediate logits in a static device array
- * of the library instead of allocated scratch. x_dev [n][hidden], logit_bias_dev [n_expert] (optional), sel_dev
- * [n][topk] and w_dev [n][topk] are device pointers; the call is ordered on `stream` (NULL = the legacy default
+ * of the library instead of allocated scratch. x_dev [n][hidden] (16-byte aligned), logit_bias_dev [n_expert]
+ * (optional), sel_dev [n][topk] and w_dev [n][topk] are device pointers; the call is ordered on `stream` (NULL = the legacy default
  * stream) and returns without synchronising. Limits: n <= 64 and n_expert <= 512 (the array is 64 x 512 fp32 =
  * 128 KiB, held by every GPU that loads the library until exit); larger calls return INZG_BAD_ARG. The first call on
  * a device looks up the array's device address (cudaGetSymbolAddress) and should come before any stream capture.

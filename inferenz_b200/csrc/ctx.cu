@@ -446,7 +446,7 @@ static int enqueue_forward(inzg_ctx *c, const LayerSlot &L, int n, const float *
         if (ovr_on_device)
             cudaMemcpyAsync(c->logits, ovr, sizeof(float) * (size_t)n * E, cudaMemcpyDeviceToDevice, st);
     } else {
-        launches += launch_router_logits(L.router, X, n, H, E, bias, c->logits, st);
+        launches += launch_router_logits(L.router, X, n, H, E, bias, c->logits, c->meta, st);
     }
     mark(1);
     RouteDev R{};
@@ -517,6 +517,10 @@ inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, fl
     const float *ovr = opt ? opt->logits_override : nullptr;
     const float *bias = opt ? opt->logit_bias : nullptr;
     if (!L.has_experts || (!L.has_router && !ovr)) return fail(c, INZG_NOT_READY, "moe_forward: layer not loaded");
+    // the kernels move token rows with 16-byte vector loads and bulk copies
+    if (dev_io && ((reinterpret_cast<uintptr_t>(xin) | reinterpret_cast<uintptr_t>(y) |
+                    reinterpret_cast<uintptr_t>(ovr)) & 15))
+        return fail(c, INZG_BAD_ARG, "moe_forward: device xin, y and logits_override must be 16-byte aligned");
     cudaSetDevice(cf.device);
     cudaStream_t st = opt && opt->stream ? static_cast<cudaStream_t>(opt->stream) : c->stream;
     const int H = cf.hidden, E = cf.n_expert;

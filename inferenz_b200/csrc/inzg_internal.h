@@ -63,14 +63,15 @@ struct RouteDev {
     int32_t *units;      // [E] experts with cnt > 0, ascending
     int32_t *meta;       // [16] counters: 0 nunits, 1 n_dec_units, 2 n_gemm_units, 3 n_dec_items_gu, 4 n_dec_items_dn,
                          //      5 n_gemm_tiles_gu, 6 n_gemm_tiles_dn, 7 device error code, 8/9 decode GEMV work
-                         //      queues (gate|up, down)
+                         //      queues (gate|up, down), 10 router error code
     int32_t *dec_units;  // [E] decode-path experts, most tokens first
     int32_t *gemm_units; // [E] prefill-path experts
     int32_t *gemm_tiles; // [E * tiles] (unit index << 16 | token tile) for the GEMM path
 };
 
 constexpr int kMetaNUnits = 0, kMetaNDec = 1, kMetaNGemm = 2, kMetaDecItemsGU = 3, kMetaDecItemsDN = 4,
-              kMetaGemmTilesGU = 5, kMetaGemmTilesDN = 6, kMetaError = 7, kMetaWorkGU = 8, kMetaWorkDN = 9;
+              kMetaGemmTilesGU = 5, kMetaGemmTilesDN = 6, kMetaError = 7, kMetaWorkGU = 8, kMetaWorkDN = 9,
+              kMetaRouterError = 10;  // the router's own error word, folded into kMetaError by the route kernel
 
 // device error codes (sticky, first one wins)
 constexpr int kErrNone = 0, kErrBadExpert = 1, kErrBadSlot = 2, kErrOverflow = 3, kErrTimeout = 4;
@@ -104,5 +105,11 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
 }
 
 __device__ __forceinline__ void set_error(int32_t *meta, int code) { atomicCAS(&meta[kMetaError], 0, code); }
+
+// first device error of this call: what the router recorded (it runs before the route kernel clears the word)
+__device__ __forceinline__ void begin_call_errors(int32_t *meta) {
+    meta[kMetaError] = meta[kMetaRouterError];
+    meta[kMetaRouterError] = kErrNone;
+}
 
 }  // namespace inzg

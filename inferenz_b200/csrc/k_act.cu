@@ -147,13 +147,13 @@ int launch_gather_gemm_rows(const int8_t *q, const float *s, int K, int nkb, con
 // holds elements b*B + L*VPL + r. Butterfly stage len pairs (i, i+len): inside a lane when len < VPL, else with lane
 // L ^ (len / VPL) through a shuffle; the lower element gets a + b, the upper a - b, exactly as the reference.
 template <int NB, int VPL>
-__device__ __forceinline__ void warp_rotate(float (&v)[NB][VPL], uint32_t seed, float norm, int lane) {
+__device__ __forceinline__ void warp_rotate(float (&v)[NB][VPL], uint32_t seed, float norm, int lane, int base = 0) {
     constexpr int B = 32 * VPL;
 #pragma unroll
     for (int b = 0; b < NB; b++)
 #pragma unroll
         for (int r = 0; r < VPL; r++)
-            if (rot_sign_bit(seed, (uint32_t)(b * B + lane * VPL + r))) v[b][r] = -v[b][r];
+            if (rot_sign_bit(seed, (uint32_t)(base + b * B + lane * VPL + r))) v[b][r] = -v[b][r];
 #pragma unroll
     for (int len = 1; len < B; len <<= 1) {
         if (len < VPL) {
@@ -247,68 +247,88 @@ __device__ __forceinline__ void warp_quantize(const float (&v)[NB][VPL], int n, 
     (void)n;
 }
 
-// one warp per token: x [n][H] (H = NB * 256), rotation block 256
+// one warp per (token, 256-element rotation block): x [n][H] (H = NB * 256); the block is also a 256-block of the
+// prefill numerics and holds four 64-groups of the decode numerics, so every warp works alone
 template <int NB>
-__global__ void __launch_bounds__(128) act_quant_x_warp_kernel(const float *__restrict__ X, int n, uint32_t seed,
+__global__ void __launch_bounds__(256) act_quant_x_warp_kernel(const float *__restrict__ X, int n, uint32_t seed,
                                                                float norm, int8_t *__restrict__ q64,
                                                                float2 *__restrict__ sb64, int8_t *__restrict__ q256,
                                                                float *__restrict__ s256) {
     constexpr int VPL = 8, H = NB * 256;
     const int lane = threadIdx.x & 31;
-    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int wi = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int t = wi / NB, b = wi % NB;
     if (t >= n) return;
-    float v[NB][VPL];
-    const float *x = X + (size_t)t * H;
-#pragma unroll
-    for (int b = 0; b < NB; b++) {
-        const float4 a = reinterpret_cast<const float4 *>(x + b * 256 + lane * 8)[0];
-        const float4 c = reinterpret_cast<const float4 *>(x + b * 256 + lane * 8)[1];
-        v[b][0] = a.x; v[b][1] = a.y; v[b][2] = a.z; v[b][3] = a.w;
-        v[b][4] = c.x; v[b][5] = c.y; v[b][6] = c.z; v[b][7] = c.w;
-    }
-    warp_rotate<NB, VPL>(v, seed, norm, lane);
-    warp_quantize<NB, VPL>(v, H, lane, q64 + (size_t)t * H, sb64 + (size_t)t * (H / kGroup),
-                           q256 ? q256 + (size_t)t * H : nullptr, q256 ? s256 + (size_t)t * (H / kKB) : nullptr);
+    float v[1][VPL];
+    const float *x = X + (size_t)t * H + b * 256;
+    const float4 a = reinterpret_cast<const float4 *>(x + lane * 8)[0];
+    const float4 c = reinterpret_cast<const float4 *>(x + lane * 8)[1];
+    v[0][0] = a.x; v[0][1] = a.y; v[0][2] = a.z; v[0][3] = a.w;
+    v[0][4] = c.x; v[0][5] = c.y; v[0][6] = c.z; v[0][7] = c.w;
+    warp_rotate<1, VPL>(v, seed, norm, lane, b * 256);
+    const size_t o = (size_t)t * H + b * 256;
+    warp_quantize<1, VPL>(v, 256, lane, q64 + o, sb64 + o / kGroup, q256 ? q256 + o : nullptr,
+                          q256 ? s256 + (size_t)t * (H / kKB) + b : nullptr);
 }
 
-// one warp per entry: h = silu(g) * u over FF = NB * 128 values, rotation block 128, quantized for the expert's path
+// One block of NB warps per entry: h = silu(g) * u over FF = NB * 128 values (siluf, src/model_fwd.c:43), warp w
+// rotates block w (rotation block 128). Decode-path entries quantize per 64-group inside each warp; prefill-path
+// entries quantize per 256-block (blocks 2w, 2w+1 -- the last one partial), the two warps of a block meeting in
+// shared memory for its amax.
 template <int NB>
-__global__ void __launch_bounds__(128) swiglu_quant_warp_kernel(const float *__restrict__ GU, int n_entries,
-                                                                const int32_t *__restrict__ eexp,
-                                                                const int32_t *__restrict__ upath, uint32_t seed,
-                                                                float norm, int8_t *__restrict__ q64,
-                                                                float2 *__restrict__ sb64, int8_t *__restrict__ q256,
-                                                                float *__restrict__ s256) {
-    constexpr int VPL = 4, FF = NB * 128;
-    const int lane = threadIdx.x & 31;
-    const int pos = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+__global__ void __launch_bounds__(NB * 32) swiglu_quant_warp_kernel(const float *__restrict__ GU, int n_entries,
+                                                                    const int32_t *__restrict__ eexp,
+                                                                    const int32_t *__restrict__ upath, uint32_t seed,
+                                                                    float norm, int8_t *__restrict__ q64,
+                                                                    float2 *__restrict__ sb64, int8_t *__restrict__ q256,
+                                                                    float *__restrict__ s256) {
+    constexpr int VPL = 4, FF = NB * 128, NKB = (FF + kKB - 1) / kKB;
+    __shared__ float amax_w[NB];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int pos = blockIdx.x;
     if (pos >= n_entries) return;
     const float *g = GU + (size_t)pos * 2 * FF;
-    float v[NB][VPL];
-#pragma unroll
-    for (int b = 0; b < NB; b++) {
-        const float4 a = reinterpret_cast<const float4 *>(g + b * 128 + lane * 4)[0];
-        const float4 u = reinterpret_cast<const float4 *>(g + FF + b * 128 + lane * 4)[0];
+    float v[1][VPL];
+    {
+        const float4 a = reinterpret_cast<const float4 *>(g + w * 128 + lane * 4)[0];
+        const float4 u = reinterpret_cast<const float4 *>(g + FF + w * 128 + lane * 4)[0];
         const float av[4] = {a.x, a.y, a.z, a.w}, uv[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-        for (int r = 0; r < 4; r++)  // siluf (src/model_fwd.c:43): x / (1 + expf(-x)), then * up
-            v[b][r] = __fmul_rn(__fdiv_rn(av[r], __fadd_rn(1.0f, (float)exp(-(double)av[r]))), uv[r]);
+        for (int r = 0; r < 4; r++)
+            v[0][r] = __fmul_rn(__fdiv_rn(av[r], __fadd_rn(1.0f, (float)exp(-(double)av[r]))), uv[r]);
     }
-    warp_rotate<NB, VPL>(v, seed, norm, lane);
+    warp_rotate<1, VPL>(v, seed, norm, lane, w * 128);
     const bool gemm = upath[eexp[pos]] != 0;
-    constexpr int nkb = (FF + kKB - 1) / kKB;
-    if (gemm) warp_quantize<NB, VPL>(v, FF, lane, nullptr, nullptr, q256 + (size_t)pos * FF, s256 + (size_t)pos * nkb);
-    else warp_quantize<NB, VPL>(v, FF, lane, q64 + (size_t)pos * FF, sb64 + (size_t)pos * (FF / kGroup), nullptr, nullptr);
+    if (!gemm) {
+        const size_t o = (size_t)pos * FF + w * 128;
+        warp_quantize<1, VPL>(v, 128, lane, q64 + o, sb64 + o / kGroup, nullptr, nullptr);
+        return;
+    }
+    float am = 0.0f;
+#pragma unroll
+    for (int r = 0; r < VPL; r++) am = fmaxf(am, fabsf(v[0][r]));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    if (lane == 0) amax_w[w] = am;
+    __syncthreads();
+    const int kb = w >> 1;
+    const float amax = (2 * kb + 1 < NB) ? fmaxf(amax_w[2 * kb], amax_w[2 * kb + 1]) : amax_w[2 * kb];
+    const float sc = __fdiv_rn(amax, 127.0f);
+    const float inv = sc > 0 ? __fdiv_rn(1.0f, sc) : 0.0f;
+    int q[4];
+#pragma unroll
+    for (int r = 0; r < 4; r++) q[r] = __float2int_rn(__fmul_rn(v[0][r], inv));
+    *reinterpret_cast<uint32_t *>(q256 + (size_t)pos * FF + w * 128 + lane * 4) = pack4(q[0], q[1], q[2], q[3]);
+    if (lane == 0 && (w & 1) == 0) s256[(size_t)pos * NKB + kb] = sc;
 }
 
 int launch_act_quant_x(const float *X, int n, int H, int rot, uint32_t seed, int8_t *q64, float2 *sb64, int8_t *q256,
                        float *s256, cudaStream_t st) {
     const float norm = rot > 1 ? 1.0f / sqrtf((float)rot) : 1.0f;
-    const int blocks = (n + 3) / 4;
     if (rot == 256 && H == 2048) {
-        act_quant_x_warp_kernel<8><<<blocks, 128, 0, st>>>(X, n, seed, norm, q64, sb64, q256, s256);
+        act_quant_x_warp_kernel<8><<<n, 256, 0, st>>>(X, n, seed, norm, q64, sb64, q256, s256);
     } else if (rot == 256 && H == 2560) {
-        act_quant_x_warp_kernel<10><<<blocks, 128, 0, st>>>(X, n, seed, norm, q64, sb64, q256, s256);
+        act_quant_x_warp_kernel<10><<<(n * 10 + 7) / 8, 256, 0, st>>>(X, n, seed, norm, q64, sb64, q256, s256);
     } else {
         act_quant_x_kernel<<<n, 256, H * sizeof(float), st>>>(X, n, H, rot, seed, norm, q64, sb64, q256, s256);
     }
@@ -319,8 +339,8 @@ int launch_swiglu_quant(const float *GU, int FF, int n_entries, const int32_t *e
                         uint32_t seed, int8_t *q64, float2 *sb64, int8_t *q256, float *s256, cudaStream_t st) {
     const float norm = rot > 1 ? 1.0f / sqrtf((float)rot) : 1.0f;
     if (rot == 128 && FF == 640) {
-        swiglu_quant_warp_kernel<5><<<(n_entries + 3) / 4, 128, 0, st>>>(GU, n_entries, eexp, upath, seed, norm, q64,
-                                                                          sb64, q256, s256);
+        swiglu_quant_warp_kernel<5><<<n_entries, 160, 0, st>>>(GU, n_entries, eexp, upath, seed, norm, q64, sb64, q256,
+                                                               s256);
         return 1;
     }
     swiglu_quant_kernel<<<n_entries, 128, FF * sizeof(float), st>>>(GU, FF, n_entries, eexp, upath, rot, seed, norm, q64,

@@ -9,7 +9,7 @@ namespace inzg {
 void router_set_attributes(int H);
 void launch_router_repack(const uint16_t *W, uint4 *Wr, int E, int H, cudaStream_t st);
 int launch_router_logits(const uint4 *Wr, const float *X, int n, int H, int E, const float *bias, float *logits,
-                         cudaStream_t st);
+                         int32_t *meta, cudaStream_t st);
 int launch_softmax_topk(const float *logits, int n, int E, int topk, int32_t *sel, float *w, float *probs,
                         cudaStream_t st);
 

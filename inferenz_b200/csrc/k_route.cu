@@ -16,6 +16,10 @@
 #include "k_launch.h"
 #include "k_softmax.cuh"
 
+#include <cooperative_groups.h>
+
+namespace cg = cooperative_groups;
+
 namespace inzg {
 
 constexpr int kChunk = 32;
@@ -117,6 +121,9 @@ __global__ void __launch_bounds__(1024) route_scan_kernel(int n, int topk, int E
     }
     order_dec_units(is_dec, c, e, dec_units, meta, bins);
     if (e == blockDim.x - 1) {
+        const int rerr = meta[kMetaRouterError];  // the router ran before this call's counters were cleared
+        if (rerr) set_error(meta, rerr);
+        meta[kMetaRouterError] = kErrNone;
         meta[kMetaNUnits] = su[e];
         meta[kMetaNDec] = sd[e];
         meta[kMetaNGemm] = sg[e];
@@ -163,7 +170,7 @@ __global__ void __launch_bounds__(1024) route_small_kernel(const int32_t *__rest
     __shared__ int32_t sc[1024], su[1024], sd[1024], sg[1024], st[1024], bins[32];
     const int e = threadIdx.x, nk = n * topk;
     for (int i = e; i < nk; i += blockDim.x) ss[i] = sel[i];
-    if (e == 0) R.meta[kMetaError] = kErrNone;  // this call's sticky error code starts clear
+    if (e == 0) begin_call_errors(R.meta);  // this call's sticky error code starts with the router's
     __syncthreads();
     int c = 0, first = 0x7F7F7F7F;
     if (e < E)
@@ -246,39 +253,53 @@ __device__ __forceinline__ int block_scan_incl(int v, int *ws) {
     return v;
 }
 
-// Small calls (n <= 64) in one block of 1024 threads: softmax + top-k per token (warp per token), then the dispatch
-// lists: per entry its expert's count, first-touch key and its rank among the earlier entries of the same expert
-// (entries in (token, k) order, so ranks follow the reference's token order), the per-expert scans, and the scatter.
-constexpr int kFusedMax = 64;
-__global__ void __launch_bounds__(1024) route_fused_kernel(const float *__restrict__ logits, int n, int E, int topk,
-                                                           float *__restrict__ probs_out, int gu_items_per_unit,
-                                                           int dn_items_per_unit, int gemm_tn, RouteDev R,
-                                                           int32_t *__restrict__ upath, int32_t *__restrict__ eexp) {
+// Small calls (n <= 64) in one cluster of kRouteCluster blocks of 1024 threads. Softmax + top-k run one warp per
+// token, the tokens spread over the cluster's SMs (token t on block t % kRouteCluster), each warp writing its token's
+// selections straight into block 0's shared memory (distributed shared memory). After the cluster barrier block 0
+// alone builds the dispatch lists. Each expert keeps a 64-bit mask of the tokens that chose it, so its count is a
+// popcount, its first-touch key is the first token's slot, and an entry's rank in the expert's token-ordered list is
+// the popcount of the lower tokens -- the reference's order, without a scan over earlier entries.
+constexpr int kFusedMax = 64, kRouteCluster = 8;
+__global__ void __cluster_dims__(kRouteCluster, 1, 1) __launch_bounds__(1024)
+    route_fused_kernel(const float *__restrict__ logits, int n, int E, int topk, float *__restrict__ probs_out,
+                       int gu_items_per_unit, int dn_items_per_unit, int gemm_tn, RouteDev R,
+                       int32_t *__restrict__ upath, int32_t *__restrict__ eexp) {
     extern __shared__ __align__(16) float ex[];  // [32][E] softmax scratch
-    __shared__ int32_t ss[kFusedMax * kMaxTopK], scnt[1024], sfirst[1024], soff[1024], ws[32], bins[32];
+    __shared__ unsigned long long emask[1024];
+    __shared__ int32_t ss[kFusedMax * kMaxTopK], soff[1024], ws[32], bins[32];
     __shared__ float sw[kFusedMax * kMaxTopK];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
     const int tid = threadIdx.x, warp = tid >> 5, nk = n * topk;
-    if (tid == 0) R.meta[kMetaError] = kErrNone;
-    for (int e = tid; e < E; e += blockDim.x) { scnt[e] = 0; sfirst[e] = 0x7F7F7F7F; }
-    for (int t = warp; t < n; t += blockDim.x >> 5)
+    int32_t *ss0 = cluster.map_shared_rank(ss, 0);
+    float *sw0 = cluster.map_shared_rank(sw, 0);
+    for (int t = rank + kRouteCluster * warp; t < n; t += kRouteCluster * (blockDim.x >> 5))
         softmax_topk_warp(logits + (size_t)t * E, E, topk, ex + (size_t)warp * E,
-                          probs_out ? probs_out + (size_t)t * E : nullptr, ss + t * topk, sw + t * topk);
-    __syncthreads();
-    int rank = 0, e_i = -1;
+                          probs_out ? probs_out + (size_t)t * E : nullptr, ss0 + t * topk, sw0 + t * topk);
+    if (rank == 0) {
+        if (tid == 0) begin_call_errors(R.meta);
+        for (int e = tid; e < E; e += blockDim.x) emask[e] = 0ull;
+    }
+    cluster.sync();  // every token's selections are in block 0 (release / acquire at cluster scope)
+    if (rank != 0) return;
+    int e_i = -1;
     if (tid < nk) {
         e_i = ss[tid];
         R.sel[tid] = e_i;
         R.w[tid] = sw[tid];
         if (e_i < 0 || e_i >= E) { set_error(R.meta, kErrBadExpert); e_i = -1; }
-        else {
-            atomicAdd(&scnt[e_i], 1);
-            atomicMin(&sfirst[e_i], tid);
-            for (int j = 0; j < tid; j++) rank += ss[j] == e_i;
-        }
+        else atomicOr(&emask[e_i], 1ull << (tid / topk));
     }
     __syncthreads();
     const int e = tid;
-    const int c = e < E ? scnt[e] : 0;
+    const unsigned long long mask = e < E ? emask[e] : 0ull;
+    const int c = __popcll(mask);
+    int first = 0x7F7F7F7F;
+    if (c) {
+        const int t0 = __ffsll((long long)mask) - 1;
+        for (int k = 0; k < topk; k++)
+            if (ss[t0 * topk + k] == e) first = t0 * topk + k;
+    }
     const int is_unit = c > 0, is_dec = is_unit && (n <= 8 || c < kGemmMinT), is_gemm = is_unit && !is_dec;
     const int tiles = is_gemm ? (c + gemm_tn - 1) / gemm_tn : 0;
     // two scans: counts | tiles (11 bits each), units | decode | prefill counts (10 bits each)
@@ -291,7 +312,7 @@ __global__ void __launch_bounds__(1024) route_fused_kernel(const float *__restri
         soff[e] = off;
         R.cnt[e] = c;
         R.off[e] = off;
-        R.first[e] = sfirst[e];
+        R.first[e] = first;
         if (e == E - 1) R.off[E] = c_incl;
         upath[e] = is_gemm;
         if (is_unit) R.units[u_incl - 1] = e;
@@ -313,8 +334,9 @@ __global__ void __launch_bounds__(1024) route_fused_kernel(const float *__restri
     }
     __syncthreads();
     if (tid < nk && e_i >= 0) {
-        const int pos = soff[e_i] + rank;
-        R.etok[pos] = tid / topk;
+        const int t = tid / topk;
+        const int pos = soff[e_i] + __popcll(emask[e_i] & ((1ull << t) - 1ull));
+        R.etok[pos] = t;
         R.eslot[pos] = tid;
         R.ew[pos] = sw[tid];
         eexp[pos] = e_i;
@@ -325,8 +347,8 @@ int launch_route_fused(const RouteDev &R, const float *logits, float *probs, int
                        int dn_items_per_unit, int gemm_tn, int32_t *upath, int32_t *eexp, cudaStream_t st) {
     if (R.n > kFusedMax || R.E > 1024 || R.n * R.topk > kFusedMax * kMaxTopK) return -1;
     const size_t smem = (size_t)32 * R.E * sizeof(float);
-    route_fused_kernel<<<1, 1024, smem, st>>>(logits, R.n, R.E, R.topk, probs, gu_items_per_unit, dn_items_per_unit,
-                                              gemm_tn, R, upath, eexp);
+    route_fused_kernel<<<kRouteCluster, 1024, smem, st>>>(logits, R.n, R.E, R.topk, probs, gu_items_per_unit,
+                                                          dn_items_per_unit, gemm_tn, R, upath, eexp);
     return 1;
 }
 
@@ -345,7 +367,7 @@ int launch_route(const RouteDev &R, int nchunk, int gu_items_per_unit, int dn_it
     }
     cudaMemsetAsync(R.ccnt, 0, sizeof(int32_t) * (size_t)nchunk * E, st);
     cudaMemsetAsync(R.first, 0x7F, sizeof(int32_t) * (size_t)E, st);
-    cudaMemsetAsync(R.meta, 0, sizeof(int32_t) * 16, st);
+    cudaMemsetAsync(R.meta, 0, sizeof(int32_t) * kMetaRouterError, st);  // the router's word is folded in by route_scan
     const int blocks = (nchunk + 3) / 4;
     route_count_kernel<<<blocks, 128, 0, st>>>(R.sel, n, topk, E, R.ccnt, R.first, R.meta);
     const int threads = (E + 31) / 32 * 32;

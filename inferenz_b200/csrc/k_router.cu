@@ -9,6 +9,7 @@
 #include "inzg_internal.h"
 #include "k_launch.h"
 #include "k_softmax.cuh"
+#include "k_async.cuh"
 
 #include <cuda_fp16.h>
 
@@ -71,49 +72,66 @@ __device__ __forceinline__ void write_logit(float acc, int l, int tt, int nt, in
     }
 }
 
-// Few tokens: one thread per (expert, lane) and TT tokens, 4 experts per warp, warps per block = blockDim/32.
-// Latency-bound (2 MB of weights, chains of H/8 dependent FMAs): the weights of the next 8 chunks are loaded while
-// the current 8 are used.
-template <int TT>
-__global__ void __launch_bounds__(128) router_small_kernel(const uint4 *__restrict__ Wr, const float *__restrict__ X,
-                                                            int n, int H, int E, const float *__restrict__ bias,
-                                                            float *__restrict__ logits) {
-    extern __shared__ __align__(16) float xs[];
-    const int S = H / 8, SC = S / 8, SP = S + 4;
+// Few tokens: thread (q, l) of a warp owns lane l of two experts, 8b + q and 8b + 4 + q (one from each of two
+// consecutive quads of the re-laid-out router), for TT tokens. The block requests everything at once with bulk
+// copies -- its 2 x WPB quads of weights (contiguous in Wr) and the TT token rows in natural layout -- then runs the
+// chains from shared memory: per 8 chain steps one 16-byte load of weights per expert and one 4-byte load of x per
+// step and token (the warp's 8 lanes read 8 consecutive floats; the 4 q's share them), each x feeding two FMAs.
+template <int TT, int WPB>
+__global__ void __launch_bounds__(WPB * 32) router_small_kernel(const uint4 *__restrict__ Wr, const float *__restrict__ X,
+                                                                 int n, int H, int E, const float *__restrict__ bias,
+                                                                 float *__restrict__ logits, int32_t *__restrict__ meta) {
+    extern __shared__ __align__(128) uint8_t rsm[];
+    const int S = H / 8, SC = S / 8;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(rsm);
+    uint4 *ws = reinterpret_cast<uint4 *>(rsm + 128);                            // [2 * WPB quads][SC][32]
+    float *xs = reinterpret_cast<float *>(rsm + 128 + (size_t)2 * WPB * SC * 512);  // [TT][H]
     const int t0 = blockIdx.y * TT, nt = min(TT, n - t0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int eq = blockIdx.x * (blockDim.x >> 5) + warp;
-    const int e = eq * 4 + (lane >> 3), l = lane & 7;
-    const uint4 *wp = Wr + (size_t)eq * SC * 32 + lane;
-    uint4 cur[8], nxt[8];
-    const bool live = eq * 4 < E;
-#pragma unroll
-    for (int j = 0; j < 8; j++) cur[j] = live && j < SC ? __ldg(wp + (size_t)j * 32) : make_uint4(0, 0, 0, 0);
-    stage_x<TT>(xs, X, t0, nt, H);
+    const int eq0 = blockIdx.x * 2 * WPB, nq = min(2 * WPB, E / 4 - eq0);  // expert quads of this block
+    if (nq <= 0) return;
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mbar_expect_tx(bar, (uint32_t)(nq * SC * 512 + nt * H * 4));
+        bulk_g2s(ws, Wr + (size_t)eq0 * SC * 32, (uint32_t)(nq * SC * 512), bar);
+        for (int tt = 0; tt < nt; tt++) bulk_g2s(xs + (size_t)tt * H, X + (size_t)(t0 + tt) * H, (uint32_t)(H * 4), bar);
+    }
     __syncthreads();
-    if (!live) return;
-    float acc[TT];
+    if (!mbar_wait_bounded(bar, 0)) {  // the copies did not land: record it, wait once more (bounded), leave
+        if (lane == 0 && meta) atomicCAS(&meta[kMetaRouterError], 0, kErrTimeout);
+        mbar_wait_bounded(bar, 0);
+        return;
+    }
+    const int qa = 2 * warp, l = lane & 7;
+    if (qa >= nq) return;
+    const bool hb = qa + 1 < nq;
+    const uint4 *wa = ws + (size_t)qa * SC * 32 + lane, *wb = wa + (size_t)SC * 32;
+    const float *xl = xs + l;
+    float A[TT], B[TT];
 #pragma unroll
-    for (int tt = 0; tt < TT; tt++) acc[tt] = 0.0f;
-    for (int g0 = 0; g0 < SC; g0 += 8) {
+    for (int tt = 0; tt < TT; tt++) A[tt] = B[tt] = 0.0f;
+#pragma unroll 1
+    for (int jc = 0; jc < SC; jc++) {
+        float w1[8], w2[8];
+        h8(wa[(size_t)jc * 32], w1);
+        h8(hb ? wb[(size_t)jc * 32] : make_uint4(0, 0, 0, 0), w2);
 #pragma unroll
-        for (int j = 0; j < 8; j++)
-            nxt[j] = g0 + 8 + j < SC ? __ldg(wp + (size_t)(g0 + 8 + j) * 32) : make_uint4(0, 0, 0, 0);
+        for (int s = 0; s < 8; s++) {
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            if (g0 + j < SC) {
-                float w[8];
-                h8(cur[j], w);
-#pragma unroll
-                for (int tt = 0; tt < TT; tt++)
-                    acc[tt] = chain8(acc[tt], w, xs + (size_t)tt * 8 * SP + l * SP + (g0 + j) * 8);
+            for (int tt = 0; tt < TT; tt++) {
+                const float x = xl[(size_t)tt * H + (jc * 8 + s) * 8];
+                A[tt] = __fmaf_rn(w1[s], x, A[tt]);
+                B[tt] = __fmaf_rn(w2[s], x, B[tt]);
             }
         }
-#pragma unroll
-        for (int j = 0; j < 8; j++) cur[j] = nxt[j];
     }
+    const int ea = (eq0 + qa) * 4 + (lane >> 3), eb = ea + 4;
 #pragma unroll
-    for (int tt = 0; tt < TT; tt++) write_logit(acc[tt], l, tt, nt, t0, e, E, bias, logits);
+    for (int tt = 0; tt < TT; tt++) {
+        write_logit(A[tt], l, tt, nt, t0, ea, E, bias, logits);
+        if (hb) write_logit(B[tt], l, tt, nt, t0, eb, E, bias, logits);
+    }
 }
 
 // Many tokens: FMA-bound (4.3 G FMA at 4096 tokens). Thread = (lane l, 2 experts from two quads, 8 tokens): each
@@ -194,26 +212,29 @@ void launch_router_repack(const uint16_t *W, uint4 *Wr, int E, int H, cudaStream
 }
 
 static size_t router_smem(int TT, int H) { return (size_t)TT * 8 * (H / 8 + 4) * sizeof(float); }
+static size_t router_small_smem(int TT, int WPB, int H) { return 128 + (size_t)2 * WPB * H * 8 + (size_t)TT * H * 4; }
 
 void router_set_attributes(int H) {
     cudaFuncSetAttribute(router_large_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_smem(kLT, H));
-    cudaFuncSetAttribute(router_small_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_smem(4, H));
-    cudaFuncSetAttribute(router_small_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_smem(2, H));
+    cudaFuncSetAttribute(router_small_kernel<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_small_smem(1, 1, H));
+    cudaFuncSetAttribute(router_small_kernel<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_small_smem(2, 1, H));
+    cudaFuncSetAttribute(router_small_kernel<4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_small_smem(4, 1, H));
+    cudaFuncSetAttribute(router_small_kernel<8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_small_smem(8, 1, H));
 }
 
 int launch_router_logits(const uint4 *Wr, const float *X, int n, int H, int E, const float *bias, float *logits,
-                         cudaStream_t st) {
-    // few tokens: one warp (4 experts) per block so the 2 MB router spreads over every SM; many tokens: 64 experts
-    // x 8 tokens per block, FMA-bound
-    if (n <= 2) {
-        dim3 grid(E / 4, n);
-        router_small_kernel<1><<<grid, 32, router_smem(1, H), st>>>(Wr, X, n, H, E, bias, logits);
-    } else if (n <= 8) {
-        dim3 grid(E / 4, (n + 1) / 2);
-        router_small_kernel<2><<<grid, 32, router_smem(2, H), st>>>(Wr, X, n, H, E, bias, logits);
+                         int32_t *meta, cudaStream_t st) {
+    // few tokens: every block pulls its experts' weights and the token tile in one go; one warp (4 experts) per block
+    // up to 8 tokens so the 2 MB router spreads over every SM. Many tokens: 64 experts x 8 tokens per block, FMA-bound.
+    if (n <= 1) {
+        router_small_kernel<1, 1><<<dim3((E / 4 + 1) / 2, n), 32, router_small_smem(1, 1, H), st>>>(Wr, X, n, H, E, bias, logits, meta);
+    } else if (n <= 2) {
+        router_small_kernel<2, 1><<<dim3((E / 4 + 1) / 2, 1), 32, router_small_smem(2, 1, H), st>>>(Wr, X, n, H, E, bias, logits, meta);
+    } else if (n <= 4) {
+        router_small_kernel<4, 1><<<dim3((E / 4 + 1) / 2, 1), 32, router_small_smem(4, 1, H), st>>>(Wr, X, n, H, E, bias, logits, meta);
     } else if (n <= 64) {
-        dim3 grid(E / 8, (n + 3) / 4);
-        router_small_kernel<4><<<grid, 64, router_smem(4, H), st>>>(Wr, X, n, H, E, bias, logits);
+        router_small_kernel<8, 1><<<dim3((E / 4 + 1) / 2, (n + 7) / 8), 32, router_small_smem(8, 1, H), st>>>(Wr, X, n, H, E, bias,
+                                                                                                  logits, meta);
     } else {
         dim3 grid((E + 63) / 64, (n + kLT - 1) / kLT);
         router_large_kernel<<<grid, 256, router_smem(kLT, H), st>>>(Wr, X, n, H, E, bias, logits);

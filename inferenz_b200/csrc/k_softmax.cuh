@@ -26,23 +26,30 @@ __device__ __forceinline__ float cephes_exp(float x) {
 
 constexpr int kMaxPerLane = 32;  // E <= 1024, E % 32 == 0
 
+// order-preserving map of a float to an unsigned key (for warp max reductions on redux.sync)
+__device__ __forceinline__ uint32_t f2ord(float x) {
+    const uint32_t b = __float_as_uint(x);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float ord2f(uint32_t k) { return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k); }
+
 // One warp, one token: lg [E] logits -> sel [topk], w [topk]; ex: E floats of shared scratch for this warp;
 // probs (optional) [E]. Lane j holds elements j + 32 m.
+// Top-k: k rounds; each lane keeps its best untaken probability (ties: smaller m, i.e. smaller index), the warp
+// takes the largest value (redux max over the probability bits + 1; probabilities are >= 0, so the bits are
+// ordered) and, among the lanes holding it, the smallest index (redux min) -- the reference's (value desc, index asc).
 __device__ __forceinline__ void softmax_topk_warp(const float *__restrict__ lg, int E, int topk, float *ex,
                                                   float *__restrict__ probs, int32_t *sel, float *w) {
     const int lane = threadIdx.x & 31, per = E / 32;
     float v[kMaxPerLane];
-    float mx = -INFINITY;
+    uint32_t mk = 0;
 #pragma unroll
     for (int m = 0; m < kMaxPerLane; m++)
         if (m < per) {
             v[m] = lg[lane + 32 * m];
-            mx = v[m] > mx ? v[m] : mx;
+            mk = max(mk, f2ord(v[m]));
         }
-    for (int o = 16; o; o >>= 1) {
-        const float q = __shfl_xor_sync(0xffffffffu, mx, o);
-        mx = q > mx ? q : mx;
-    }
+    const float mx = ord2f(__reduce_max_sync(0xffffffffu, mk));
 #pragma unroll
     for (int m = 0; m < kMaxPerLane; m++)
         if (m < per) {
@@ -52,8 +59,10 @@ __device__ __forceinline__ void softmax_topk_warp(const float *__restrict__ lg, 
     __syncwarp();
     // 8 lane sums: accumulator l adds elements l, l+8, l+16, ... in order (the reference's 8-wide running sum)
     float part = 0.0f;
-    if (lane < 8)
+    if (lane < 8) {
+#pragma unroll 8
         for (int i = lane; i < E; i += 8) part = __fadd_rn(part, ex[i]);
+    }
     const float sum = __shfl_sync(0xffffffffu, hsum8_lanes(part), 0);
     const float inv = __fdiv_rn(1.0f, sum);
 #pragma unroll
@@ -62,28 +71,24 @@ __device__ __forceinline__ void softmax_topk_warp(const float *__restrict__ lg, 
             v[m] = __fmul_rn(v[m], inv);
             if (probs) probs[lane + 32 * m] = v[m];
         }
-    // top-k: k rounds of a warp arg-max under (value desc, index asc); the winner is removed by its owner
     unsigned taken = 0;  // bit m: element lane + 32 m already selected
-    float wsum = 0.0f;
-    float wk = 0.0f;
+    float wsum = 0.0f, wk = 0.0f;
     int ik = 0;
     for (int k = 0; k < topk; k++) {
-        float bv = -INFINITY;
-        int bi = 0x7FFFFFFF;
+        uint32_t bk = 0;
+        int bm = 0;
 #pragma unroll
         for (int m = 0; m < kMaxPerLane; m++)
             if (m < per && !((taken >> m) & 1u)) {
-                const int i = lane + 32 * m;
-                if (v[m] > bv || (v[m] == bv && i < bi)) { bv = v[m]; bi = i; }
+                const uint32_t key = __float_as_uint(v[m]) + 1u;
+                if (key > bk) { bk = key; bm = m; }
             }
-        for (int o = 16; o; o >>= 1) {
-            const float qv = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int qi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (qv > bv || (qv == bv && qi < bi)) { bv = qv; bi = qi; }
-        }
-        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-        wsum = __fadd_rn(wsum, bv);          // identical in every lane: (((0 + p0) + p1) + ...)
-        if (lane == k) { wk = bv; ik = bi; }  // lane k keeps rank k (topk <= 16)
+        const uint32_t wmax = __reduce_max_sync(0xffffffffu, bk);
+        const uint32_t widx = __reduce_min_sync(0xffffffffu, bk == wmax ? (uint32_t)(lane + 32 * bm) : 0xFFFFFFFFu);
+        if ((int)(widx & 31) == lane) taken |= 1u << (widx >> 5);
+        const float pv = __uint_as_float(wmax - 1u);
+        wsum = __fadd_rn(wsum, pv);            // identical in every lane: (((0 + p0) + p1) + ...)
+        if (lane == k) { wk = pv; ik = (int)widx; }  // lane k keeps rank k (topk <= 16)
     }
     if (lane < topk) {
         sel[lane] = ik;

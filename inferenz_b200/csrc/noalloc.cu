@@ -79,6 +79,10 @@ extern "C" INZG_EXPORT inzg_status inzg_route_topk_noalloc(inzg_ctx *ctx, int la
         inzg__set_error(ctx, "route_topk_noalloc: null device pointer");
         return INZG_BAD_ARG;
     }
+    if (reinterpret_cast<uintptr_t>(x_dev) & 15) {  // token rows are moved by bulk copies
+        inzg__set_error(ctx, "route_topk_noalloc: x_dev must be 16-byte aligned");
+        return INZG_BAD_ARG;
+    }
     cudaError_t e = cudaSetDevice(device);
     float *logits = e == cudaSuccess ? scratch_for(device, &e) : nullptr;
     if (!logits) {
@@ -86,7 +90,8 @@ extern "C" INZG_EXPORT inzg_status inzg_route_topk_noalloc(inzg_ctx *ctx, int la
         return INZG_CUDA;
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    inzg::launch_router_logits(static_cast<const uint4 *>(router), x_dev, n, H, E, logit_bias_dev, logits, st);
+    // (no status word on this path: a router copy that never lands is not reported to the caller)
+    inzg::launch_router_logits(static_cast<const uint4 *>(router), x_dev, n, H, E, logit_bias_dev, logits, nullptr, st);
     inzg::launch_softmax_topk(logits, n, E, K, sel_dev, w_dev, nullptr, st);
     e = cudaGetLastError();
     if (e != cudaSuccess) {
