@@ -134,6 +134,38 @@ INZG_EXPORT inzg_status inzg_route_topk_noalloc(inzg_ctx *ctx, int layer, int n,
                                                 const float *logit_bias_dev, int32_t *sel_dev, float *w_dev,
                                                 void *stream);
 
+/* ---- Expert parallelism (no counterpart in the reference, which runs on one host). A rank owns experts
+ * [e_first, e_first + n_local) of a layer and its share of the batch's tokens. Per layer: inzg_route on the rank's
+ * tokens; ship every token row to the ranks owning its selected experts (NCCL all-to-all in the caller);
+ * inzg_moe_experts on the rows received; ship the per-slot outputs back; inzg_combine. Each expert sees the same
+ * tokens as in a single-GPU call, so its numeric path and outputs are the single-GPU ones bit for bit. All pointers
+ * are device pointers (16-byte aligned where rows are copied); calls are ordered on `stream` (NULL = the context's
+ * stream) and return without synchronising; inzg_device_status synchronises and reports device-side checks. */
+
+/* Experts [e_first, e_first + n_local) of the layer: blobs holds those n_local blobs in order. inzg_pool_add_layer
+ * is the whole range (0, n_expert); inzg_moe_forward needs the whole range. */
+INZG_EXPORT inzg_status inzg_pool_add_layer_range(inzg_ctx *ctx, int layer, int expert_type, const void *blobs,
+                                                  uint64_t blob_bytes, int e_first, int n_local);
+
+/* Router, softmax and top-k of n tokens (the routing stage of inzg_moe_forward): sel_dev [n][topk] (expert ids),
+ * w_dev [n][topk] (renormalised weights). logit_bias_dev: the test hook, optional. */
+INZG_EXPORT inzg_status inzg_route(inzg_ctx *ctx, int layer, int n, const float *x_dev, const float *logit_bias_dev,
+                                   int32_t *sel_dev, float *w_dev, void *stream);
+
+/* The experts this rank owns, on m received token rows x_dev [m][hidden]: sel_dev [m][topk] holds, per row and rank
+ * k, the LOCAL expert index (global id - e_first) or -1 when that expert lives on another rank; w_dev [m][topk] the
+ * routing weights. n_batch is the whole batch's token count across ranks (the reference decodes every expert when
+ * it is <= 8). Writes out_dev[r][k][hidden] = w * expert(x_r) for the entries present; other slots are untouched. */
+INZG_EXPORT inzg_status inzg_moe_experts(inzg_ctx *ctx, int layer, int m, const float *x_dev, const int32_t *sel_dev,
+                                         const float *w_dev, int n_batch, float *out_dev, void *stream);
+
+/* y_dev[t] = ((0 + s[t][0]) + s[t][1]) + ... + s[t][topk-1] for slots_dev [n][topk][hidden] (src/model_fwd.c:1134-1140). */
+INZG_EXPORT inzg_status inzg_combine(inzg_ctx *ctx, int n, const float *slots_dev, float *y_dev, void *stream);
+
+/* Waits for `stream` and reports the device-side checks of the calls since the last routing step
+ * (INZG_TIMEOUT / INZG_DEVICE_CHECK). */
+INZG_EXPORT inzg_status inzg_device_status(inzg_ctx *ctx, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -51,6 +51,11 @@ SIGNATURES = {
     "inzg_stage_times": (I, [P, P, P, I]),
     "inzg_stage_name": (ctypes.c_char_p, [I]),
     "inzg_route_topk_noalloc": (I, [P, I, I, P, P, P, P, P]),
+    "inzg_pool_add_layer_range": (I, [P, I, I, P, U64, I, I]),
+    "inzg_route": (I, [P, I, I, P, P, P, P, P]),
+    "inzg_moe_experts": (I, [P, I, I, P, P, P, I, P, P]),
+    "inzg_combine": (I, [P, I, P, P, P]),
+    "inzg_device_status": (I, [P, P]),
     # inzg_tools.h
     "inzg_synth_jump": (U64, [U64, U64]),
     "inzg_synth_randn": (U64, [U64, I64, F, P]),

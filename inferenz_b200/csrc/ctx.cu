@@ -40,6 +40,7 @@ struct TmaMap {
 
 struct LayerSlot {
     bool has_router = false, has_experts = false;
+    int e_first = 0;            // the pool holds experts [e_first, e_first + dev.E) of the layer's n_expert
     bool has_maps = false;
     TmaMap map_gu, map_dn;      // TMA maps over the prefill-path int8 weights
     uint4 *router = nullptr;
@@ -313,12 +314,20 @@ inzg_status inzg_set_router(inzg_ctx *c, int layer, const uint16_t *w, int rows,
 
 inzg_status inzg_pool_add_layer(inzg_ctx *c, int layer, int type, const void *blobs, uint64_t blob_bytes, int n_expert) {
     if (!c) return INZG_BAD_ARG;
+    if (n_expert != c->cfg.n_expert) return fail(c, INZG_BAD_ARG, "pool_add_layer: n_expert differs from the context");
+    return inzg_pool_add_layer_range(c, layer, type, blobs, blob_bytes, 0, n_expert);
+}
+
+inzg_status inzg_pool_add_layer_range(inzg_ctx *c, int layer, int type, const void *blobs, uint64_t blob_bytes,
+                                      int e_first, int n_local) {
+    if (!c) return INZG_BAD_ARG;
     const inzg_config &cf = c->cfg;
     if (layer < 0 || layer >= cf.n_layers || !blobs) return fail(c, INZG_BAD_ARG, "pool_add_layer: bad layer or pointer");
-    if (n_expert != cf.n_expert) return fail(c, INZG_BAD_ARG, "pool_add_layer: n_expert differs from the context");
+    if (e_first < 0 || n_local < 1 || e_first + n_local > cf.n_expert)
+        return fail(c, INZG_BAD_ARG, "pool_add_layer: expert range outside the layer's experts");
     if (type != INZG_T_Q4L && type != INZG_T_Q8G)
         return fail(c, INZG_UNSUPPORTED, "pool_add_layer: expert type must be Q4L or Q8G");
-    const int H = cf.hidden, FF = cf.ff, E = cf.n_expert;
+    const int H = cf.hidden, FF = cf.ff, E = n_local;
     const uint64_t gu_bytes = inzg_qmat_bytes(type, 2 * FF, H), dn_bytes = inzg_qmat_bytes(type, H, FF);
     if (blob_bytes < gu_bytes + dn_bytes) return fail(c, INZG_BAD_ARG, "pool_add_layer: blob smaller than its matrices");
     // validate every blob the way q_bind_lin does (src/model_fwd.c:87-96, 853-855): magic, type, rows, cols
@@ -333,7 +342,7 @@ inzg_status inzg_pool_add_layer(inzg_ctx *c, int layer, int type, const void *bl
         if (hg.magic != kMagic || hd.magic != kMagic || hg.type != type || hd.type != type || hg.rows != (uint32_t)(2 * FF) ||
             hg.cols != (uint32_t)H || hd.rows != (uint32_t)H || hd.cols != (uint32_t)FF) {
             char msg[128];
-            snprintf(msg, sizeof(msg), "expert blob is corrupt (expert %d)", e);
+            snprintf(msg, sizeof(msg), "expert blob is corrupt (expert %d)", e_first + e);
             return fail(c, INZG_CORRUPT_BLOB, msg);
         }
         // one activation quantization per layer input needs one rotation for all experts' gate|up (and down)
@@ -347,6 +356,7 @@ inzg_status inzg_pool_add_layer(inzg_ctx *c, int layer, int type, const void *bl
     drop_graphs(c);
     LayerSlot &L = c->layers[layer];
     LayerDev &D = L.dev;
+    L.e_first = e_first;
     D.type = type;
     D.H = H;
     D.FF = FF;
@@ -450,7 +460,7 @@ static int enqueue_forward(inzg_ctx *c, const LayerSlot &L, int n, const float *
     }
     mark(1);
     RouteDev R{};
-    R.n = n; R.topk = K; R.E = E;
+    R.n = n; R.topk = K; R.E = E; R.n_rule = n; R.absent_ok = 0;
     R.sel = c->sel; R.w = c->w; R.cnt = c->cnt; R.off = c->off; R.first = c->first; R.etok = c->etok; R.eslot = c->eslot;
     R.ew = c->ew; R.ccnt = c->ccnt; R.units = c->units; R.meta = c->meta; R.dec_units = c->dec_units;
     R.gemm_units = c->gemm_units; R.gemm_tiles = c->gemm_tiles;
@@ -517,6 +527,8 @@ inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, fl
     const float *ovr = opt ? opt->logits_override : nullptr;
     const float *bias = opt ? opt->logit_bias : nullptr;
     if (!L.has_experts || (!L.has_router && !ovr)) return fail(c, INZG_NOT_READY, "moe_forward: layer not loaded");
+    if (L.e_first != 0 || L.dev.E != cf.n_expert)
+        return fail(c, INZG_NOT_READY, "moe_forward: the pool holds a subset of the experts (use inzg_moe_experts)");
     // the kernels move token rows with 16-byte vector loads and bulk copies
     if (dev_io && ((reinterpret_cast<uintptr_t>(xin) | reinterpret_cast<uintptr_t>(y) |
                     reinterpret_cast<uintptr_t>(ovr)) & 15))
@@ -611,6 +623,111 @@ inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, fl
             snprintf(msg, sizeof(msg), "moe_forward: device check failed (code %d)", meta[kMetaError]);
             return fail(c, meta[kMetaError] == kErrTimeout ? INZG_TIMEOUT : INZG_DEVICE_CHECK, msg);
         }
+    }
+    return INZG_OK;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Expert-parallel building blocks. A rank routes its own tokens (inzg_route), ships each token's row to the ranks
+// owning its experts, runs the experts it owns on the rows it received (inzg_moe_experts: the same kernels as the
+// whole-layer forward, entries of other ranks marked absent), ships the per-slot outputs home and combines them in
+// rank order (inzg_combine). Every expert sees exactly the tokens it would see on one GPU, so its numeric path and
+// its outputs are the single-GPU ones bit for bit.
+
+inzg_status inzg_route(inzg_ctx *c, int layer, int n, const float *x_dev, const float *logit_bias_dev, int32_t *sel_dev,
+                       float *w_dev, void *stream) {
+    if (!c) return INZG_BAD_ARG;
+    const inzg_config &cf = c->cfg;
+    if (layer < 0 || layer >= cf.n_layers) return fail(c, INZG_BAD_ARG, "route: bad layer");
+    if (n <= 0 || n > cf.max_tokens || !x_dev || !sel_dev || !w_dev) return fail(c, INZG_BAD_ARG, "route: bad n or pointer");
+    if (reinterpret_cast<uintptr_t>(x_dev) & 15) return fail(c, INZG_BAD_ARG, "route: x must be 16-byte aligned");
+    LayerSlot &L = c->layers[layer];
+    if (!L.has_router) return fail(c, INZG_NOT_READY, "route: layer has no router");
+    cudaSetDevice(cf.device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    launch_router_logits(L.router, x_dev, n, cf.hidden, cf.n_expert, logit_bias_dev, c->logits, c->meta, st);
+    launch_softmax_topk(c->logits, n, cf.n_expert, cf.topk, sel_dev, w_dev, nullptr, st);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? INZG_OK : cuda_fail(c, e, "route: kernel launch");
+}
+
+inzg_status inzg_moe_experts(inzg_ctx *c, int layer, int m, const float *x_dev, const int32_t *sel_dev,
+                             const float *w_dev, int n_batch, float *out_dev, void *stream) {
+    if (!c) return INZG_BAD_ARG;
+    const inzg_config &cf = c->cfg;
+    if (layer < 0 || layer >= cf.n_layers) return fail(c, INZG_BAD_ARG, "moe_experts: bad layer");
+    if (m <= 0 || m > cf.max_tokens || n_batch < 1 || !x_dev || !sel_dev || !w_dev || !out_dev)
+        return fail(c, INZG_BAD_ARG, "moe_experts: bad m, n_batch or pointer");
+    if ((reinterpret_cast<uintptr_t>(x_dev) | reinterpret_cast<uintptr_t>(out_dev)) & 15)
+        return fail(c, INZG_BAD_ARG, "moe_experts: x and out must be 16-byte aligned");
+    LayerSlot &L = c->layers[layer];
+    if (!L.has_experts) return fail(c, INZG_NOT_READY, "moe_experts: layer has no experts");
+    const LayerDev &D = L.dev;
+    cudaSetDevice(cf.device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    if (launch_gemv_decode(D, -1, RouteDev{}, nullptr, nullptr, nullptr, 0, 0, st) < 0)
+        return fail(c, INZG_UNSUPPORTED, "moe_experts: no decode kernel for this geometry");
+    const int H = cf.hidden, K = cf.topk, FF = cf.ff, E = D.E;
+    const int NE = m * K;
+    const bool any_gemm = n_batch > 8 && NE >= kGemmMinT;
+    launch_act_quant_x(x_dev, m, H, D.gu_rot, D.gu_seed, c->xq64, c->xsb64, any_gemm ? c->xq256 : nullptr, c->xs256, st);
+    RouteDev R{};
+    R.n = m; R.topk = K; R.E = E; R.n_rule = n_batch; R.absent_ok = 1;
+    R.sel = const_cast<int32_t *>(sel_dev); R.w = const_cast<float *>(w_dev);
+    R.cnt = c->cnt; R.off = c->off; R.first = c->first; R.etok = c->etok; R.eslot = c->eslot;
+    R.ew = c->ew; R.ccnt = c->ccnt; R.units = c->units; R.meta = c->meta; R.dec_units = c->dec_units;
+    R.gemm_units = c->gemm_units; R.gemm_tiles = c->gemm_tiles;
+    launch_route(R, (m + 31) / 32, gemv_items_per_unit(D, 0), gemv_items_per_unit(D, 1), gemm_token_tile(), c->upath,
+                 c->eexp, st);
+    const bool tc = c->have_tc && L.has_maps;
+    const int nkbH = (H + kKB - 1) / kKB;
+    const int max_tiles = (NE + gemm_token_tile() - 1) / gemm_token_tile() + std::min(E, NE / kGemmMinT) + 1;
+    const int grid = c->num_sms * 4;
+    launch_gemv_decode(D, 0, R, c->xq64, c->xsb64, c->GU, 2 * FF, c->num_sms, st);
+    if (any_gemm) {
+        if (tc) {
+            launch_gather_gemm_rows(c->xq256, c->xs256, H, nkbH, c->etok, c->eexp, c->upath, NE, c->xqe, c->xse, st);
+            launch_gemm_tc(0, L.map_gu.bytes, c->map_xqe.bytes, D.ws_gu, 2 * FF, H, R, c->xse, c->GU, 2 * FF, max_tiles, st);
+        } else {
+            launch_gemm_v1(D, 0, R, c->xq256, c->xs256, c->GU, 2 * FF, grid, st);
+        }
+    }
+    launch_swiglu_quant(c->GU, FF, NE, c->eexp, c->upath, D.dn_rot, D.dn_seed, c->dq64, c->dsb64, c->dq256, c->ds256, st);
+    launch_gemv_decode(D, 1, R, c->dq64, c->dsb64, out_dev, H, c->num_sms, st);
+    if (any_gemm) {
+        if (tc) launch_gemm_tc(1, L.map_dn.bytes, c->map_dq.bytes, D.ws_dn, H, FF, R, c->ds256, out_dev, H, max_tiles, st);
+        else launch_gemm_v1(D, 1, R, c->dq256, c->ds256, out_dev, H, grid, st);
+    }
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? INZG_OK : cuda_fail(c, e, "moe_experts: kernel launch");
+}
+
+inzg_status inzg_combine(inzg_ctx *c, int n, const float *slots_dev, float *y_dev, void *stream) {
+    if (!c) return INZG_BAD_ARG;
+    const inzg_config &cf = c->cfg;
+    if (n <= 0 || !slots_dev || !y_dev) return fail(c, INZG_BAD_ARG, "combine: bad n or pointer");
+    if ((reinterpret_cast<uintptr_t>(slots_dev) | reinterpret_cast<uintptr_t>(y_dev)) & 15)
+        return fail(c, INZG_BAD_ARG, "combine: pointers must be 16-byte aligned");
+    cudaSetDevice(cf.device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    launch_combine(slots_dev, n, cf.hidden, cf.topk, y_dev, c->num_sms, st);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? INZG_OK : cuda_fail(c, e, "combine: kernel launch");
+}
+
+inzg_status inzg_device_status(inzg_ctx *c, void *stream) {
+    if (!c) return INZG_BAD_ARG;
+    cudaSetDevice(c->cfg.device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    int32_t meta[16];
+    cudaError_t e = cudaMemcpyAsync(meta, c->meta, sizeof(meta), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(c, e, "device_status");
+    const int code = meta[kMetaError] != kErrNone ? meta[kMetaError] : meta[kMetaRouterError];
+    if (code != kErrNone) {
+        char msg[96];
+        snprintf(msg, sizeof(msg), "device check failed (code %d)", code);
+        return fail(c, code == kErrTimeout ? INZG_TIMEOUT : INZG_DEVICE_CHECK, msg);
     }
     return INZG_OK;
 }

@@ -51,6 +51,9 @@ struct LayerDev {
 // Routing products of one forward call (device).
 struct RouteDev {
     int n, topk, E;
+    int n_rule;          // batch size of the decode-numerics rule (n <= 8: every expert decodes): n, or the whole
+                         // batch across ranks when this call holds one rank's share of an expert-parallel batch
+    int absent_ok;       // entries with a negative expert id are not on this rank (expert parallel), not errors
     int32_t *sel;        // [n][topk]
     float *w;            // [n][topk]  renormalised
     int32_t *cnt;        // [E] tokens per expert

@@ -56,8 +56,8 @@ __device__ __forceinline__ int chunk_rank(const int32_t (*s)[kMaxTopK], int topk
 }
 
 __global__ void __launch_bounds__(128) route_count_kernel(const int32_t *__restrict__ sel, int n, int topk, int E,
-                                                          int32_t *__restrict__ ccnt, int32_t *__restrict__ first,
-                                                          int32_t *__restrict__ meta) {
+                                                          int absent_ok, int32_t *__restrict__ ccnt,
+                                                          int32_t *__restrict__ first, int32_t *__restrict__ meta) {
     __shared__ int32_t s[4][kChunk][kMaxTopK];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int chunk = blockIdx.x * 4 + warp;
@@ -69,6 +69,7 @@ __global__ void __launch_bounds__(128) route_count_kernel(const int32_t *__restr
     if (!valid) return;
     for (int k = 0; k < topk; k++) {
         const int e = s[warp][lane][k];
+        if (e < 0 && absent_ok) continue;
         if (e < 0 || e >= E) { set_error(meta, kErrBadExpert); continue; }
         atomicAdd(&ccnt[(size_t)chunk * E + e], 1);
         atomicMin(&first[e], t * topk + k);
@@ -76,7 +77,8 @@ __global__ void __launch_bounds__(128) route_count_kernel(const int32_t *__restr
 }
 
 // one block of E threads (E <= 1024)
-__global__ void __launch_bounds__(1024) route_scan_kernel(int n, int topk, int E, int nchunk, int gu_items_per_unit,
+__global__ void __launch_bounds__(1024) route_scan_kernel(int n, int n_rule, int absent_ok, int topk, int E, int nchunk,
+                                                          int gu_items_per_unit,
                                                           int dn_items_per_unit, int gemm_tn,
                                                           int32_t *__restrict__ ccnt, int32_t *__restrict__ cnt,
                                                           int32_t *__restrict__ off, int32_t *__restrict__ units,
@@ -94,7 +96,7 @@ __global__ void __launch_bounds__(1024) route_scan_kernel(int n, int topk, int E
         }
     const int c = e < E ? run : 0;
     const int is_unit = c > 0;
-    const int is_dec = is_unit && (n <= 8 || c < kGemmMinT);
+    const int is_dec = is_unit && (n_rule <= 8 || c < kGemmMinT);
     const int is_gemm = is_unit && !is_dec;
     const int tiles = is_gemm ? (c + gemm_tn - 1) / gemm_tn : 0;
     sc[e] = c; su[e] = is_unit; sd[e] = is_dec; sg[e] = is_gemm; st[e] = tiles;
@@ -131,7 +133,7 @@ __global__ void __launch_bounds__(1024) route_scan_kernel(int n, int topk, int E
         meta[kMetaDecItemsDN] = sd[e] * dn_items_per_unit;
         meta[kMetaGemmTilesGU] = st[e];
         meta[kMetaGemmTilesDN] = st[e];
-        if (sc[e] != n * topk) set_error(meta, kErrOverflow);
+        if (absent_ok ? sc[e] > n * topk : sc[e] != n * topk) set_error(meta, kErrOverflow);
     }
 }
 
@@ -178,9 +180,9 @@ __global__ void __launch_bounds__(1024) route_small_kernel(const int32_t *__rest
             if (ss[i] == e) { c++; first = min(first, i); }
     if (e == 0)
         for (int i = 0; i < nk; i++)
-            if (ss[i] < 0 || ss[i] >= E) set_error(R.meta, kErrBadExpert);
+            if ((ss[i] < 0 && !R.absent_ok) || ss[i] >= E) set_error(R.meta, kErrBadExpert);
     const int is_unit = c > 0;
-    const int is_dec = is_unit && (n <= 8 || c < kGemmMinT);
+    const int is_dec = is_unit && (R.n_rule <= 8 || c < kGemmMinT);
     const int is_gemm = is_unit && !is_dec;
     const int tiles = is_gemm ? (c + gemm_tn - 1) / gemm_tn : 0;
     sc[e] = c; su[e] = is_unit; sd[e] = is_dec; sg[e] = is_gemm; st[e] = tiles;
@@ -224,7 +226,7 @@ __global__ void __launch_bounds__(1024) route_small_kernel(const int32_t *__rest
         R.meta[kMetaDecItemsDN] = sd[e] * dn_items_per_unit;
         R.meta[kMetaGemmTilesGU] = st[e];
         R.meta[kMetaGemmTilesDN] = st[e];
-        if (sc[e] != nk) set_error(R.meta, kErrOverflow);
+        if (R.absent_ok ? sc[e] > nk : sc[e] != nk) set_error(R.meta, kErrOverflow);
     }
 }
 
@@ -369,9 +371,9 @@ int launch_route(const RouteDev &R, int nchunk, int gu_items_per_unit, int dn_it
     cudaMemsetAsync(R.first, 0x7F, sizeof(int32_t) * (size_t)E, st);
     cudaMemsetAsync(R.meta, 0, sizeof(int32_t) * kMetaRouterError, st);  // the router's word is folded in by route_scan
     const int blocks = (nchunk + 3) / 4;
-    route_count_kernel<<<blocks, 128, 0, st>>>(R.sel, n, topk, E, R.ccnt, R.first, R.meta);
+    route_count_kernel<<<blocks, 128, 0, st>>>(R.sel, n, topk, E, R.absent_ok, R.ccnt, R.first, R.meta);
     const int threads = (E + 31) / 32 * 32;
-    route_scan_kernel<<<1, threads, 0, st>>>(n, topk, E, nchunk, gu_items_per_unit, dn_items_per_unit, gemm_tn, R.ccnt,
+    route_scan_kernel<<<1, threads, 0, st>>>(n, R.n_rule, R.absent_ok, topk, E, nchunk, gu_items_per_unit, dn_items_per_unit, gemm_tn, R.ccnt,
                                              R.cnt, R.off, R.units, R.dec_units, R.gemm_units, R.gemm_tiles, upath, R.meta);
     route_scatter_kernel<<<blocks, 128, 0, st>>>(R.sel, R.w, n, topk, E, R.ccnt, R.off, R.etok, R.eslot, R.ew, eexp);
     return 3;

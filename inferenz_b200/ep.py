@@ -1,0 +1,125 @@
+"""Expert parallelism for the MoE layer: experts sharded over ranks, tokens over ranks, two all-to-all exchanges.
+
+Rank g of G owns experts [g*E/G, (g+1)*E/G) and its share of the batch's tokens. One layer call on every rank:
+
+1. route its tokens (router, softmax, top-k: bit-exact per token, src/model_fwd.c:997-1011);
+2. dispatch: send each token's fp32 row once to every rank owning at least one of its selected experts, with the
+   token's (local expert index or -1, weight) for that rank -- all-to-all;
+3. run the experts it owns on the rows it received (libinzg ``inzg_moe_experts``): every expert receives every
+   token of the batch that selected it, so its numeric path (decode when it has < 12 tokens or the batch has
+   <= 8 tokens, src/model_fwd.c:229-249) and its outputs equal the single-GPU call bit for bit;
+4. combine: send each (token, rank-k) output back to the token's rank -- all-to-all -- which adds the ten slots in
+   rank order (src/model_fwd.c:1134-1140), again bit for bit.
+
+The exchanges use ``torch.distributed`` (NCCL over NVLink between GPUs; gloo in the CPU tests of this module's
+logic). The per-rank compute is a backend: :class:`DeviceBackend` drives libinzg on the rank's GPU.
+"""
+import torch
+import torch.distributed as dist
+
+
+class DeviceBackend:
+    """libinzg on this rank's GPU: a MoePool holding experts [e_first, e_first + n_local) of every layer used."""
+
+    def __init__(self, pool, stream=None):
+        self.pool = pool
+        self.stream = stream
+
+    def _st(self):
+        s = self.stream if self.stream is not None else torch.cuda.current_stream(self.pool.device)
+        return s.cuda_stream
+
+    def route(self, layer, x, bias=None):
+        n = x.shape[0]
+        sel = torch.empty((n, self.pool.topk), dtype=torch.int32, device=x.device)
+        w = torch.empty((n, self.pool.topk), dtype=torch.float32, device=x.device)
+        self.pool.route_device(layer, n, x.data_ptr(), sel.data_ptr(), w.data_ptr(),
+                               None if bias is None else bias.data_ptr(), self._st())
+        return sel, w
+
+    def experts(self, layer, x, sel, w, n_batch):
+        m = x.shape[0]
+        out = torch.empty((m, self.pool.topk, self.pool.hidden), dtype=torch.float32, device=x.device)
+        if m:
+            self.pool.experts_device(layer, m, x.data_ptr(), sel.data_ptr(), w.data_ptr(), n_batch, out.data_ptr(),
+                                     self._st())
+        return out
+
+    def combine(self, slots):
+        n = slots.shape[0]
+        y = torch.empty((n, slots.shape[2]), dtype=torch.float32, device=slots.device)
+        self.pool.combine_device(n, slots.data_ptr(), y.data_ptr(), self._st())
+        return y
+
+
+class ExpertParallelMoE:
+    """The routed MoE layer over ``world`` ranks with ``n_expert / world`` experts each (see the module docstring)."""
+
+    def __init__(self, backend, n_expert, topk, hidden, rank=None, world=None, group=None):
+        self.be = backend
+        self.E, self.K, self.H = n_expert, topk, hidden
+        self.group = group
+        self.rank = dist.get_rank(group) if rank is None else rank
+        self.world = dist.get_world_size(group) if world is None else world
+        if n_expert % self.world:
+            raise ValueError("n_expert must be a multiple of the number of ranks")
+        self.e_per = n_expert // self.world
+        self.last = {}
+
+    def expert_range(self, rank=None):
+        r = self.rank if rank is None else rank
+        return r * self.e_per, self.e_per
+
+    def _a2a(self, out, inp, out_splits, in_splits):
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+
+    def moe_block(self, layer, x, bias=None, n_batch=None):
+        """y [n][H] for this rank's tokens x [n][H] (fp32, on the backend's device)."""
+        G, K, H = self.world, self.K, self.H
+        dev = x.device
+        n = x.shape[0]
+        if n_batch is None:
+            t = torch.tensor([n], dtype=torch.int64, device=dev)
+            dist.all_reduce(t, group=self.group)
+            n_batch = int(t.item())
+        sel, w = self.be.route(layer, x, bias)
+        owner = (sel // self.e_per).long()                                   # [n][K] rank owning each selection
+        hit = torch.zeros((n, G), dtype=torch.bool, device=dev)
+        hit.scatter_(1, owner, True)                                         # token t goes to rank d once
+        pairs = hit.t().nonzero()                                            # (d, t), d-major, t ascending
+        send_d, send_t = pairs[:, 0], pairs[:, 1]
+        send_counts = hit.sum(0).to(torch.int64)
+        recv_counts = torch.empty_like(send_counts)
+        self._a2a(recv_counts, send_counts, None, None)
+        sel_t, own_t = sel[send_t], owner[send_t]
+        local = torch.where(own_t == send_d[:, None], sel_t - (send_d[:, None] * self.e_per).to(torch.int32),
+                            torch.full_like(sel_t, -1))
+        meta_send = torch.cat([local, w[send_t].view(torch.int32)], 1).contiguous()
+        x_send = x[send_t].contiguous()
+        s_splits, r_splits = send_counts.tolist(), recv_counts.tolist()
+        m = sum(r_splits)
+        x_recv = torch.empty((m, H), dtype=torch.float32, device=dev)
+        meta_recv = torch.empty((m, 2 * K), dtype=torch.int32, device=dev)
+        self._a2a(x_recv, x_send, r_splits, s_splits)
+        self._a2a(meta_recv, meta_send, r_splits, s_splits)
+        sel_recv = meta_recv[:, :K].contiguous()
+        w_recv = meta_recv[:, K:].contiguous().view(torch.float32)
+        out = self.be.experts(layer, x_recv, sel_recv, w_recv, n_batch)     # [m][K][H]
+        present = sel_recv >= 0
+        back = out[present].contiguous()                                     # (row, k) row-major
+        rows_src = torch.repeat_interleave(torch.arange(G, device=dev), torch.tensor(r_splits, device=dev))
+        back_counts = torch.zeros(G, dtype=torch.int64, device=dev)
+        back_counts.index_add_(0, rows_src, present.sum(1).to(torch.int64))
+        home_counts = torch.bincount(owner.flatten(), minlength=G).to(torch.int64)
+        b_send, b_recv = back_counts.tolist(), home_counts.tolist()
+        res = torch.empty((sum(b_recv), H), dtype=torch.float32, device=dev)
+        self._a2a(res, back, b_recv, b_send)
+        # results arrive per owner rank d; inside d in this rank's send order (t ascending, then k ascending)
+        tk = torch.cat([(owner == d).nonzero() for d in range(G)], 0)
+        slots = torch.empty((n, K, H), dtype=torch.float32, device=dev)
+        slots[tk[:, 0], tk[:, 1]] = res
+        self.last = {"sel": sel, "w": w, "m": m, "dispatch_rows": int(x_send.shape[0]), "results": int(res.shape[0])}
+        return self.be.combine(slots)
+
+
+__all__ = ["DeviceBackend", "ExpertParallelMoE"]

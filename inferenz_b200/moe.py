@@ -62,6 +62,31 @@ class MoePool:
         self._check(lib.inzg_pool_add_layer(self._ctx, layer, expert_type, _ptr(b), blob_bytes, self.n_expert),
                     "pool_add_layer")
 
+    def add_layer_range(self, layer, expert_type, blobs, blob_bytes, e_first, n_local):
+        """Experts [e_first, e_first + n_local) only (expert parallelism); blobs holds those n_local blobs."""
+        b = np.ascontiguousarray(blobs, dtype=np.uint8)
+        assert b.size >= blob_bytes * n_local
+        self._check(lib.inzg_pool_add_layer_range(self._ctx, layer, expert_type, _ptr(b), blob_bytes, e_first, n_local),
+                    "pool_add_layer_range")
+
+    # -- expert-parallel building blocks (device pointers as ints; stream-ordered, no synchronisation) --
+    def route_device(self, layer, n, x_ptr, sel_ptr, w_ptr, bias_ptr=None, stream=None):
+        self._check(lib.inzg_route(self._ctx, layer, n, ctypes.c_void_p(x_ptr), bias_ptr and ctypes.c_void_p(bias_ptr),
+                                   ctypes.c_void_p(sel_ptr), ctypes.c_void_p(w_ptr), stream and ctypes.c_void_p(stream)),
+                    "route")
+
+    def experts_device(self, layer, m, x_ptr, sel_ptr, w_ptr, n_batch, out_ptr, stream=None):
+        self._check(lib.inzg_moe_experts(self._ctx, layer, m, ctypes.c_void_p(x_ptr), ctypes.c_void_p(sel_ptr),
+                                         ctypes.c_void_p(w_ptr), n_batch, ctypes.c_void_p(out_ptr),
+                                         stream and ctypes.c_void_p(stream)), "moe_experts")
+
+    def combine_device(self, n, slots_ptr, y_ptr, stream=None):
+        self._check(lib.inzg_combine(self._ctx, n, ctypes.c_void_p(slots_ptr), ctypes.c_void_p(y_ptr),
+                                     stream and ctypes.c_void_p(stream)), "combine")
+
+    def device_status(self, stream=None):
+        self._check(lib.inzg_device_status(self._ctx, stream and ctypes.c_void_p(stream)), "device_status")
+
     # -- forward --
     def moe_block(self, layer, xin, bias=None, logits_override=None, dump=False, y=None, graph=True, simt_gemm=False):
         """y [n][H] = routed MoE layer of xin [n][H] (host arrays; copies in and out inside the call)."""

@@ -82,5 +82,14 @@ def layer_blobs(layer, expert_type=T_Q4L, H=2048, FF=640, E=512, experts=None):
     return out, bb
 
 
-__all__ = ["router", "hidden", "normal_bias", "zipf_bias", "normal_logits", "layer_blobs", "blob_bytes", "expert_fp32",
-           "T_Q4L", "T_Q8G"]
+def layer_blobs_range(layer, expert_type, H, FF, e0, e1):
+    """Blobs of experts [e0, e1) of a synthetic layer (the same bytes as layer_blobs), [(e1 - e0) * blob_bytes]."""
+    bb = blob_bytes(expert_type, H, FF)
+    out = np.zeros((e1 - e0) * bb, np.uint8)
+    if lib.inzg_synth_layer_blobs(layer, expert_type, H, FF, e0, e1, _p(out)) != 0:
+        raise RuntimeError("inzg_synth_layer_blobs failed")
+    return out, bb
+
+
+__all__ = ["router", "hidden", "normal_bias", "zipf_bias", "normal_logits", "layer_blobs", "layer_blobs_range",
+           "blob_bytes", "expert_fp32", "T_Q4L", "T_Q8G"]

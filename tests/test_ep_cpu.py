@@ -1,0 +1,99 @@
+"""Expert-parallel exchange logic on CPU: world_size 2 (and 4) gloo ranks against one process.
+
+The backend is a deterministic stand-in for the GPU kernels (routing from a fixed projection, an expert that scales
+its rows by the expert id): the test checks that the dispatch, the local expert indices, the return of every
+(token, rank-k) result and the rank-order combine reproduce the single-process layer exactly. The real kernels' EP
+parity is tests/test_gpu_ep.py.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from inferenz_b200.ep import ExpertParallelMoE
+
+E, K, H = 32, 4, 16
+
+
+class FakeBackend:
+    def __init__(self, rank, e_per):
+        self.e_first = rank * e_per
+        g = torch.Generator().manual_seed(7)
+        self.P = torch.randn((H, E), generator=g)
+
+    def route(self, layer, x, bias=None):
+        # row by row: a matmul over the whole batch is not bitwise batch-invariant on the CPU
+        logits = torch.stack([(x[r:r + 1] @ self.P)[0] for r in range(x.shape[0])]) if x.shape[0] else x.new_zeros((0, E))
+        p = torch.softmax(logits, dim=1)
+        w, sel = torch.topk(p, K, dim=1)
+        return sel.to(torch.int32), (w / w.sum(1, keepdim=True)).to(torch.float32)
+
+    def experts(self, layer, x, sel, w, n_batch):
+        out = torch.full((x.shape[0], K, H), float("nan"))
+        for r in range(x.shape[0]):
+            for k in range(K):
+                if sel[r, k] >= 0:
+                    e = int(sel[r, k]) + self.e_first
+                    out[r, k] = w[r, k] * (x[r] * (e + 1) + n_batch)
+        return out
+
+    def combine(self, slots):
+        y = torch.zeros((slots.shape[0], H))
+        for k in range(K):
+            y = y + slots[:, k]
+        return y
+
+
+def reference(x):
+    be = FakeBackend(0, E)
+    sel, w = be.route(0, x)
+    return be.combine(be.experts(0, x, sel, w, x.shape[0]))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, counts, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(11)
+        x_all = torch.randn((sum(counts), H), generator=g)
+        lo = sum(counts[:rank])
+        x = x_all[lo:lo + counts[rank]]
+        ep = ExpertParallelMoE(FakeBackend(rank, E // world), E, K, H)
+        y = ep.moe_block(0, x)
+        q.put((rank, y.numpy(), ep.last["dispatch_rows"], ep.last["results"]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,counts", [(2, [5, 7]), (2, [1, 0]), (4, [3, 1, 4, 2])])
+def test_ep_exchange_matches_single_process(world, counts):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, counts, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    g = torch.Generator().manual_seed(11)
+    x_all = torch.randn((sum(counts), H), generator=g)
+    want = reference(x_all).numpy()
+    total_results = 0
+    for rank, y, _, nres in sorted(res):
+        lo = sum(counts[:rank])
+        assert np.array_equal(y.view(np.uint32), want[lo:lo + counts[rank]].view(np.uint32))
+        total_results += nres
+    assert total_results == sum(counts) * K  # every (token, rank-k) result came home exactly once
