@@ -2,15 +2,19 @@
 
 Workload (headline, N=1): BASELINE configs[1] -- one MoE layer, d=2048, 512 experts, top-10, FF 640, Q4L experts
 (synthetic, seeded, quantized with the engine's own quantizer), F16 router, decode batch of 32 tokens with a
-per-expert N(0,1) logit bias. Sub-results under "extra": configs[0] shape (1 token) and configs[2] (4096-token
-prefill, Zipf(1.1) bias).
+per-expert N(0,1) logit bias. Sub-results under "extra": configs[0] shape (1 token), configs[2] (4096-token
+prefill, Zipf(1.1) bias) and configs[3] (Q8G experts, 2048 tokens, router logits replaced by N(0,1)).
 
 value  = tokens/s with inputs resident in HBM; each timed step is one layer call timed with CUDA events on the
          launching stream; the L2 is flushed (512 MB write) before every step, outside the timed events.
 e2e    = the same through the public host API (MoePool.moe_block on pinned host buffers): H2D of the step's input and
          D2H of its output inside the timed region (host wall clock around the synchronous call).
 --impl reference: the reference's own CPU implementation of the layer (oracle/_ref, all host cores).
-Multi-GPU (--gpus N, one process per GPU): N independent replicas (the expert-parallel path is not built yet).
+Multi-GPU (--gpus N under torchrun, one process per GPU): expert parallelism. Rank g holds
+experts [g*512/N, (g+1)*512/N) and decodes its own 32 tokens (weak scaling: 32*N tokens per step); a step routes
+the rank's tokens, sends each token row once to every GPU owning one of its experts (NCCL all-to-all), runs the local
+experts, returns every (token, rank-k) output (NCCL all-to-all) and combines in rank order. value = all ranks'
+tokens / the max over ranks of the summed per-step CUDA-event times.
 """
 import argparse
 import json
@@ -30,6 +34,9 @@ H, FF, E, K = 2048, 640, 512, 10
 GU_PAYLOAD = 2 * FF * (H // 64) * 34        # gate|up indices + fp16 scales, Q4L (header excluded)
 DN_PAYLOAD = H * (FF // 64) * 34
 EXPERT_BYTES_Q4L = 2089088                   # both matrices incl. their 64-byte headers (inz_qmat_bytes)
+GU_PAYLOAD_Q8G = 2 * FF * (H // 64) * 66    # Q8G: 64 index bytes + fp16 scale per 64-group
+DN_PAYLOAD_Q8G = H * (FF // 64) * 66
+EXPERT_BYTES_Q8G = 4055168
 ROUTER_BYTES = E * H * 2
 
 
@@ -99,16 +106,19 @@ def make_inputs(cfg, n):
         bias = synth.normal_bias(E)
     elif cfg == "prefill4096":
         bias = synth.zipf_bias(E)
+    elif cfg == "q8g2048":
+        override = synth.normal_logits(n, E)  # router logits replaced by N(0,1), seed 4
     return x, bias, override
 
 
-def time_device(pool, torch, x, bias, steps, warmup, flush, layer=0):
+def time_device(pool, torch, x, bias, steps, warmup, flush, layer=0, override=None):
     """Per-step CUDA-event time (ms) of the layer on HBM-resident inputs."""
     n = x.shape[0]
     dev = torch.device("cuda", pool.device)
     xd = torch.from_numpy(x).to(dev)
     yd = torch.empty_like(xd)
     bd = None if bias is None else torch.from_numpy(bias).to(dev)
+    od = None if override is None else torch.from_numpy(override).to(dev)
     # a dedicated (non-default) stream: the flush, the events and the layer all run on it
     stream = torch.cuda.Stream(dev)
     sh = stream.cuda_stream
@@ -116,7 +126,7 @@ def time_device(pool, torch, x, bias, steps, warmup, flush, layer=0):
 
     def call():
         pool.moe_block_device(layer, n, xd.data_ptr(), yd.data_ptr(), None if bd is None else bd.data_ptr(),
-                              stream=sh)
+                              None if od is None else od.data_ptr(), stream=sh)
 
     torch.cuda.synchronize(dev)
     with torch.cuda.stream(stream):
@@ -134,12 +144,13 @@ def time_device(pool, torch, x, bias, steps, warmup, flush, layer=0):
     return [a.elapsed_time(b) for a, b in evs], yd
 
 
-def profile_stages(pool, torch, x, bias, reps, flush, layer=0):
+def profile_stages(pool, torch, x, bias, reps, flush, layer=0, override=None):
     n = x.shape[0]
     dev = torch.device("cuda", pool.device)
     xd = torch.from_numpy(x).to(dev)
     yd = torch.empty_like(xd)
     bd = None if bias is None else torch.from_numpy(bias).to(dev)
+    od = None if override is None else torch.from_numpy(override).to(dev)
     stream = torch.cuda.Stream(dev)
     sh = stream.cuda_stream
     torch.cuda.synchronize(dev)
@@ -148,11 +159,11 @@ def profile_stages(pool, torch, x, bias, reps, flush, layer=0):
         for _ in range(reps):
             flush.zero_()
             pool.moe_block_device(layer, n, xd.data_ptr(), yd.data_ptr(), None if bd is None else bd.data_ptr(),
-                                  stream=sh, profile=True)
+                                  None if od is None else od.data_ptr(), stream=sh, profile=True)
     torch.cuda.synchronize(dev)
     st, calls = pool.stage_times(reset=True)
     # routing summary of this input (one dumped call)
-    pool.moe_block(layer, x, bias=bias, dump=True)
+    pool.moe_block(layer, x, bias=bias, logits_override=override, dump=True)
     pool.route_dump(n)
     s = pool.stats()
     return {k: v / max(calls, 1) for k, v in st.items()}, s
@@ -177,15 +188,16 @@ def time_e2e(pool, torch, x, bias, steps, warmup, flush):
     return ts, h2d, d2h, yp
 
 
-def stage_roofline(stage_ms, stats, n, hbm):
+def stage_roofline(stage_ms, stats, n, hbm, q8g=False):
     """Algorithmic bytes per launch of each stage; the dominant stage's achieved GB/s."""
     dec, gemm = stats["dec_units"], stats["gemm_units"]
+    gu, dn = (GU_PAYLOAD_Q8G, DN_PAYLOAD_Q8G) if q8g else (GU_PAYLOAD, DN_PAYLOAD)
     algo = {
         "router_logits": ROUTER_BYTES + n * H * 4 + n * E * 4,
-        "gate_up_gemv": dec * GU_PAYLOAD,
-        "down_gemv": dec * DN_PAYLOAD,
-        "gate_up_gemm": gemm * GU_PAYLOAD,
-        "down_gemm": gemm * DN_PAYLOAD,
+        "gate_up_gemv": dec * gu,
+        "down_gemv": dec * dn,
+        "gate_up_gemm": gemm * gu,
+        "down_gemm": gemm * dn,
     }
     total = sum(stage_ms.values())
     if total <= 0:
@@ -205,56 +217,53 @@ def run_mine(args):
 
     from inferenz_b200 import MoePool, synth
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    rank, world, local = 0, 1, 0  # one GPU (--gpus N > 1 runs run_ep)
     dev = torch.device("cuda", local)
     hbm, bf16, peak_kind = peaks()
     t0 = time.time()
     blobs, bb = synth.layer_blobs(0, synth.T_Q4L, H, FF, E)
     gen_s = time.time() - t0
     R = synth.router(0, E, H)
-    pool = MoePool(H, FF, E, K, max_tokens=4096, n_layers=1, device=local)
+    pool = MoePool(H, FF, E, K, max_tokens=4096, n_layers=2, device=local)
     pool.set_router(0, R)
     pool.add_layer(0, synth.T_Q4L, blobs, bb)
+    q8 = not args.headline_only and args.only in (None, "q8g2048")
+    if q8:  # the same layer with Q8G experts (slot 1; its router logits come from the override)
+        t1 = time.time()
+        b8, bb8 = synth.layer_blobs(0, synth.T_Q8G, H, FF, E)
+        pool.add_layer(1, synth.T_Q8G, b8, bb8)
+        del b8
+        gen_s += time.time() - t1
     flush = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
 
     results = {}
     plan = [("decode32", 32, args.steps, args.warmup)]
     if not args.headline_only:
-        plan += [("decode1", 1, max(args.steps // 2, 10), args.warmup), ("prefill4096", 4096, max(args.steps // 50, 5), 3)]
+        plan += [("decode1", 1, max(args.steps // 2, 10), args.warmup), ("prefill4096", 4096, max(args.steps // 50, 5), 3),
+                 ("q8g2048", 2048, max(args.steps // 50, 5), 3)]
     if args.only:
-        plan = [p for p in plan if p[0] == args.only] or [(args.only, {"decode1": 1, "decode32": 32, "prefill4096": 4096}[args.only], args.steps, args.warmup)]
+        plan = [p for p in plan if p[0] == args.only] or [(args.only, {"decode1": 1, "decode32": 32, "prefill4096": 4096,
+                                                                       "q8g2048": 2048}[args.only], args.steps, args.warmup)]
     clocks_summary = None
     for name, n, steps, warm in plan:
-        x, bias, _ = make_inputs(name, n)
-        if dist:
-            dist.barrier()
+        x, bias, ovr = make_inputs(name, n)
+        layer = 1 if name == "q8g2048" else 0
         torch.cuda.synchronize(dev)
         if name == "decode32":
             with Clocks(local) as ck:
-                ts, yd = time_device(pool, torch, x, bias, steps, warm, flush)
+                ts, yd = time_device(pool, torch, x, bias, steps, warm, flush, layer, ovr)
             clocks_summary = ck.summary()
         else:
-            ts, yd = time_device(pool, torch, x, bias, steps, warm, flush)
+            ts, yd = time_device(pool, torch, x, bias, steps, warm, flush, layer, ovr)
         torch.cuda.synchronize(dev)
-        if dist:
-            dist.barrier()
         total_ms = sum(ts)
-        if dist:
-            tt = torch.tensor([total_ms], dtype=torch.float64, device=dev)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            total_ms = float(tt.item())
-        stage_ms, stats = profile_stages(pool, torch, x, bias, 0 if args.only else max(3, min(20, steps)), flush)
-        roof = stage_roofline(stage_ms, stats, n, hbm)
+        stage_ms, stats = profile_stages(pool, torch, x, bias, 0 if args.only else max(3, min(20, steps)), flush,
+                                         layer, ovr)
+        roof = stage_roofline(stage_ms, stats, n, hbm, q8g=layer == 1)
         U = stats["units"]
-        layer_bytes = ROUTER_BYTES + U * EXPERT_BYTES_Q4L + 2 * n * H * 4
+        # the override replaces the router in configs[3]: no router bytes there
+        layer_bytes = (0 if ovr is not None else ROUTER_BYTES) + U * (EXPERT_BYTES_Q8G if layer == 1 else
+                                                                      EXPERT_BYTES_Q4L) + 2 * n * H * 4
         ms_step = total_ms / steps
         results[name] = {
             "n_tokens": n, "steps": steps, "ms_per_step": round(ms_step, 5),
@@ -295,7 +304,7 @@ def run_mine(args):
             "config": {"workload": "BASELINE configs[1]: MoE layer, decode batch of 32 tokens, d=2048, 512 experts, "
                                    "top-10, FF 640, Q4L experts, F16 router, N(0,1) per-expert logit bias",
                        "global_batch": 32 * world, "seq_len": 1,
-                       "parallelism": "replicas" if world > 1 else "single GPU",
+                       "parallelism": "single GPU",
                        "l2": "flushed (512 MB write) before every timed step"},
             "roofline": roof or None,
             "layer_roofline": head["layer_roofline"],
@@ -308,9 +317,111 @@ def run_mine(args):
         }
         print(json.dumps(line))
     pool.close()
-    if dist:
+
+
+def run_ep(args):
+    """--gpus N > 1: the expert-parallel decode step (see the module docstring)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from inferenz_b200 import MoePool, synth
+    from inferenz_b200.ep import DeviceBackend, ExpertParallelMoE
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    dev = torch.device("cuda", local)
+    hbm, _, peak_kind = peaks()
+    n_loc = 32
+    e0, nl = rank * E // world, E // world
+    t0 = time.time()
+    blobs, bb = synth.layer_blobs_range(0, synth.T_Q4L, H, FF, e0, e0 + nl)
+    gen_s = time.time() - t0
+    pool = MoePool(H, FF, E, K, max_tokens=n_loc * world, n_layers=1, device=local)
+    pool.set_router(0, synth.router(0, E, H))
+    pool.add_layer_range(0, synth.T_Q4L, blobs, bb, e0, nl)
+    stream = torch.cuda.Stream(dev)
+    ep = ExpertParallelMoE(DeviceBackend(pool, stream), E, K, H)
+    x_all = synth.hidden(n_loc * world, H)
+    xd = torch.from_numpy(x_all[rank * n_loc:(rank + 1) * n_loc].copy()).to(dev)
+    bd = torch.from_numpy(synth.normal_bias(E)).to(dev)
+    flush = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    nb = n_loc * world
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            flush.zero_()
+            ep.moe_block(0, xd, bd, n_batch=nb)
+        ep.moe_block(0, xd, bd, n_batch=nb, stats=True)
+        local_units = ep.last["local_units"]
+        stream.synchronize()
         dist.barrier()
-        dist.destroy_process_group()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        with Clocks(local) as ck:
+            for a, b in evs:
+                flush.zero_()
+                a.record(stream)
+                ep.moe_block(0, xd, bd, n_batch=nb)
+                b.record(stream)
+            stream.synchronize()
+        pool.device_status(stream.cuda_stream)
+        total = torch.tensor([sum(a.elapsed_time(b) for a, b in evs)], dtype=torch.float64, device=dev)
+        dist.all_reduce(total, op=dist.ReduceOp.MAX)
+        total_ms = float(total.item())
+        # end to end: the step's tokens from pinned host memory and its output back to the host, wall clock
+        xp = torch.from_numpy(x_all[rank * n_loc:(rank + 1) * n_loc].copy()).pin_memory()
+        yp = torch.empty((n_loc, H), dtype=torch.float32).pin_memory()
+        e2e_steps = max(args.steps // 4, 5)
+        dist.barrier()
+        ts = []
+        for _ in range(e2e_steps):
+            flush.zero_()
+            stream.synchronize()
+            t1 = time.perf_counter()
+            xd.copy_(xp, non_blocking=True)
+            y = ep.moe_block(0, xd, bd, n_batch=nb)
+            yp.copy_(y, non_blocking=True)
+            stream.synchronize()
+            ts.append(time.perf_counter() - t1)
+        e2e_t = torch.tensor([sum(ts)], dtype=torch.float64, device=dev)
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+        units_t = torch.tensor([local_units], dtype=torch.int64, device=dev)
+        dist.all_reduce(units_t)
+    ms_step = total_ms / args.steps
+    value = nb * args.steps / (total_ms * 1e-3)
+    units_all = int(units_t.item())
+    # per GPU: router + its experts' weights + its tokens in and out
+    bytes_gpu = ROUTER_BYTES + local_units * EXPERT_BYTES_Q4L + 2 * n_loc * H * 4
+    if rank == 0:
+        ach = bytes_gpu / (ms_step * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 x Q4L (fp32 accumulate)", "data": "synthetic (seeded; no dataset)",
+            "config": {"workload": "BASELINE configs[1] per GPU, expert-parallel: MoE layer, decode batch of 32 tokens "
+                                   "per GPU, d=2048, 512 experts (512/N per GPU), top-10, FF 640, Q4L experts, F16 "
+                                   "router, N(0,1) per-expert logit bias; NCCL all-to-all dispatch and combine",
+                       "global_batch": nb, "seq_len": 1, "parallelism": f"ep{world}",
+                       "l2": "flushed (512 MB write) before every step"},
+            "roofline": {"bound": "hbm", "kernel": "layer step per GPU (router + local experts, incl. NCCL exchange)",
+                         "algorithmic_bytes": bytes_gpu, "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(ach / hbm, 4), "peak_kind": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)",
+                         "traffic": None},
+            "cpu_baseline": None,
+            "e2e": {"value": round(nb * e2e_steps / float(e2e_t.item()), 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": n_loc * H * 4 * world, "d2h_bytes_per_step": n_loc * H * 4 * world},
+            "clocks": ck.summary(),
+            "gpu_launches": 11 * args.steps,
+            "detail": {"experts_touched_all_gpus": units_all, "experts_touched_rank0": local_units,
+                       "layer_gen_s_rank0": round(gen_s, 1)},
+        }
+        print(json.dumps(line))
+    dist.barrier()
+    pool.close()
+    dist.destroy_process_group()
 
 
 def cpu_reference(cfg, n, budget_s=12.0, blobs=None, bb=None, R=None, steps=None, warmup=1):
@@ -374,13 +485,15 @@ def main():
     ap.add_argument("--headline-only", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--only", choices=["decode1", "decode32", "prefill4096"], default=None,
+    ap.add_argument("--only", choices=["decode1", "decode32", "prefill4096", "q8g2048"], default=None,
                     help="time a single workload (profiling runs); the JSON line then reports that workload")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        run_ep(args)
     else:
         run_mine(args)
 

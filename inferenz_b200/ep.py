@@ -73,8 +73,9 @@ class ExpertParallelMoE:
     def _a2a(self, out, inp, out_splits, in_splits):
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
 
-    def moe_block(self, layer, x, bias=None, n_batch=None):
-        """y [n][H] for this rank's tokens x [n][H] (fp32, on the backend's device)."""
+    def moe_block(self, layer, x, bias=None, n_batch=None, stats=False):
+        """y [n][H] for this rank's tokens x [n][H] (fp32, on the backend's device). stats: also count the local
+        experts that received tokens (self.last["local_units"]; one extra device synchronisation)."""
         G, K, H = self.world, self.K, self.H
         dev = x.device
         n = x.shape[0]
@@ -119,6 +120,9 @@ class ExpertParallelMoE:
         slots = torch.empty((n, K, H), dtype=torch.float32, device=dev)
         slots[tk[:, 0], tk[:, 1]] = res
         self.last = {"sel": sel, "w": w, "m": m, "dispatch_rows": int(x_send.shape[0]), "results": int(res.shape[0])}
+        if stats:
+            used = sel_recv[present].long()
+            self.last["local_units"] = int((torch.bincount(used, minlength=self.e_per) > 0).sum()) if used.numel() else 0
         return self.be.combine(slots)
 
 
