@@ -323,6 +323,10 @@ def run_ep(args):
     """--gpus N > 1: the expert-parallel decode step (see the module docstring)."""
     import datetime
 
+    # the ranks share the host's cores for the synthetic layer's generation: give each its share (torchrun sets
+    # OMP_NUM_THREADS=1; the generator reads it when the library loads, below)
+    lw = int(os.environ.get("LOCAL_WORLD_SIZE", os.environ.get("WORLD_SIZE", "1")))
+    os.environ["OMP_NUM_THREADS"] = str(max(1, (os.cpu_count() or 1) // max(lw, 1)))
     import torch
     import torch.distributed as dist
 
@@ -351,12 +355,35 @@ def run_ep(args):
     bd = torch.from_numpy(synth.normal_bias(E)).to(dev)
     flush = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     nb = n_loc * world
+
+    def ep_step():  # fixed-size exchanges: no host synchronisation inside the step
+        return ep.moe_block_fixed(0, xd, bd, n_batch=nb, capacity=n_loc)
+
+    graph, graph_err, y_graph = None, None, None
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             flush.zero_()
-            ep.moe_block(0, xd, bd, n_batch=nb)
+            ep_step()
         ep.moe_block(0, xd, bd, n_batch=nb, stats=True)
         local_units = ep.last["local_units"]
+        stream.synchronize()
+        dist.barrier()
+        try:  # the whole step, NCCL exchanges included, as one CUDA graph
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
+                y_graph = ep_step()
+            graph.replay()
+            stream.synchronize()
+        except Exception as exc:  # every rank falls back together below
+            graph, graph_err = None, f"{type(exc).__name__}: {exc}"[:200]
+        ok = torch.tensor([1 if graph is not None else 0], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if int(ok.item()) == 0:
+            graph = None
+        step = graph.replay if graph is not None else ep_step
+        for _ in range(3):
+            flush.zero_()
+            step()
         stream.synchronize()
         dist.barrier()
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -364,7 +391,7 @@ def run_ep(args):
             for a, b in evs:
                 flush.zero_()
                 a.record(stream)
-                ep.moe_block(0, xd, bd, n_batch=nb)
+                step()
                 b.record(stream)
             stream.synchronize()
         pool.device_status(stream.cuda_stream)
@@ -382,8 +409,8 @@ def run_ep(args):
             stream.synchronize()
             t1 = time.perf_counter()
             xd.copy_(xp, non_blocking=True)
-            y = ep.moe_block(0, xd, bd, n_batch=nb)
-            yp.copy_(y, non_blocking=True)
+            y = step()
+            yp.copy_(y_graph if graph is not None else y, non_blocking=True)
             stream.synchronize()
             ts.append(time.perf_counter() - t1)
         e2e_t = torch.tensor([sum(ts)], dtype=torch.float64, device=dev)
@@ -416,10 +443,16 @@ def run_ep(args):
             "clocks": ck.summary(),
             "gpu_launches": 11 * args.steps,
             "detail": {"experts_touched_all_gpus": units_all, "experts_touched_rank0": local_units,
-                       "layer_gen_s_rank0": round(gen_s, 1)},
+                       "layer_gen_s_rank0": round(gen_s, 1), "exchange": "fixed-size all-to-all (32 rows per rank pair)",
+                       "cuda_graph": graph is not None, "graph_error": graph_err},
         }
         print(json.dumps(line))
     dist.barrier()
+    # a graph holding NCCL calls must be released before the process group: drop every reference to it
+    step = y_graph = graph = None
+    import gc
+    gc.collect()
+    torch.cuda.synchronize(dev)
     pool.close()
     dist.destroy_process_group()
 

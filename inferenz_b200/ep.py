@@ -126,4 +126,39 @@ class ExpertParallelMoE:
         return self.be.combine(slots)
 
 
+    def moe_block_fixed(self, layer, x, bias=None, n_batch=None, capacity=None):
+        """The same layer with fixed-size exchanges: every rank sends each rank a block of ``capacity`` token rows
+        (its n <= capacity tokens, entries of other ranks marked -1) and receives a block of ``capacity`` x topk
+        results back, so no count crosses to the host and the step can be captured in a CUDA graph. For decode-sized
+        batches; the bytes grow with world x capacity x topk."""
+        G, K, H = self.world, self.K, self.H
+        dev = x.device
+        n = x.shape[0]
+        C = n if capacity is None else capacity
+        if n > C:
+            raise ValueError("more tokens than the exchange capacity")
+        nb = n_batch if n_batch is not None else n * G
+        sel, w = self.be.route(layer, x, bias)
+        owner = (sel // self.e_per).to(torch.int32)                          # [n][K]
+        d = torch.arange(G, device=dev, dtype=torch.int32)[:, None, None]     # [G][1][1]
+        local = torch.where(owner[None] == d, sel[None] - d * self.e_per, torch.full_like(sel[None], -1))  # [G][n][K]
+        meta_send = torch.full((G, C, 2 * K), -1, dtype=torch.int32, device=dev)
+        meta_send[:, :n, :K] = local
+        meta_send[:, :n, K:] = w.view(torch.int32)[None]
+        x_send = torch.zeros((G, C, H), dtype=torch.float32, device=dev)
+        x_send[:, :n] = x[None]
+        x_recv = torch.empty_like(x_send)
+        meta_recv = torch.empty_like(meta_send)
+        self._a2a(x_recv, x_send, None, None)
+        self._a2a(meta_recv, meta_send, None, None)
+        meta_recv = meta_recv.view(G * C, 2 * K)
+        out = self.be.experts(layer, x_recv.view(G * C, H), meta_recv[:, :K].contiguous(),
+                              meta_recv[:, K:].contiguous().view(torch.float32), nb)  # [G*C][K][H]
+        back = torch.empty_like(out)
+        self._a2a(back, out, None, None)                                     # block d: rank d's results for my rows
+        idx = (owner.long() * C + torch.arange(n, device=dev)[:, None]) * K + torch.arange(K, device=dev)[None, :]
+        slots = back.view(G * C * K, H)[idx.view(-1)].view(n, K, H)
+        return self.be.combine(slots)
+
+
 __all__ = ["DeviceBackend", "ExpertParallelMoE"]

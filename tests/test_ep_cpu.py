@@ -71,7 +71,8 @@ def _worker(rank, world, port, counts, q):
         x = x_all[lo:lo + counts[rank]]
         ep = ExpertParallelMoE(FakeBackend(rank, E // world), E, K, H)
         y = ep.moe_block(0, x)
-        q.put((rank, y.numpy(), ep.last["dispatch_rows"], ep.last["results"]))
+        yf = ep.moe_block_fixed(0, x, n_batch=sum(counts), capacity=max(counts))
+        q.put((rank, y.numpy(), yf.numpy(), ep.last["dispatch_rows"], ep.last["results"]))
     finally:
         dist.destroy_process_group()
 
@@ -92,8 +93,9 @@ def test_ep_exchange_matches_single_process(world, counts):
     x_all = torch.randn((sum(counts), H), generator=g)
     want = reference(x_all).numpy()
     total_results = 0
-    for rank, y, _, nres in sorted(res):
+    for rank, y, yf, _, nres in sorted(res, key=lambda r: r[0]):
         lo = sum(counts[:rank])
         assert np.array_equal(y.view(np.uint32), want[lo:lo + counts[rank]].view(np.uint32))
+        assert np.array_equal(yf.view(np.uint32), want[lo:lo + counts[rank]].view(np.uint32))
         total_results += nres
     assert total_results == sum(counts) * K  # every (token, rank-k) result came home exactly once
