@@ -338,6 +338,8 @@ def run_ep(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    # host-side bookkeeping (barriers, per-rank timings) on gloo, apart from the communicator the graph captures
+    host = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=300))
     dev = torch.device("cuda", local)
     hbm, _, peak_kind = peaks()
     n_loc = 32
@@ -367,7 +369,7 @@ def run_ep(args):
         ep.moe_block(0, xd, bd, n_batch=nb, stats=True)
         local_units = ep.last["local_units"]
         stream.synchronize()
-        dist.barrier()
+        dist.barrier(group=host)
         try:  # the whole step, NCCL exchanges included, as one CUDA graph
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
@@ -376,8 +378,8 @@ def run_ep(args):
             stream.synchronize()
         except Exception as exc:  # every rank falls back together below
             graph, graph_err = None, f"{type(exc).__name__}: {exc}"[:200]
-        ok = torch.tensor([1 if graph is not None else 0], device=dev)
-        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        ok = torch.tensor([1 if graph is not None else 0])
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=host)
         if int(ok.item()) == 0:
             graph = None
         step = graph.replay if graph is not None else ep_step
@@ -385,7 +387,7 @@ def run_ep(args):
             flush.zero_()
             step()
         stream.synchronize()
-        dist.barrier()
+        dist.barrier(group=host)
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
         with Clocks(local) as ck:
             for a, b in evs:
@@ -395,14 +397,12 @@ def run_ep(args):
                 b.record(stream)
             stream.synchronize()
         pool.device_status(stream.cuda_stream)
-        total = torch.tensor([sum(a.elapsed_time(b) for a, b in evs)], dtype=torch.float64, device=dev)
-        dist.all_reduce(total, op=dist.ReduceOp.MAX)
-        total_ms = float(total.item())
+        my_total = sum(a.elapsed_time(b) for a, b in evs)
         # end to end: the step's tokens from pinned host memory and its output back to the host, wall clock
         xp = torch.from_numpy(x_all[rank * n_loc:(rank + 1) * n_loc].copy()).pin_memory()
         yp = torch.empty((n_loc, H), dtype=torch.float32).pin_memory()
         e2e_steps = max(args.steps // 4, 5)
-        dist.barrier()
+        dist.barrier(group=host)
         ts = []
         for _ in range(e2e_steps):
             flush.zero_()
@@ -413,13 +413,16 @@ def run_ep(args):
             yp.copy_(y_graph if graph is not None else y, non_blocking=True)
             stream.synchronize()
             ts.append(time.perf_counter() - t1)
-        e2e_t = torch.tensor([sum(ts)], dtype=torch.float64, device=dev)
-        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
-        units_t = torch.tensor([local_units], dtype=torch.int64, device=dev)
-        dist.all_reduce(units_t)
+    # per rank: device ms over the timed steps, end-to-end seconds, local experts touched
+    mine = torch.tensor([my_total, sum(ts), float(local_units)], dtype=torch.float64)
+    every = [torch.zeros(3, dtype=torch.float64) for _ in range(world)]
+    dist.all_gather(every, mine, group=host)
+    per_rank = [[round(float(v), 4) for v in t.tolist()] for t in every]
+    total_ms = max(r[0] for r in per_rank)
+    e2e_s = max(r[1] for r in per_rank)
     ms_step = total_ms / args.steps
     value = nb * args.steps / (total_ms * 1e-3)
-    units_all = int(units_t.item())
+    units_all = int(sum(r[2] for r in per_rank))
     # per GPU: router + its experts' weights + its tokens in and out
     bytes_gpu = ROUTER_BYTES + local_units * EXPERT_BYTES_Q4L + 2 * n_loc * H * 4
     if rank == 0:
@@ -438,16 +441,17 @@ def run_ep(args):
                          "frac": round(ach / hbm, 4), "peak_kind": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)",
                          "traffic": None},
             "cpu_baseline": None,
-            "e2e": {"value": round(nb * e2e_steps / float(e2e_t.item()), 1), "unit": "tokens/s",
+            "e2e": {"value": round(nb * e2e_steps / e2e_s, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": n_loc * H * 4 * world, "d2h_bytes_per_step": n_loc * H * 4 * world},
             "clocks": ck.summary(),
             "gpu_launches": 11 * args.steps,
             "detail": {"experts_touched_all_gpus": units_all, "experts_touched_rank0": local_units,
                        "layer_gen_s_rank0": round(gen_s, 1), "exchange": "fixed-size all-to-all (32 rows per rank pair)",
-                       "cuda_graph": graph is not None, "graph_error": graph_err},
+                       "cuda_graph": graph is not None, "graph_error": graph_err,
+                       "per_rank_device_ms_e2e_s_units": per_rank},
         }
         print(json.dumps(line))
-    dist.barrier()
+    dist.barrier(group=host)
     # a graph holding NCCL calls must be released before the process group: drop every reference to it
     step = y_graph = graph = None
     import gc
