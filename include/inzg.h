@@ -65,8 +65,8 @@ typedef struct {
 #define INZG_NO_GRAPH 8u    /* launch the kernels one by one instead of replaying the cached CUDA graph */
 #define INZG_GEMM_SIMT 16u  /* prefill-path experts on the CUDA-core int8 GEMM instead of tcgen05 (cross-check) */
 
-/* stages timed under INZG_PROFILE (the reference's diag stages are coarser: DG_ROUTER, DG_EXPERT_*) */
-#define INZG_N_STAGES 10
+/* stages timed under INZG_PROFILE (the reference's diag stages are coarser: DG_ROUTER, DG_EXPERT_*, DG_SHARED) */
+#define INZG_N_STAGES 11
 
 typedef struct {
     unsigned flags;
@@ -100,8 +100,16 @@ INZG_EXPORT inzg_status inzg_set_router(inzg_ctx *ctx, int layer, const uint16_t
 INZG_EXPORT inzg_status inzg_pool_add_layer(inzg_ctx *ctx, int layer, int expert_type, const void *blobs, uint64_t blob_bytes,
                                 int n_expert);
 
-/* The routed MoE layer: y[n][hidden] = sum over the top-k experts of w_k * down(silu(gate x) * up x), in rank order,
- * OVERWRITING y (src/model_fwd.c:1033, 1134-1140). xin [n][hidden] fp32. Same per-expert numeric path as the
+/* The layer's shared expert (src/model_fwd.c:1041-1069, 1141-1148; the engine's `sh.gate_up`, `sh.down` and
+ * `sh.gate` tensors, src/engine.c:175-177): blob holds the gate|up matrix (2*ff x hidden) followed by the down matrix
+ * (hidden x ff) at inzg_qmat_bytes(type, 2*ff, hidden) -- the layout of one expert blob; gate [hidden] fp32. Once
+ * set, inzg_moe_forward adds y += sigmoid(gate . x) * down(silu(gate_up x) * up x) per token after the routed sum,
+ * with the reference's numerics (lin_mm's path rule: decode numerics below 12 tokens, GEMM numerics otherwise). */
+INZG_EXPORT inzg_status inzg_set_shared(inzg_ctx *ctx, int layer, int expert_type, const void *blob, uint64_t blob_bytes,
+                                        const float *gate);
+
+/* The MoE layer: y[n][hidden] = sum over the top-k experts of w_k * down(silu(gate x) * up x), in rank order,
+ * OVERWRITING y (src/model_fwd.c:1033, 1134-1140), plus the shared expert when one is set (inzg_set_shared). xin [n][hidden] fp32. Same per-expert numeric path as the
  * reference: experts with fewer than 12 tokens (or every expert when n <= 8) use the decode numerics
  * (src/quant.c:611-671, 767-953), the others the prefill GEMM numerics (src/quant.c:1407-1668). */
 INZG_EXPORT inzg_status inzg_moe_forward(inzg_ctx *ctx, int layer, int n, const float *xin, float *y, const inzg_moe_opts *opt);
@@ -161,6 +169,12 @@ INZG_EXPORT inzg_status inzg_moe_experts(inzg_ctx *ctx, int layer, int m, const 
 
 /* y_dev[t] = ((0 + s[t][0]) + s[t][1]) + ... + s[t][topk-1] for slots_dev [n][topk][hidden] (src/model_fwd.c:1134-1140). */
 INZG_EXPORT inzg_status inzg_combine(inzg_ctx *ctx, int n, const float *slots_dev, float *y_dev, void *stream);
+
+/* The shared expert of `layer` on this rank's n tokens: y_dev[t] += sigmoid(gate . x_t) * shared(x_t), after the
+ * rank's inzg_combine (the reference adds it after the routed sum). n_batch: the whole batch's token count, which picks
+ * the numeric path as in a single-GPU call. */
+INZG_EXPORT inzg_status inzg_shared_expert(inzg_ctx *ctx, int layer, int n, const float *x_dev, float *y_dev,
+                                           int n_batch, void *stream);
 
 /* Waits for `stream` and reports the device-side checks of the calls since the last routing step
  * (INZG_TIMEOUT / INZG_DEVICE_CHECK). */

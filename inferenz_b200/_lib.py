@@ -11,7 +11,7 @@ LIB_PATH = os.path.join(_HERE, "libinzg.so")
 
 T_F16, T_Q4L, T_Q8G = 1, 102, 103
 IO_DEVICE, DUMP_ROUTE, PROFILE, NO_GRAPH, GEMM_SIMT = 1, 2, 4, 8, 16
-N_STAGES = 10
+N_STAGES = 11
 
 STATUS = {0: "INZG_OK", 1: "INZG_BAD_ARG", 2: "INZG_CORRUPT_BLOB", 3: "INZG_OOM", 4: "INZG_CUDA", 5: "INZG_NCCL",
           6: "INZG_TIMEOUT", 7: "INZG_DEVICE_CHECK", 8: "INZG_UNSUPPORTED", 9: "INZG_NOT_READY"}
@@ -56,6 +56,8 @@ SIGNATURES = {
     "inzg_moe_experts": (I, [P, I, I, P, P, P, I, P, P]),
     "inzg_combine": (I, [P, I, P, P, P]),
     "inzg_device_status": (I, [P, P]),
+    "inzg_set_shared": (I, [P, I, I, P, U64, P]),
+    "inzg_shared_expert": (I, [P, I, I, P, P, I, P]),
     # inzg_tools.h
     "inzg_synth_jump": (U64, [U64, U64]),
     "inzg_synth_randn": (U64, [U64, I64, F, P]),

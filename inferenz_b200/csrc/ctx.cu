@@ -81,6 +81,8 @@ struct inzg_ctx {
     int num_sms = 0;
     cudaStream_t stream = nullptr;
     std::vector<LayerSlot> layers;
+    std::vector<LayerSlot> shared;           // per layer: the shared expert as a one-expert pool (inzg_set_shared)
+    std::vector<float *> sh_gate;            // per layer: the shared expert's gate vector [hidden]
     std::string err;
     inzg_stats stats{};
     // scratch
@@ -97,6 +99,11 @@ struct inzg_ctx {
     int8_t *dq64 = nullptr, *dq256 = nullptr;
     float2 *dsb64 = nullptr;
     float *ds256 = nullptr;
+    // the shared expert's one-unit dispatch list
+    int32_t *sh_cnt = nullptr, *sh_off = nullptr, *sh_first = nullptr, *sh_etok = nullptr, *sh_eslot = nullptr;
+    int32_t *sh_eexp = nullptr, *sh_upath = nullptr, *sh_units = nullptr, *sh_dec = nullptr, *sh_gemm = nullptr;
+    int32_t *sh_tiles = nullptr, *sh_meta = nullptr;
+    float *sh_ew = nullptr;
     int8_t *xqe = nullptr;      // prefill-path token activations in entry order [n*topk][H]
     float *xse = nullptr;       // their block scales [n*topk][H/256]
     TmaMap map_xqe, map_dq;     // TMA maps over xqe and dq256
@@ -132,7 +139,7 @@ struct inzg_ctx {
 
 static const char *kStageNames[INZG_N_STAGES] = {"router_logits", "softmax_topk_route", "act_quant", "route",
                                                  "gate_up_gemv", "gate_up_gemm", "swiglu_quant", "down_gemv",
-                                                 "down_gemm", "combine"};
+                                                 "down_gemm", "combine", "shared_expert"};
 
 static void drop_graphs(inzg_ctx *c) {
     for (auto &g : c->graphs) cudaGraphExecDestroy(g.exec);
@@ -172,7 +179,8 @@ static void free_scratch(inzg_ctx *c) {
     void *ptrs[] = {c->xin, c->y, c->logits, c->probs, c->bias, c->sel, c->w, c->xq64, c->xq256, c->xsb64,
                     c->xs256, c->cnt, c->off, c->first, c->etok, c->eslot, c->ccnt, c->units, c->meta, c->dec_units,
                     c->gemm_units, c->gemm_tiles, c->upath, c->eexp, c->ew, c->GU, c->mo, c->dq64, c->dq256, c->dsb64,
-                    c->ds256, c->xqe, c->xse};
+                    c->ds256, c->xqe, c->xse, c->sh_cnt, c->sh_off, c->sh_first, c->sh_etok, c->sh_eslot,
+                    c->sh_eexp, c->sh_upath, c->sh_units, c->sh_dec, c->sh_gemm, c->sh_tiles, c->sh_meta, c->sh_ew};
     for (void *p : ptrs)
         if (p) cudaFree(p);
 }
@@ -199,6 +207,8 @@ inzg_ctx *inzg_create(const inzg_config *cfg, inzg_status *status) {
     inzg_ctx *c = new inzg_ctx();
     c->cfg = *cfg;
     c->layers.resize(cfg->n_layers);
+    c->shared.resize(cfg->n_layers);
+    c->sh_gate.assign(cfg->n_layers, nullptr);
     cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, cfg->device);
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
         delete c;
@@ -242,6 +252,19 @@ inzg_ctx *inzg_create(const inzg_config *cfg, inzg_status *status) {
     c->ds256 = dalloc<float>(NE * nkbF, ok);
     c->xqe = dalloc<int8_t>(NE * H, ok);
     c->xse = dalloc<float>(NE * nkbH, ok);
+    c->sh_cnt = dalloc<int32_t>(1, ok);
+    c->sh_off = dalloc<int32_t>(2, ok);
+    c->sh_first = dalloc<int32_t>(1, ok);
+    c->sh_etok = dalloc<int32_t>(T, ok);
+    c->sh_eslot = dalloc<int32_t>(T, ok);
+    c->sh_eexp = dalloc<int32_t>(T, ok);
+    c->sh_ew = dalloc<float>(T, ok);
+    c->sh_upath = dalloc<int32_t>(1, ok);
+    c->sh_units = dalloc<int32_t>(1, ok);
+    c->sh_dec = dalloc<int32_t>(1, ok);
+    c->sh_gemm = dalloc<int32_t>(1, ok);
+    c->sh_tiles = dalloc<int32_t>(T / 16 + 2, ok);
+    c->sh_meta = dalloc<int32_t>(16, ok);
     if (!ok) {
         free_scratch(c);
         cudaStreamDestroy(c->stream);
@@ -267,11 +290,15 @@ void inzg_destroy(inzg_ctx *c) {
     if (!c) return;
     cudaSetDevice(c->cfg.device);
     cudaStreamSynchronize(c->stream);
-    for (auto &L : c->layers) {
-        if (L.router) cudaFree(L.router);
-        if (L.pool) cudaFree(L.pool);
-        if (L.luts) cudaFree(L.luts);
-    }
+    for (auto *v : {&c->layers, &c->shared})
+        for (auto &L : *v) {
+            if (L.router) cudaFree(L.router);
+            if (L.pool) cudaFree(L.pool);
+            if (L.luts) cudaFree(L.luts);
+            if (L.gemm_w) cudaFree(L.gemm_w);
+        }
+    for (float *g : c->sh_gate)
+        if (g) cudaFree(g);
     drop_graphs(c);
     for (int i = 0; i <= INZG_N_STAGES; i++)
         if (c->ev[i]) cudaEventDestroy(c->ev[i]);
@@ -318,11 +345,11 @@ inzg_status inzg_pool_add_layer(inzg_ctx *c, int layer, int type, const void *bl
     return inzg_pool_add_layer_range(c, layer, type, blobs, blob_bytes, 0, n_expert);
 }
 
-inzg_status inzg_pool_add_layer_range(inzg_ctx *c, int layer, int type, const void *blobs, uint64_t blob_bytes,
-                                      int e_first, int n_local) {
-    if (!c) return INZG_BAD_ARG;
+// Validate, upload and re-lay out experts [e_first, e_first + n_local) into slot L (a layer's routed pool, or a
+// layer's shared expert as a one-expert pool).
+static inzg_status load_pool(inzg_ctx *c, LayerSlot &L, int type, const void *blobs, uint64_t blob_bytes, int e_first,
+                             int n_local) {
     const inzg_config &cf = c->cfg;
-    if (layer < 0 || layer >= cf.n_layers || !blobs) return fail(c, INZG_BAD_ARG, "pool_add_layer: bad layer or pointer");
     if (e_first < 0 || n_local < 1 || e_first + n_local > cf.n_expert)
         return fail(c, INZG_BAD_ARG, "pool_add_layer: expert range outside the layer's experts");
     if (type != INZG_T_Q4L && type != INZG_T_Q8G)
@@ -354,7 +381,6 @@ inzg_status inzg_pool_add_layer_range(inzg_ctx *c, int layer, int type, const vo
         return fail(c, INZG_CORRUPT_BLOB, "pool_add_layer: rotation block does not divide the matrix width");
     cudaSetDevice(cf.device);
     drop_graphs(c);
-    LayerSlot &L = c->layers[layer];
     LayerDev &D = L.dev;
     L.e_first = e_first;
     D.type = type;
@@ -424,13 +450,82 @@ inzg_status inzg_pool_add_layer_range(inzg_ctx *c, int layer, int type, const vo
     if (err != cudaSuccess) return cuda_fail(c, err, "pool_add_layer repack");
     L.has_experts = true;
     c->stats.pool_bytes = 0;
-    for (auto &S : c->layers)
-        if (S.has_experts) c->stats.pool_bytes += S.dev.slab_bytes * S.dev.E;
+    for (auto *v : {&c->layers, &c->shared})
+        for (auto &S : *v)
+            if (S.has_experts) c->stats.pool_bytes += S.dev.slab_bytes * S.dev.E;
     return INZG_OK;
 }
 
+inzg_status inzg_pool_add_layer_range(inzg_ctx *c, int layer, int type, const void *blobs, uint64_t blob_bytes,
+                                      int e_first, int n_local) {
+    if (!c) return INZG_BAD_ARG;
+    if (layer < 0 || layer >= c->cfg.n_layers || !blobs) return fail(c, INZG_BAD_ARG, "pool_add_layer: bad layer or pointer");
+    return load_pool(c, c->layers[layer], type, blobs, blob_bytes, e_first, n_local);
+}
+
+inzg_status inzg_set_shared(inzg_ctx *c, int layer, int type, const void *blob, uint64_t blob_bytes, const float *gate) {
+    if (!c) return INZG_BAD_ARG;
+    const inzg_config &cf = c->cfg;
+    if (layer < 0 || layer >= cf.n_layers || !blob || !gate)
+        return fail(c, INZG_BAD_ARG, "set_shared: bad layer or pointer");
+    const inzg_status st = load_pool(c, c->shared[layer], type, blob, blob_bytes, 0, 1);
+    if (st != INZG_OK) return st;
+    if (!c->sh_gate[layer] && cudaMalloc(&c->sh_gate[layer], sizeof(float) * cf.hidden) != cudaSuccess) {
+        cudaGetLastError();
+        c->shared[layer].has_experts = false;
+        return fail(c, INZG_OOM, "set_shared: gate vector");
+    }
+    const cudaError_t e = cudaMemcpy(c->sh_gate[layer], gate, sizeof(float) * cf.hidden, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(c, e, "set_shared");
+    return INZG_OK;
+}
+
+// The shared expert of layer `layer` on X [n][H], adding sigmoid(gate . x) * D into y (src/model_fwd.c:1041-1069,
+// 1141-1148). n_rule: the batch size of the lin_mm path rule (decode below GEMM_MIN_T tokens). quantized: X's
+// gate|up quantization for both numeric paths is already in the scratch with this rotation (the routed part's).
+static int enqueue_shared(inzg_ctx *c, int layer, int n, const float *X, float *y, int n_rule, bool quantized,
+                          cudaStream_t st) {
+    const inzg_config &cf = c->cfg;
+    const LayerSlot &S = c->shared[layer];
+    const LayerDev &D = S.dev;
+    const int H = cf.hidden, FF = cf.ff;
+    const int gemm = n_rule >= kGemmMinT;
+    int launches = 0;
+    if (!quantized)
+        launches += launch_act_quant_x(X, n, H, D.gu_rot, D.gu_seed, c->xq64, c->xsb64, gemm ? c->xq256 : nullptr,
+                                       c->xs256, st);
+    RouteDev R{};
+    R.n = n; R.topk = 1; R.E = 1; R.n_rule = n_rule; R.absent_ok = 0;
+    R.cnt = c->sh_cnt; R.off = c->sh_off; R.first = c->sh_first; R.etok = c->sh_etok; R.eslot = c->sh_eslot;
+    R.ew = c->sh_ew; R.units = c->sh_units; R.meta = c->sh_meta; R.dec_units = c->sh_dec; R.gemm_units = c->sh_gemm;
+    R.gemm_tiles = c->sh_tiles;
+    launches += launch_shared_route(R, n, gemm, gemv_items_per_unit(D, 0), gemv_items_per_unit(D, 1), gemm_token_tile(),
+                                    c->sh_upath, c->sh_eexp, st);
+    const bool tc = c->have_tc && S.has_maps;
+    const int max_tiles = (n + gemm_token_tile() - 1) / gemm_token_tile() + 1;
+    const int grid = c->num_sms * 4;
+    if (!gemm) {
+        launches += launch_gemv_decode(D, 0, R, c->xq64, c->xsb64, c->GU, 2 * FF, c->num_sms, st);
+    } else if (tc) {
+        launches += launch_gather_gemm_rows(c->xq256, c->xs256, H, (H + kKB - 1) / kKB, c->sh_etok, c->sh_eexp,
+                                            c->sh_upath, n, c->xqe, c->xse, st);
+        launches += launch_gemm_tc(0, S.map_gu.bytes, c->map_xqe.bytes, D.ws_gu, 2 * FF, H, R, c->xse, c->GU, 2 * FF,
+                                   max_tiles, st);
+    } else {
+        launches += launch_gemm_v1(D, 0, R, c->xq256, c->xs256, c->GU, 2 * FF, grid, st);
+    }
+    launches += launch_swiglu_quant(c->GU, FF, n, c->sh_eexp, c->sh_upath, D.dn_rot, D.dn_seed, c->dq64, c->dsb64,
+                                    c->dq256, c->ds256, st);
+    if (!gemm) launches += launch_gemv_decode(D, 1, R, c->dq64, c->dsb64, c->mo, H, c->num_sms, st);
+    else if (tc) launches += launch_gemm_tc(1, S.map_dn.bytes, c->map_dq.bytes, D.ws_dn, H, FF, R, c->ds256, c->mo, H,
+                                           max_tiles, st);
+    else launches += launch_gemm_v1(D, 1, R, c->dq256, c->ds256, c->mo, H, grid, st);
+    launches += launch_shared_add(X, c->sh_gate[layer], c->mo, y, n, H, c->sh_meta, c->meta, st);
+    return launches;
+}
+
 // Enqueue the whole layer on `st`. ev != nullptr: record ev[i] before stage i and ev[N] at the end.
-static int enqueue_forward(inzg_ctx *c, const LayerSlot &L, int n, const float *X, float *yd, const float *bias,
+static int enqueue_forward(inzg_ctx *c, int layer, const LayerSlot &L, int n, const float *X, float *yd, const float *bias,
                            const float *ovr, bool ovr_on_device, bool dump, bool simt_gemm, cudaEvent_t *ev,
                            cudaStream_t st) {
     const inzg_config &cf = c->cfg;
@@ -513,6 +608,12 @@ static int enqueue_forward(inzg_ctx *c, const LayerSlot &L, int n, const float *
     mark(9);
     launches += launch_combine(c->mo, n, H, K, yd, c->num_sms, st);
     mark(10);
+    if (c->shared[layer].has_experts) {  // y += sigmoid(gate . x) * shared(x), after the routed sum (:1141-1148)
+        const LayerDev &S = c->shared[layer].dev;
+        const bool same_rot = S.gu_rot == D.gu_rot && S.gu_seed == D.gu_seed;
+        launches += enqueue_shared(c, layer, n, X, yd, n, same_rot, st);
+    }
+    mark(11);
     return launches;
 }
 
@@ -555,7 +656,7 @@ inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, fl
     float *yd = dev_io ? y : c->y;
     int launches = 0;
     if (profile || (flags & INZG_NO_GRAPH)) {
-        launches = enqueue_forward(c, L, n, X, yd, bias, ovr, dev_io, dump, flags & INZG_GEMM_SIMT,
+        launches = enqueue_forward(c, layer, L, n, X, yd, bias, ovr, dev_io, dump, flags & INZG_GEMM_SIMT,
                                    profile ? c->ev : nullptr, st);
     } else {
         inzg_ctx::GraphKey key{layer, n, X, yd, bias, ovr, flags & (INZG_IO_DEVICE | INZG_DUMP_ROUTE | INZG_GEMM_SIMT)};
@@ -566,7 +667,7 @@ inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, fl
             cudaStream_t cs = c->capture_stream;
             e = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
             if (e != cudaSuccess) return cuda_fail(c, e, "moe_forward: begin capture");
-            const int nl = enqueue_forward(c, L, n, X, yd, bias, ovr, dev_io, dump, flags & INZG_GEMM_SIMT, nullptr, cs);
+            const int nl = enqueue_forward(c, layer, L, n, X, yd, bias, ovr, dev_io, dump, flags & INZG_GEMM_SIMT, nullptr, cs);
             cudaGraph_t graph = nullptr;
             e = cudaStreamEndCapture(cs, &graph);
             if (e != cudaSuccess || nl < 0) {
@@ -713,6 +814,23 @@ inzg_status inzg_combine(inzg_ctx *c, int n, const float *slots_dev, float *y_de
     launch_combine(slots_dev, n, cf.hidden, cf.topk, y_dev, c->num_sms, st);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? INZG_OK : cuda_fail(c, e, "combine: kernel launch");
+}
+
+inzg_status inzg_shared_expert(inzg_ctx *c, int layer, int n, const float *x_dev, float *y_dev, int n_batch,
+                               void *stream) {
+    if (!c) return INZG_BAD_ARG;
+    const inzg_config &cf = c->cfg;
+    if (layer < 0 || layer >= cf.n_layers) return fail(c, INZG_BAD_ARG, "shared_expert: bad layer");
+    if (n <= 0 || n > cf.max_tokens || n_batch < n || !x_dev || !y_dev)
+        return fail(c, INZG_BAD_ARG, "shared_expert: bad n, n_batch or pointer");
+    if ((reinterpret_cast<uintptr_t>(x_dev) | reinterpret_cast<uintptr_t>(y_dev)) & 15)
+        return fail(c, INZG_BAD_ARG, "shared_expert: pointers must be 16-byte aligned");
+    if (!c->shared[layer].has_experts) return fail(c, INZG_NOT_READY, "shared_expert: layer has no shared expert");
+    cudaSetDevice(cf.device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    enqueue_shared(c, layer, n, x_dev, y_dev, n_batch, false, st);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? INZG_OK : cuda_fail(c, e, "shared_expert: kernel launch");
 }
 
 inzg_status inzg_device_status(inzg_ctx *c, void *stream) {

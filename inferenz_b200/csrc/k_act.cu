@@ -322,6 +322,41 @@ __global__ void __launch_bounds__(NB * 32) swiglu_quant_warp_kernel(const float 
     if (lane == 0 && (w & 1) == 0) s256[(size_t)pos * NKB + kb] = sc;
 }
 
+// Shared-expert gate and add (src/model_fwd.c:1141-1148), one block per token:
+//   sg = sigmoidf(dot_f32(sh_gate, x)) -- dot_f32 (src/model_fwd.c:24-34) keeps two 8-lane fma accumulators over
+//   16-element blocks (s0: elements 16i + l, s1: 16i + 8 + l), adds them lane-wise and reduces with hsum8;
+//   sigmoidf = 1 / (1 + expf(-x)), exp in double rounded once (as SiLU's) --
+// then y = fma(sg, D, y) per element (the reference build contracts `y += sg * D` into one fma).
+// Also carries the shared unit's device error word into the call's.
+__global__ void __launch_bounds__(256) shared_add_kernel(const float *__restrict__ X, const float *__restrict__ gate,
+                                                         const float *__restrict__ D, float *__restrict__ y, int H,
+                                                         const int32_t *__restrict__ sh_meta, int32_t *__restrict__ meta) {
+    __shared__ float sg_s;
+    const int t = blockIdx.x, tid = threadIdx.x;
+    const float *x = X + (size_t)t * H;
+    if (tid < 32) {
+        // lanes 0-7: s0 lane l; lanes 8-15: s1 lane l (element 16i + 8 + l); each a chain over the 16-blocks in order
+        float a = 0.0f;
+        if (tid < 16)
+            for (int i = 0; i + 16 <= H; i += 16) a = __fmaf_rn(gate[i + tid], x[i + tid], a);
+        const float v = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 8));  // s0 + s1, lane-wise (lanes 0-7)
+        const float s = hsum8_lanes(v);                                     // valid in lanes 0-7
+        if (tid == 0) sg_s = __fdiv_rn(1.0f, __fadd_rn(1.0f, (float)exp(-(double)s)));  // H % 16 == 0: no tail
+    }
+    __syncthreads();
+    const float sg = sg_s;
+    float *yt = y + (size_t)t * H;
+    const float *dt = D + (size_t)t * H;
+    for (int c = tid; c < H; c += blockDim.x) yt[c] = __fmaf_rn(sg, dt[c], yt[c]);
+    if (t == 0 && tid == 0 && sh_meta[kMetaError] != kErrNone) set_error(meta, sh_meta[kMetaError]);
+}
+
+int launch_shared_add(const float *X, const float *gate, const float *D, float *y, int n, int H, const int32_t *sh_meta,
+                      int32_t *meta, cudaStream_t st) {
+    shared_add_kernel<<<n, 256, 0, st>>>(X, gate, D, y, H, sh_meta, meta);
+    return 1;
+}
+
 int launch_act_quant_x(const float *X, int n, int H, int rot, uint32_t seed, int8_t *q64, float2 *sb64, int8_t *q256,
                        float *s256, cudaStream_t st) {
     const float norm = rot > 1 ? 1.0f / sqrtf((float)rot) : 1.0f;

@@ -24,6 +24,10 @@ int launch_act_quant_x(const float *X, int n, int H, int rot, uint32_t seed, int
 int launch_swiglu_quant(const float *GU, int FF, int n_entries, const int32_t *eexp, const int32_t *upath, int rot,
                         uint32_t seed, int8_t *q64, float2 *sb64, int8_t *q256, float *s256, cudaStream_t st);
 int launch_combine(const float *mo, int n, int H, int topk, float *y, int num_sms, cudaStream_t st);
+int launch_shared_add(const float *X, const float *gate, const float *D, float *y, int n, int H, const int32_t *sh_meta,
+                      int32_t *meta, cudaStream_t st);
+int launch_shared_route(const RouteDev &R, int n, int gemm, int gu_items_per_unit, int dn_items_per_unit, int gemm_tn,
+                        int32_t *upath, int32_t *eexp, cudaStream_t st);
 
 void gemv_set_attributes();
 int launch_gemv_decode(const LayerDev &L, int kind, const RouteDev &R, const int8_t *aq, const float2 *asb, float *out,

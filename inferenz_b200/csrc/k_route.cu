@@ -345,6 +345,48 @@ __global__ void __cluster_dims__(kRouteCluster, 1, 1) __launch_bounds__(1024)
     }
 }
 
+// The shared expert as a one-unit dispatch list (src/model_fwd.c:1047-1068): expert 0 of its own pool takes every
+// token t of the call at entry t (output slot t, weight 1: the gate is applied by shared_add_kernel); its numeric path
+// is the lin_mm rule on the whole batch, decode below GEMM_MIN_T tokens (src/model_fwd.c:234).
+__global__ void shared_route_kernel(int n, int gemm, int gu_items_per_unit, int dn_items_per_unit, int gemm_tn,
+                                   RouteDev R, int32_t *__restrict__ upath, int32_t *__restrict__ eexp) {
+    const int tiles = gemm ? (n + gemm_tn - 1) / gemm_tn : 0;
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        R.cnt[0] = n;
+        R.off[0] = 0;
+        R.off[1] = n;
+        R.first[0] = 0;
+        upath[0] = gemm;
+        R.units[0] = 0;
+        if (gemm) R.gemm_units[0] = 0;
+        else R.dec_units[0] = 0;
+        R.meta[kMetaNUnits] = 1;
+        R.meta[kMetaNDec] = !gemm;
+        R.meta[kMetaNGemm] = gemm;
+        R.meta[kMetaDecItemsGU] = gemm ? 0 : gu_items_per_unit;
+        R.meta[kMetaDecItemsDN] = gemm ? 0 : dn_items_per_unit;
+        R.meta[kMetaGemmTilesGU] = tiles;
+        R.meta[kMetaGemmTilesDN] = tiles;
+        R.meta[kMetaError] = kErrNone;
+        R.meta[kMetaWorkGU] = 0;
+        R.meta[kMetaWorkDN] = 0;
+    }
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        R.etok[i] = i;
+        R.eslot[i] = i;
+        R.ew[i] = 1.0f;
+        eexp[i] = 0;
+    }
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < tiles; i += gridDim.x * blockDim.x) R.gemm_tiles[i] = i;
+}
+
+int launch_shared_route(const RouteDev &R, int n, int gemm, int gu_items_per_unit, int dn_items_per_unit, int gemm_tn,
+                        int32_t *upath, int32_t *eexp, cudaStream_t st) {
+    shared_route_kernel<<<(n + 255) / 256, 256, 0, st>>>(n, gemm, gu_items_per_unit, dn_items_per_unit, gemm_tn, R, upath,
+                                                         eexp);
+    return 1;
+}
+
 int launch_route_fused(const RouteDev &R, const float *logits, float *probs, int gu_items_per_unit,
                        int dn_items_per_unit, int gemm_tn, int32_t *upath, int32_t *eexp, cudaStream_t st) {
     if (R.n > kFusedMax || R.E > 1024 || R.n * R.topk > kFusedMax * kMaxTopK) return -1;

@@ -51,12 +51,19 @@ class DeviceBackend:
         self.pool.combine_device(n, slots.data_ptr(), y.data_ptr(), self._st())
         return y
 
+    def shared(self, layer, x, y, n_batch):
+        """y += sigmoid(gate . x) * shared_expert(x) in place (the pool's shared expert of `layer`)."""
+        if x.shape[0]:
+            self.pool.shared_device(layer, x.shape[0], x.data_ptr(), y.data_ptr(), n_batch, self._st())
+        return y
+
 
 class ExpertParallelMoE:
     """The routed MoE layer over ``world`` ranks with ``n_expert / world`` experts each (see the module docstring)."""
 
-    def __init__(self, backend, n_expert, topk, hidden, rank=None, world=None, group=None):
+    def __init__(self, backend, n_expert, topk, hidden, rank=None, world=None, group=None, shared_layers=()):
         self.be = backend
+        self.shared_layers = set(shared_layers)  # layers whose shared expert (replicated) each rank applies
         self.E, self.K, self.H = n_expert, topk, hidden
         self.group = group
         self.rank = dist.get_rank(group) if rank is None else rank
@@ -120,11 +127,13 @@ class ExpertParallelMoE:
         slots = torch.empty((n, K, H), dtype=torch.float32, device=dev)
         slots[tk[:, 0], tk[:, 1]] = res
         self.last = {"sel": sel, "w": w, "m": m, "dispatch_rows": int(x_send.shape[0]), "results": int(res.shape[0])}
+        y = self.be.combine(slots)
+        if layer in self.shared_layers:
+            y = self.be.shared(layer, x, y, n_batch)
         if stats:
             used = sel_recv[present].long()
             self.last["local_units"] = int((torch.bincount(used, minlength=self.e_per) > 0).sum()) if used.numel() else 0
-        return self.be.combine(slots)
-
+        return y
 
     def moe_block_fixed(self, layer, x, bias=None, n_batch=None, capacity=None):
         """The same layer with fixed-size exchanges: every rank sends each rank a block of ``capacity`` token rows
@@ -158,7 +167,10 @@ class ExpertParallelMoE:
         self._a2a(back, out, None, None)                                     # block d: rank d's results for my rows
         idx = (owner.long() * C + torch.arange(n, device=dev)[:, None]) * K + torch.arange(K, device=dev)[None, :]
         slots = back.view(G * C * K, H)[idx.view(-1)].view(n, K, H)
-        return self.be.combine(slots)
+        y = self.be.combine(slots)
+        if layer in self.shared_layers:
+            y = self.be.shared(layer, x, y, nb)
+        return y
 
 
 __all__ = ["DeviceBackend", "ExpertParallelMoE"]

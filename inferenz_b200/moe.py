@@ -69,6 +69,13 @@ class MoePool:
         self._check(lib.inzg_pool_add_layer_range(self._ctx, layer, expert_type, _ptr(b), blob_bytes, e_first, n_local),
                     "pool_add_layer_range")
 
+    def set_shared(self, layer, expert_type, blob, blob_bytes, gate):
+        """The layer's shared expert: blob = gate|up then down (one expert blob's layout), gate [H] float32."""
+        b = np.ascontiguousarray(blob, dtype=np.uint8)
+        g = np.ascontiguousarray(gate, dtype=np.float32)
+        assert g.shape == (self.hidden,) and b.size >= blob_bytes
+        self._check(lib.inzg_set_shared(self._ctx, layer, expert_type, _ptr(b), blob_bytes, _ptr(g)), "set_shared")
+
     # -- expert-parallel building blocks (device pointers as ints; stream-ordered, no synchronisation) --
     def route_device(self, layer, n, x_ptr, sel_ptr, w_ptr, bias_ptr=None, stream=None):
         self._check(lib.inzg_route(self._ctx, layer, n, ctypes.c_void_p(x_ptr), bias_ptr and ctypes.c_void_p(bias_ptr),
@@ -83,6 +90,10 @@ class MoePool:
     def combine_device(self, n, slots_ptr, y_ptr, stream=None):
         self._check(lib.inzg_combine(self._ctx, n, ctypes.c_void_p(slots_ptr), ctypes.c_void_p(y_ptr),
                                      stream and ctypes.c_void_p(stream)), "combine")
+
+    def shared_device(self, layer, n, x_ptr, y_ptr, n_batch, stream=None):
+        self._check(lib.inzg_shared_expert(self._ctx, layer, n, ctypes.c_void_p(x_ptr), ctypes.c_void_p(y_ptr), n_batch,
+                                           stream and ctypes.c_void_p(stream)), "shared_expert")
 
     def device_status(self, stream=None):
         self._check(lib.inzg_device_status(self._ctx, stream and ctypes.c_void_p(stream)), "device_status")

@@ -145,6 +145,7 @@ class Ref:
             ("ref_act_quantize", None, [P, I, I, U32, P, P, P]), ("ref_matmul_decode", None, [P, I, P, P]),
             ("ref_matmul_gemm", None, [P, I, P, P]), ("ref_xq", None, [P, I, I, I, U32, P, P, P]),
             ("ref_moe_routed", I, [P, P, P, U64, I, P, P, P, P, P, P, P, P, P, P]),
+            ("ref_shared", I, [P, P, U64, I, P, I, P, P, P]),
         ]:
             fn = getattr(L, name)
             fn.restype = res
@@ -186,6 +187,19 @@ class Ref:
             d["units"] = d["units"][:nu]
         d["y"] = y
         return d
+
+
+    def shared(self, blob, gu_bytes, typ, gate, xin, y):
+        """y + sigmoid(gate . x) * shared_expert(x), the reference's own shared-expert step; returns (y_new, D)."""
+        n, H = xin.shape
+        yo = np.ascontiguousarray(y, np.float32).copy()
+        D = np.zeros((n, H), np.float32)
+        rc = self.lib.ref_shared(self.ctx, _p(np.ascontiguousarray(blob, np.uint8)), gu_bytes, typ,
+                                 _p(np.ascontiguousarray(gate, np.float32)), n,
+                                 _p(np.ascontiguousarray(xin, np.float32)), _p(yo), _p(D))
+        if rc != 0:
+            raise RuntimeError("reference: shared expert matrices do not match")
+        return yo, D
 
 
 def routing(orc, router, xin, bias=None, override=None, topk=10):

@@ -19,6 +19,9 @@
  *                                        experts resident in RAM and a test-only router bias / logit override
  *                                        between the router and the softmax (no such hook exists in the
  *                                        reference; it is needed for the skewed-routing configurations).
+ *   ref_shared                        -- the shared expert of moe_block (src/model_fwd.c:1041-1069 without the
+ *                                        lookahead, and :1141-1148) around the reference's lin_mm, siluf,
+ *                                        sigmoidf and dot_f32.
  */
 #include "model.h"
 #undef Q_H
@@ -283,4 +286,35 @@ API int ref_moe_routed(void *ctx, const uint16_t *router, const uint8_t *blobs, 
     if (unit_expert_out) for (int i = 0; i < nu; i++) unit_expert_out[i] = units[i].expert;
     if (moe_out_out) memcpy(moe_out_out, e->moe_out, sizeof(float) * (size_t)n * Q_TOPK * Q_H);
     return nu;
+}
+
+/* ---- the shared expert ----
+ * gate|up (lin_mm, :1047-1050), SiLU * up in place (:1064-1067), down (lin_mm, :1068), then per token
+ * y += sigmoid(sh_gate . x) * D (:1141-1148). blob: the gate|up matrix followed by the down matrix at gu_bytes (the
+ * expert-blob layout); gate [H] fp32; y [n][H] is updated in place; D_out [n][H] optional.
+ * Returns 0, or -1 on a matrix that does not match the shared expert's shape. */
+_Static_assert(Q_SHARED_FF == Q_FF, "the harness reuses the expert scratch for the shared expert");
+API int ref_shared(void *ctx, const uint8_t *blob, uint64_t gu_bytes, int type, const float *gate, int n,
+                   const float *xin, float *y, float *D_out) {
+    ref_ctx *c = ctx;
+    inz_engine *e = c->e;
+    if (n <= 0 || n > Q_MAX_T) return -1;
+    lin gu, dn;
+    if (!q_bind_lin(&gu, type, 2 * Q_SHARED_FF, Q_H, blob) || !q_bind_lin(&dn, type, Q_H, Q_SHARED_FF, blob + gu_bytes))
+        return -1;
+    float *GU = e->ex_gu, *D = e->ex_d;
+    lin_mm(e, &gu, xin, Q_H, n, GU, 2 * Q_SHARED_FF);
+    for (int t = 0; t < n; t++) {
+        float *r = GU + (size_t)t * 2 * Q_SHARED_FF;
+        for (int k = 0; k < Q_SHARED_FF; k++) r[k] = siluf(r[k]) * r[Q_SHARED_FF + k];
+    }
+    lin_mm(e, &dn, GU, 2 * Q_SHARED_FF, n, D, Q_H);
+    for (int t = 0; t < n; t++) {
+        const float sg = sigmoidf(dot_f32(gate, xin + (size_t)t * Q_H, Q_H));
+        float *yt = y + (size_t)t * Q_H;
+        const float *dt = D + (size_t)t * Q_H;
+        for (int k = 0; k < Q_H; k++) yt[k] += sg * dt[k];
+    }
+    if (D_out) memcpy(D_out, D, sizeof(float) * (size_t)n * Q_H);
+    return 0;
 }

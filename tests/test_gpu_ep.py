@@ -103,10 +103,13 @@ def _single_rank(port, q):
         bias = synth.normal_bias(E)
         bias[[5, 77]] += 9.0
         blobs, bb = synth.layer_blobs(0, synth.T_Q4L, H, FF, E)
+        sh_blob, sh_bb = synth.layer_blobs_range(777, synth.T_Q8G, H, FF, 0, 1)
+        gate = (np.random.default_rng(5).standard_normal(H) * 0.05).astype(np.float32)
         with MoePool(H, FF, E, K, max_tokens=n, n_layers=1, device=0) as pool:
             pool.set_router(0, synth.router(0, E, H))
             pool.add_layer(0, synth.T_Q4L, blobs, bb)
-            ep = ExpertParallelMoE(DeviceBackend(pool), E, K, H)
+            pool.set_shared(0, synth.T_Q8G, sh_blob, sh_bb, gate)
+            ep = ExpertParallelMoE(DeviceBackend(pool), E, K, H, shared_layers={0})
             y = ep.moe_block(0, torch.from_numpy(x_all).cuda(), bias=torch.from_numpy(bias).cuda()).cpu().numpy()
             y_one = pool.moe_block(0, x_all, bias=bias)
         q.put((y, y_one))
@@ -115,7 +118,8 @@ def _single_rank(port, q):
 
 
 def test_expert_parallel_building_blocks_single_rank():
-    """inzg_route + inzg_moe_experts + inzg_combine on one rank equal inzg_moe_forward bit for bit."""
+    """inzg_route + inzg_moe_experts + inzg_combine + inzg_shared_expert on one rank equal inzg_moe_forward (with the
+    layer's shared expert) bit for bit."""
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
