@@ -6,17 +6,24 @@
 // tensor core accumulates s8 x s8 in s32), and the output is f = fma((float)dot_b, ws_b * xs_b, f) over the blocks
 // in order -- the reference's own float sequence, so a GEMM-path expert output is the reference's bits.
 //
-// Tile: 128 weight rows x 128 tokens of one expert per CTA; K in 128-byte halves (two per 256-block).
+// Work item: 128 weight rows x 128 tokens of one expert; K in 128-byte halves (two per 256-block). Persistent: one CTA
+// per SM walks the items blockIdx.x, blockIdx.x + gridDim.x, ... (row blocks of one token tile are consecutive, so
+// neighbouring SMs share the tile's activations in L2); every role counts stages and accumulators across items, so
+// the next item's loads and MMAs overlap the previous item's epilogue.
 //   warp 0      TMA producer: A (weights, [E*rows][K] int8) and B (tokens, [entries][K] int8) boxes of 128 x 128 bytes,
 //               128-byte swizzle, into a 4-stage ring (no multicast)
-//   warp 1      allocates 256 TMEM columns (two 128-column int32 accumulators), one lane issues 4 MMAs (K = 32) per
-//               half; tcgen05.commit frees the smem stage and, after a block's 8 MMAs, hands the accumulator over
+//   warp 1      allocates 256 TMEM columns once (two 128-column int32 accumulators), one lane issues 4 MMAs (K = 32)
+//               per half; tcgen05.commit frees the smem stage and, after a block's 8 MMAs, hands the accumulator over
 //   warps 2-5   epilogue: thread = weight row = TMEM lane; per block tcgen05.ld of its 128 int32 dots, the per-block
-//               FMA into 128 fp32 registers, then the accumulator is released; at the end the tile is written
+//               FMA into 128 fp32 registers, then the accumulator is released; at the item's end its outputs are
+//               written. (float)dot is 12582912 + dot read as a float minus 12582912 (exact: |dot| <= 256*128*127 <
+//               2^22), two full-rate instructions instead of a quarter-rate conversion.
 // Every mbarrier wait is bounded; on expiry the CTA records an error (INZG_TIMEOUT to the host), drains what it
 // issued, frees its TMEM and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+
+#include <algorithm>
 
 #include "inzg_internal.h"
 #include "k_launch.h"
@@ -29,9 +36,10 @@ constexpr int kStageBytes = (TBM + TBN) * TBK;  // 32 KiB
 
 struct TcShared {
     uint64_t full[TSTAGES], empty[TSTAGES], acc_full[2], acc_empty[2], drain;
+    uint64_t xs_full[2];               // the 128 epilogue threads have written xs[parity]
     uint32_t tmem_base;
-    int abort;
-    float xs[TBN * 8];  // token block scales, [n][block] (K <= 2048: at most 8 blocks)
+    int abort, never;                  // never: drains ignore the abort flag
+    alignas(16) float xs[2][8][TBN];  // token block scales per item parity, [block][token] (K <= 2048: <= 8 blocks)
 };
 
 
@@ -84,19 +92,14 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                                                          float *__restrict__ out, int out_ld, int meta_tiles) {
     extern __shared__ __align__(1024) uint8_t dyn[];
     const int nrb = rows / TBM;
-    const int tile = blockIdx.x / nrb, rb = blockIdx.x % nrb;
-    if (tile >= R.meta[meta_tiles]) return;  // uniform over the CTA: nothing allocated yet
-    const int tv = R.gemm_tiles[tile];
-    const int e = R.gemm_units[tv >> 16], tt = tv & 0xFFFF;
-    const int base = R.off[e], ntok = R.cnt[e];
-    const int t0 = tt * TBN, nt = min(TBN, ntok - t0);
+    const int nitems = R.meta[meta_tiles] * nrb;
+    if ((int)blockIdx.x >= nitems) return;  // uniform over the CTA: nothing allocated yet
     const int nkh = K / TBK, nkb = (K + kKB - 1) / kKB;
     uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dyn) + 1023) & ~uintptr_t(1023));
     TcShared &S = *reinterpret_cast<TcShared *>(ring + TSTAGES * kStageBytes);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     volatile int *abort = &S.abort;
-    __shared__ int never;  // drains ignore the abort flag: what was issued must land before the CTA leaves
-    if (threadIdx.x == 0) never = 0;
+    volatile int *never = &S.never;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < TSTAGES; s++) {
@@ -108,18 +111,15 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
             mbar_init(&S.acc_empty[b], 128);
         }
         mbar_init(&S.drain, 1);
+        mbar_init(&S.xs_full[0], 128);
+        mbar_init(&S.xs_full[1], 128);
         S.abort = 0;
+        S.never = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(&S.tmem_base)));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-    }
-    if (warp >= 2) {  // token scales of the tile's tokens (zero past the expert's tokens)
-        for (int i = threadIdx.x - 64; i < TBN * nkb; i += 128) {
-            const int n = i / nkb, b = i % nkb;
-            S.xs[n * 8 + b] = n < nt ? xs_e[(size_t)(base + t0 + n) * nkb + b] : 0.0f;
-        }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
@@ -128,79 +128,120 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
-        int issued = 0;
         if (lane == 0) {
-            const int arow = e * rows + rb * TBM, brow = base + t0;
-            for (int kh = 0; kh < nkh; kh++) {
-                const int s = kh % TSTAGES;
-                if (kh >= TSTAGES && !mbar_wait(&S.empty[s], ((kh / TSTAGES) - 1) & 1, abort)) {
-                    S.abort = 1;
-                    break;
+            int kg = 0;  // stages issued by this CTA
+            bool ok = true;
+            for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
+                const int tile = item / nrb, rb = item % nrb;
+                const int tv = R.gemm_tiles[tile];
+                const int e = R.gemm_units[tv >> 16];
+                const int arow = e * rows + rb * TBM, brow = R.off[e] + (tv & 0xFFFF) * TBN;
+                for (int kh = 0; kh < nkh; kh++, kg++) {
+                    const int s = kg % TSTAGES;
+                    if (kg >= TSTAGES && !mbar_wait(&S.empty[s], ((kg / TSTAGES) - 1) & 1, abort)) {
+                        S.abort = 1;
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *stage = ring + s * kStageBytes;
+                    mbar_expect_tx(&S.full[s], kStageBytes);
+                    tma_load_2d(stage, &mapA, kh * TBK, arow, &S.full[s]);
+                    tma_load_2d(stage + TBM * TBK, &mapB, kh * TBK, brow, &S.full[s]);
                 }
-                uint8_t *stage = ring + s * kStageBytes;
-                mbar_expect_tx(&S.full[s], kStageBytes);
-                tma_load_2d(stage, &mapA, kh * TBK, arow, &S.full[s]);
-                tma_load_2d(stage + TBM * TBK, &mapB, kh * TBK, brow, &S.full[s]);
-                issued = kh + 1;
             }
-            // drain: every issued copy has landed before the CTA may leave (bounded)
-            for (int kh = max(0, issued - TSTAGES); kh < issued; kh++)
-                mbar_wait(&S.full[kh % TSTAGES], (kh / TSTAGES) & 1, &never);
+            // drain: every issued copy has landed before the CTA may leave (bounded; each slot's latest phase)
+            for (int k = max(0, kg - TSTAGES); k < kg; k++) mbar_wait(&S.full[k % TSTAGES], (k / TSTAGES) & 1, never);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             bool ok = true;
-            for (int kh = 0; kh < nkh && ok; kh++) {
-                const int s = kh % TSTAGES, b = kh / 2, buf = b & 1;
-                const bool first_half = (kh & 1) == 0;
-                if (first_half && b >= 2 && !mbar_wait(&S.acc_empty[buf], ((b / 2) - 1) & 1, abort)) { ok = false; break; }
-                if (!mbar_wait(&S.full[s], (kh / TSTAGES) & 1, abort)) { ok = false; break; }
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint8_t *stage = ring + s * kStageBytes;
-                const uint64_t da = umma_desc(stage), db = umma_desc(stage + TBM * TBK);
-                const uint32_t d = tmem + buf * TBN;
+            int kg = 0, bg = 0;  // stages consumed, blocks accumulated by this CTA
+            for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
+                for (int kh = 0; kh < nkh; kh++, kg++) {
+                    const int s = kg % TSTAGES, buf = bg & 1;
+                    const bool first_half = (kh & 1) == 0;
+                    if (first_half && bg >= 2 && !mbar_wait(&S.acc_empty[buf], ((bg / 2) - 1) & 1, abort)) { ok = false; break; }
+                    if (!mbar_wait(&S.full[s], (kg / TSTAGES) & 1, abort)) { ok = false; break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint8_t *stage = ring + s * kStageBytes;
+                    const uint64_t da = umma_desc(stage), db = umma_desc(stage + TBM * TBK);
+                    const uint32_t d = tmem + buf * TBN;
 #pragma unroll
-                for (int k = 0; k < TBK / 32; k++)  // 4 MMAs of K = 32 bytes; the descriptor start moves 32 B
-                    mma_i8(d, da + (uint64_t)(k * 2), db + (uint64_t)(k * 2), kIdesc, (first_half && k == 0) ? 0u : 1u);
-                mma_commit(&S.empty[s]);                                  // stage reusable once these MMAs finish
-                if (!first_half || kh == nkh - 1) mma_commit(&S.acc_full[buf]);  // block b's dot products are done
+                    for (int k = 0; k < TBK / 32; k++)  // 4 MMAs of K = 32 bytes; the descriptor start moves 32 B
+                        mma_i8(d, da + (uint64_t)(k * 2), db + (uint64_t)(k * 2), kIdesc, (first_half && k == 0) ? 0u : 1u);
+                    mma_commit(&S.empty[s]);  // stage reusable once these MMAs finish
+                    if (!first_half || kh == nkh - 1) {  // block's dot products are done
+                        mma_commit(&S.acc_full[buf]);
+                        bg++;
+                    }
+                }
             }
             if (!ok) S.abort = 1;
             // every MMA issued by this CTA has completed before TMEM and shared memory are released (bounded)
             mma_commit(&S.drain);
-            mbar_wait(&S.drain, 0, &never);
+            mbar_wait(&S.drain, 0, never);
         }
         __syncwarp();
     } else {
         // ---------------- epilogue: thread = weight row ----------------
         const int sub = warp & 3;  // TMEM lanes 32*sub .. 32*sub+31
-        const int r = sub * 32 + lane, row = rb * TBM + r;
-        const float *wsr = wsc + ((size_t)e * rows + row) * nkb;
-        float f[TBN];
-#pragma unroll
-        for (int n = 0; n < TBN; n++) f[n] = 0.0f;
+        const int r = sub * 32 + lane;
+        const int et = threadIdx.x - 64;  // 0..127 among the epilogue threads
         bool ok = true;
-        for (int b = 0; b < nkb && ok; b++) {
-            const int buf = b & 1;
-            if (!mbar_wait(&S.acc_full[buf], (b / 2) & 1, abort)) { ok = false; break; }
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const float wsb = wsr[b];
-#pragma unroll
-            for (int c = 0; c < TBN / 32; c++) {
-                int v[32];
-                tmem_ld32(tmem + ((uint32_t)(sub * 32) << 16) + buf * TBN + c * 32, v);
-#pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    const int n = c * 32 + j;
-                    f[n] = __fmaf_rn((float)v[j], __fmul_rn(wsb, S.xs[n * 8 + b]), f[n]);
-                }
+        int bg = 0, it = 0;
+        for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, it++) {
+            const int tile = item / nrb, rb = item % nrb;
+            const int tv = R.gemm_tiles[tile];
+            const int e = R.gemm_units[tv >> 16];
+            const int base = R.off[e], t0 = (tv & 0xFFFF) * TBN, nt = min(TBN, R.cnt[e] - t0);
+            const int row = rb * TBM + r;
+            float(*xs)[TBN] = S.xs[it & 1];
+            // the item's token scales (zero past the expert's tokens). Buffer it&1 was last read two items ago: a
+            // thread gets here only after every epilogue thread has written item it-1's scales, i.e. left item it-2.
+            for (int i = et; i < TBN * nkb; i += 128) {
+                const int n = i % TBN, b = i / TBN;
+                xs[b][n] = n < nt ? xs_e[(size_t)(base + t0 + n) * nkb + b] : 0.0f;
             }
-            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-            mbar_arrive(&S.acc_empty[buf]);
-        }
-        if (!ok) S.abort = 1;
-        if (ok) {
+            mbar_arrive(&S.xs_full[it & 1]);
+            if (!mbar_wait(&S.xs_full[it & 1], (it >> 1) & 1, abort)) {
+                ok = false;
+                S.abort = 1;
+                break;
+            }
+            const float *wsr = wsc + ((size_t)e * rows + row) * nkb;
+            float f[TBN];
+#pragma unroll
+            for (int n = 0; n < TBN; n++) f[n] = 0.0f;
+            for (int b = 0; b < nkb; b++, bg++) {
+                const int buf = bg & 1;
+                if (!mbar_wait(&S.acc_full[buf], (bg / 2) & 1, abort)) {
+                    ok = false;
+                    S.abort = 1;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const float wsb = __ldg(wsr + b);
+#pragma unroll
+                for (int c = 0; c < TBN / 32; c++) {
+                    int v[32];
+                    tmem_ld32(tmem + ((uint32_t)(sub * 32) << 16) + buf * TBN + c * 32, v);
+#pragma unroll
+                    for (int j4 = 0; j4 < 8; j4++) {
+                        const float4 x4 = *reinterpret_cast<const float4 *>(&xs[b][c * 32 + j4 * 4]);
+                        const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+                        for (int q = 0; q < 4; q++) {
+                            const int n = c * 32 + j4 * 4 + q;
+                            const float dot = __fadd_rn(__int_as_float(v[j4 * 4 + q] + 0x4B400000), -12582912.0f);
+                            f[n] = __fmaf_rn(dot, __fmul_rn(wsb, xv[q]), f[n]);
+                        }
+                    }
+                }
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                mbar_arrive(&S.acc_empty[buf]);
+            }
+            if (!ok) break;
 #pragma unroll
             for (int n = 0; n < TBN; n++) {
                 if (n < nt) {
@@ -210,6 +251,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                 }
             }
         }
+        if (!ok) S.abort = 1;
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
@@ -258,7 +300,12 @@ int launch_gemm_tc(int kind, const void *mapA, const void *mapB, const float *ws
                    const float *xs_e, float *out, int out_ld, int max_tiles, cudaStream_t st) {
     if (rows % TBM || K % TBK || K > 8 * kKB) return -1;
     const int mt = kind == 0 ? kMetaGemmTilesGU : kMetaGemmTilesDN;
-    const int grid = max_tiles * (rows / TBM);
+    static int sms[64] = {0};  // persistent grid: one CTA per SM (at most the items the call can have)
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    const int nsm = dev >= 0 && dev < 64 && sms[dev] > 0 ? sms[dev] : 148;
+    const int grid = std::min(nsm, max_tiles * (rows / TBM));
     const CUtensorMap &a = *reinterpret_cast<const CUtensorMap *>(mapA);
     const CUtensorMap &b = *reinterpret_cast<const CUtensorMap *>(mapB);
     if (kind == 0) gemm_tc_kernel<0><<<grid, 192, gemm_tc_smem(), st>>>(a, b, wsc, rows, K, R, xs_e, out, out_ld, mt);
