@@ -14,10 +14,11 @@
 //               128-byte swizzle, into a 4-stage ring (no multicast)
 //   warp 1      allocates 256 TMEM columns once (two 128-column int32 accumulators), one lane issues 4 MMAs (K = 32)
 //               per half; tcgen05.commit frees the smem stage and, after a block's 8 MMAs, hands the accumulator over
-//   warps 2-5   epilogue: thread = weight row = TMEM lane; per block tcgen05.ld of its 128 int32 dots, the per-block
-//               FMA into 128 fp32 registers, then the accumulator is released; at the item's end its outputs are
-//               written. (float)dot is 12582912 + dot read as a float minus 12582912 (exact: |dot| <= 256*128*127 <
-//               2^22), two full-rate instructions instead of a quarter-rate conversion.
+//   warps 2-9   epilogue: thread = (weight row = TMEM lane, half of the tile's tokens); per block tcgen05.ld of its 64
+//               int32 dots, the per-block FMA into 64 fp32 registers, then the accumulator is released; at the item's
+//               end its outputs are written. (float)dot is dot + the bits of 1.5 * 2^23, read as a float, minus
+//               12582912 (exact: |dot| <= 256*128*127 < 2^22): two full-rate instructions instead of a quarter-rate
+//               conversion.
 // Every mbarrier wait is bounded; on expiry the CTA records an error (INZG_TIMEOUT to the host), drains what it
 // issued, frees its TMEM and returns.
 #include <cuda.h>
@@ -32,14 +33,19 @@
 namespace inzg {
 
 constexpr int TBM = 128, TBN = 128, TBK = 128, TSTAGES = 4;
+constexpr int kEpiWarps = 8, kEpiThreads = kEpiWarps * 32, kHalfN = TBN / 2;  // two epilogue warps per TMEM quadrant
+constexpr int kThreads = 64 + kEpiThreads;
+constexpr int kMagicI = 0x4B400000;  // 1.5 * 2^23 as a float: kMagicI + x reads as 12582912 + x for |x| < 2^22
 constexpr int kStageBytes = (TBM + TBN) * TBK;  // 32 KiB
 
 struct TcShared {
     uint64_t full[TSTAGES], empty[TSTAGES], acc_full[2], acc_empty[2], drain;
-    uint64_t xs_full[2];               // the 128 epilogue threads have written xs[parity]
+    uint64_t xs_full[2];               // every epilogue thread has written the item's xs / oslot / ow [parity]
     uint32_t tmem_base;
     int abort, never;                  // never: drains ignore the abort flag
     alignas(16) float xs[2][8][TBN];  // token block scales per item parity, [block][token] (K <= 2048: <= 8 blocks)
+    int oslot[2][TBN];                 // down matrix: each token's output slot and routing weight, per item parity
+    float ow[2][TBN];
 };
 
 
@@ -85,7 +91,7 @@ constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TBN
 
 // KIND 0: gate|up, out = GU[entry][row]; KIND 1: down, out = moe_out[slot][row] = w * f.
 template <int KIND>
-__global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA,
+__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA,
                                                          const __grid_constant__ CUtensorMap mapB,
                                                          const float *__restrict__ wsc, int rows, int K,
                                                          RouteDev R, const float *__restrict__ xs_e,
@@ -108,11 +114,11 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&S.acc_full[b], 1);
-            mbar_init(&S.acc_empty[b], 128);
+            mbar_init(&S.acc_empty[b], kEpiThreads);
         }
         mbar_init(&S.drain, 1);
-        mbar_init(&S.xs_full[0], 128);
-        mbar_init(&S.xs_full[1], 128);
+        mbar_init(&S.xs_full[0], kEpiThreads);
+        mbar_init(&S.xs_full[1], kEpiThreads);
         S.abort = 0;
         S.never = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -184,24 +190,40 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
         }
         __syncwarp();
     } else {
-        // ---------------- epilogue: thread = weight row ----------------
-        const int sub = warp & 3;  // TMEM lanes 32*sub .. 32*sub+31
-        const int r = sub * 32 + lane;
-        const int et = threadIdx.x - 64;  // 0..127 among the epilogue threads
+        // ---------------- epilogue: thread = (weight row, half of the tile's tokens) ----------------
+        // TMEM lane quadrant = warp % 4 (the lanes a warp may access); warps 2-5 take tokens 0-63, warps 6-9 64-127
+        const int sub = warp & 3, half = (warp - 2) >> 2;
+        const int r = sub * 32 + lane, c0 = half * kHalfN;
+        const int et = threadIdx.x - 64;  // 0..255 among the epilogue threads
         bool ok = true;
         int bg = 0, it = 0;
-        for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, it++) {
-            const int tile = item / nrb, rb = item % nrb;
+        // the next item's metadata is loaded one item ahead
+        auto item_meta = [&](int item, int &e, int &base, int &t0, int &nt, int &rb) {
+            const int tile = item / nrb;
+            rb = item % nrb;
             const int tv = R.gemm_tiles[tile];
-            const int e = R.gemm_units[tv >> 16];
-            const int base = R.off[e], t0 = (tv & 0xFFFF) * TBN, nt = min(TBN, R.cnt[e] - t0);
+            e = R.gemm_units[tv >> 16];
+            base = R.off[e];
+            t0 = (tv & 0xFFFF) * TBN;
+            nt = min(TBN, R.cnt[e] - t0);
+        };
+        int e, base, t0, nt, rb;
+        item_meta(blockIdx.x, e, base, t0, nt, rb);
+        for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, it++) {
+            int ne = 0, nbase = 0, nt0 = 0, nnt = 0, nrb_ = 0;
+            if (item + (int)gridDim.x < nitems) item_meta(item + gridDim.x, ne, nbase, nt0, nnt, nrb_);
             const int row = rb * TBM + r;
             float(*xs)[TBN] = S.xs[it & 1];
-            // the item's token scales (zero past the expert's tokens). Buffer it&1 was last read two items ago: a
-            // thread gets here only after every epilogue thread has written item it-1's scales, i.e. left item it-2.
-            for (int i = et; i < TBN * nkb; i += 128) {
+            // the item's token scales (zero past the expert's tokens) and, for the down matrix, each token's output
+            // slot and weight. Buffer it&1 was last read two items ago: a thread gets here only after every epilogue
+            // thread has written item it-1's, i.e. left item it-2.
+            for (int i = et; i < TBN * nkb; i += kEpiThreads) {
                 const int n = i % TBN, b = i / TBN;
                 xs[b][n] = n < nt ? xs_e[(size_t)(base + t0 + n) * nkb + b] : 0.0f;
+            }
+            if (KIND == 1 && et < TBN) {
+                S.oslot[it & 1][et] = et < nt ? R.eslot[base + t0 + et] : 0;
+                S.ow[it & 1][et] = et < nt ? R.ew[base + t0 + et] : 0.0f;
             }
             mbar_arrive(&S.xs_full[it & 1]);
             if (!mbar_wait(&S.xs_full[it & 1], (it >> 1) & 1, abort)) {
@@ -210,30 +232,30 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                 break;
             }
             const float *wsr = wsc + ((size_t)e * rows + row) * nkb;
-            float f[TBN];
+            float f[kHalfN];
 #pragma unroll
-            for (int n = 0; n < TBN; n++) f[n] = 0.0f;
+            for (int n = 0; n < kHalfN; n++) f[n] = 0.0f;
             for (int b = 0; b < nkb; b++, bg++) {
                 const int buf = bg & 1;
+                const float wsb = __ldg(wsr + b);  // in flight while the block's MMAs finish
                 if (!mbar_wait(&S.acc_full[buf], (bg / 2) & 1, abort)) {
                     ok = false;
                     S.abort = 1;
                     break;
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const float wsb = __ldg(wsr + b);
 #pragma unroll
-                for (int c = 0; c < TBN / 32; c++) {
+                for (int c = 0; c < kHalfN / 32; c++) {
                     int v[32];
-                    tmem_ld32(tmem + ((uint32_t)(sub * 32) << 16) + buf * TBN + c * 32, v);
+                    tmem_ld32(tmem + ((uint32_t)(sub * 32) << 16) + buf * TBN + c0 + c * 32, v);
 #pragma unroll
                     for (int j4 = 0; j4 < 8; j4++) {
-                        const float4 x4 = *reinterpret_cast<const float4 *>(&xs[b][c * 32 + j4 * 4]);
+                        const float4 x4 = *reinterpret_cast<const float4 *>(&xs[b][c0 + c * 32 + j4 * 4]);
                         const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
 #pragma unroll
                         for (int q = 0; q < 4; q++) {
                             const int n = c * 32 + j4 * 4 + q;
-                            const float dot = __fadd_rn(__int_as_float(v[j4 * 4 + q] + 0x4B400000), -12582912.0f);
+                            const float dot = __fadd_rn(__int_as_float(v[j4 * 4 + q] + kMagicI), -12582912.0f);
                             f[n] = __fmaf_rn(dot, __fmul_rn(wsb, xv[q]), f[n]);
                         }
                     }
@@ -243,13 +265,14 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
             }
             if (!ok) break;
 #pragma unroll
-            for (int n = 0; n < TBN; n++) {
-                if (n < nt) {
-                    const int pos = base + t0 + n;
-                    if (KIND == 0) out[(size_t)pos * out_ld + row] = f[n];
-                    else out[(size_t)R.eslot[pos] * out_ld + row] = __fmul_rn(R.ew[pos], f[n]);
+            for (int n = 0; n < kHalfN; n++) {
+                const int tn = c0 + n;
+                if (tn < nt) {
+                    if (KIND == 0) out[(size_t)(base + t0 + tn) * out_ld + row] = f[n];
+                    else out[(size_t)S.oslot[it & 1][tn] * out_ld + row] = __fmul_rn(S.ow[it & 1][tn], f[n]);
                 }
             }
+            e = ne; base = nbase; t0 = nt0; nt = nnt; rb = nrb_;
         }
         if (!ok) S.abort = 1;
     }
@@ -308,8 +331,8 @@ int launch_gemm_tc(int kind, const void *mapA, const void *mapB, const float *ws
     const int grid = std::min(nsm, max_tiles * (rows / TBM));
     const CUtensorMap &a = *reinterpret_cast<const CUtensorMap *>(mapA);
     const CUtensorMap &b = *reinterpret_cast<const CUtensorMap *>(mapB);
-    if (kind == 0) gemm_tc_kernel<0><<<grid, 192, gemm_tc_smem(), st>>>(a, b, wsc, rows, K, R, xs_e, out, out_ld, mt);
-    else gemm_tc_kernel<1><<<grid, 192, gemm_tc_smem(), st>>>(a, b, wsc, rows, K, R, xs_e, out, out_ld, mt);
+    if (kind == 0) gemm_tc_kernel<0><<<grid, kThreads, gemm_tc_smem(), st>>>(a, b, wsc, rows, K, R, xs_e, out, out_ld, mt);
+    else gemm_tc_kernel<1><<<grid, kThreads, gemm_tc_smem(), st>>>(a, b, wsc, rows, K, R, xs_e, out, out_ld, mt);
     return 1;
 }
 
