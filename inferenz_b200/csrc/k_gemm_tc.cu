@@ -15,10 +15,11 @@
 //   warp 1      allocates 256 TMEM columns once (two 128-column int32 accumulators), one lane issues 4 MMAs (K = 32)
 //               per half; tcgen05.commit frees the smem stage and, after a block's 8 MMAs, hands the accumulator over
 //   warps 2-9   epilogue: thread = (weight row = TMEM lane, half of the tile's tokens); per block tcgen05.ld of its 64
-//               int32 dots, the per-block FMA into 64 fp32 registers, then the accumulator is released; at the item's
-//               end its outputs are written. (float)dot is dot + the bits of 1.5 * 2^23, read as a float, minus
-//               12582912 (exact: |dot| <= 256*128*127 < 2^22): two full-rate instructions instead of a quarter-rate
-//               conversion.
+//               int32 dots, the per-block FMA into 64 fp32 registers (packed f32x2 add / mul / fma, two tokens per
+//               instruction), then the accumulator is refilled and released; at the item's end its outputs are
+//               written. Each accumulator starts at the bits of 1.5 * 2^23 (tcgen05.st after every read), so a block's
+//               int32 dot reads as the float 12582912 + dot and one add of -12582912 gives (float)dot exactly
+//               (|dot| <= 256*128*127 < 2^22), in place of a quarter-rate conversion.
 // Every mbarrier wait is bounded; on expiry the CTA records an error (INZG_TIMEOUT to the host), drains what it
 // issued, frees its TMEM and returns.
 #include <cuda.h>
@@ -41,6 +42,7 @@ constexpr int kStageBytes = (TBM + TBN) * TBK;  // 32 KiB
 struct TcShared {
     uint64_t full[TSTAGES], empty[TSTAGES], acc_full[2], acc_empty[2], drain;
     uint64_t xs_full[2];               // every epilogue thread has written the item's xs / oslot / ow [parity]
+    uint64_t xs_empty[2];              // every epilogue thread has finished the item that used buffer [parity]
     uint32_t tmem_base;
     int abort, never;                  // never: drains ignore the abort flag
     alignas(16) float xs[2][8][TBN];  // token block scales per item parity, [block][token] (K <= 2048: <= 8 blocks)
@@ -86,6 +88,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, int (&v)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// 32 consecutive columns of this warp's 32 TMEM lanes set to `c`
+__device__ __forceinline__ void tmem_fill32(uint32_t taddr, int c) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+        "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(c)
+        : "memory");
+}
+
 // instruction descriptor: s32 accumulate, s8 x s8, both K-major, N = TBN, M = TBM
 constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TBN >> 3) << 17) | ((uint32_t)(TBM >> 4) << 24);
 
@@ -119,6 +129,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         mbar_init(&S.drain, 1);
         mbar_init(&S.xs_full[0], kEpiThreads);
         mbar_init(&S.xs_full[1], kEpiThreads);
+        mbar_init(&S.xs_empty[0], kEpiThreads);
+        mbar_init(&S.xs_empty[1], kEpiThreads);
         S.abort = 0;
         S.never = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -131,6 +143,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = S.tmem_base;
+    if (warp >= 2) {  // both accumulators start at the bits of 1.5 * 2^23 (the epilogue's int -> float step)
+        const uint32_t q = tmem + ((uint32_t)((warp & 3) * 32) << 16) + ((warp - 2) >> 2) * kHalfN;
+        for (int b = 0; b < 2; b++)
+            for (int c = 0; c < kHalfN; c += 32) tmem_fill32(q + b * TBN + c, kMagicI);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
@@ -175,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                     const uint32_t d = tmem + buf * TBN;
 #pragma unroll
                     for (int k = 0; k < TBK / 32; k++)  // 4 MMAs of K = 32 bytes; the descriptor start moves 32 B
-                        mma_i8(d, da + (uint64_t)(k * 2), db + (uint64_t)(k * 2), kIdesc, (first_half && k == 0) ? 0u : 1u);
+                        mma_i8(d, da + (uint64_t)(k * 2), db + (uint64_t)(k * 2), kIdesc, 1u);  // onto 1.5 * 2^23
                     mma_commit(&S.empty[s]);  // stage reusable once these MMAs finish
                     if (!first_half || kh == nkh - 1) {  // block's dot products are done
                         mma_commit(&S.acc_full[buf]);
@@ -207,34 +228,63 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
             t0 = (tv & 0xFFFF) * TBN;
             nt = min(TBN, R.cnt[e] - t0);
         };
-        int e, base, t0, nt, rb;
-        item_meta(blockIdx.x, e, base, t0, nt, rb);
-        for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, it++) {
-            int ne = 0, nbase = 0, nt0 = 0, nnt = 0, nrb_ = 0;
-            if (item + (int)gridDim.x < nitems) item_meta(item + gridDim.x, ne, nbase, nt0, nnt, nrb_);
-            const int row = rb * TBM + r;
-            float(*xs)[TBN] = S.xs[it & 1];
-            // the item's token scales (zero past the expert's tokens) and, for the down matrix, each token's output
-            // slot and weight. Buffer it&1 was last read two items ago: a thread gets here only after every epilogue
-            // thread has written item it-1's, i.e. left item it-2.
-            for (int i = et; i < TBN * nkb; i += kEpiThreads) {
-                const int n = i % TBN, b = i / TBN;
-                xs[b][n] = n < nt ? xs_e[(size_t)(base + t0 + n) * nkb + b] : 0.0f;
+        // An item's token scales (zero past the expert's tokens) and, for the down matrix, each token's output slot
+        // and weight are staged in shared memory one item ahead: loaded into registers when the item before it
+        // starts, stored after that item's first block, so the loads overlap its MMAs.
+        constexpr int kPre = 8 * TBN / kEpiThreads;  // scales per thread (nkb <= 8)
+        float pre[kPre];
+        int pslot = 0;
+        float pw = 0.0f;
+        auto load_next = [&](int base_, int t0_, int nt_) {
+#pragma unroll
+            for (int k = 0; k < kPre; k++) {
+                const int i = et + k * kEpiThreads, n = i % TBN, b = i / TBN;
+                pre[k] = (b < nkb && n < nt_) ? __ldg(xs_e + (size_t)(base_ + t0_ + n) * nkb + b) : 0.0f;
             }
             if (KIND == 1 && et < TBN) {
-                S.oslot[it & 1][et] = et < nt ? R.eslot[base + t0 + et] : 0;
-                S.ow[it & 1][et] = et < nt ? R.ew[base + t0 + et] : 0.0f;
+                pslot = et < nt_ ? R.eslot[base_ + t0_ + et] : 0;
+                pw = et < nt_ ? R.ew[base_ + t0_ + et] : 0.0f;
             }
-            mbar_arrive(&S.xs_full[it & 1]);
+        };
+        // item j's data into buffer j&1, once every epilogue thread has finished item j-2 (its last reader)
+        auto store_next = [&](int j) -> bool {
+            const int pb = j & 1;
+            if (j >= 2 && !mbar_wait(&S.xs_empty[pb], ((j - 2) >> 1) & 1, abort)) return false;
+#pragma unroll
+            for (int k = 0; k < kPre; k++) {
+                const int i = et + k * kEpiThreads;
+                if (i / TBN < nkb) S.xs[pb][i / TBN][i % TBN] = pre[k];
+            }
+            if (KIND == 1 && et < TBN) {
+                S.oslot[pb][et] = pslot;
+                S.ow[pb][et] = pw;
+            }
+            mbar_arrive(&S.xs_full[pb]);
+            return true;
+        };
+        int e, base, t0, nt, rb;
+        item_meta(blockIdx.x, e, base, t0, nt, rb);
+        load_next(base, t0, nt);
+        store_next(0);
+        for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, it++) {
+            const bool has_next = item + (int)gridDim.x < nitems;
+            int ne = 0, nbase = 0, nt0 = 0, nnt = 0, nrb_ = 0;
+            if (has_next) item_meta(item + gridDim.x, ne, nbase, nt0, nnt, nrb_);
+            const int row = rb * TBM + r;
+            float(*xs)[TBN] = S.xs[it & 1];
             if (!mbar_wait(&S.xs_full[it & 1], (it >> 1) & 1, abort)) {
                 ok = false;
                 S.abort = 1;
                 break;
             }
+            if (has_next) load_next(nbase, nt0, nnt);
             const float *wsr = wsc + ((size_t)e * rows + row) * nkb;
-            float f[kHalfN];
+            // f[j] holds tokens c0 + 2j, c0 + 2j + 1: the packed f32x2 instructions round each lane like their scalar
+            // forms, so f is the scalar sequence's bits. 32-token chunks past the tile's last token are not read.
+            float2 f[kHalfN / 2];
 #pragma unroll
-            for (int n = 0; n < kHalfN; n++) f[n] = 0.0f;
+            for (int j = 0; j < kHalfN / 2; j++) f[j] = make_float2(0.0f, 0.0f);
+            const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
             for (int b = 0; b < nkb; b++, bg++) {
                 const int buf = bg & 1;
                 const float wsb = __ldg(wsr + b);  // in flight while the block's MMAs finish
@@ -244,34 +294,49 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                     break;
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const float2 ws2 = make_float2(wsb, wsb);
 #pragma unroll
                 for (int c = 0; c < kHalfN / 32; c++) {
-                    int v[32];
-                    tmem_ld32(tmem + ((uint32_t)(sub * 32) << 16) + buf * TBN + c0 + c * 32, v);
+                    const uint32_t ta = tmem + ((uint32_t)(sub * 32) << 16) + buf * TBN + c0 + c * 32;
+                    if (c0 + c * 32 < nt) {
+                        int v[32];
+                        tmem_ld32(ta, v);
 #pragma unroll
-                    for (int j4 = 0; j4 < 8; j4++) {
-                        const float4 x4 = *reinterpret_cast<const float4 *>(&xs[b][c0 + c * 32 + j4 * 4]);
-                        const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
-#pragma unroll
-                        for (int q = 0; q < 4; q++) {
-                            const int n = c * 32 + j4 * 4 + q;
-                            const float dot = __fadd_rn(__int_as_float(v[j4 * 4 + q] + kMagicI), -12582912.0f);
-                            f[n] = __fmaf_rn(dot, __fmul_rn(wsb, xv[q]), f[n]);
+                        for (int j4 = 0; j4 < 8; j4++) {
+                            const float4 x4 = *reinterpret_cast<const float4 *>(&xs[b][c0 + c * 32 + j4 * 4]);
+                            const float2 p01 = __fmul2_rn(ws2, make_float2(x4.x, x4.y));
+                            const float2 p23 = __fmul2_rn(ws2, make_float2(x4.z, x4.w));
+                            const float2 d01 = __fadd2_rn(
+                                make_float2(__int_as_float(v[j4 * 4]), __int_as_float(v[j4 * 4 + 1])), neg_magic);
+                            const float2 d23 = __fadd2_rn(
+                                make_float2(__int_as_float(v[j4 * 4 + 2]), __int_as_float(v[j4 * 4 + 3])), neg_magic);
+                            const int j = c * 16 + j4 * 2;
+                            f[j] = __ffma2_rn(d01, p01, f[j]);
+                            f[j + 1] = __ffma2_rn(d23, p23, f[j + 1]);
                         }
                     }
+                    tmem_fill32(ta, kMagicI);  // the next block in this buffer accumulates onto 1.5 * 2^23 again
                 }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 mbar_arrive(&S.acc_empty[buf]);
+                if (b == 0 && has_next && !store_next(it + 1)) {
+                    ok = false;
+                    S.abort = 1;
+                    break;
+                }
             }
             if (!ok) break;
 #pragma unroll
-            for (int n = 0; n < kHalfN; n++) {
-                const int tn = c0 + n;
+            for (int j = 0; j < kHalfN; j++) {
+                const int tn = c0 + j;
+                const float fj = (j & 1) ? f[j >> 1].y : f[j >> 1].x;
                 if (tn < nt) {
-                    if (KIND == 0) out[(size_t)(base + t0 + tn) * out_ld + row] = f[n];
-                    else out[(size_t)S.oslot[it & 1][tn] * out_ld + row] = __fmul_rn(S.ow[it & 1][tn], f[n]);
+                    if (KIND == 0) out[(size_t)(base + t0 + tn) * out_ld + row] = fj;
+                    else out[(size_t)S.oslot[it & 1][tn] * out_ld + row] = __fmul_rn(S.ow[it & 1][tn], fj);
                 }
             }
+            mbar_arrive(&S.xs_empty[it & 1]);  // this thread has finished reading buffer it&1
             e = ne; base = nbase; t0 = nt0; nt = nnt; rb = nrb_;
         }
         if (!ok) S.abort = 1;
