@@ -44,6 +44,7 @@ struct LayerSlot {
     bool has_maps = false;
     TmaMap map_gu, map_dn;      // TMA maps over the prefill-path int8 weights
     uint4 *router = nullptr;
+    float *router32 = nullptr;  // the same router in fp32, laid out for the many-token kernel (nullptr: not used)
     uint8_t *pool = nullptr;
     uint8_t *luts = nullptr;
     uint8_t *gemm_w = nullptr;  // one allocation: w8_gu | w8_dn | ws_gu | ws_dn
@@ -95,6 +96,7 @@ struct inzg_ctx {
     int32_t *cnt = nullptr, *off = nullptr, *first = nullptr, *etok = nullptr, *eslot = nullptr, *ccnt = nullptr;
     int32_t *units = nullptr, *meta = nullptr, *dec_units = nullptr, *gemm_units = nullptr, *gemm_tiles = nullptr;
     int32_t *upath = nullptr, *eexp = nullptr;
+    uint64_t *cmask = nullptr;
     float *ew = nullptr, *GU = nullptr, *mo = nullptr;
     int8_t *dq64 = nullptr, *dq256 = nullptr;
     float2 *dsb64 = nullptr;
@@ -180,7 +182,8 @@ static void free_scratch(inzg_ctx *c) {
                     c->xs256, c->cnt, c->off, c->first, c->etok, c->eslot, c->ccnt, c->units, c->meta, c->dec_units,
                     c->gemm_units, c->gemm_tiles, c->upath, c->eexp, c->ew, c->GU, c->mo, c->dq64, c->dq256, c->dsb64,
                     c->ds256, c->xqe, c->xse, c->sh_cnt, c->sh_off, c->sh_first, c->sh_etok, c->sh_eslot,
-                    c->sh_eexp, c->sh_upath, c->sh_units, c->sh_dec, c->sh_gemm, c->sh_tiles, c->sh_meta, c->sh_ew};
+                    c->sh_eexp, c->sh_upath, c->sh_units, c->sh_dec, c->sh_gemm, c->sh_tiles, c->sh_meta, c->sh_ew,
+                    c->cmask};
     for (void *p : ptrs)
         if (p) cudaFree(p);
 }
@@ -217,7 +220,7 @@ inzg_ctx *inzg_create(const inzg_config *cfg, inzg_status *status) {
     }
     const size_t T = cfg->max_tokens, H = cfg->hidden, E = cfg->n_expert, K = cfg->topk, FF = cfg->ff;
     const size_t NE = T * K, nkbH = (H + kKB - 1) / kKB, nkbF = (FF + kKB - 1) / kKB;
-    const size_t nchunk = (T + 31) / 32;
+    const size_t nchunk = (size_t)route_chunks((int)T);
     bool ok = true;
     c->xin = dalloc<float>(T * H, ok);
     c->y = dalloc<float>(T * H, ok);
@@ -238,6 +241,7 @@ inzg_ctx *inzg_create(const inzg_config *cfg, inzg_status *status) {
     c->eexp = dalloc<int32_t>(NE, ok);
     c->ew = dalloc<float>(NE, ok);
     c->ccnt = dalloc<int32_t>(nchunk * E, ok);
+    c->cmask = dalloc<uint64_t>(nchunk * E, ok);
     c->units = dalloc<int32_t>(E, ok);
     c->meta = dalloc<int32_t>(16, ok);
     c->dec_units = dalloc<int32_t>(E, ok);
@@ -293,6 +297,7 @@ void inzg_destroy(inzg_ctx *c) {
     for (auto *v : {&c->layers, &c->shared})
         for (auto &L : *v) {
             if (L.router) cudaFree(L.router);
+            if (L.router32) cudaFree(L.router32);
             if (L.pool) cudaFree(L.pool);
             if (L.luts) cudaFree(L.luts);
             if (L.gemm_w) cudaFree(L.gemm_w);
@@ -327,9 +332,14 @@ inzg_status inzg_set_router(inzg_ctx *c, int layer, const uint16_t *w, int rows,
         cudaFree(tmp);
         return fail(c, INZG_OOM, "set_router: router buffer");
     }
+    if (router_gemm_fits(rows, cols) && !L.router32 && cudaMalloc(&L.router32, bytes * 2) != cudaSuccess) {
+        cudaFree(tmp);
+        return fail(c, INZG_OOM, "set_router: router buffer");
+    }
     e = cudaMemcpyAsync(tmp, w, bytes, cudaMemcpyHostToDevice, c->stream);
     if (e == cudaSuccess) {
         launch_router_repack(tmp, L.router, rows, cols, c->stream);
+        if (L.router32) launch_router_repack32(tmp, L.router32, rows, cols, c->stream);
         e = cudaStreamSynchronize(c->stream);
     }
     cudaFree(tmp);
@@ -551,13 +561,13 @@ static int enqueue_forward(inzg_ctx *c, int layer, const LayerSlot &L, int n, co
         if (ovr_on_device)
             cudaMemcpyAsync(c->logits, ovr, sizeof(float) * (size_t)n * E, cudaMemcpyDeviceToDevice, st);
     } else {
-        launches += launch_router_logits(L.router, X, n, H, E, bias, c->logits, c->meta, st);
+        launches += launch_router_logits(L.router, L.router32, X, n, H, E, bias, c->logits, c->meta, st);
     }
     mark(1);
     RouteDev R{};
     R.n = n; R.topk = K; R.E = E; R.n_rule = n; R.absent_ok = 0;
     R.sel = c->sel; R.w = c->w; R.cnt = c->cnt; R.off = c->off; R.first = c->first; R.etok = c->etok; R.eslot = c->eslot;
-    R.ew = c->ew; R.ccnt = c->ccnt; R.units = c->units; R.meta = c->meta; R.dec_units = c->dec_units;
+    R.ew = c->ew; R.ccnt = c->ccnt; R.cmask = c->cmask; R.units = c->units; R.meta = c->meta; R.dec_units = c->dec_units;
     R.gemm_units = c->gemm_units; R.gemm_tiles = c->gemm_tiles;
     const bool tc = !simt_gemm && c->have_tc && L.has_maps;
     const int fused = launch_route_fused(R, c->logits, dump ? c->probs : nullptr, gemv_items_per_unit(D, 0), gemv_items_per_unit(D, 1),
@@ -573,8 +583,7 @@ static int enqueue_forward(inzg_ctx *c, int layer, const LayerSlot &L, int n, co
         launches += launch_act_quant_x(X, n, H, D.gu_rot, D.gu_seed, c->xq64, c->xsb64, any_gemm ? c->xq256 : nullptr,
                                        c->xs256, st);
     mark(3);
-    const int nchunk = (n + 31) / 32;
-    if (fused <= 0) launches += launch_route(R, nchunk, gemv_items_per_unit(D, 0), gemv_items_per_unit(D, 1), gemm_token_tile(), c->upath, c->eexp, st);
+    if (fused <= 0) launches += launch_route(R, gemv_items_per_unit(D, 0), gemv_items_per_unit(D, 1), gemm_token_tile(), c->upath, c->eexp, st);
     const int nkbH = (H + kKB - 1) / kKB;
     const int max_tiles = (NE + gemm_token_tile() - 1) / gemm_token_tile() + std::min(E, NE / kGemmMinT) + 1;
     if (branch) cudaStreamWaitEvent(st, c->join, 0);
@@ -746,7 +755,8 @@ inzg_status inzg_route(inzg_ctx *c, int layer, int n, const float *x_dev, const 
     if (!L.has_router) return fail(c, INZG_NOT_READY, "route: layer has no router");
     cudaSetDevice(cf.device);
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
-    launch_router_logits(L.router, x_dev, n, cf.hidden, cf.n_expert, logit_bias_dev, c->logits, c->meta, st);
+    launch_router_logits(L.router, L.router32, x_dev, n, cf.hidden, cf.n_expert, logit_bias_dev, c->logits, c->meta,
+                         st);
     launch_softmax_topk(c->logits, n, cf.n_expert, cf.topk, sel_dev, w_dev, nullptr, st);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? INZG_OK : cuda_fail(c, e, "route: kernel launch");
@@ -776,9 +786,9 @@ inzg_status inzg_moe_experts(inzg_ctx *c, int layer, int m, const float *x_dev, 
     R.n = m; R.topk = K; R.E = E; R.n_rule = n_batch; R.absent_ok = 1;
     R.sel = const_cast<int32_t *>(sel_dev); R.w = const_cast<float *>(w_dev);
     R.cnt = c->cnt; R.off = c->off; R.first = c->first; R.etok = c->etok; R.eslot = c->eslot;
-    R.ew = c->ew; R.ccnt = c->ccnt; R.units = c->units; R.meta = c->meta; R.dec_units = c->dec_units;
+    R.ew = c->ew; R.ccnt = c->ccnt; R.cmask = c->cmask; R.units = c->units; R.meta = c->meta; R.dec_units = c->dec_units;
     R.gemm_units = c->gemm_units; R.gemm_tiles = c->gemm_tiles;
-    launch_route(R, (m + 31) / 32, gemv_items_per_unit(D, 0), gemv_items_per_unit(D, 1), gemm_token_tile(), c->upath,
+    launch_route(R, gemv_items_per_unit(D, 0), gemv_items_per_unit(D, 1), gemm_token_tile(), c->upath,
                  c->eexp, st);
     const bool tc = c->have_tc && L.has_maps;
     const int nkbH = (H + kKB - 1) / kKB;

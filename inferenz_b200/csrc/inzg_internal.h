@@ -62,7 +62,8 @@ struct RouteDev {
     int32_t *etok;       // [n*topk] token of each entry
     int32_t *eslot;      // [n*topk] slot t*topk+k of each entry
     float *ew;           // [n*topk] weight of each entry
-    int32_t *ccnt;       // [nchunk][E] per-32-token-chunk counts, then their exclusive prefix per expert
+    int32_t *ccnt;       // [nchunk][E] per-64-token-chunk counts, then their exclusive prefix per expert
+    uint64_t *cmask;     // [nchunk][E] per-chunk token masks: bit t % 64 set when token t chose the expert
     int32_t *units;      // [E] experts with cnt > 0, ascending
     int32_t *meta;       // [16] counters: 0 nunits, 1 n_dec_units, 2 n_gemm_units, 3 n_dec_items_gu, 4 n_dec_items_dn,
                          //      5 n_gemm_tiles_gu, 6 n_gemm_tiles_dn, 7 device error code, 8/9 decode GEMV work

@@ -8,16 +8,20 @@ namespace inzg {
 
 void router_set_attributes(int H);
 void launch_router_repack(const uint16_t *W, uint4 *Wr, int E, int H, cudaStream_t st);
-int launch_router_logits(const uint4 *Wr, const float *X, int n, int H, int E, const float *bias, float *logits,
-                         int32_t *meta, cudaStream_t st);
+void launch_router_repack32(const uint16_t *W, float *Wf, int E, int H, cudaStream_t st);
+bool router_gemm_fits(int E, int H);
+// Wf: the fp32 copy (nullptr: the f16 kernels only)
+int launch_router_logits(const uint4 *Wr, const float *Wf, const float *X, int n, int H, int E, const float *bias,
+                         float *logits, int32_t *meta, cudaStream_t st);
 int launch_softmax_topk(const float *logits, int n, int E, int topk, int32_t *sel, float *w, float *probs,
                         cudaStream_t st);
 
 int launch_route_fused(const RouteDev &R, const float *logits, float *probs, int gu_items_per_unit,
                        int dn_items_per_unit, int gemm_tn, int32_t *upath, int32_t *eexp, cudaStream_t st);
 void route_set_attributes(int E);
-int launch_route(const RouteDev &R, int nchunk, int gu_items_per_unit, int dn_items_per_unit, int gemm_tn,
+int launch_route(const RouteDev &R, int gu_items_per_unit, int dn_items_per_unit, int gemm_tn,
                  int32_t *upath, int32_t *eexp, cudaStream_t st);
+int route_chunks(int n);  // chunks of the large-n route (64 tokens each): rows of RouteDev::ccnt / cmask
 
 int launch_act_quant_x(const float *X, int n, int H, int rot, uint32_t seed, int8_t *q64, float2 *sb64, int8_t *q256,
                        float *s256, cudaStream_t st);

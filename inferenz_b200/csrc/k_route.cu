@@ -3,12 +3,12 @@
 // The reference builds, per token in order, "units" = per-expert lists of (token, slot = t*topk + k, weight)
 // (src/model_fwd.c:1001-1031). The lists here hold the same entries, sorted by expert and, within an expert, by
 // token -- the order the reference appends them -- without atomics on positions, so the result is deterministic:
-//   route_count   per 32-token chunk (one warp): chunk-local rank of every (t, k) among the chunk's tokens that chose
-//                 the same expert, per-chunk counts, first-touch key per expert
-//   route_scan    one block: per-expert prefix over chunks, counts, offsets, expert lists and the per-expert numeric
-//                 path (decode numerics when n <= 8 or the expert has < GEMM_MIN_T tokens, src/model_fwd.c:229-249,
-//                 1070), work counts for the expert kernels
-//   route_scatter per chunk: entry position = off[e] + chunk prefix + rank
+//   route_mask    per 64-token chunk (one block): a 64-bit token mask per expert (shared-memory atomicOr), the
+//                 chunk's count per expert = the mask's popcount
+//   route_scan    one block: per-expert prefix over chunks, counts, offsets, first-touch keys, expert lists and the
+//                 per-expert numeric path (decode numerics when n <= 8 or the expert has < GEMM_MIN_T tokens,
+//                 src/model_fwd.c:229-249, 1070), work counts for the expert kernels
+//   route_scatter per chunk: entry position = off[e] + chunk prefix + popcount of the expert's mask below the token
 // The decode-path expert list is the one list in scheduling order: heaviest experts (most tokens) first, so the
 // decode GEMV's work queue ends on light items. Every output position is fixed by the entry lists, so that order
 // (which is not deterministic within one token count) never changes a result.
@@ -22,7 +22,7 @@ namespace cg = cooperative_groups;
 
 namespace inzg {
 
-constexpr int kChunk = 32;
+constexpr int kChunk = 64;  // tokens per route chunk: one 64-bit mask word per expert
 
 // Decode experts in descending token count (bins by count, positions inside a bin by shared atomics); every thread
 // of the block calls it. bins: 32 ints of shared scratch. Also clears the decode GEMV work-queue counters.
@@ -47,32 +47,27 @@ __device__ void order_dec_units(int is_dec, int c, int e, int32_t *__restrict__ 
     if (is_dec) dec_units[atomicAdd(&bins[16 + b], 1)] = e;
 }
 
-// rank of (lane's token, k) among the earlier tokens of the chunk that selected the same expert
-__device__ __forceinline__ int chunk_rank(const int32_t (*s)[kMaxTopK], int topk, int t, int e) {
-    int r = 0;
-    for (int u = 0; u < t; u++)
-        for (int k = 0; k < topk; k++) r += s[u][k] == e;
-    return r;
-}
-
-__global__ void __launch_bounds__(128) route_count_kernel(const int32_t *__restrict__ sel, int n, int topk, int E,
-                                                          int absent_ok, int32_t *__restrict__ ccnt,
-                                                          int32_t *__restrict__ first, int32_t *__restrict__ meta) {
-    __shared__ int32_t s[4][kChunk][kMaxTopK];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int chunk = blockIdx.x * 4 + warp;
-    const int t = chunk * kChunk + lane;
-    const bool valid = t < n;
-    for (int k = 0; k < topk; k++) s[warp][lane][k] = valid ? sel[(size_t)t * topk + k] : -1;
-    __syncwarp();
-    if (chunk * kChunk >= n) return;
-    if (!valid) return;
-    for (int k = 0; k < topk; k++) {
-        const int e = s[warp][lane][k];
+// Chunk masks: bit (t % 64) of cmask[chunk][e] is set when token t chose expert e. A token that names one expert
+// twice is an error (a top-k row holds distinct experts).
+__global__ void __launch_bounds__(256) route_mask_kernel(const int32_t *__restrict__ sel, int n, int topk, int E,
+                                                         int absent_ok, int32_t *__restrict__ ccnt,
+                                                         uint64_t *__restrict__ cmask, int32_t *__restrict__ meta) {
+    __shared__ unsigned long long m[1024];
+    const int chunk = blockIdx.x, t0 = chunk * kChunk;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) m[e] = 0ull;
+    __syncthreads();
+    const int nt = min(kChunk, n - t0);
+    for (int i = threadIdx.x; i < nt * topk; i += blockDim.x) {
+        const int e = sel[(size_t)t0 * topk + i];
         if (e < 0 && absent_ok) continue;
         if (e < 0 || e >= E) { set_error(meta, kErrBadExpert); continue; }
-        atomicAdd(&ccnt[(size_t)chunk * E + e], 1);
-        atomicMin(&first[e], t * topk + k);
+        const unsigned long long bit = 1ull << (i / topk);
+        if (atomicOr(&m[e], bit) & bit) set_error(meta, kErrBadExpert);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        cmask[(size_t)chunk * E + e] = m[e];
+        ccnt[(size_t)chunk * E + e] = __popcll(m[e]);
     }
 }
 
@@ -80,6 +75,9 @@ __global__ void __launch_bounds__(128) route_count_kernel(const int32_t *__restr
 __global__ void __launch_bounds__(1024) route_scan_kernel(int n, int n_rule, int absent_ok, int topk, int E, int nchunk,
                                                           int gu_items_per_unit,
                                                           int dn_items_per_unit, int gemm_tn,
+                                                          const int32_t *__restrict__ sel,
+                                                          const uint64_t *__restrict__ cmask,
+                                                          int32_t *__restrict__ first,
                                                           int32_t *__restrict__ ccnt, int32_t *__restrict__ cnt,
                                                           int32_t *__restrict__ off, int32_t *__restrict__ units,
                                                           int32_t *__restrict__ dec_units, int32_t *__restrict__ gemm_units,
@@ -87,13 +85,28 @@ __global__ void __launch_bounds__(1024) route_scan_kernel(int n, int n_rule, int
                                                           int32_t *__restrict__ meta) {
     __shared__ int32_t sc[1024], su[1024], sd[1024], sg[1024], st[1024], bins[32];
     const int e = threadIdx.x;
-    int run = 0;
+    int run = 0, fc = -1;  // fc: first chunk in which the expert was chosen
     if (e < E)
-        for (int c = 0; c < nchunk; c++) {
-            const int v = ccnt[(size_t)c * E + e];
-            ccnt[(size_t)c * E + e] = run;
-            run += v;
+        for (int c0 = 0; c0 < nchunk; c0 += 16) {  // 16 independent loads in flight, then the running prefix
+            int v[16];
+#pragma unroll
+            for (int j = 0; j < 16; j++) v[j] = c0 + j < nchunk ? ccnt[(size_t)(c0 + j) * E + e] : 0;
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                if (c0 + j < nchunk) ccnt[(size_t)(c0 + j) * E + e] = run;
+                if (fc < 0 && v[j] > 0) fc = c0 + j;
+                run += v[j];
+            }
         }
+    if (e < E) {  // first-touch key: the first token's slot t*topk+k
+        int key = 0x7F7F7F7F;
+        if (fc >= 0) {
+            const int t = fc * kChunk + __ffsll((long long)cmask[(size_t)fc * E + e]) - 1;
+            for (int k = 0; k < topk; k++)
+                if (sel[(size_t)t * topk + k] == e) { key = t * topk + k; break; }
+        }
+        first[e] = key;
+    }
     const int c = e < E ? run : 0;
     const int is_unit = c > 0;
     const int is_dec = is_unit && (n_rule <= 8 || c < kGemmMinT);
@@ -137,26 +150,23 @@ __global__ void __launch_bounds__(1024) route_scan_kernel(int n, int n_rule, int
     }
 }
 
-__global__ void __launch_bounds__(128) route_scatter_kernel(const int32_t *__restrict__ sel, const float *__restrict__ w,
+__global__ void __launch_bounds__(256) route_scatter_kernel(const int32_t *__restrict__ sel, const float *__restrict__ w,
                                                             int n, int topk, int E, const int32_t *__restrict__ ccnt,
+                                                            const uint64_t *__restrict__ cmask,
                                                             const int32_t *__restrict__ off, int32_t *__restrict__ etok,
                                                             int32_t *__restrict__ eslot, float *__restrict__ ew,
                                                             int32_t *__restrict__ eexp) {
-    __shared__ int32_t s[4][kChunk][kMaxTopK];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int chunk = blockIdx.x * 4 + warp;
-    const int t = chunk * kChunk + lane;
-    const bool valid = t < n;
-    for (int k = 0; k < topk; k++) s[warp][lane][k] = valid ? sel[(size_t)t * topk + k] : -1;
-    __syncwarp();
-    if (!valid) return;
-    for (int k = 0; k < topk; k++) {
-        const int e = s[warp][lane][k];
+    const int chunk = blockIdx.x, t0 = chunk * kChunk;
+    const int nt = min(kChunk, n - t0);
+    for (int i = threadIdx.x; i < nt * topk; i += blockDim.x) {
+        const int slot = t0 * topk + i, e = sel[slot];
         if (e < 0 || e >= E) continue;
-        const int pos = off[e] + ccnt[(size_t)chunk * E + e] + chunk_rank(s[warp], topk, lane, e);
-        etok[pos] = t;
-        eslot[pos] = t * topk + k;
-        ew[pos] = w[(size_t)t * topk + k];
+        const int tl = i / topk;
+        const uint64_t below = cmask[(size_t)chunk * E + e] & ((1ull << tl) - 1ull);
+        const int pos = off[e] + ccnt[(size_t)chunk * E + e] + __popcll(below);
+        etok[pos] = t0 + tl;
+        eslot[pos] = slot;
+        ew[pos] = w[slot];
         eexp[pos] = e;
     }
 }
@@ -400,7 +410,7 @@ void route_set_attributes(int E) {
     cudaFuncSetAttribute(route_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 32 * E * (int)sizeof(float));
 }
 
-int launch_route(const RouteDev &R, int nchunk, int gu_items_per_unit, int dn_items_per_unit, int gemm_tn,
+int launch_route(const RouteDev &R, int gu_items_per_unit, int dn_items_per_unit, int gemm_tn,
                  int32_t *upath, int32_t *eexp, cudaStream_t st) {
     const int n = R.n, topk = R.topk, E = R.E;
     if (n <= kSmallRouteMax) {
@@ -409,16 +419,18 @@ int launch_route(const RouteDev &R, int nchunk, int gu_items_per_unit, int dn_it
                                                   R, upath, eexp);
         return 1;
     }
-    cudaMemsetAsync(R.ccnt, 0, sizeof(int32_t) * (size_t)nchunk * E, st);
-    cudaMemsetAsync(R.first, 0x7F, sizeof(int32_t) * (size_t)E, st);
+    const int nchunk = route_chunks(n);
     cudaMemsetAsync(R.meta, 0, sizeof(int32_t) * kMetaRouterError, st);  // the router's word is folded in by route_scan
-    const int blocks = (nchunk + 3) / 4;
-    route_count_kernel<<<blocks, 128, 0, st>>>(R.sel, n, topk, E, R.absent_ok, R.ccnt, R.first, R.meta);
+    route_mask_kernel<<<nchunk, 256, 0, st>>>(R.sel, n, topk, E, R.absent_ok, R.ccnt, R.cmask, R.meta);
     const int threads = (E + 31) / 32 * 32;
-    route_scan_kernel<<<1, threads, 0, st>>>(n, R.n_rule, R.absent_ok, topk, E, nchunk, gu_items_per_unit, dn_items_per_unit, gemm_tn, R.ccnt,
-                                             R.cnt, R.off, R.units, R.dec_units, R.gemm_units, R.gemm_tiles, upath, R.meta);
-    route_scatter_kernel<<<blocks, 128, 0, st>>>(R.sel, R.w, n, topk, E, R.ccnt, R.off, R.etok, R.eslot, R.ew, eexp);
+    route_scan_kernel<<<1, threads, 0, st>>>(n, R.n_rule, R.absent_ok, topk, E, nchunk, gu_items_per_unit, dn_items_per_unit,
+                                             gemm_tn, R.sel, R.cmask, R.first, R.ccnt, R.cnt, R.off, R.units,
+                                             R.dec_units, R.gemm_units, R.gemm_tiles, upath, R.meta);
+    route_scatter_kernel<<<nchunk, 256, 0, st>>>(R.sel, R.w, n, topk, E, R.ccnt, R.cmask, R.off, R.etok, R.eslot, R.ew,
+                                                 eexp);
     return 3;
 }
+
+int route_chunks(int n) { return (n + kChunk - 1) / kChunk; }
 
 }  // namespace inzg

@@ -13,6 +13,8 @@
 
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 namespace inzg {
 
 // W [E][H] f16 -> Wr (see above). One thread per output uint4.
@@ -192,6 +194,128 @@ __global__ void __launch_bounds__(256) router_large_kernel(const uint4 *__restri
     }
 }
 
+// Many tokens, fp32 router copy: eight SIMT sub-GEMMs, one per chain lane l (warp l of the block):
+// C_l[t][e] = sum_j f16(W[e][8j+l]) * x[t][8j+l], j in order, one FMA each -- the reference's accumulator l of (e, t);
+// the block then adds the eight in the reference's tree. Block = 64 tokens x 32 experts; thread (warp l, token group
+// tg = lane & 7, expert group eg = lane >> 3) holds tokens tg + 8i (i < 8) x experts 8 eg + m (m < 8): per chain step
+// 8 scalar loads of x, 2 vector loads of weights and 64 FMAs (32 packed f32x2 FMAs, each lane rounded as its own FMA).
+// Per 16-step chunk the block's fp32 weights arrive in one 16 KB bulk copy (layout [l][j][e], made at upload) and the
+// 64 token rows' 128 floats in one bulk copy each, into rows padded to 132 floats so that the 8 token groups of a
+// load sit on distinct banks. Two chunks in flight; two blocks per SM.
+constexpr int kRT = 64, kRE = 32, kRJ = 16, kRStages = 2, kRRow = kRJ * 8 + 4;
+constexpr int kRWBytes = 8 * kRJ * kRE * 4, kRXBytes = kRT * kRRow * 4, kRStageBytes = kRWBytes + kRXBytes;
+constexpr int kRRedStride = kRE + 1;  // reduction rows [l][t][e], padded: a warp's 32 lanes hit 32 banks
+constexpr int kRouterGemmMinTokens = 512;  // below: the f16 kernel, whose 8-token tiles spread over every SM
+
+size_t router_gemm_smem() {
+    const size_t red = (size_t)8 * kRT * kRRedStride * 4, stages = (size_t)kRStages * kRStageBytes;
+    return 128 + (red > stages ? red : stages);
+}
+
+// W [E][H] f16 -> Wf [E/32][H/128][8][16][32] fp32 (see above). One thread per output float.
+__global__ void router_repack32_kernel(const uint16_t *__restrict__ W, float *__restrict__ Wf, int E, int H) {
+    const int nch = H / (8 * kRJ);
+    const int64_t total = (int64_t)E * H;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int e_ = (int)(i % kRE), j_ = (int)((i / kRE) % kRJ), l = (int)((i / (kRE * kRJ)) % 8);
+        const int c = (int)((i / (kRE * kRJ * 8)) % nch), eb = (int)(i / ((int64_t)kRE * kRJ * 8 * nch));
+        Wf[i] = h2f(W[(size_t)(eb * kRE + e_) * H + 8 * (c * kRJ + j_) + l]);
+    }
+}
+
+__global__ void __launch_bounds__(256, 2) router_gemm_kernel(const float *__restrict__ Wf, const float *__restrict__ X,
+                                                            int n, int H, int E, const float *__restrict__ bias,
+                                                            float *__restrict__ logits, int32_t *__restrict__ meta) {
+    extern __shared__ __align__(128) uint8_t rgs[];
+    uint64_t *bar = reinterpret_cast<uint64_t *>(rgs);
+    uint8_t *stage0 = rgs + 128;
+    const int eb = blockIdx.x, t0 = blockIdx.y * kRT, nt = min(kRT, n - t0);
+    const int nch = H / (8 * kRJ);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tg = lane & 7, eg = lane >> 3;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kRStages; s++) mbar_init(&bar[s], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    // warp 0 requests chunk c into stage c % kRStages: lane 0 the weights, every lane some token rows
+    auto issue = [&](int c) {
+        const int s = c % kRStages;
+        uint8_t *st = stage0 + (size_t)s * kRStageBytes;
+        if (lane == 0) {
+            mbar_expect_tx(&bar[s], (uint32_t)(kRWBytes + nt * kRJ * 8 * 4));
+            bulk_g2s(st, Wf + ((size_t)eb * nch + c) * (8 * kRJ * kRE), kRWBytes, &bar[s]);
+        }
+        __syncwarp();
+        float *xs = reinterpret_cast<float *>(st + kRWBytes);
+        for (int tt = lane; tt < nt; tt += 32)
+            bulk_g2s(xs + (size_t)tt * kRRow, X + (size_t)(t0 + tt) * H + c * kRJ * 8, kRJ * 8 * 4, &bar[s]);
+    };
+    if (warp == 0)
+        for (int c = 0; c < kRStages && c < nch; c++) issue(c);
+    float2 acc[8][4];  // [token i][expert pair]: experts 8 eg + 2p, 8 eg + 2p + 1
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int p = 0; p < 4; p++) acc[i][p] = make_float2(0.0f, 0.0f);
+    int failed = -1;  // the chunk whose copies did not land (the same for every thread)
+    for (int c = 0; c < nch; c++) {
+        const int s = c % kRStages;
+        const bool got = mbar_wait_bounded(&bar[s], (c / kRStages) & 1);
+        if (__syncthreads_or(!got)) {
+            failed = c;
+            break;
+        }
+        const uint8_t *st = stage0 + (size_t)s * kRStageBytes;
+        const float *wl = reinterpret_cast<const float *>(st) + warp * (kRJ * kRE) + eg * 8;
+        const float *xl = reinterpret_cast<const float *>(st + kRWBytes) + tg * kRRow + warp;
+#pragma unroll 4
+        for (int j = 0; j < kRJ; j++) {
+            const float4 wa = *reinterpret_cast<const float4 *>(wl + j * kRE);
+            const float4 wb = *reinterpret_cast<const float4 *>(wl + j * kRE + 4);
+            const float2 w2[4] = {make_float2(wa.x, wa.y), make_float2(wa.z, wa.w), make_float2(wb.x, wb.y),
+                                  make_float2(wb.z, wb.w)};
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const float xv = xl[(size_t)i * 8 * kRRow + j * 8];
+                const float2 x2 = make_float2(xv, xv);
+#pragma unroll
+                for (int p = 0; p < 4; p++) acc[i][p] = __ffma2_rn(w2[p], x2, acc[i][p]);
+            }
+        }
+        __syncthreads();  // every warp is done with stage s
+        if (warp == 0 && c + kRStages < nch) issue(c + kRStages);
+    }
+    if (failed >= 0) {  // the copies did not land: record it, wait (bounded) for what is in flight, leave
+        if (threadIdx.x == 0 && meta) atomicCAS(&meta[kMetaRouterError], 0, kErrTimeout);
+        for (int c = failed; c < nch && c < failed + kRStages; c++) mbar_wait_bounded(&bar[c % kRStages], (c / kRStages) & 1);
+        return;
+    }
+    // the eight chain lanes of every (token, expert) meet in shared memory: red[l][t][e]
+    float *red = reinterpret_cast<float *>(stage0);
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            float *r = red + ((size_t)warp * kRT + tg + 8 * i) * kRRedStride + eg * 8 + 2 * p;
+            r[0] = acc[i][p].x;
+            r[1] = acc[i][p].y;
+        }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < kRT * kRE; idx += blockDim.x) {
+        const int t = idx / kRE, e_ = idx % kRE;
+        float a[8];
+#pragma unroll
+        for (int l = 0; l < 8; l++) a[l] = red[((size_t)l * kRT + t) * kRRedStride + e_];
+        float v = __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[4]), __fadd_rn(a[2], a[6])),
+                            __fadd_rn(__fadd_rn(a[1], a[5]), __fadd_rn(a[3], a[7])));
+        const int e = eb * kRE + e_;
+        if (t < nt) {
+            if (bias) v = __fadd_rn(v, bias[e]);  // test hook: logits[x] += bias[x] before the softmax
+            logits[(size_t)(t0 + t) * E + e] = v;
+        }
+    }
+}
+
 // One warp per token: the routing weights of every token (see k_softmax.cuh).
 __global__ void __launch_bounds__(256) softmax_topk_kernel(const float *__restrict__ logits, int n, int E, int topk,
                                                             int32_t *__restrict__ sel, float *__restrict__ wsel,
@@ -211,19 +335,27 @@ void launch_router_repack(const uint16_t *W, uint4 *Wr, int E, int H, cudaStream
     router_repack_kernel<<<blocks, 256, 0, st>>>(W, Wr, E, H);
 }
 
+void launch_router_repack32(const uint16_t *W, float *Wf, int E, int H, cudaStream_t st) {
+    const int64_t total = (int64_t)E * H;
+    router_repack32_kernel<<<(int)std::min<int64_t>((total + 255) / 256, 65535), 256, 0, st>>>(W, Wf, E, H);
+}
+
+bool router_gemm_fits(int E, int H) { return E % kRE == 0 && H % (8 * kRJ) == 0; }
+
 static size_t router_smem(int TT, int H) { return (size_t)TT * 8 * (H / 8 + 4) * sizeof(float); }
 static size_t router_small_smem(int TT, int WPB, int H) { return 128 + (size_t)2 * WPB * H * 8 + (size_t)TT * H * 4; }
 
 void router_set_attributes(int H) {
     cudaFuncSetAttribute(router_large_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_smem(kLT, H));
+    cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_gemm_smem());
     cudaFuncSetAttribute(router_small_kernel<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_small_smem(1, 1, H));
     cudaFuncSetAttribute(router_small_kernel<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_small_smem(2, 1, H));
     cudaFuncSetAttribute(router_small_kernel<4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_small_smem(4, 1, H));
     cudaFuncSetAttribute(router_small_kernel<8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_small_smem(8, 1, H));
 }
 
-int launch_router_logits(const uint4 *Wr, const float *X, int n, int H, int E, const float *bias, float *logits,
-                         int32_t *meta, cudaStream_t st) {
+int launch_router_logits(const uint4 *Wr, const float *Wf, const float *X, int n, int H, int E, const float *bias,
+                         float *logits, int32_t *meta, cudaStream_t st) {
     // few tokens: every block pulls its experts' weights and the token tile in one go; one warp (4 experts) per block
     // up to 8 tokens so the 2 MB router spreads over every SM. Many tokens: 64 experts x 8 tokens per block, FMA-bound.
     if (n <= 1) {
@@ -235,6 +367,9 @@ int launch_router_logits(const uint4 *Wr, const float *X, int n, int H, int E, c
     } else if (n <= 64) {
         router_small_kernel<8, 1><<<dim3((E / 4 + 1) / 2, (n + 7) / 8), 32, router_small_smem(8, 1, H), st>>>(Wr, X, n, H, E, bias,
                                                                                                   logits, meta);
+    } else if (Wf && n >= kRouterGemmMinTokens && router_gemm_fits(E, H)) {
+        router_gemm_kernel<<<dim3(E / kRE, (n + kRT - 1) / kRT), 256, router_gemm_smem(), st>>>(Wf, X, n, H, E, bias,
+                                                                                              logits, meta);
     } else {
         dim3 grid((E + 63) / 64, (n + kLT - 1) / kLT);
         router_large_kernel<<<grid, 256, router_smem(kLT, H), st>>>(Wr, X, n, H, E, bias, logits);

@@ -91,7 +91,8 @@ extern "C" INZG_EXPORT inzg_status inzg_route_topk_noalloc(inzg_ctx *ctx, int la
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     // (no status word on this path: a router copy that never lands is not reported to the caller)
-    inzg::launch_router_logits(static_cast<const uint4 *>(router), x_dev, n, H, E, logit_bias_dev, logits, nullptr, st);
+    inzg::launch_router_logits(static_cast<const uint4 *>(router), nullptr, x_dev, n, H, E, logit_bias_dev, logits, nullptr,
+                               st);
     inzg::launch_softmax_topk(logits, n, E, K, sel_dev, w_dev, nullptr, st);
     e = cudaGetLastError();
     if (e != cudaSuccess) {
