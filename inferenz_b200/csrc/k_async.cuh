@@ -2,6 +2,7 @@
 // Every wait is bounded: a wait that runs out returns false and the caller records kErrTimeout.
 #pragma once
 
+#include <cuda.h>
 #include <stdint.h>
 
 namespace inzg {
@@ -52,6 +53,15 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// one tiled tensor copy global -> shared (this CTA, no multicast) of the box at (x, y); x * element size must be a
+// multiple of 16 bytes
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
 }
 

@@ -51,12 +51,6 @@ struct TcShared {
 };
 
 
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-        ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
 
 // K-major operand in shared memory, 128-byte swizzle: 8-row atoms of 1024 bytes, SBO = 1024 B, LBO unused (1)
 __device__ __forceinline__ uint64_t umma_desc(const void *smem) {
@@ -373,6 +367,20 @@ bool make_tma_map_i8(void *map_out, const void *base, uint64_t rows, uint64_t co
     const cuuint32_t estr[2] = {1, 1};
     return fn(reinterpret_cast<CUtensorMap *>(map_out), CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims,
               strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 2-D fp32 map over [rows][cols] (row pitch = cols floats) with box_rows x 32-float boxes and 128-byte swizzle; rows
+// past `rows` read as zeros
+bool make_tma_map_f32(void *map_out, const float *base, uint64_t rows, uint64_t cols, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn || (cols * 4) % 16 || reinterpret_cast<uintptr_t>(base) % 16) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 4};
+    const cuuint32_t box[2] = {32u, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(reinterpret_cast<CUtensorMap *>(map_out), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base),
+              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 

@@ -41,6 +41,7 @@ int launch_gemm_v1(const LayerDev &L, int kind, const RouteDev &R, const int8_t 
                    int out_ld, int grid, cudaStream_t st);
 int gemm_token_tile();
 bool make_tma_map_i8(void *map_out, const void *base, uint64_t rows, uint64_t cols, int box_rows);
+bool make_tma_map_f32(void *map_out, const float *base, uint64_t rows, uint64_t cols, int box_rows);
 size_t gemm_tc_smem();
 void gemm_tc_set_attributes();
 int launch_gemm_tc(int kind, const void *mapA, const void *mapB, const float *wsc, int rows, int K, const RouteDev &R,

@@ -11,6 +11,7 @@
 #include "k_softmax.cuh"
 #include "k_async.cuh"
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -200,16 +201,18 @@ __global__ void __launch_bounds__(256) router_large_kernel(const uint4 *__restri
 // tg = lane & 7, expert group eg = lane >> 3) holds tokens tg + 8i (i < 8) x experts 8 eg + m (m < 8): per chain step
 // 8 scalar loads of x, 2 vector loads of weights and 64 FMAs (32 packed f32x2 FMAs, each lane rounded as its own FMA).
 // Per 16-step chunk the block's fp32 weights arrive in one 16 KB bulk copy (layout [l][j][e], made at upload) and the
-// 64 token rows' 128 floats in one bulk copy each, into rows padded to 132 floats so that the 8 token groups of a
-// load sit on distinct banks. Two chunks in flight; two blocks per SM.
-constexpr int kRT = 64, kRE = 32, kRJ = 16, kRStages = 2, kRRow = kRJ * 8 + 4;
-constexpr int kRWBytes = 8 * kRJ * kRE * 4, kRXBytes = kRT * kRRow * 4, kRStageBytes = kRWBytes + kRXBytes;
+// 64 token rows' 128 floats in four 64 x 32-float tensor copies with 128-byte swizzle: the 16-byte column group g of
+// row t lands at group g ^ (t % 8), so the 8 token groups of a load (t % 8 = tg) sit on distinct banks; rows past
+// the call's tokens read as zeros. Two chunks in flight, one block barrier per chunk; two blocks per SM.
+constexpr int kRT = 64, kRE = 32, kRJ = 16, kRStages = 2;
+constexpr int kRWBytes = 8 * kRJ * kRE * 4, kRBoxBytes = kRT * 32 * 4, kRXBytes = (kRJ * 8 / 32) * kRBoxBytes;
+constexpr int kRStageBytes = kRWBytes + kRXBytes;  // a multiple of 1024: every box starts 1024-byte aligned
 constexpr int kRRedStride = kRE + 1;  // reduction rows [l][t][e], padded: a warp's 32 lanes hit 32 banks
-constexpr int kRouterGemmMinTokens = 512;  // below: the f16 kernel, whose 8-token tiles spread over every SM
+constexpr int kRouterGemmMinTokens = 320;  // below: the f16 kernel, whose 8-token tiles spread over every SM
 
 size_t router_gemm_smem() {
     const size_t red = (size_t)8 * kRT * kRRedStride * 4, stages = (size_t)kRStages * kRStageBytes;
-    return 128 + (red > stages ? red : stages);
+    return 1024 + (red > stages ? red : stages);
 }
 
 // W [E][H] f16 -> Wf [E/32][H/128][8][16][32] fp32 (see above). One thread per output float.
@@ -223,12 +226,13 @@ __global__ void router_repack32_kernel(const uint16_t *__restrict__ W, float *__
     }
 }
 
-__global__ void __launch_bounds__(256, 2) router_gemm_kernel(const float *__restrict__ Wf, const float *__restrict__ X,
-                                                            int n, int H, int E, const float *__restrict__ bias,
+__global__ void __launch_bounds__(256, 2) router_gemm_kernel(const __grid_constant__ CUtensorMap mapX,
+                                                            const float *__restrict__ Wf, int n, int H, int E,
+                                                            const float *__restrict__ bias,
                                                             float *__restrict__ logits, int32_t *__restrict__ meta) {
-    extern __shared__ __align__(128) uint8_t rgs[];
-    uint64_t *bar = reinterpret_cast<uint64_t *>(rgs);
-    uint8_t *stage0 = rgs + 128;
+    extern __shared__ uint8_t rgs_raw[];
+    __shared__ uint64_t bar[kRStages];
+    uint8_t *stage0 = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(rgs_raw) + 1023) & ~uintptr_t(1023));
     const int eb = blockIdx.x, t0 = blockIdx.y * kRT, nt = min(kRT, n - t0);
     const int nch = H / (8 * kRJ);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tg = lane & 7, eg = lane >> 3;
@@ -237,21 +241,23 @@ __global__ void __launch_bounds__(256, 2) router_gemm_kernel(const float *__rest
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    // warp 0 requests chunk c into stage c % kRStages: lane 0 the weights, every lane some token rows
+    // one thread requests chunk c into stage c % kRStages
     auto issue = [&](int c) {
         const int s = c % kRStages;
         uint8_t *st = stage0 + (size_t)s * kRStageBytes;
-        if (lane == 0) {
-            mbar_expect_tx(&bar[s], (uint32_t)(kRWBytes + nt * kRJ * 8 * 4));
-            bulk_g2s(st, Wf + ((size_t)eb * nch + c) * (8 * kRJ * kRE), kRWBytes, &bar[s]);
-        }
-        __syncwarp();
-        float *xs = reinterpret_cast<float *>(st + kRWBytes);
-        for (int tt = lane; tt < nt; tt += 32)
-            bulk_g2s(xs + (size_t)tt * kRRow, X + (size_t)(t0 + tt) * H + c * kRJ * 8, kRJ * 8 * 4, &bar[s]);
+        mbar_expect_tx(&bar[s], (uint32_t)kRStageBytes);
+        bulk_g2s(st, Wf + ((size_t)eb * nch + c) * (8 * kRJ * kRE), kRWBytes, &bar[s]);
+#pragma unroll
+        for (int b = 0; b < kRJ * 8 / 32; b++)
+            tma_load_2d(st + kRWBytes + b * kRBoxBytes, &mapX, c * kRJ * 8 + b * 32, t0, &bar[s]);
     };
-    if (warp == 0)
+    if (threadIdx.x == 0)
         for (int c = 0; c < kRStages && c < nch; c++) issue(c);
+    // x[t][8j + l] of chunk-local step j: box j / 4, column 8 (j % 4) + l, i.e. 16-byte group 2 (j % 4) + l / 4
+    // (swizzled with t % 8 = tg) and word l % 4; token t = tg + 8i adds 8i rows of 32 floats
+    int xoff[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) xoff[q] = tg * 32 + (((2 * q + (warp >> 2)) ^ tg) * 4) + (warp & 3);
     float2 acc[8][4];  // [token i][expert pair]: experts 8 eg + 2p, 8 eg + 2p + 1
 #pragma unroll
     for (int i = 0; i < 8; i++)
@@ -261,33 +267,42 @@ __global__ void __launch_bounds__(256, 2) router_gemm_kernel(const float *__rest
     for (int c = 0; c < nch; c++) {
         const int s = c % kRStages;
         const bool got = mbar_wait_bounded(&bar[s], (c / kRStages) & 1);
-        if (__syncthreads_or(!got)) {
+        if (got) {
+            const uint8_t *st = stage0 + (size_t)s * kRStageBytes;
+            const float *wl = reinterpret_cast<const float *>(st) + warp * (kRJ * kRE) + eg * 8;
+            const float *xb = reinterpret_cast<const float *>(st + kRWBytes);
+#pragma unroll 4
+            for (int j = 0; j < kRJ; j++) {
+                const float4 wa = *reinterpret_cast<const float4 *>(wl + j * kRE);
+                const float4 wb = *reinterpret_cast<const float4 *>(wl + j * kRE + 4);
+                const float2 w2[4] = {make_float2(wa.x, wa.y), make_float2(wa.z, wa.w), make_float2(wb.x, wb.y),
+                                      make_float2(wb.z, wb.w)};
+                const float *xl = xb + (j >> 2) * (kRBoxBytes / 4) + xoff[j & 3];
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const float xv = xl[i * 8 * 32];
+                    const float2 x2 = make_float2(xv, xv);
+#pragma unroll
+                    for (int p = 0; p < 4; p++) acc[i][p] = __ffma2_rn(w2[p], x2, acc[i][p]);
+                }
+            }
+        }
+        if (__syncthreads_or(!got)) {  // every warp is done with stage s (or the copies did not land)
             failed = c;
             break;
         }
-        const uint8_t *st = stage0 + (size_t)s * kRStageBytes;
-        const float *wl = reinterpret_cast<const float *>(st) + warp * (kRJ * kRE) + eg * 8;
-        const float *xl = reinterpret_cast<const float *>(st + kRWBytes) + tg * kRRow + warp;
-#pragma unroll 4
-        for (int j = 0; j < kRJ; j++) {
-            const float4 wa = *reinterpret_cast<const float4 *>(wl + j * kRE);
-            const float4 wb = *reinterpret_cast<const float4 *>(wl + j * kRE + 4);
-            const float2 w2[4] = {make_float2(wa.x, wa.y), make_float2(wa.z, wa.w), make_float2(wb.x, wb.y),
-                                  make_float2(wb.z, wb.w)};
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const float xv = xl[(size_t)i * 8 * kRRow + j * 8];
-                const float2 x2 = make_float2(xv, xv);
-#pragma unroll
-                for (int p = 0; p < 4; p++) acc[i][p] = __ffma2_rn(w2[p], x2, acc[i][p]);
-            }
+        if (threadIdx.x == 0 && c + kRStages < nch) {
+            fence_proxy_async_smem();
+            issue(c + kRStages);
         }
-        __syncthreads();  // every warp is done with stage s
-        if (warp == 0 && c + kRStages < nch) issue(c + kRStages);
     }
-    if (failed >= 0) {  // the copies did not land: record it, wait (bounded) for what is in flight, leave
-        if (threadIdx.x == 0 && meta) atomicCAS(&meta[kMetaRouterError], 0, kErrTimeout);
-        for (int c = failed; c < nch && c < failed + kRStages; c++) mbar_wait_bounded(&bar[c % kRStages], (c / kRStages) & 1);
+    if (failed >= 0) {  // record it, wait (bounded) for what is in flight, leave
+        if (threadIdx.x == 0) {
+            if (meta) atomicCAS(&meta[kMetaRouterError], 0, kErrTimeout);
+            for (int c = failed; c < nch && c < failed + kRStages; c++)
+                mbar_wait_bounded(&bar[c % kRStages], (c / kRStages) & 1);
+        }
+        __syncthreads();
         return;
     }
     // the eight chain lanes of every (token, expert) meet in shared memory: red[l][t][e]
@@ -356,6 +371,7 @@ void router_set_attributes(int H) {
 
 int launch_router_logits(const uint4 *Wr, const float *Wf, const float *X, int n, int H, int E, const float *bias,
                          float *logits, int32_t *meta, cudaStream_t st) {
+    CUtensorMap mapX;
     // few tokens: every block pulls its experts' weights and the token tile in one go; one warp (4 experts) per block
     // up to 8 tokens so the 2 MB router spreads over every SM. Many tokens: 64 experts x 8 tokens per block, FMA-bound.
     if (n <= 1) {
@@ -367,8 +383,8 @@ int launch_router_logits(const uint4 *Wr, const float *Wf, const float *X, int n
     } else if (n <= 64) {
         router_small_kernel<8, 1><<<dim3((E / 4 + 1) / 2, (n + 7) / 8), 32, router_small_smem(8, 1, H), st>>>(Wr, X, n, H, E, bias,
                                                                                                   logits, meta);
-    } else if (Wf && n >= kRouterGemmMinTokens && router_gemm_fits(E, H)) {
-        router_gemm_kernel<<<dim3(E / kRE, (n + kRT - 1) / kRT), 256, router_gemm_smem(), st>>>(Wf, X, n, H, E, bias,
+    } else if (Wf && n >= kRouterGemmMinTokens && router_gemm_fits(E, H) && make_tma_map_f32(&mapX, X, n, H, kRT)) {
+        router_gemm_kernel<<<dim3(E / kRE, (n + kRT - 1) / kRT), 256, router_gemm_smem(), st>>>(mapX, Wf, n, H, E, bias,
                                                                                               logits, meta);
     } else {
         dim3 grid((E + 63) / 64, (n + kLT - 1) / kLT);
