@@ -221,6 +221,12 @@ inzg_ctx *inzg_create(const inzg_config *cfg, inzg_status *status) {
     const size_t T = cfg->max_tokens, H = cfg->hidden, E = cfg->n_expert, K = cfg->topk, FF = cfg->ff;
     const size_t NE = T * K, nkbH = (H + kKB - 1) / kKB, nkbF = (FF + kKB - 1) / kKB;
     const size_t nchunk = (size_t)route_chunks((int)T);
+    if (NE / (size_t)gemm_token_tile() + E >= 65536) {  // the dispatch scan counts GEMM tiles in 16 bits
+        cudaStreamDestroy(c->stream);
+        delete c;
+        st = INZG_BAD_ARG;
+        return nullptr;
+    }
     bool ok = true;
     c->xin = dalloc<float>(T * H, ok);
     c->y = dalloc<float>(T * H, ok);
@@ -906,11 +912,13 @@ inzg_status inzg_moe_route_dump(inzg_ctx *c, int n, int32_t *sel, float *w, floa
     if (e == cudaSuccess) e = cudaMemcpy(meta, c->meta, sizeof(meta), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return cuda_fail(c, e, "route_dump");
     const int nu = meta[kMetaNUnits];
-    std::vector<int32_t> units(nu), first(E);
+    std::vector<int32_t> units(nu), ssel((size_t)n * K), first(E, 0x7F7F7F7F);
     if (nu > 0) e = cudaMemcpy(units.data(), c->units, sizeof(int32_t) * nu, cudaMemcpyDeviceToHost);
-    if (e == cudaSuccess) e = cudaMemcpy(first.data(), c->first, sizeof(int32_t) * E, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(ssel.data(), c->sel, sizeof(int32_t) * (size_t)n * K, cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return cuda_fail(c, e, "route_dump");
     // first-touch order of the reference's units: ascending first slot t*topk+k
+    for (size_t i = ssel.size(); i-- > 0;)
+        if (ssel[i] >= 0 && ssel[i] < E) first[ssel[i]] = (int32_t)i;
     std::sort(units.begin(), units.end(), [&](int a, int b) { return first[a] < first[b]; });
     if (unit_expert) std::copy(units.begin(), units.end(), unit_expert);
     if (n_units) *n_units = nu;

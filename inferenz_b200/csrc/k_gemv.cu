@@ -11,9 +11,11 @@
 // Tensor pipe: the lane partials I_lg come straight out of the int8 MMA (mma.m16n8k32, u8 x s8 -> s32). The K = 32 of
 // one MMA holds 4 lanes x 8 elements (element i < 4: x[4l+i], else x[32+4l+i-4]); the activation operand is
 // block-diagonal -- column n carries lane n's 8 activations in lane n's rows and zeros elsewhere -- so D[row][n] is
-// exactly I_n. Two MMAs (lanes 0-3, lanes 4-7) give all 8 partials of a 16-row tile for one token. Thread (r, t) of the
-// MMA holds lanes 2t, 2t+1 of rows r and r+8, folds them into its accumulators with the reference's fma, and hsum8
-// becomes two quad shuffles that pair the lanes as the reference does: ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7)).
+// exactly I_n. Two tokens share the 8 columns (token A lanes in columns 0-3, token B in 4-7), so two MMAs (lanes 0-3,
+// lanes 4-7) give all 8 partials of a 16-row tile for two tokens. Thread (r, t) of the MMA holds, for token t >> 1,
+// lanes 2(t&1), 2(t&1)+1 of both MMAs for rows r and r+8, folds them into its accumulators with the reference's fma
+// (packed f32x2 instructions, each lane rounded as its own fma), and hsum8 becomes one add per lane pair and one quad
+// shuffle that pair the lanes as the reference does: ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7)).
 //
 // Pipeline (one CTA per SM, persistent): an item is 128 rows (8 row tiles) of one decode expert's matrix. A producer
 // warp takes items from the call's work queue (experts with the most tokens first), brings the item's token
@@ -117,26 +119,31 @@ __device__ __forceinline__ bool dec_item(DecShared &S, const uint8_t *stages, co
     using G = DecGeo<Q8, NG, KIND>;
     volatile int *abort = &S.abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gr = lane >> 2, t = lane & 3;
-    // block-diagonal activation operand: thread (n = gr, t) supplies lane n's activations x[32 (t&1) + 4n .. +3]
-    // when (n & 1) == (t >> 1), in MMA n >> 2, register (n >> 1) & 1
+    // Tokens go through the MMAs in pairs (A = 2p, B = 2p + 1). Column n = gr of the activation operand carries token
+    // 2p + (n >> 2), chain lane 4h + (n & 3) in MMA h, block-diagonally: its 8 activations sit in the K rows of lane
+    // n & 3 and the rest of the column is zero. Thread (gr, t) holds K rows 4t..4t+3 (register 0) and 16+4t.. (register
+    // 1), i.e. the first or second half (t & 1) of lane t >> 1 (register 0) or lane 2 + (t >> 1) (register 1).
     // (0/1 factors: the operand is selected with an integer multiply, which issues on the FMA pipe)
-    const bool act_on = (gr & 1) == (t >> 1);
-    const uint32_t m00 = act_on && gr < 4 && !((gr >> 1) & 1) ? one : 0u, m01 = act_on && gr < 4 && ((gr >> 1) & 1) ? one : 0u;
-    const uint32_t m10 = act_on && gr >= 4 && !((gr >> 1) & 1) ? one : 0u, m11 = act_on && gr >= 4 && ((gr >> 1) & 1) ? one : 0u;
+    const int lc = gr & 3;
+    const uint32_t s0 = lc == (t >> 1) ? one : 0u, s1 = lc == 2 + (t >> 1) ? one : 0u;
     const uint32_t k16 = one << 16;
-    const uint8_t *xq = ib + 32 * (t & 1) + 4 * gr;
+    const uint8_t *xq = ib + (size_t)(gr >> 2) * G::K + 32 * (t & 1) + 4 * lc;
     const float2 *xsb = reinterpret_cast<const float2 *>(ib + G::IB_SB);
     // scale pairs (d[r][g], d[r+8][g]) of this warp's row tile: word (g / 4) * 32 + gr * 4 + g % 4
     const uint32_t *wd = reinterpret_cast<const uint32_t *>(ib + G::IB_D + (size_t)warp * G::GD * 128) + gr * 4;
     const uint4 T = it.lut;
     const bool valid = it.e >= 0;
     const int ntok = it.ntok;
+    constexpr int NP = (TC + 1) / 2;
+    const int jcol = gr >> 2, jd = t >> 1;  // token of this thread's operand column / of its accumulator columns
 
-    float acc[TC][4];  // [token][row r lane 2t, row r lane 2t+1, row r+8 lane 2t, row r+8 lane 2t+1]
+    // acc[p][h][r]: token 2p + jd, row gr + 8r, chain lanes 4h + 2(t & 1) and 4h + 2(t & 1) + 1
+    float2 acc[NP][2][2];
 #pragma unroll
-    for (int j = 0; j < TC; j++)
+    for (int p = 0; p < NP; p++)
 #pragma unroll
-        for (int i = 0; i < 4; i++) acc[j][i] = 0.0f;
+        for (int h = 0; h < 2; h++) acc[p][h][0] = acc[p][h][1] = make_float2(0.0f, 0.0f);
+    const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
 
     // one 64-group: g global index, i index inside the stage
     auto group = [&](const uint8_t *wq, int g, int i) {
@@ -155,21 +162,28 @@ __device__ __forceinline__ bool dec_item(DecShared &S, const uint8_t *stages, co
             A1[2] = lut16(hi16(w.z, k16), hi16(x.z, k16), T, one); A1[3] = lut16(hi16(w.w, k16), hi16(x.w, k16), T, one);
         }
         const float2 dd = h2f16x2(wd[(g >> 2) * 32 + (g & 3)]);
-        const float d0 = dd.x, d8 = dd.y;
 #pragma unroll
-        for (int j = 0; j < TC; j++) {
-            if (j >= ntok) continue;
-            const uint32_t xv = *reinterpret_cast<const uint32_t *>(xq + (size_t)j * G::K + g * kGroup);
-            const float sx = xsb[j * NG + g].x;
-            // the accumulator starts at the bits of 1.5 * 2^23: D then holds 12582912 + I as a float (|I| < 2^22)
-            int D[4];
-            mma_u8s8_c(D, A0[0], A0[1], A0[2], A0[3], xv * m00, xv * m01, 0x4B400000);
-            mma_u8s8(D, A1[0], A1[1], A1[2], A1[3], xv * m10, xv * m11);
-            const float ds0 = __fmul_rn(d0, sx), ds8 = __fmul_rn(d8, sx);
-            acc[j][0] = __fmaf_rn(__fadd_rn(__int_as_float(D[0]), -12582912.0f), ds0, acc[j][0]);
-            acc[j][1] = __fmaf_rn(__fadd_rn(__int_as_float(D[1]), -12582912.0f), ds0, acc[j][1]);
-            acc[j][2] = __fmaf_rn(__fadd_rn(__int_as_float(D[2]), -12582912.0f), ds8, acc[j][2]);
-            acc[j][3] = __fmaf_rn(__fadd_rn(__int_as_float(D[3]), -12582912.0f), ds8, acc[j][3]);
+        for (int p = 0; p < NP; p++) {
+            if (2 * p >= ntok) continue;
+            const bool col_live = 2 * p + jcol < ntok;
+            const uint8_t *xp = xq + (size_t)(2 * p) * G::K + g * kGroup;
+            const uint32_t x0 = col_live ? *reinterpret_cast<const uint32_t *>(xp) : 0u;
+            const uint32_t x1 = col_live ? *reinterpret_cast<const uint32_t *>(xp + 16) : 0u;
+            const float sx = 2 * p + jd < ntok ? xsb[(2 * p + jd) * NG + g].x : 0.0f;
+            // the accumulators start at the bits of 1.5 * 2^23: D then holds 12582912 + I as a float (|I| < 2^22)
+            int D0[4], D1[4];
+            mma_u8s8_c(D0, A0[0], A0[1], A0[2], A0[3], x0 * s0, x0 * s1, 0x4B400000);
+            mma_u8s8_c(D1, A1[0], A1[1], A1[2], A1[3], x1 * s0, x1 * s1, 0x4B400000);
+            const float ds0 = __fmul_rn(dd.x, sx), ds8 = __fmul_rn(dd.y, sx);
+            const float2 m0 = make_float2(ds0, ds0), m8 = make_float2(ds8, ds8);
+            acc[p][0][0] = __ffma2_rn(__fadd2_rn(make_float2(__int_as_float(D0[0]), __int_as_float(D0[1])), neg_magic),
+                                      m0, acc[p][0][0]);
+            acc[p][0][1] = __ffma2_rn(__fadd2_rn(make_float2(__int_as_float(D0[2]), __int_as_float(D0[3])), neg_magic),
+                                      m8, acc[p][0][1]);
+            acc[p][1][0] = __ffma2_rn(__fadd2_rn(make_float2(__int_as_float(D1[0]), __int_as_float(D1[1])), neg_magic),
+                                      m0, acc[p][1][0]);
+            acc[p][1][1] = __ffma2_rn(__fadd2_rn(make_float2(__int_as_float(D1[2]), __int_as_float(D1[3])), neg_magic),
+                                      m8, acc[p][1][1]);
         }
     };
 
@@ -192,18 +206,11 @@ __device__ __forceinline__ bool dec_item(DecShared &S, const uint8_t *stages, co
     }
     if (!valid) return true;
 
-#pragma unroll
-    for (int j = 0; j < TC; j++) {
-        if (j >= ntok) continue;
-        float a[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) a[i] = __fadd_rn(acc[j][i], __shfl_xor_sync(0xffffffffu, acc[j][i], 2));
-#pragma unroll
-        for (int i = 0; i < 4; i++) a[i] = __fadd_rn(a[i], __shfl_xor_sync(0xffffffffu, a[i], 1));
-        // bias chains: b = fma chain of d_g * bsum_g (Q8G: one per row, in order; Q4L: 8 chains g % 8 over the first
-        // ng & ~7 groups, hsum8, then the remaining groups in order). Thread t keeps Q4L chains 2t, 2t+1 of both rows.
+    // bias chains of token j for rows gr, gr + 8: b = fma chain of d_g * bsum_g (Q8G: one per row, in order; Q4L: 8
+    // chains g % 8 over the first ng & ~7 groups, hsum8, then the remaining groups in order). Thread t keeps Q4L chains
+    // 2t, 2t+1 of both rows; every thread of the quad ends with both rows' values.
+    auto bias_rows = [&](int j, float (&b)[2]) {
         const float2 *sb = xsb + j * NG;
-        float b[2];  // row r, row r + 8
         if (Q8) {
 #pragma unroll 4
             for (int h = 0; h < 2; h++) {
@@ -240,10 +247,29 @@ __device__ __forceinline__ bool dec_item(DecShared &S, const uint8_t *stages, co
                 b[1] = __fmaf_rn(h2f16(dv >> 16), sb[g].y, b[1]);
             }
         }
-        if (t < 2) {
-            const float s8 = __fadd_rn(a[2 * t], a[2 * t + 1]);
-            const float y = __fsub_rn(s8, __fmul_rn(Q8 ? 128.0f : (float)kLutBias, t ? b[1] : b[0]));
-            const int row = (it.rb * G::WARPS + warp) * 16 + gr + 8 * t;
+    };
+
+#pragma unroll
+    for (int p = 0; p < NP; p++) {
+        if (2 * p >= ntok) continue;
+        // hsum8 of token 2p + jd, rows gr and gr + 8: this thread holds lanes {2u, 2u+1, 4+2u, 5+2u} (u = t & 1), its
+        // partner t ^ 1 the others: ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7))
+        float sr[2];
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const float u0 = __fadd_rn(acc[p][0][r].x, acc[p][1][r].x), u1 = __fadd_rn(acc[p][0][r].y, acc[p][1][r].y);
+            const float v0 = __fadd_rn(u0, __shfl_xor_sync(0xffffffffu, u0, 1));
+            const float v1 = __fadd_rn(u1, __shfl_xor_sync(0xffffffffu, u1, 1));
+            sr[r] = __fadd_rn(v0, v1);
+        }
+        float bA[2], bB[2] = {0.0f, 0.0f};
+        bias_rows(2 * p, bA);
+        if (2 * p + 1 < ntok) bias_rows(2 * p + 1, bB);  // uniform over the warp
+        const int j = 2 * p + jd, r = t & 1;
+        if (j < ntok) {
+            const float b = jd ? (r ? bB[1] : bB[0]) : (r ? bA[1] : bA[0]);
+            const float y = __fsub_rn(r ? sr[1] : sr[0], __fmul_rn(Q8 ? 128.0f : (float)kLutBias, b));
+            const int row = (it.rb * G::WARPS + warp) * 16 + gr + 8 * r;
             if (KIND == 0) out[(size_t)(it.base + j) * out_ld + row] = y;
             else out[(size_t)it.oslot[j] * out_ld + row] = __fmul_rn(it.ow[j], y);
         }

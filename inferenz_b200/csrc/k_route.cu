@@ -5,7 +5,7 @@
 // token -- the order the reference appends them -- without atomics on positions, so the result is deterministic:
 //   route_mask    per 64-token chunk (one block): a 64-bit token mask per expert (shared-memory atomicOr), the
 //                 chunk's count per expert = the mask's popcount
-//   route_scan    one block: per-expert prefix over chunks, counts, offsets, first-touch keys, expert lists and the
+//   route_scan    one block: per-expert prefix over chunks, counts, offsets, expert lists and the
 //                 per-expert numeric path (decode numerics when n <= 8 or the expert has < GEMM_MIN_T tokens,
 //                 src/model_fwd.c:229-249, 1070), work counts for the expert kernels
 //   route_scatter per chunk: entry position = off[e] + chunk prefix + popcount of the expert's mask below the token
@@ -71,67 +71,79 @@ __global__ void __launch_bounds__(256) route_mask_kernel(const int32_t *__restri
     }
 }
 
+// inclusive block-wide scan of (a, p) over the threads of the block (blockDim.x <= 1024): shuffles inside each warp,
+// the warp totals through shared memory (two block barriers). p carries four 16-bit counters side by side.
+__device__ __forceinline__ void block_scan2(int &a, uint64_t &p, int *wa, uint64_t *wp) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int ta = __shfl_up_sync(0xffffffffu, a, o);
+        const uint64_t tp = __shfl_up_sync(0xffffffffu, p, o);
+        if (lane >= o) { a += ta; p += tp; }
+    }
+    if (lane == 31) { wa[w] = a; wp[w] = p; }
+    __syncthreads();
+    if (w == 0) {
+        int x = lane < nw ? wa[lane] : 0;
+        uint64_t y = lane < nw ? wp[lane] : 0ull;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int tx = __shfl_up_sync(0xffffffffu, x, o);
+            const uint64_t ty = __shfl_up_sync(0xffffffffu, y, o);
+            if (lane >= o) { x += tx; y += ty; }
+        }
+        if (lane < nw) { wa[lane] = x; wp[lane] = y; }  // inclusive prefix of the warp totals
+    }
+    __syncthreads();
+    if (w > 0) { a += wa[w - 1]; p += wp[w - 1]; }
+}
+
 // one block of E threads (E <= 1024)
 __global__ void __launch_bounds__(1024) route_scan_kernel(int n, int n_rule, int absent_ok, int topk, int E, int nchunk,
                                                           int gu_items_per_unit,
                                                           int dn_items_per_unit, int gemm_tn,
-                                                          const int32_t *__restrict__ sel,
-                                                          const uint64_t *__restrict__ cmask,
-                                                          int32_t *__restrict__ first,
                                                           int32_t *__restrict__ ccnt, int32_t *__restrict__ cnt,
                                                           int32_t *__restrict__ off, int32_t *__restrict__ units,
                                                           int32_t *__restrict__ dec_units, int32_t *__restrict__ gemm_units,
                                                           int32_t *__restrict__ gemm_tiles, int32_t *__restrict__ upath,
                                                           int32_t *__restrict__ meta) {
-    __shared__ int32_t sc[1024], su[1024], sd[1024], sg[1024], st[1024], bins[32];
+    __shared__ int32_t wa[32], bins[32];
+    __shared__ uint64_t wp[32];
     const int e = threadIdx.x;
-    int run = 0, fc = -1;  // fc: first chunk in which the expert was chosen
+    int run = 0;
     if (e < E)
-        for (int c0 = 0; c0 < nchunk; c0 += 16) {  // 16 independent loads in flight, then the running prefix
-            int v[16];
+        for (int c0 = 0; c0 < nchunk; c0 += 32) {  // 32 independent loads in flight, then the running prefix
+            int v[32];
 #pragma unroll
-            for (int j = 0; j < 16; j++) v[j] = c0 + j < nchunk ? ccnt[(size_t)(c0 + j) * E + e] : 0;
+            for (int j = 0; j < 32; j++) v[j] = c0 + j < nchunk ? ccnt[(size_t)(c0 + j) * E + e] : 0;
 #pragma unroll
-            for (int j = 0; j < 16; j++) {
+            for (int j = 0; j < 32; j++) {
                 if (c0 + j < nchunk) ccnt[(size_t)(c0 + j) * E + e] = run;
-                if (fc < 0 && v[j] > 0) fc = c0 + j;
                 run += v[j];
             }
         }
-    if (e < E) {  // first-touch key: the first token's slot t*topk+k
-        int key = 0x7F7F7F7F;
-        if (fc >= 0) {
-            const int t = fc * kChunk + __ffsll((long long)cmask[(size_t)fc * E + e]) - 1;
-            for (int k = 0; k < topk; k++)
-                if (sel[(size_t)t * topk + k] == e) { key = t * topk + k; break; }
-        }
-        first[e] = key;
-    }
     const int c = e < E ? run : 0;
     const int is_unit = c > 0;
     const int is_dec = is_unit && (n_rule <= 8 || c < kGemmMinT);
     const int is_gemm = is_unit && !is_dec;
     const int tiles = is_gemm ? (c + gemm_tn - 1) / gemm_tn : 0;
-    sc[e] = c; su[e] = is_unit; sd[e] = is_dec; sg[e] = is_gemm; st[e] = tiles;
-    __syncthreads();
-    // inclusive Hillis-Steele scans over the five arrays
-    for (int o = 1; o < blockDim.x; o <<= 1) {
-        int a = 0, b = 0, d = 0, g = 0, h = 0;
-        if (e >= o) { a = sc[e - o]; b = su[e - o]; d = sd[e - o]; g = sg[e - o]; h = st[e - o]; }
-        __syncthreads();
-        if (e >= o) { sc[e] += a; su[e] += b; sd[e] += d; sg[e] += g; st[e] += h; }
-        __syncthreads();
-    }
+    // inclusive scans: entries; units | decode units | GEMM units | GEMM tiles (16 bits each: <= 1024 experts,
+    // tiles <= n * topk / gemm_tn + E, checked on the host)
+    int sc = c;
+    uint64_t sp = (uint64_t)is_unit | ((uint64_t)is_dec << 16) | ((uint64_t)is_gemm << 32) | ((uint64_t)tiles << 48);
+    block_scan2(sc, sp, wa, wp);
+    const int su = (int)(sp & 0xFFFF), sd = (int)((sp >> 16) & 0xFFFF), sg = (int)((sp >> 32) & 0xFFFF),
+              stl = (int)(sp >> 48);
     if (e < E) {
         cnt[e] = c;
-        off[e] = sc[e] - c;
-        if (e == E - 1) off[E] = sc[e];
+        off[e] = sc - c;
+        if (e == E - 1) off[E] = sc;
         upath[e] = is_gemm;
-        if (is_unit) units[su[e] - 1] = e;
+        if (is_unit) units[su - 1] = e;
         if (is_gemm) {
-            gemm_units[sg[e] - 1] = e;
-            const int base = st[e] - tiles;
-            for (int i = 0; i < tiles; i++) gemm_tiles[base + i] = ((sg[e] - 1) << 16) | i;
+            gemm_units[sg - 1] = e;
+            const int base = stl - tiles;
+            for (int i = 0; i < tiles; i++) gemm_tiles[base + i] = ((sg - 1) << 16) | i;
         }
     }
     order_dec_units(is_dec, c, e, dec_units, meta, bins);
@@ -139,14 +151,14 @@ __global__ void __launch_bounds__(1024) route_scan_kernel(int n, int n_rule, int
         const int rerr = meta[kMetaRouterError];  // the router ran before this call's counters were cleared
         if (rerr) set_error(meta, rerr);
         meta[kMetaRouterError] = kErrNone;
-        meta[kMetaNUnits] = su[e];
-        meta[kMetaNDec] = sd[e];
-        meta[kMetaNGemm] = sg[e];
-        meta[kMetaDecItemsGU] = sd[e] * gu_items_per_unit;
-        meta[kMetaDecItemsDN] = sd[e] * dn_items_per_unit;
-        meta[kMetaGemmTilesGU] = st[e];
-        meta[kMetaGemmTilesDN] = st[e];
-        if (absent_ok ? sc[e] > n * topk : sc[e] != n * topk) set_error(meta, kErrOverflow);
+        meta[kMetaNUnits] = su;
+        meta[kMetaNDec] = sd;
+        meta[kMetaNGemm] = sg;
+        meta[kMetaDecItemsGU] = sd * gu_items_per_unit;
+        meta[kMetaDecItemsDN] = sd * dn_items_per_unit;
+        meta[kMetaGemmTilesGU] = stl;
+        meta[kMetaGemmTilesDN] = stl;
+        if (absent_ok ? sc > n * topk : sc != n * topk) set_error(meta, kErrOverflow);
     }
 }
 
@@ -424,8 +436,8 @@ int launch_route(const RouteDev &R, int gu_items_per_unit, int dn_items_per_unit
     route_mask_kernel<<<nchunk, 256, 0, st>>>(R.sel, n, topk, E, R.absent_ok, R.ccnt, R.cmask, R.meta);
     const int threads = (E + 31) / 32 * 32;
     route_scan_kernel<<<1, threads, 0, st>>>(n, R.n_rule, R.absent_ok, topk, E, nchunk, gu_items_per_unit, dn_items_per_unit,
-                                             gemm_tn, R.sel, R.cmask, R.first, R.ccnt, R.cnt, R.off, R.units,
-                                             R.dec_units, R.gemm_units, R.gemm_tiles, upath, R.meta);
+                                             gemm_tn, R.ccnt, R.cnt, R.off, R.units, R.dec_units, R.gemm_units,
+                                             R.gemm_tiles, upath, R.meta);
     route_scatter_kernel<<<nchunk, 256, 0, st>>>(R.sel, R.w, n, topk, E, R.ccnt, R.cmask, R.off, R.etok, R.eslot, R.ew,
                                                  eexp);
     return 3;
