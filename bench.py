@@ -486,9 +486,7 @@ def cpu_reference(cfg, n, budget_s=12.0, blobs=None, bb=None, R=None, steps=None
         t0 = time.perf_counter()
         call()
         ts.append(time.perf_counter() - t0)
-        if steps is not None and len(ts) >= steps:
-            break
-        if steps is None and (time.perf_counter() - t_start > budget_s or len(ts) >= 2000):
+        if len(ts) >= (steps if steps is not None else 2000) or time.perf_counter() - t_start > budget_s:
             break
     med = statistics.median(ts)
     return {"value": round(n / med, 1), "unit": "tokens/s", "cores": cores, "kind": kind,
@@ -500,14 +498,19 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    cpu = cpu_reference("decode32", 32, steps=args.steps, warmup=max(args.warmup, 1))
+    # the same global batch as this arm at N GPUs (32 decode tokens per GPU, the EP bench's inputs), as one CPU call;
+    # at most about 90 s of timed calls, so the run ends within minutes whatever --steps asks
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    n = 32 * world
+    cpu = cpu_reference("decode32", n, budget_s=90.0, steps=args.steps, warmup=max(args.warmup, 1))
     line = {"metric": METRIC, "value": cpu["value"], "unit": "tokens/s", "impl": "reference",
-            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": cpu["ms_median"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8 x Q4L (fp32 accumulate)", "data": "synthetic (seeded; no dataset)",
-            "config": {"workload": "BASELINE configs[1]: MoE layer, decode batch of 32 tokens, d=2048, 512 experts, "
-                                   "top-10, FF 640, Q4L experts, F16 router, N(0,1) per-expert logit bias",
-                       "global_batch": 32, "seq_len": 1, "parallelism": "CPU threads (reference thread pool)"},
+            "config": {"workload": "BASELINE configs[1]: MoE layer, decode batch of 32 tokens per GPU of the GPU arm, "
+                                   "d=2048, 512 experts, top-10, FF 640, Q4L experts, F16 router, N(0,1) per-expert "
+                                   "logit bias; the whole batch as one call of the reference's CPU layer",
+                       "global_batch": n, "seq_len": 1, "parallelism": "CPU threads (reference thread pool)"},
             "cpu_baseline": cpu,
             "e2e": {"value": cpu["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
