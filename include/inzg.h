@@ -100,6 +100,34 @@ INZG_EXPORT inzg_status inzg_set_router(inzg_ctx *ctx, int layer, const uint16_t
 INZG_EXPORT inzg_status inzg_pool_add_layer(inzg_ctx *ctx, int layer, int expert_type, const void *blobs, uint64_t blob_bytes,
                                 int n_expert);
 
+/* ---- Experts straight from the engine's GGUF model file: the lookups of setup_experts (src/engine.c:336-351) over
+ * the file as the reference's gguf_open reads it (src/gguf.c:80-160: GGUF v2/v3, data at the header's end rounded
+ * up to "general.alignment", a tensor's size = distance to the next tensor's offset). Host code; the file stays
+ * mapped read-only until inzg_gguf_close. */
+typedef struct inzg_gguf inzg_gguf;
+typedef struct {
+    int expert_type;       /* "inz.expert_type"; absent: INZG_T_Q8G, the engine's default (src/engine.c:338) */
+    uint64_t blob_bytes;   /* "inz.expert_blob_bytes" (0 when absent) */
+    int n_layers;          /* "blk.%d.experts" present for layers 0 .. n_layers-1 */
+    int has_mtp;           /* "mtp.experts" present: the engine numbers it layer n_layers (src/engine.c:343-348) */
+    uint64_t alignment;    /* "general.alignment" (32 when absent) */
+    uint64_t data_offset;  /* file offset of the tensor data section */
+} inzg_gguf_info;
+
+/* Opens and parses `path`; NULL on failure with the reason in err (err_len bytes, may be NULL). info: optional. */
+INZG_EXPORT inzg_gguf *inzg_gguf_open(const char *path, inzg_gguf_info *info, char *err, size_t err_len);
+INZG_EXPORT inzg_status inzg_gguf_get_info(const inzg_gguf *g, inzg_gguf_info *info);
+/* Layer `layer`'s expert tensor (layer == n_layers: "mtp.experts"): *data points into the mapping, *nbytes is its size
+ * (padding to the next tensor included), *file_offset its absolute offset; each output optional. INZG_BAD_ARG when
+ * the file has no such tensor. */
+INZG_EXPORT inzg_status inzg_gguf_experts(const inzg_gguf *g, int layer, const void **data, uint64_t *nbytes,
+                                          uint64_t *file_offset);
+/* Pool slot `layer` of ctx from the file's layer `gguf_layer`, with setup_experts' checks (blob size a positive
+ * multiple of 4096 and the tensor at least n_expert blobs long, src/engine.c:340-350; INZG_CORRUPT_BLOB otherwise),
+ * then inzg_pool_add_layer on the mapped blobs of the file's expert type. */
+INZG_EXPORT inzg_status inzg_pool_add_layer_gguf(inzg_ctx *ctx, int layer, const inzg_gguf *g, int gguf_layer);
+INZG_EXPORT void inzg_gguf_close(inzg_gguf *g);
+
 /* The layer's shared expert (src/model_fwd.c:1041-1069, 1141-1148; the engine's `sh.gate_up`, `sh.down` and
  * `sh.gate` tensors, src/engine.c:175-177): blob holds the gate|up matrix (2*ff x hidden) followed by the down matrix
  * (hidden x ff) at inzg_qmat_bytes(type, 2*ff, hidden) -- the layout of one expert blob; gate [hidden] fp32. Once

@@ -6,4 +6,5 @@ configurations. Importing the package requires the built library (no fallback pa
 """
 from ._lib import LIB_PATH, InzgError, T_F16, T_Q4L, T_Q8G, lib  # noqa: F401
 from .moe import MoePool  # noqa: F401
+from .gguf import GgufExperts  # noqa: F401
 from . import synth  # noqa: F401

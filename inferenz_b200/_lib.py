@@ -27,6 +27,11 @@ class MoeOpts(ctypes.Structure):
                 ("stream", ctypes.c_void_p)]
 
 
+class GgufInfo(ctypes.Structure):
+    _fields_ = [("expert_type", ctypes.c_int), ("blob_bytes", ctypes.c_uint64), ("n_layers", ctypes.c_int),
+                ("has_mtp", ctypes.c_int), ("alignment", ctypes.c_uint64), ("data_offset", ctypes.c_uint64)]
+
+
 class Stats(ctypes.Structure):
     _fields_ = [("calls", ctypes.c_uint64), ("tokens", ctypes.c_uint64), ("units", ctypes.c_uint64),
                 ("dec_units", ctypes.c_uint64), ("gemm_units", ctypes.c_uint64), ("pool_bytes", ctypes.c_uint64),
@@ -58,6 +63,11 @@ SIGNATURES = {
     "inzg_device_status": (I, [P, P]),
     "inzg_set_shared": (I, [P, I, I, P, U64, P]),
     "inzg_shared_expert": (I, [P, I, I, P, P, I, P]),
+    "inzg_gguf_open": (P, [ctypes.c_char_p, ctypes.POINTER(GgufInfo), ctypes.c_char_p, ctypes.c_size_t]),
+    "inzg_gguf_get_info": (I, [P, ctypes.POINTER(GgufInfo)]),
+    "inzg_gguf_experts": (I, [P, I, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(U64), ctypes.POINTER(U64)]),
+    "inzg_pool_add_layer_gguf": (I, [P, I, P, I]),
+    "inzg_gguf_close": (None, [P]),
     # inzg_tools.h
     "inzg_synth_jump": (U64, [U64, U64]),
     "inzg_synth_randn": (U64, [U64, I64, F, P]),

@@ -355,6 +355,26 @@ inzg_status inzg_set_router(inzg_ctx *c, int layer, const uint16_t *w, int rows,
     return INZG_OK;
 }
 
+// setup_experts' checks on the file (src/engine.c:339-350), then the pool upload from the mapping
+inzg_status inzg_pool_add_layer_gguf(inzg_ctx *c, int layer, const inzg_gguf *g, int gguf_layer) {
+    if (!c) return INZG_BAD_ARG;
+    inzg_gguf_info info;
+    if (inzg_gguf_get_info(g, &info) != INZG_OK) return fail(c, INZG_BAD_ARG, "pool_add_layer_gguf: no GGUF file");
+    char name[64];
+    if (gguf_layer < info.n_layers) snprintf(name, sizeof(name), "blk.%d.experts", gguf_layer);
+    else snprintf(name, sizeof(name), "mtp.experts");
+    const void *data = nullptr;
+    uint64_t nbytes = 0;
+    if (inzg_gguf_experts(g, gguf_layer, &data, &nbytes, nullptr) != INZG_OK)
+        return fail(c, INZG_BAD_ARG, std::string("pool_add_layer_gguf: the file has no ") + name);
+    if (!info.blob_bytes || info.blob_bytes % 4096)
+        return fail(c, INZG_CORRUPT_BLOB, "pool_add_layer_gguf: expert blob size " + std::to_string(info.blob_bytes) +
+                                              " is not a positive multiple of 4096");
+    if (nbytes / info.blob_bytes < (uint64_t)c->cfg.n_expert)
+        return fail(c, INZG_CORRUPT_BLOB, std::string("pool_add_layer_gguf: missing or short ") + name);
+    return inzg_pool_add_layer(c, layer, info.expert_type, data, info.blob_bytes, c->cfg.n_expert);
+}
+
 inzg_status inzg_pool_add_layer(inzg_ctx *c, int layer, int type, const void *blobs, uint64_t blob_bytes, int n_expert) {
     if (!c) return INZG_BAD_ARG;
     if (n_expert != c->cfg.n_expert) return fail(c, INZG_BAD_ARG, "pool_add_layer: n_expert differs from the context");

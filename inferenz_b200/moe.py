@@ -62,6 +62,12 @@ class MoePool:
         self._check(lib.inzg_pool_add_layer(self._ctx, layer, expert_type, _ptr(b), blob_bytes, self.n_expert),
                     "pool_add_layer")
 
+    def add_layer_gguf(self, layer, gguf, gguf_layer=None):
+        """Pool slot `layer` from an open :class:`inferenz_b200.gguf.GgufExperts` file (its layer `gguf_layer`,
+        default `layer`), with the engine's checks on the file; uploads straight from the file mapping."""
+        self._check(lib.inzg_pool_add_layer_gguf(self._ctx, layer, gguf.handle, layer if gguf_layer is None else gguf_layer),
+                    "pool_add_layer_gguf")
+
     def add_layer_range(self, layer, expert_type, blobs, blob_bytes, e_first, n_local):
         """Experts [e_first, e_first + n_local) only (expert parallelism); blobs holds those n_local blobs."""
         b = np.ascontiguousarray(blobs, dtype=np.uint8)

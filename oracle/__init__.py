@@ -202,6 +202,44 @@ class Ref:
         return yo, D
 
 
+class RefGguf:
+    """The reference's own GGUF reader and writer (src/gguf.c) through _ref/libinzref_gguf.so (ref_gguf.c)."""
+
+    def __init__(self):
+        path = os.path.join(REF_DIR, "libinzref_gguf.so")
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        self.lib = ctypes.CDLL(path)
+        self.lib.ref_gguf_tensor.restype = I
+        self.lib.ref_gguf_tensor.argtypes = [ctypes.c_char_p, ctypes.c_char_p, P, P, P, P, P, ctypes.c_char_p,
+                                             ctypes.c_size_t]
+        self.lib.ref_gguf_write.restype = I
+        self.lib.ref_gguf_write.argtypes = [ctypes.c_char_p, U64, I, I, U32, U64, I, P, U64]
+
+    def tensor(self, path, name):
+        """setup_experts' view of tensor `name` (src/engine.c:337-350): None when gguf_open fails or the tensor is
+        absent, else a dict of its absolute offset and size, the expert type, blob size and alignment."""
+        off, nb, al = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
+        et, bb = ctypes.c_int64(), ctypes.c_int64()
+        err = ctypes.create_string_buffer(256)
+        rc = self.lib.ref_gguf_tensor(str(path).encode(), name.encode(), ctypes.byref(off), ctypes.byref(nb),
+                                      ctypes.byref(et), ctypes.byref(bb), ctypes.byref(al), err, len(err))
+        if rc != 0:
+            return None
+        return {"offset": off.value, "nbytes": nb.value, "expert_type": et.value, "blob_bytes": bb.value,
+                "alignment": al.value}
+
+    def write(self, path, blobs, blob_bytes, n_expert, n_layers, mtp=False, expert_type=T_Q4L, alignment=32,
+              extra_floats=0):
+        """A model-shaped GGUF written by the reference's writer (ref_gguf.c). blobs: the expert tensors of the
+        n_layers layers (then mtp.experts when mtp), n_expert * blob_bytes bytes each, back to back."""
+        b = np.ascontiguousarray(blobs, dtype=np.uint8)
+        assert b.size == blob_bytes * n_expert * (n_layers + int(mtp))
+        rc = self.lib.ref_gguf_write(str(path).encode(), alignment, n_layers, int(mtp), expert_type, blob_bytes,
+                                     n_expert, _p(b), extra_floats)
+        assert rc == 0, "reference GGUF writer failed"
+
+
 def routing(orc, router, xin, bias=None, override=None, topk=10):
     """Experts selected per token (oracle arithmetic), to know which experts a test must quantize."""
     lg = override.copy() if override is not None else orc.router_logits(router, xin)
