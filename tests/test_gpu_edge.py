@@ -5,6 +5,7 @@
   crosses the reference's path rule (GEMM_MIN_T = 12, src/model_fwd.c:126, 229-249) onto the GEMM numerics; at 300
   each expert spans three token tiles of the tcgen05 GEMM, the last one ragged.
 * Ragged batch sizes (not multiples of 8, 32 or 64) with a skewed N(0,1) logit bias.
+* Exact ties in the router probabilities: the top-k follows the reference's order (lower index first).
 * Sizes the context refuses: 0 tokens and more than its max_tokens (INZG_BAD_ARG, nothing launched).
 
 Bar: routing bit-exact, outputs within 1e-3 relative L2 per token (north_star).
@@ -79,3 +80,14 @@ def test_refused_sizes():
             with pytest.raises(InzgError) as ei:
                 pool.moe_block(0, bad)
             assert ei.value.status == 1  # INZG_BAD_ARG
+
+
+def test_exact_ties_pick_the_lower_index(orc):
+    # integer-valued logits: most probabilities tie exactly, and the top-k must follow the reference's total order
+    # (probability descending, then index ascending: src/sampler.c:95-127, tests/test_regressions.py:17-31)
+    n = 32
+    ov = np.round(synth.normal_logits(n) * 1.5).astype(np.float32)
+    sel = oracle.routing(orc, synth.router(0, E, H), synth.hidden(n, H), override=ov)
+    p = np.take_along_axis(ov, sel, axis=1)
+    assert (np.diff(p, axis=1) == 0).any()  # the case has ties inside the top-10
+    _run_case(orc, n, override=ov)
