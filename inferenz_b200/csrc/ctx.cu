@@ -535,7 +535,7 @@ static int enqueue_shared(inzg_ctx *c, int layer, int n, const float *X, float *
     R.cnt = c->sh_cnt; R.off = c->sh_off; R.first = c->sh_first; R.etok = c->sh_etok; R.eslot = c->sh_eslot;
     R.ew = c->sh_ew; R.units = c->sh_units; R.meta = c->sh_meta; R.dec_units = c->sh_dec; R.gemm_units = c->sh_gemm;
     R.gemm_tiles = c->sh_tiles;
-    launches += launch_shared_route(R, n, gemm, gemv_items_per_unit(D, 0), gemv_items_per_unit(D, 1), gemm_token_tile(),
+    launches += launch_shared_route(R, n, gemm, gemv_items_per_unit(D, 0, R.n), gemv_items_per_unit(D, 1, R.n), gemm_token_tile(),
                                     c->sh_upath, c->sh_eexp, st);
     const bool tc = c->have_tc && S.has_maps;
     const int max_tiles = (n + gemm_token_tile() - 1) / gemm_token_tile() + 1;
@@ -596,7 +596,7 @@ static int enqueue_forward(inzg_ctx *c, int layer, const LayerSlot &L, int n, co
     R.ew = c->ew; R.ccnt = c->ccnt; R.cmask = c->cmask; R.units = c->units; R.meta = c->meta; R.dec_units = c->dec_units;
     R.gemm_units = c->gemm_units; R.gemm_tiles = c->gemm_tiles;
     const bool tc = !simt_gemm && c->have_tc && L.has_maps;
-    const int fused = launch_route_fused(R, c->logits, dump ? c->probs : nullptr, gemv_items_per_unit(D, 0), gemv_items_per_unit(D, 1),
+    const int fused = launch_route_fused(R, c->logits, dump ? c->probs : nullptr, gemv_items_per_unit(D, 0, R.n), gemv_items_per_unit(D, 1, R.n),
                                          gemm_token_tile(), c->upath, c->eexp, st);
     if (fused > 0) {
         launches += fused;
@@ -609,7 +609,7 @@ static int enqueue_forward(inzg_ctx *c, int layer, const LayerSlot &L, int n, co
         launches += launch_act_quant_x(X, n, H, D.gu_rot, D.gu_seed, c->xq64, c->xsb64, any_gemm ? c->xq256 : nullptr,
                                        c->xs256, st);
     mark(3);
-    if (fused <= 0) launches += launch_route(R, gemv_items_per_unit(D, 0), gemv_items_per_unit(D, 1), gemm_token_tile(), c->upath, c->eexp, st);
+    if (fused <= 0) launches += launch_route(R, gemv_items_per_unit(D, 0, R.n), gemv_items_per_unit(D, 1, R.n), gemm_token_tile(), c->upath, c->eexp, st);
     const int nkbH = (H + kKB - 1) / kKB;
     const int max_tiles = (NE + gemm_token_tile() - 1) / gemm_token_tile() + std::min(E, NE / kGemmMinT) + 1;
     if (branch) cudaStreamWaitEvent(st, c->join, 0);
@@ -814,7 +814,7 @@ inzg_status inzg_moe_experts(inzg_ctx *c, int layer, int m, const float *x_dev, 
     R.cnt = c->cnt; R.off = c->off; R.first = c->first; R.etok = c->etok; R.eslot = c->eslot;
     R.ew = c->ew; R.ccnt = c->ccnt; R.cmask = c->cmask; R.units = c->units; R.meta = c->meta; R.dec_units = c->dec_units;
     R.gemm_units = c->gemm_units; R.gemm_tiles = c->gemm_tiles;
-    launch_route(R, gemv_items_per_unit(D, 0), gemv_items_per_unit(D, 1), gemm_token_tile(), c->upath,
+    launch_route(R, gemv_items_per_unit(D, 0, R.n), gemv_items_per_unit(D, 1, R.n), gemm_token_tile(), c->upath,
                  c->eexp, st);
     const bool tc = c->have_tc && L.has_maps;
     const int nkbH = (H + kKB - 1) / kKB;

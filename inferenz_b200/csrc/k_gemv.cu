@@ -75,11 +75,15 @@ __device__ __forceinline__ void mma_u8s8_c(int (&d)[4], uint32_t a0, uint32_t a1
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c));
 }
 
-template <bool Q8, int NG, int KIND>
+template <bool Q8, int NG, int KIND, int W = 8>
 struct DecGeo {
-    static constexpr int WARPS = 8;                  // consumer warps; one 16-row tile each -> 128 rows per item
-    static constexpr int STAGES = 4;
-    static constexpr int KC = Q8 ? 4 : 8;            // 64-groups per stage
+    // Consumer warps, one 16-row tile each: an item is up to W row tiles of one expert matrix (the last item of a
+    // matrix holds the remaining tiles). W = 8: 9 warps per CTA, items of 128 rows, for calls of a few tokens whose
+    // items are fewer than the SMs. W = 15: 16 warps per CTA -- 4 per SM sub-partition, whose 16 K registers then
+    // allow 128 per thread -- so twice the warps hide the latency of the decode -> MMA -> fold chains.
+    static constexpr int WARPS = W;
+    static constexpr int STAGES = (W > 8 && NG >= 40) ? 3 : 4;
+    static constexpr int KC = W > 8 ? (Q8 ? 2 : 4) : (Q8 ? 4 : 8);  // 64-groups per stage
     static constexpr int NCH = (NG + KC - 1) / KC;   // stages per item
     static constexpr int NG8 = NG & ~7;
     static constexpr int WB = Q8 ? 32 : 16;          // weight bytes per lane per group
@@ -100,7 +104,7 @@ struct DecGeo {
 // (e == kDecEnd: the work queue is empty).
 constexpr int kDecEnd = -3;
 struct DecItem {
-    int e, base, ntok, rb;
+    int e, base, ntok, rb, ntiles;
     uint4 lut;
     int oslot[16];
     float ow[16];
@@ -113,10 +117,10 @@ struct DecShared {
 };
 
 // Consumer: the item's TC >= ntok tokens on this warp's 16-row tile. q: running stage counter (advanced by NCH).
-template <bool Q8, int NG, int KIND, int TC>
+template <bool Q8, int NG, int KIND, int W, int TC>
 __device__ __forceinline__ bool dec_item(DecShared &S, const uint8_t *stages, const uint8_t *ib, const DecItem &it,
                                          int &q, float *__restrict__ out, int out_ld, uint32_t one) {
-    using G = DecGeo<Q8, NG, KIND>;
+    using G = DecGeo<Q8, NG, KIND, W>;
     volatile int *abort = &S.abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gr = lane >> 2, t = lane & 3;
     // Tokens go through the MMAs in pairs (A = 2p, B = 2p + 1). Column n = gr of the activation operand carries token
@@ -132,7 +136,7 @@ __device__ __forceinline__ bool dec_item(DecShared &S, const uint8_t *stages, co
     // scale pairs (d[r][g], d[r+8][g]) of this warp's row tile: word (g / 4) * 32 + gr * 4 + g % 4
     const uint32_t *wd = reinterpret_cast<const uint32_t *>(ib + G::IB_D + (size_t)warp * G::GD * 128) + gr * 4;
     const uint4 T = it.lut;
-    const bool valid = it.e >= 0;
+    const bool valid = it.e >= 0 && warp < it.ntiles;  // the last item of a matrix may hold fewer tiles than warps
     const int ntok = it.ntok;
     constexpr int NP = (TC + 1) / 2;
     const int jcol = gr >> 2, jd = t >> 1;  // token of this thread's operand column / of its accumulator columns
@@ -277,19 +281,19 @@ __device__ __forceinline__ bool dec_item(DecShared &S, const uint8_t *stages, co
     return true;
 }
 
-template <bool Q8, int NG, int KIND>
-__global__ void __launch_bounds__(DecGeo<Q8, NG, KIND>::THREADS, 1)
+template <bool Q8, int NG, int KIND, int W>
+__global__ void __launch_bounds__(DecGeo<Q8, NG, KIND, W>::THREADS, 1)
     gemv_decode_kernel(const uint8_t *__restrict__ pool, uint64_t slab_bytes, MatLayout M, const uint8_t *__restrict__ luts,
                        int lut_off, int E, RouteDev R, const int8_t *__restrict__ aq, const float2 *__restrict__ asb,
                        float *__restrict__ out, int out_ld, int meta_items, int meta_work, uint32_t one) {
-    using G = DecGeo<Q8, NG, KIND>;
+    using G = DecGeo<Q8, NG, KIND, W>;
     extern __shared__ __align__(1024) uint8_t smem[];
     DecShared &S = *reinterpret_cast<DecShared *>(smem);
     uint8_t *stages = smem + G::HDR;
     uint8_t *ibufs = stages + (size_t)G::STAGES * G::STAGE;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nitems = R.meta[meta_items];
-    const int per = M.rows / (16 * G::WARPS);
+    const int tiles = M.rows / 16, per = (tiles + G::WARPS - 1) / G::WARPS;  // items per matrix
     if ((int)blockIdx.x >= nitems) return;
     if (threadIdx.x == 0) {
         for (int i = 0; i < G::STAGES; i++) { mbar_init(&S.full[i], 1); mbar_init(&S.empty[i], G::WARPS); }
@@ -338,16 +342,16 @@ __global__ void __launch_bounds__(DecGeo<Q8, NG, KIND>::THREADS, 1)
                 row = KIND == 0 ? __ldg(R.etok + base + lane) : base + lane;
                 if (KIND == 1) { D.oslot[lane] = __ldg(R.eslot + base + lane); D.ow[lane] = __ldg(R.ew + base + lane); }
             }
-            const int rt0 = (item % per) * G::WARPS;
+            const int rt0 = (item % per) * G::WARPS, nt = tiles - rt0 < G::WARPS ? tiles - rt0 : G::WARPS;
             const uint8_t *slab = pool + (size_t)(e < 0 ? 0 : e) * slab_bytes;
             if (lane == 0) {
-                D.e = e; D.base = base; D.ntok = ntok; D.rb = item % per;
+                D.e = e; D.base = base; D.ntok = ntok; D.rb = item % per; D.ntiles = nt;
                 D.lut = (!Q8 && e >= 0) ? __ldg(reinterpret_cast<const uint4 *>(luts + (size_t)e * 32 + lut_off))
                                         : make_uint4(0, 0, 0, 0);
             }
             __syncwarp();
             uint8_t *ib = ibufs + (size_t)ab * G::IBUF;
-            const uint32_t dbytes = e >= 0 ? (uint32_t)(G::WARPS * G::GD * 128) : 0u;
+            const uint32_t dbytes = e >= 0 ? (uint32_t)(nt * G::GD * 128) : 0u;
             if (lane == 0) mbar_expect_tx(&S.afull[ab], (uint32_t)(ntok * (G::K + NG * 8)) + dbytes);
             __syncwarp();
             if (KIND == 0) {
@@ -362,18 +366,18 @@ __global__ void __launch_bounds__(DecGeo<Q8, NG, KIND>::THREADS, 1)
             if (lane == 31 && e >= 0)
                 bulk_g2s(ib + G::IB_D, slab + M.d_off + (size_t)rt0 * G::GD * 128, dbytes, &S.afull[ab]);
             na++;
-            // weights of the item's 8 row tiles, one stage per KC groups
+            // weights of the item's nt row tiles, one stage per KC groups
             for (int c = 0; c < G::NCH; c++, q++) {
                 const int s = q % G::STAGES;
                 if (q >= G::STAGES && !mbar_wait(&S.empty[s], ((q / G::STAGES) + 1) & 1, abort)) { ok = false; break; }
                 const int g0 = c * G::KC, kc = NG - g0 < G::KC ? NG - g0 : G::KC;
                 const uint32_t wbytes = (uint32_t)(kc * 32 * G::WB);
                 if (lane == 0) {
-                    if (e >= 0) mbar_expect_tx(&S.full[s], G::WARPS * wbytes);
+                    if (e >= 0) mbar_expect_tx(&S.full[s], nt * wbytes);
                     else mbar_arrive(&S.full[s]);
                 }
                 __syncwarp();
-                if (e >= 0 && lane < G::WARPS)
+                if (e >= 0 && lane < nt)
                     bulk_g2s(stages + (size_t)s * G::STAGE + (size_t)lane * G::WQ,
                              slab + M.q_off + ((size_t)(rt0 + lane) * NG + g0) * 32 * G::WB, wbytes, &S.full[s]);
             }
@@ -403,13 +407,13 @@ __global__ void __launch_bounds__(DecGeo<Q8, NG, KIND>::THREADS, 1)
         const uint8_t *ib = ibufs + (size_t)ab * G::IBUF;
         const int nt = it.ntok;
         bool ok;
-        if (nt <= 1) ok = dec_item<Q8, NG, KIND, 1>(S, stages, ib, it, q, out, out_ld, one);
-        else if (nt <= 2) ok = dec_item<Q8, NG, KIND, 2>(S, stages, ib, it, q, out, out_ld, one);
-        else if (nt <= 3) ok = dec_item<Q8, NG, KIND, 3>(S, stages, ib, it, q, out, out_ld, one);
-        else if (nt <= 4) ok = dec_item<Q8, NG, KIND, 4>(S, stages, ib, it, q, out, out_ld, one);
-        else if (nt <= 6) ok = dec_item<Q8, NG, KIND, 6>(S, stages, ib, it, q, out, out_ld, one);
-        else if (nt <= 8) ok = dec_item<Q8, NG, KIND, 8>(S, stages, ib, it, q, out, out_ld, one);
-        else ok = dec_item<Q8, NG, KIND, 12>(S, stages, ib, it, q, out, out_ld, one);
+        if (nt <= 1) ok = dec_item<Q8, NG, KIND, W, 1>(S, stages, ib, it, q, out, out_ld, one);
+        else if (nt <= 2) ok = dec_item<Q8, NG, KIND, W, 2>(S, stages, ib, it, q, out, out_ld, one);
+        else if (nt <= 3) ok = dec_item<Q8, NG, KIND, W, 3>(S, stages, ib, it, q, out, out_ld, one);
+        else if (nt <= 4) ok = dec_item<Q8, NG, KIND, W, 4>(S, stages, ib, it, q, out, out_ld, one);
+        else if (nt <= 6) ok = dec_item<Q8, NG, KIND, W, 6>(S, stages, ib, it, q, out, out_ld, one);
+        else if (nt <= 8) ok = dec_item<Q8, NG, KIND, W, 8>(S, stages, ib, it, q, out, out_ld, one);
+        else ok = dec_item<Q8, NG, KIND, W, 12>(S, stages, ib, it, q, out, out_ld, one);
         if (!ok) break;
         __syncwarp();
         if (lane == 0) mbar_arrive(&S.aempty[ab]);
@@ -419,23 +423,28 @@ __global__ void __launch_bounds__(DecGeo<Q8, NG, KIND>::THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-template <bool Q8, int NG, int KIND>
+template <bool Q8, int NG, int KIND, int W>
 static void launch_one(const LayerDev &L, const MatLayout &M, const RouteDev &R, const int8_t *aq, const float2 *asb,
                        float *out, int out_ld, int meta_items, int num_sms, cudaStream_t st) {
-    using G = DecGeo<Q8, NG, KIND>;
+    using G = DecGeo<Q8, NG, KIND, W>;
     static_assert(G::SMEM <= 227 * 1024, "decode GEMV shared memory");
     static_assert(sizeof(DecShared) <= G::HDR, "decode GEMV header");
-    cudaFuncSetAttribute(gemv_decode_kernel<Q8, NG, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
-    gemv_decode_kernel<Q8, NG, KIND><<<num_sms, G::THREADS, G::SMEM, st>>>(
+    static_assert(G::WARPS < 32, "one producer lane per row tile");
+    cudaFuncSetAttribute(gemv_decode_kernel<Q8, NG, KIND, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
+    gemv_decode_kernel<Q8, NG, KIND, W><<<num_sms, G::THREADS, G::SMEM, st>>>(
         L.pool, L.slab_bytes, M, L.luts, KIND == 0 ? 0 : 16, L.E, R, aq, asb, out, out_ld, meta_items,
         KIND == 0 ? kMetaWorkGU : kMetaWorkDN, 1u);
 }
 
-constexpr int kRowsPerItem = 128;  // 8 consumer warps x 16 rows
+// Row tiles per item for a call of n token rows: wide items (15 tiles, 16 warps per CTA) once the call has enough
+// work to occupy every SM (4 tokens give about 40 experts: 200 gate|up and 360 down items); 8 tiles below that, so a
+// few experts still spread over many SMs. The route kernels size the work queue with the same rule.
+static int tiles_per_item(int n) { return n >= 4 ? 15 : 8; }
 
-int gemv_items_per_unit(const LayerDev &L, int kind) {
+int gemv_items_per_unit(const LayerDev &L, int kind, int n) {
     const MatLayout &M = kind == 0 ? L.gu : L.dn;
-    return M.rows / kRowsPerItem;
+    const int W = tiles_per_item(n);
+    return (M.rows / 16 + W - 1) / W;
 }
 
 // Returns the number of kernels launched, 0 for a geometry probe (kind 2/3), or -1 if the geometry has no
@@ -450,12 +459,18 @@ int launch_gemv_decode(const LayerDev &L, int kind, const RouteDev &R, const int
     const MatLayout &M = kind == 0 ? L.gu : L.dn;
     const int mi = kind == 0 ? kMetaDecItemsGU : kMetaDecItemsDN;
     const bool q8 = L.type == INZG_T_Q8G;
-    if (M.rows % kRowsPerItem) return -1;
+    if (M.rows % 16) return -1;
+    const bool wide = tiles_per_item(R.n) == 15;
 #define INZG_GEMV_CASE(Q, N)                                                                                     \
     if (q8 == Q && M.ng == N) {                                                                                  \
         if (probe) return 0;                                                                                     \
-        if (kind == 0) launch_one<Q, N, 0>(L, M, R, aq, asb, out, out_ld, mi, num_sms, st);                     \
-        else launch_one<Q, N, 1>(L, M, R, aq, asb, out, out_ld, mi, num_sms, st);                               \
+        if (kind == 0) {                                                                                         \
+            if (wide) launch_one<Q, N, 0, 15>(L, M, R, aq, asb, out, out_ld, mi, num_sms, st);                  \
+            else launch_one<Q, N, 0, 8>(L, M, R, aq, asb, out, out_ld, mi, num_sms, st);                        \
+        } else {                                                                                                 \
+            if (wide) launch_one<Q, N, 1, 15>(L, M, R, aq, asb, out, out_ld, mi, num_sms, st);                  \
+            else launch_one<Q, N, 1, 8>(L, M, R, aq, asb, out, out_ld, mi, num_sms, st);                        \
+        }                                                                                                        \
         return 1;                                                                                                \
     }
     INZG_GEMV_CASE(false, 32)   // Q4L K = 2048

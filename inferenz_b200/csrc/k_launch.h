@@ -36,7 +36,7 @@ int launch_shared_route(const RouteDev &R, int n, int gemm, int gu_items_per_uni
 void gemv_set_attributes();
 int launch_gemv_decode(const LayerDev &L, int kind, const RouteDev &R, const int8_t *aq, const float2 *asb, float *out,
                        int out_ld, int num_sms, cudaStream_t st);
-int gemv_items_per_unit(const LayerDev &L, int kind);
+int gemv_items_per_unit(const LayerDev &L, int kind, int n);  // n: token rows of the call (R.n)
 int launch_gemm_v1(const LayerDev &L, int kind, const RouteDev &R, const int8_t *aq, const float *as, float *out,
                    int out_ld, int grid, cudaStream_t st);
 int gemm_token_tile();
