@@ -17,12 +17,13 @@
 // (packed f32x2 instructions, each lane rounded as its own fma), and hsum8 becomes one add per lane pair and one quad
 // shuffle that pair the lanes as the reference does: ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7)).
 //
-// Pipeline (one CTA per SM, persistent): an item is 128 rows (8 row tiles) of one decode expert's matrix. A producer
-// warp takes items from the call's work queue (experts with the most tokens first), brings the item's token
-// activations, their (s, bsum) and the 8 row tiles' scales into a double-buffered item buffer, and streams the
-// weights in stages of 8 (Q4L) or 4 (Q8G) 64-groups through a 4-deep ring -- all with bulk copies (cp.async.bulk on the
-// TMA engine, completion counted on mbarriers). 8 consumer warps each own one 16-row tile of the item: per group, the
-// LUT decode of the weight fragment, then two MMAs and the reference's fma per token. The bias chains need only the
+// Pipeline (one CTA per SM, persistent): an item is up to W row tiles of 16 rows of one decode expert's matrix (W = 15
+// for calls of 4 tokens or more, 8 below; the last item of a matrix holds the remaining tiles). A producer warp takes
+// items from the call's work queue (experts with the most tokens first), brings the item's token activations, their
+// (s, bsum) and the item's row-tile scales into a double-buffered item buffer, and streams the weights in stages of
+// 2-8 64-groups through a 3- or 4-deep ring -- all with bulk copies (cp.async.bulk on the TMA engine, completion
+// counted on mbarriers). W consumer warps each own one 16-row tile of the item: per group, the LUT decode of the
+// weight fragment, then two MMAs and the reference's fma per token. The bias chains need only the
 // scales and bsum, so they run once per item in the epilogue. Every wait is bounded; a CTA that gives up records
 // INZG_TIMEOUT and drains its copies before it leaves.
 #include "inzg_internal.h"
@@ -92,7 +93,7 @@ struct DecGeo {
     static constexpr int STAGE = WARPS * WQ;
     static constexpr int K = NG * kGroup;
     static constexpr int MT = 12;                    // most tokens of a decode expert: 11 (8 when n <= 8)
-    // item buffer: token activations [MT][K], their (s, bsum) [MT][NG], the 8 row tiles' scales [8][GD][8][4][2]
+    // item buffer: token activations [MT][K], their (s, bsum) [MT][NG], the row tiles' scales [WARPS][GD][8][4][2]
     static constexpr int IB_SB = MT * K, IB_D = IB_SB + MT * NG * 8;
     static constexpr int IBUF = ((IB_D + WARPS * GD * 128) + 127) / 128 * 128;
     static constexpr int HDR = 1024;
