@@ -461,7 +461,7 @@ def run_ep(args):
     dist.destroy_process_group()
 
 
-def cpu_reference(cfg, n, budget_s=12.0, blobs=None, bb=None, R=None, steps=None, warmup=1):
+def cpu_reference(cfg, n, budget_s=12.0, blobs=None, bb=None, R=None, steps=None, warmup=3):
     """The reference's own CPU layer (oracle/_ref, all host threads) on a bounded sample of the workload."""
     import oracle
     from inferenz_b200 import synth
