@@ -40,6 +40,16 @@ EXPERT_BYTES_Q8G = 4055168
 ROUTER_BYTES = E * H * 2
 
 
+NVLINK_GBS = 770.0  # peer copy, per direction per GPU, measured on this pool's B200s (900 GB/s nominal)
+
+
+def ep_fixed_exchange_bytes(world, capacity, hidden=H, topk=K):
+    """Bytes one GPU sends -- and receives -- over NVLink per step of ExpertParallelMoE.moe_block_fixed: to each of
+    the world-1 other ranks a block of `capacity` fp32 token rows with their (local expert, weight) pairs, and the
+    capacity x topk fp32 result rows back. The block a rank keeps for itself crosses no link."""
+    return (world - 1) * capacity * (4 * hidden + 8 * topk + 4 * topk * hidden)
+
+
 def peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -425,6 +435,7 @@ def run_ep(args):
     units_all = int(sum(r[2] for r in per_rank))
     # per GPU: router + its experts' weights + its tokens in and out
     bytes_gpu = ROUTER_BYTES + local_units * EXPERT_BYTES_Q4L + 2 * n_loc * H * 4
+    xb = ep_fixed_exchange_bytes(world, n_loc)  # the step's NVLink bytes per GPU and direction
     if rank == 0:
         ach = bytes_gpu / (ms_step * 1e-3) / 1e9
         line = {
@@ -440,6 +451,9 @@ def run_ep(args):
                          "algorithmic_bytes": bytes_gpu, "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(ach / hbm, 4), "peak_kind": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)",
                          "traffic": None},
+            "nvlink": {"bytes_out_per_gpu": xb, "achieved": round(xb / (ms_step * 1e-3) / 1e9, 1),
+                       "peak": NVLINK_GBS, "unit": "GB/s", "frac": round(xb / (ms_step * 1e-3) / 1e9 / NVLINK_GBS, 4),
+                       "peak_kind": "measured peer copy per direction (900 nominal)"},
             "cpu_baseline": None,
             "e2e": {"value": round(nb * e2e_steps / e2e_s, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": n_loc * H * 4 * world, "d2h_bytes_per_step": n_loc * H * 4 * world},

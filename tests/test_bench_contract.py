@@ -1,6 +1,7 @@
 """bench.py's reference arm on the CPU: one JSON line with the keys the benchmark contract asks for, and under
 torchrun only rank 0 prints it (the other ranks exit 0 without work). The arm times the reference's own compiled
-MoE layer (oracle/_ref), or the oracle's C restatement when the reference could not be built here."""
+MoE layer (oracle/_ref), or the oracle's C restatement when the reference could not be built here. Also the
+NVLink byte count the expert-parallel line reports its link fraction from."""
 import json
 import os
 import subprocess
@@ -38,3 +39,11 @@ def test_reference_arm_prints_one_contract_line():
 
 def test_reference_arm_other_ranks_exit_quietly():
     assert _bench({"RANK": "1", "WORLD_SIZE": "2"}) == []
+
+
+def test_ep_exchange_bytes():
+    sys.path.insert(0, ROOT)
+    import bench
+    assert bench.ep_fixed_exchange_bytes(1, 32) == 0  # one GPU: nothing crosses a link
+    # 8 GPUs, 32 rows per rank pair: 7 peers x 32 x (8192 B row + 80 B (expert, weight) pairs + 81920 B of results)
+    assert bench.ep_fixed_exchange_bytes(8, 32) == 7 * 32 * (8192 + 80 + 81920) == 20203008
