@@ -72,3 +72,32 @@ def test_no_gpu_create_reports_cuda():
     st = ctypes.c_int(-1)
     assert not lib.inzg_create(ctypes.byref(Config(2048, 640, 512, 10, 16, 1, 0)), ctypes.byref(st))
     assert st.value == 4  # INZG_CUDA
+
+
+def test_c_host_compiles_links_and_runs(tmp_path):
+    """The public header is plain C: tests/c_host/moe_host.c (the engine's wiring, in C11) compiles with -Werror,
+    links against libinzg.so and reads a GGUF; without a GPU it stops at inzg_create with INZG_CUDA (exit 2)."""
+    import shutil
+    import subprocess
+    import sys
+    gcc = shutil.which("gcc", path="/usr/bin") or shutil.which("gcc")
+    if not gcc:
+        pytest.skip("no C compiler")
+    from inferenz_b200 import _lib
+    exe = str(tmp_path / "moe_host")
+    libdir = os.path.dirname(_lib.LIB_PATH)
+    subprocess.run([gcc, "-std=c11", "-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include"),
+                    os.path.join(ROOT, "tests", "c_host", "moe_host.c"), "-L", libdir, "-linzg",
+                    f"-Wl,-rpath,{libdir}", "-o", exe], check=True)
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import gguf_file as gf
+    model = str(tmp_path / "m.gguf")
+    gf.write(model, [("inz.expert_type", gf.U32, 102), ("inz.expert_blob_bytes", gf.U64, 4096)],
+             [("blk.0.experts", b"\0" * 8192), ("mtp.experts", b"\0" * 8192)])
+    p = subprocess.run([exe, model], capture_output=True, text=True, timeout=120)
+    assert "gguf: expert_type 102 blob_bytes 4096 layers 1 mtp 1" in p.stdout
+    import torch
+    if not torch.cuda.is_available():
+        assert p.returncode == 2 and "inzg_create: CUDA error" in p.stdout
+    bad = subprocess.run([exe, str(tmp_path / "missing.gguf")], capture_output=True, text=True, timeout=60)
+    assert bad.returncode == 1 and "open" in bad.stderr
