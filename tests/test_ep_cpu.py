@@ -1,4 +1,4 @@
-"""Expert-parallel exchange logic on CPU: world_size 2 (and 4) gloo ranks against one process.
+"""Expert-parallel exchange logic on CPU: 2, 4 and 8 gloo ranks (the scaling run's sizes) against one process.
 
 The backend is a deterministic stand-in for the GPU kernels (routing from a fixed projection, an expert that scales
 its rows by the expert id): the test checks that the dispatch, the local expert indices, the return of every
@@ -77,7 +77,8 @@ def _worker(rank, world, port, counts, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,counts", [(2, [5, 7]), (2, [1, 0]), (4, [3, 1, 4, 2])])
+@pytest.mark.parametrize("world,counts", [(2, [5, 7]), (2, [1, 0]), (4, [3, 1, 4, 2]),
+                                          (8, [4, 0, 2, 5, 1, 3, 0, 6])])
 def test_ep_exchange_matches_single_process(world, counts):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
