@@ -16,6 +16,7 @@ class GgufExperts:
         info = GgufInfo()
         err = ctypes.create_string_buffer(512)
         h = lib.inzg_gguf_open(str(path).encode(), ctypes.byref(info), err, len(err))
+        self._h = None
         if not h:
             raise InzgError(1, err.value.decode())
         self._h = h
@@ -53,6 +54,12 @@ class GgufExperts:
         if self._h:
             lib.inzg_gguf_close(self._h)
             self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
     def __enter__(self):
         return self
