@@ -100,3 +100,41 @@ def test_ep_exchange_matches_single_process(world, counts):
         assert np.array_equal(yf.view(np.uint32), want[lo:lo + counts[rank]].view(np.uint32))
         total_results += nres
     assert total_results == sum(counts) * K  # every (token, rank-k) result came home exactly once
+
+
+def _dead_peer_worker(rank, world, port, q):
+    import datetime
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:  # leaves before its side of the exchange: no collective posted, the process exits
+        q.put((rank, "left", 0.0))
+        return
+    x = torch.randn((3, H), generator=torch.Generator().manual_seed(1))
+    ep = ExpertParallelMoE(FakeBackend(rank, E // world), E, K, H)
+    t0 = time.time()
+    try:
+        ep.moe_block(0, x)
+        q.put((rank, "no error", time.time() - t0))
+    except Exception as e:  # the exchange reports the missing peer instead of waiting for it
+        q.put((rank, type(e).__name__, time.time() - t0))
+
+
+def test_ep_peer_that_never_posts_fails_instead_of_hanging():
+    """A rank that leaves before the dispatch exchange: the other rank's exchange ends with an error (the peer's
+    closed connection, at the latest the process group's 5 s timeout), not a hang -- the host-side detection of a
+    lost rank between steps."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dead_peer_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=120) for _ in range(2)])
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert res[1][1] == "left"
+    assert res[0][1] != "no error" and res[0][2] < 60.0, res[0]
