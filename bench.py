@@ -1,15 +1,18 @@
 """MoE-layer benchmark (the metric of BASELINE.json) on B200.
 
 Workload (headline, N=1): BASELINE configs[1] -- one MoE layer, d=2048, 512 experts, top-10, FF 640, Q4L experts
-(synthetic, seeded, quantized with the engine's own quantizer), F16 router, decode batch of 32 tokens with a
-per-expert N(0,1) logit bias. Sub-results under "extra": configs[0] shape (1 token), configs[2] (4096-token
-prefill, Zipf(1.1) bias) and configs[3] (Q8G experts, 2048 tokens, router logits replaced by N(0,1)).
+(synthetic, seeded, encoded by the engine's quantizer -- byte-identical to the reference's), F16 router, decode batch
+of 32 tokens with a per-expert N(0,1) logit bias. Sub-results under "extra": configs[0] shape (1 token), configs[2]
+(4096-token prefill, Zipf(1.1) bias) and configs[3] (Q8G experts, 2048 tokens, router logits replaced by N(0,1)).
+Every timed workload is checked once against the reference's own output on the same inputs (tests/golden/bench_*.npz,
+made by the compiled reference): routing bit for bit, outputs within 1e-3 relative L2 per token ("parity").
 
 value  = tokens/s with inputs resident in HBM; each timed step is one layer call timed with CUDA events on the
          launching stream; the L2 is flushed (512 MB write) before every step, outside the timed events.
 e2e    = the same through the public host API (MoePool.moe_block on pinned host buffers): H2D of the step's input and
          D2H of its output inside the timed region (host wall clock around the synchronous call).
---impl reference: the reference's own CPU implementation of the layer (oracle/_ref, all host cores).
+--impl reference: the reference's own CPU implementation of the layer (oracle/_ref, all host cores), on inputs drawn by
+         the oracle's generator and experts encoded by the reference's quantizer: this arm never loads libinzg.
 Multi-GPU (--gpus N under torchrun, one process per GPU): expert parallelism. Rank g holds
 experts [g*512/N, (g+1)*512/N) and decodes its own 32 tokens (weak scaling: 32*N tokens per step); a step routes
 the rank's tokens, sends each token row once to every GPU owning one of its experts (NCCL all-to-all), runs the local
@@ -40,7 +43,11 @@ EXPERT_BYTES_Q8G = 4055168
 ROUTER_BYTES = E * H * 2
 
 
-NVLINK_GBS = 770.0  # peer copy, per direction per GPU, measured on this pool's B200s (900 GB/s nominal)
+NVLINK_GBS = 770.0  # NVLink 5 peer copy per direction per GPU, the pool's published measurement (900 GB/s nominal)
+
+# the headline workload, worded identically by both arms at every N
+WORKLOAD = ("BASELINE configs[1]: MoE layer, decode batch of 32 tokens per GPU (32*N in all), d=2048, 512 experts, "
+            "top-10, FF 640, Q4L experts, F16 router, N(0,1) per-expert logit bias")
 
 
 def ep_fixed_exchange_bytes(world, capacity, hidden=H, topk=K):
@@ -121,6 +128,35 @@ def make_inputs(cfg, n):
     return x, bias, override
 
 
+def check_parity(name, route, y):
+    """One call's routing dump and output against the reference's output on the same workload
+    (tests/golden/bench_<name>.npz, made by the compiled reference): top-k, unit order and the exact bits of the
+    logits, probabilities and weights; per token, output norms and (for sampled tokens) whole rows within 1e-3
+    relative L2."""
+    import hashlib
+    path = os.path.join(ROOT, "tests", "golden", f"bench_{name}.npz")
+    if not os.path.exists(path):
+        return {"ok": False, "why": f"no fixture {os.path.basename(path)}"}
+    g = np.load(path)
+
+    def sha(a):
+        return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+    routing = {"sel": bool(np.array_equal(route["sel"], g["sel"])), "units": bool(np.array_equal(route["units"], g["units"])),
+               "w": sha(route["w"]) == str(g["w_sha"]), "logits": sha(route["logits"]) == str(g["logits_sha"]),
+               "probs": sha(route["probs"]) == str(g["probs_sha"])}
+    rows = g["y_rows"]
+    got, want = y[rows].astype(np.float64), g["y_sample"].astype(np.float64)
+    rel = np.linalg.norm(got - want, axis=1) / np.maximum(np.linalg.norm(want, axis=1), 1e-30)
+    nrm = np.linalg.norm(y.astype(np.float64), axis=1)
+    nrel = np.abs(nrm - g["y_norm"]) / np.maximum(g["y_norm"], 1e-30)
+    exact = float(np.mean(y[rows].view(np.uint32) == g["y_sample"].view(np.uint32)))
+    ok = all(routing.values()) and float(rel.max()) <= 1e-3 and float(nrel.max()) <= 1e-3
+    return {"ok": bool(ok), "routing_bit_exact": all(routing.values()), "routing": routing,
+            "rows_checked": int(len(rows)), "y_rel_l2_max": float(rel.max()), "y_norm_rel_max": float(nrel.max()),
+            "bit_identical_fraction": round(exact, 4), "reference_isa": str(g["isa"])}
+
+
 def time_device(pool, torch, x, bias, steps, warmup, flush, layer=0, override=None):
     """Per-step CUDA-event time (ms) of the layer on HBM-resident inputs."""
     n = x.shape[0]
@@ -172,10 +208,11 @@ def profile_stages(pool, torch, x, bias, reps, flush, layer=0, override=None):
                                   None if od is None else od.data_ptr(), stream=sh, profile=True)
     torch.cuda.synchronize(dev)
     st, calls = pool.stage_times(reset=True)
-    # routing summary of this input (one dumped call)
-    pool.moe_block(layer, x, bias=bias, logits_override=override, dump=True)
-    pool.route_dump(n)
+    # routing summary and parity of this input (one dumped call through the host API)
+    y = pool.moe_block(layer, x, bias=bias, logits_override=override, dump=True)
+    route = pool.route_dump(n)
     s = pool.stats()
+    s["route"], s["y"] = route, y
     return {k: v / max(calls, 1) for k, v in st.items()}, s
 
 
@@ -198,8 +235,18 @@ def time_e2e(pool, torch, x, bias, steps, warmup, flush):
     return ts, h2d, d2h, yp
 
 
-def stage_roofline(stage_ms, stats, n, hbm, q8g=False):
-    """Algorithmic bytes per launch of each stage; the dominant stage's achieved GB/s."""
+def gemm_tokens(route, n, E=E):
+    """Token-expert pairs on the prefill GEMM path: experts with >= 12 tokens, when the call has more than 8 tokens
+    (the reference's path rule, src/model_fwd.c:126, 229-249, 1071)."""
+    if n <= 8:
+        return 0
+    cnt = np.bincount(route["sel"].ravel(), minlength=E)
+    return int(cnt[cnt >= 12].sum())
+
+
+def stage_roofline(stage_ms, stats, n, hbm, q8g=False, i8_peak=None):
+    """Algorithmic bytes per launch of each stage; the dominant stage's achieved GB/s. GEMM stages also get their
+    int8 tensor-pipe fraction: ops = GEMM-path token-expert pairs x 2 x rows x K, against the measured int8 peak."""
     dec, gemm = stats["dec_units"], stats["gemm_units"]
     gu, dn = (GU_PAYLOAD_Q8G, DN_PAYLOAD_Q8G) if q8g else (GU_PAYLOAD, DN_PAYLOAD)
     algo = {
@@ -219,6 +266,16 @@ def stage_roofline(stage_ms, stats, n, hbm, q8g=False):
         ach = algo[dom] / (stage_ms[dom] * 1e-3) / 1e9
         out["roofline"] = {"bound": "hbm", "kernel": dom, "algorithmic_bytes": algo[dom], "achieved": round(ach, 1),
                            "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4)}
+    tg = gemm_tokens(stats["route"], n) if "route" in stats else 0
+    if tg and i8_peak:
+        tens = {}
+        for st, per in (("gate_up_gemm", 2 * (2 * FF) * H), ("down_gemm", 2 * H * FF)):
+            if stage_ms.get(st, 0) > 0:
+                tops = tg * per / (stage_ms[st] * 1e-3) / 1e12
+                tens[st] = {"ops": tg * per, "achieved": round(tops, 1), "peak": round(i8_peak, 1), "unit": "TOPS",
+                            "frac": round(tops / i8_peak, 4)}
+        out["tensor_roofline"] = {"bound": "tensor", "gemm_token_expert_pairs": tg, "stages": tens,
+                                  "peak_kind": "measured int8 tcgen05 probe (inzg_probe_tensor_i8)"}
     return out
 
 
@@ -230,6 +287,7 @@ def run_mine(args):
     rank, world, local = 0, 1, 0  # one GPU (--gpus N > 1 runs run_ep)
     dev = torch.device("cuda", local)
     hbm, bf16, peak_kind = peaks()
+    i8_peak = probe_i8(local)
     t0 = time.time()
     blobs, bb = synth.layer_blobs(0, synth.T_Q4L, H, FF, E)
     gen_s = time.time() - t0
@@ -269,7 +327,8 @@ def run_mine(args):
         total_ms = sum(ts)
         stage_ms, stats = profile_stages(pool, torch, x, bias, 0 if args.only else max(3, min(20, steps)), flush,
                                          layer, ovr)
-        roof = stage_roofline(stage_ms, stats, n, hbm, q8g=layer == 1)
+        roof = stage_roofline(stage_ms, stats, n, hbm, q8g=layer == 1, i8_peak=i8_peak)
+        parity = check_parity(name, stats.pop("route"), stats.pop("y"))
         U = stats["units"]
         # the override replaces the router in configs[3]: no router bytes there
         layer_bytes = (0 if ovr is not None else ROUTER_BYTES) + U * (EXPERT_BYTES_Q8G if layer == 1 else
@@ -279,7 +338,7 @@ def run_mine(args):
             "n_tokens": n, "steps": steps, "ms_per_step": round(ms_step, 5),
             "tokens_per_s": round(n * steps * world / (total_ms * 1e-3), 1),
             "units": U, "decode_units": stats["dec_units"], "gemm_units": stats["gemm_units"],
-            "launches_per_step": stats["last_launches"],
+            "launches_per_step": stats["last_launches"], "parity": parity,
             "layer_roofline": {"bound": "hbm", "algorithmic_bytes": layer_bytes,
                                "achieved": round(layer_bytes / (ms_step * 1e-3) / 1e9, 1), "peak": hbm,
                                "unit": "GB/s", "frac": round(layer_bytes / (ms_step * 1e-3) / 1e9 / hbm, 4)},
@@ -311,11 +370,10 @@ def run_mine(args):
             "metric": METRIC, "value": head["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8 x Q4L (fp32 accumulate)", "data": "synthetic (seeded; no dataset)",
-            "config": {"workload": "BASELINE configs[1]: MoE layer, decode batch of 32 tokens, d=2048, 512 experts, "
-                                   "top-10, FF 640, Q4L experts, F16 router, N(0,1) per-expert logit bias",
-                       "global_batch": 32 * world, "seq_len": 1,
-                       "parallelism": "single GPU",
-                       "l2": "flushed (512 MB write) before every timed step"},
+            "config": {"workload": WORKLOAD, "global_batch": 32 * world, "seq_len": 1},
+            "arm": {"parallelism": "single GPU", "l2": "flushed (512 MB write) before every timed step",
+                    "int8_tensor_peak_tops": i8_peak},
+            "parity": {k: v["parity"]["ok"] for k, v in results.items()},
             "roofline": roof or None,
             "layer_roofline": head["layer_roofline"],
             "cpu_baseline": cpu,
@@ -327,6 +385,16 @@ def run_mine(args):
         }
         print(json.dumps(line))
     pool.close()
+
+
+def probe_i8(device):
+    """int8 tensor-pipe peak (TOPS) of this GPU, measured by the library's tcgen05 probe; None if it fails"""
+    import ctypes
+    from inferenz_b200 import lib
+    tops, ms = ctypes.c_double(0), ctypes.c_double(0)
+    if lib.inzg_probe_tensor_i8(device, 20000, ctypes.byref(tops), ctypes.byref(ms)) != 0:
+        return None
+    return round(tops.value, 1)
 
 
 def run_ep(args):
@@ -442,11 +510,9 @@ def run_ep(args):
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8 x Q4L (fp32 accumulate)", "data": "synthetic (seeded; no dataset)",
-            "config": {"workload": "BASELINE configs[1] per GPU, expert-parallel: MoE layer, decode batch of 32 tokens "
-                                   "per GPU, d=2048, 512 experts (512/N per GPU), top-10, FF 640, Q4L experts, F16 "
-                                   "router, N(0,1) per-expert logit bias; NCCL all-to-all dispatch and combine",
-                       "global_batch": nb, "seq_len": 1, "parallelism": f"ep{world}",
-                       "l2": "flushed (512 MB write) before every step"},
+            "config": {"workload": WORKLOAD, "global_batch": nb, "seq_len": 1},
+            "arm": {"parallelism": f"ep{world}: 512/N experts per GPU, NCCL all-to-all dispatch and combine",
+                    "l2": "flushed (512 MB write) before every step"},
             "roofline": {"bound": "hbm", "kernel": "layer step per GPU (router + local experts, incl. NCCL exchange)",
                          "algorithmic_bytes": bytes_gpu, "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(ach / hbm, 4), "peak_kind": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)",
@@ -475,21 +541,35 @@ def run_ep(args):
     dist.destroy_process_group()
 
 
-def cpu_reference(cfg, n, budget_s=12.0, blobs=None, bb=None, R=None, steps=None, warmup=3):
-    """The reference's own CPU layer (oracle/_ref, all host threads) on a bounded sample of the workload."""
+def oracle_inputs(cfg, n):
+    """The same workload inputs as make_inputs, drawn by the oracle's generator (no product library)"""
     import oracle
-    from inferenz_b200 import synth
+    x = oracle.synth_hidden(n, H)
+    bias = override = None
+    if cfg == "decode32":
+        bias = oracle.normal_bias(E)
+    elif cfg == "prefill4096":
+        bias = oracle.zipf_bias(E)
+    elif cfg == "q8g2048":
+        override = oracle.normal_logits(n, E)
+    return x, bias, override
+
+
+def cpu_reference(cfg, n, budget_s=12.0, blobs=None, bb=None, R=None, steps=None, warmup=3):
+    """The reference's own CPU layer (oracle/_ref, all host threads) on a bounded sample of the workload. Without
+    blobs, the layer is built on the CPU side alone: the oracle's generator and the reference's own quantizer."""
+    import oracle
     if blobs is None:
-        blobs, bb = synth.layer_blobs(0, synth.T_Q4L, H, FF, E)
-        R = synth.router(0, E, H)
-    x, bias, _ = make_inputs(cfg, n)
+        blobs, bb = oracle.ref_layer_blobs(0, oracle.T_Q4L, H, FF, E)
+        R = oracle.synth_router(0, E, H)
+    x, bias, _ = oracle_inputs(cfg, n)
     try:
         ref = oracle.Ref(H, threads=0)
         kind, cores, call = "reference", ref.threads, (lambda: ref.moe_routed(R, blobs, bb, x, bias=bias, dumps=False))
         isa = ref.isa
     except (FileNotFoundError, OSError):
         orc = oracle.Oracle()
-        gu_bytes = int(synth.lib.inzg_qmat_bytes(synth.T_Q4L, 2 * FF, H))
+        gu_bytes = 1392704  # inz_qmat_bytes(Q4L, 2*FF, H)
         kind, cores, isa = "port", 1, "scalar C restatement"
         call = (lambda: orc.moe_routed(R, blobs, bb, gu_bytes, x, bias=bias, dumps=False))
     for _ in range(warmup):
@@ -512,8 +592,8 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    # the same global batch as this arm at N GPUs (32 decode tokens per GPU, the EP bench's inputs), as one CPU call;
-    # at most about 90 s of timed calls, so the run ends within minutes whatever --steps asks
+    # the same global batch as this arm at N GPUs (32 decode tokens per GPU), as one CPU call; at most about 90 s of
+    # timed calls, so the run ends within minutes whatever --steps asks
     world = int(os.environ.get("WORLD_SIZE", "1"))
     n = 32 * world
     cpu = cpu_reference("decode32", n, budget_s=90.0, steps=args.steps, warmup=max(args.warmup, 1))
@@ -521,10 +601,9 @@ def run_reference(args):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": cpu["ms_median"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8 x Q4L (fp32 accumulate)", "data": "synthetic (seeded; no dataset)",
-            "config": {"workload": "BASELINE configs[1]: MoE layer, decode batch of 32 tokens per GPU of the GPU arm, "
-                                   "d=2048, 512 experts, top-10, FF 640, Q4L experts, F16 router, N(0,1) per-expert "
-                                   "logit bias; the whole batch as one call of the reference's CPU layer",
-                       "global_batch": n, "seq_len": 1, "parallelism": "CPU threads (reference thread pool)"},
+            "config": {"workload": WORKLOAD, "global_batch": n, "seq_len": 1},
+            "arm": {"parallelism": "CPU threads (the reference's thread pool), the whole batch as one layer call",
+                    "inputs": "oracle generator + the reference's own quantizer (no product library loaded)"},
             "cpu_baseline": cpu,
             "e2e": {"value": cpu["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))

@@ -161,11 +161,13 @@ INZG_EXPORT const char *inzg_stage_name(int stage);
  * cudaMalloc/cudaFree would synchronise the device -- this runs the router, softmax and top-k of one layer (the
  * routing stage of inzg_moe_forward, same results bit for bit) with its intermediate logits in a static device array
  * of the library instead of allocated scratch. x_dev [n][hidden] (16-byte aligned), logit_bias_dev [n_expert]
- * (optional), sel_dev [n][topk] and w_dev [n][topk] are device pointers; the call is ordered on `stream` (NULL = the legacy default
- * stream) and returns without synchronising. Limits: n <= 64 and n_expert <= 512 (the array is 64 x 512 fp32 =
- * 128 KiB, held by every GPU that loads the library until exit); larger calls return INZG_BAD_ARG. The first call on
- * a device looks up the array's device address (cudaGetSymbolAddress) and should come before any stream capture.
- * All calls share the array: calls that overlap on the GPU race. */
+ * (optional), sel_dev [n][topk] and w_dev [n][topk] are device pointers; the call is ordered on `stream` (NULL = the
+ * context's stream, as for inzg_route) and returns without synchronising; the caller's current device is left as it
+ * was. Limits: n <= 64 and n_expert <= 512 (the array is 64 x 512 fp32 = 128 KiB, held by every GPU that loads the
+ * library until exit); larger calls return INZG_BAD_ARG. The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) and should come before any stream capture. All calls share the array: calls that
+ * overlap on the GPU race. A device-side wait that runs out leaves sel = -1 and w = NaN in every output slot and
+ * makes inzg_device_status report INZG_TIMEOUT. */
 INZG_EXPORT inzg_status inzg_route_topk_noalloc(inzg_ctx *ctx, int layer, int n, const float *x_dev,
                                                 const float *logit_bias_dev, int32_t *sel_dev, float *w_dev,
                                                 void *stream);

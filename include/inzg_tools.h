@@ -2,9 +2,9 @@
  * inzg_tools.h -- host-side tools exported by libinzg next to the MoE C ABI (inzg.h): the engine's expert
  * quantizer and the seeded synthetic inputs of the benchmark configurations. No CUDA types.
  *
- * inzg_quantize / inzg_encode_expert replace the converter's expert path (encode, src/convert.c:190-200, over
- * inz_quantize, src/quant.c:422-556) and write byte-identical blobs; inzg_synth_* draw from the LCG + Box-Muller
- * normal of the reference's tests (tests/test_quant.c:10-17).
+ * inzg_quantize* / inzg_encode_expert* replace the converter's expert path (encode, src/convert.c:190-200, over
+ * inz_quantize, src/quant.c:422-556) with a GPU encoder that writes byte-identical blobs; inzg_synth_* draw from the
+ * LCG + Box-Muller normal of the reference's tests (tests/test_quant.c:10-17).
  */
 #ifndef INZG_TOOLS_H
 #define INZG_TOOLS_H
@@ -39,19 +39,48 @@ INZG_API void inzg_synth_hidden(uint64_t seed, int n, int H, float *x);
 INZG_API size_t inzg_qmat_bytes(int type, int rows, int cols);
 /* automatic rotation block (inz_auto_rot_block, src/quant.c:166-170) */
 INZG_API int inzg_auto_rot_block(int cols);
-/* quantize W [rows][cols] to Q4L / Q8G (inz_quantize, src/quant.c:422-556; rot_block 0 = auto, < 0 = none);
- * returns 0, or -1 for an unsupported type or shape */
-INZG_API int inzg_quantize(const float *W, int rows, int cols, int type, int rot_block, uint32_t rot_seed, int threads,
-                           void *out);
 /* bytes of one expert blob (convert_expert_blob_bytes, src/convert.c:179-182) */
 INZG_API uint64_t inzg_blob_bytes(int type, int H, int FF);
-/* one expert blob from fp32 gate|up and down (the converter's recipe, src/convert.c:190-200, 565-584) */
+
+/* ---- The expert quantizer, on the GPU (the current CUDA device). It writes the bytes of the reference quantizer
+ * (inz_quantize, src/quant.c:422-556) without an importance matrix, as the converter encodes experts
+ * (src/convert.c:190-200). Each returns 0, or -1 for an unsupported type or shape, a rotation block other than
+ * 64/128/256, or a failed CUDA call. */
+
+/* W_dev [rows][cols] fp32 -> out_dev (inzg_qmat_bytes bytes), Q4L or Q8G; rot_block 0 = auto, < 0 = none
+ * (Q8G: rotated only for rot_block > 0); rot_seed 0 = the reference's default 0x5EED. Ordered on `stream`
+ * (cudaStream_t, NULL = legacy default); returns after the stream has finished. */
+INZG_API int inzg_quantize_device(const float *W_dev, int rows, int cols, int type, int rot_block, uint32_t rot_seed,
+                                  void *out_dev, void *stream);
+/* the same from and to host memory */
+INZG_API int inzg_quantize(const float *W, int rows, int cols, int type, int rot_block, uint32_t rot_seed, void *out);
+/* n expert blobs from device fp32 gate|up [n][2FF][H] and down [n][H][FF] (the converter's recipe: Q4L with the
+ * automatic rotation, Q8G rotated with the automatic block, src/convert.c:157, 190-200, 565-584) */
+INZG_API int inzg_encode_experts_device(const float *gu_dev, const float *dn_dev, int n, int type, int H, int FF,
+                                        void *blobs_dev, void *stream);
+/* one expert blob from host fp32 gate|up and down */
 INZG_API int inzg_encode_expert(const float *GU, const float *D, int type, int H, int FF, void *blob);
-/* experts [e0, e1) of a synthetic layer, generated and encoded in parallel: blobs [e1-e0][blob_bytes] */
+/* experts [e0, e1) of a synthetic layer: drawn on the host (the reference tests' exact stream) and encoded on the GPU;
+ * blobs [e1-e0][blob_bytes] in host memory */
 INZG_API int inzg_synth_layer_blobs(uint64_t seed, int type, int H, int FF, int e0, int e1, void *blobs);
-/* only the listed experts generated (in parallel); the others get valid headers and a zero payload */
+/* only the listed experts generated; the others get valid headers and a zero payload */
 INZG_API int inzg_synth_layer_blobs_subset(uint64_t seed, int type, int H, int FF, int E, const int32_t *experts,
                                            int n_experts, void *blobs);
+/* the fp32 draws of experts [e0, e0 + n) on the GPU: gu_dev [n][2FF][H], dn_dev [n][H][FF] (the same LCG stream as
+ * inzg_synth_expert, with CUDA's double log/cos/sqrt in the Box-Muller step: see inzg_synth_layer_blobs_device) */
+INZG_API int inzg_synth_experts_device(uint64_t seed, int H, int FF, int e0, int n, float *gu_dev, float *dn_dev,
+                                       void *stream);
+/* experts [e0, e1) drawn AND encoded on the GPU into device memory blobs_dev [e1-e0][blob_bytes]: the same LCG
+ * stream, with CUDA's double log/cos/sqrt in the Box-Muller step (a float draw can differ from the host stream's
+ * where the double result lies within an ulp or two of a float rounding boundary) */
+INZG_API int inzg_synth_layer_blobs_device(uint64_t seed, int type, int H, int FF, int e0, int e1, void *blobs_dev,
+                                           void *stream);
+
+/* ---- Roofline probe (the counterpart of the reference's bandwidth probe in its diagnostics, src/diag.c:363-394):
+ * the int8 tensor-pipe throughput of `device` measured with tcgen05.mma kind::i8 (128 x 256 x 32 MMAs from shared
+ * memory on every SM, `iters` x 4 per SM). *tops = int8 tera-operations per second (2 per multiply-add), *ms the
+ * timed kernel's duration (optional). Returns 0, or -1 on a CUDA failure or a wait that ran out. */
+INZG_API int inzg_probe_tensor_i8(int device, int iters, double *tops, double *ms);
 
 #ifdef __cplusplus
 }

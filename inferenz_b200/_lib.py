@@ -77,11 +77,16 @@ SIGNATURES = {
     "inzg_synth_hidden": (None, [U64, I, I, P]),
     "inzg_qmat_bytes": (ctypes.c_size_t, [I, I, I]),
     "inzg_auto_rot_block": (I, [I]),
-    "inzg_quantize": (I, [P, I, I, I, I, U32, I, P]),
     "inzg_blob_bytes": (U64, [I, I, I]),
+    "inzg_quantize_device": (I, [P, I, I, I, I, U32, P, P]),
+    "inzg_quantize": (I, [P, I, I, I, I, U32, P]),
+    "inzg_encode_experts_device": (I, [P, P, I, I, I, I, P, P]),
     "inzg_encode_expert": (I, [P, P, I, I, I, P]),
     "inzg_synth_layer_blobs": (I, [U64, I, I, I, I, I, P]),
     "inzg_synth_layer_blobs_subset": (I, [U64, I, I, I, I, P, I, P]),
+    "inzg_synth_layer_blobs_device": (I, [U64, I, I, I, I, I, P, P]),
+    "inzg_synth_experts_device": (I, [U64, I, I, I, I, P, P, P]),
+    "inzg_probe_tensor_i8": (I, [I, I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]),
 }
 
 

@@ -900,13 +900,15 @@ inzg_status inzg_stage_times(inzg_ctx *c, double *ms, uint64_t *calls, int reset
 
 // internal helpers for noalloc.cu (hidden: not part of the exported ABI)
 int inzg__router_view(const inzg_ctx *c, int layer, const void **router, int *device, int *hidden, int *n_expert,
-                      int *topk) {
+                      int *topk, void **stream, int32_t **meta) {
     if (!c || layer < 0 || layer >= c->cfg.n_layers || !c->layers[layer].has_router) return 0;
     *router = c->layers[layer].router;
     *device = c->cfg.device;
     *hidden = c->cfg.hidden;
     *n_expert = c->cfg.n_expert;
     *topk = c->cfg.topk;
+    *stream = c->stream;
+    *meta = c->meta;
     return 1;
 }
 

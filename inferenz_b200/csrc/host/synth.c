@@ -94,3 +94,9 @@ INZG_API void inzg_synth_hidden(uint64_t seed, int n, int H, float *x) {
         for (int i = 0; i < H; i++) r[i] = r[i] * k;
     }
 }
+
+void inzg__synth_experts_host(uint64_t seed, int H, int FF, const int32_t *experts, int n, float *gu, float *dn) {
+    #pragma omp parallel for schedule(dynamic, 1)
+    for (int i = 0; i < n; i++)
+        inzg_synth_expert(seed, H, FF, experts[i], gu + (size_t)i * 2 * FF * H, dn + (size_t)i * H * FF);
+}

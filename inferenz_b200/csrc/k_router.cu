@@ -101,9 +101,14 @@ __global__ void __launch_bounds__(WPB * 32) router_small_kernel(const uint4 *__r
         for (int tt = 0; tt < nt; tt++) bulk_g2s(xs + (size_t)tt * H, X + (size_t)(t0 + tt) * H, (uint32_t)(H * 4), bar);
     }
     __syncthreads();
-    if (!mbar_wait_bounded(bar, 0)) {  // the copies did not land: record it, wait once more (bounded), leave
+    if (!mbar_wait_bounded(bar, 0)) {
+        // the copies did not land in time: record it, then let thread 0 keep polling (up to 64 more bounded rounds)
+        // -- the CTA's shared memory stays allocated while any of its threads runs, so a late copy cannot land in
+        // the next CTA's (no barrier here: other threads may have seen the phase complete)
         if (lane == 0 && meta) atomicCAS(&meta[kMetaRouterError], 0, kErrTimeout);
-        mbar_wait_bounded(bar, 0);
+        if (threadIdx.x == 0)
+            for (int r = 0; r < 64 && !mbar_wait_bounded(bar, 0); r++) {
+            }
         return;
     }
     const int qa = 2 * warp, l = lane & 7;

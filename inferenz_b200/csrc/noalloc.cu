@@ -12,8 +12,13 @@
 // (it names a host-side stand-in); the device address is looked up once per device, with that device current, by
 // cudaGetSymbolAddress, and passed to the kernels. That set-up happens in the first call on each device, so the
 // first call on a device should come before any stream capture. Every call shares the array and finds the previous
-// call's logits in it; nothing must start at zero (the router kernel writes every logit it later reads). Calls whose
-// executions overlap on the GPU race on the array.
+// call's logits in it; nothing in it must start at zero (the router kernel writes every logit it later reads). Calls
+// whose executions overlap on the GPU race on the array.
+//
+// Failure reporting allocates nothing either: the router records a bounded wait that ran out in the context's own
+// status words (allocated once by inzg_create), which the call clears first; a short kernel after the top-k then
+// overwrites the call's outputs with sel = -1 and w = NaN, so logits left by an earlier call never pass for this
+// call's routing, and inzg_device_status reports INZG_TIMEOUT.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -50,11 +55,35 @@ float *scratch_for(int device, cudaError_t *err) {
     return g_dev_ptr[device];
 }
 
+// a router wait that ran out (the context's router status word is set): poison the call's outputs
+__global__ void noalloc_poison_kernel(const int32_t *__restrict__ meta, int32_t *__restrict__ sel,
+                                      float *__restrict__ w, int count) {
+    if (meta[inzg::kMetaRouterError] == inzg::kErrNone) return;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) {
+        sel[i] = -1;
+        w[i] = __int_as_float(0x7FC00000);
+    }
+}
+
+// restores the caller's current device when the call returns
+struct DeviceGuard {
+    int saved = -1;
+    DeviceGuard() {
+        if (cudaGetDevice(&saved) != cudaSuccess) {
+            cudaGetLastError();
+            saved = -1;
+        }
+    }
+    ~DeviceGuard() {
+        if (saved >= 0) cudaSetDevice(saved);
+    }
+};
+
 }  // namespace
 
-// Defined in ctx.cu: the layer's device router, the context's device and shapes (no allocation).
+// Defined in ctx.cu: the layer's device router, the context's device, shapes, stream and status words (no allocation).
 extern "C" int inzg__router_view(const inzg_ctx *ctx, int layer, const void **router, int *device, int *hidden,
-                                 int *n_expert, int *topk);
+                                 int *n_expert, int *topk, void **stream, int32_t **meta);
 extern "C" void inzg__set_error(inzg_ctx *ctx, const char *msg);
 
 extern "C" INZG_EXPORT inzg_status inzg_route_topk_noalloc(inzg_ctx *ctx, int layer, int n, const float *x_dev,
@@ -63,7 +92,9 @@ extern "C" INZG_EXPORT inzg_status inzg_route_topk_noalloc(inzg_ctx *ctx, int la
     if (!ctx) return INZG_BAD_ARG;
     const void *router = nullptr;
     int device = 0, H = 0, E = 0, K = 0;
-    if (!inzg__router_view(ctx, layer, &router, &device, &H, &E, &K)) {
+    void *ctx_stream = nullptr;
+    int32_t *meta = nullptr;
+    if (!inzg__router_view(ctx, layer, &router, &device, &H, &E, &K, &ctx_stream, &meta)) {
         inzg__set_error(ctx, "route_topk_noalloc: layer has no router");
         return INZG_NOT_READY;
     }
@@ -83,17 +114,23 @@ extern "C" INZG_EXPORT inzg_status inzg_route_topk_noalloc(inzg_ctx *ctx, int la
         inzg__set_error(ctx, "route_topk_noalloc: x_dev must be 16-byte aligned");
         return INZG_BAD_ARG;
     }
+    DeviceGuard guard;
     cudaError_t e = cudaSetDevice(device);
     float *logits = e == cudaSuccess ? scratch_for(device, &e) : nullptr;
     if (!logits) {
         inzg__set_error(ctx, "route_topk_noalloc: cudaGetSymbolAddress of the static scratch failed");
         return INZG_CUDA;
     }
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    // (no status word on this path: a router copy that never lands is not reported to the caller)
-    inzg::launch_router_logits(static_cast<const uint4 *>(router), nullptr, x_dev, n, H, E, logit_bias_dev, logits, nullptr,
+    cudaStream_t st = static_cast<cudaStream_t>(stream ? stream : ctx_stream);
+    e = cudaMemsetAsync(meta + inzg::kMetaRouterError, 0, sizeof(int32_t), st);
+    if (e != cudaSuccess) {
+        inzg__set_error(ctx, "route_topk_noalloc: clearing the status word failed");
+        return INZG_CUDA;
+    }
+    inzg::launch_router_logits(static_cast<const uint4 *>(router), nullptr, x_dev, n, H, E, logit_bias_dev, logits, meta,
                                st);
     inzg::launch_softmax_topk(logits, n, E, K, sel_dev, w_dev, nullptr, st);
+    noalloc_poison_kernel<<<1, 256, 0, st>>>(meta, sel_dev, w_dev, n * K);
     e = cudaGetLastError();
     if (e != cudaSuccess) {
         inzg__set_error(ctx, "route_topk_noalloc: kernel launch failed");

@@ -16,7 +16,10 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_DIR = os.path.join(HERE, "_ref")
-REFERENCE_TREE = "/root/reference"
+# the reference checkout to compile oracle/_ref from: $INZ_REFERENCE_TREE, else a `reference` directory beside the
+# repository
+REFERENCE_TREE = os.environ.get("INZ_REFERENCE_TREE",
+                                os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 
 P, I, U32, U64, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_float
 T_Q4L, T_Q8G = 102, 103
@@ -39,6 +42,103 @@ def host_isa():
     except Exception:
         return "avx2"
     return "avx512vnni" if ("avx512_vnni" in flags and "avx512vl" in flags) else "avx2"
+
+
+_ORC = None
+
+
+def _orc():
+    """liboracle.so with the signatures of its synthetic-input generator."""
+    global _ORC
+    if _ORC is None:
+        path = os.path.join(HERE, "liboracle.so")
+        if not os.path.exists(path):
+            build()
+        L = ctypes.CDLL(path)
+        for name, res, args in [("orc_synth_jump", U64, [U64, U64]), ("orc_synth_randn", U64, [U64, ctypes.c_int64, F, P]),
+                                ("orc_synth_expert", None, [U64, I, I, I, P, P]), ("orc_synth_router", None, [U64, I, I, P]),
+                                ("orc_synth_hidden", None, [U64, I, I, P])]:
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _ORC = L
+    return _ORC
+
+
+# Seeded synthetic inputs of the benchmark configurations, drawn by the oracle's copy of the reference tests'
+# generator (the same streams and seeds as the product's inferenz_b200.synth): experts of layer l from seed l, router
+# of layer l from seed 1000 + l, hidden states from seed 1, N(0, 1) logit bias from seed 2, N(0, 1) logits from seed 4.
+ROUTER_SEED_BASE, HIDDEN_SEED, BIAS_SEED, OVERRIDE_SEED = 1000, 1, 2, 4
+
+
+def synth_randn(seed, n, scale=1.0):
+    out = np.empty(n, np.float32)
+    _orc().orc_synth_randn(seed, n, scale, _p(out))
+    return out
+
+
+def synth_router(layer, E=512, H=2048):
+    w = np.empty((E, H), np.uint16)
+    _orc().orc_synth_router(ROUTER_SEED_BASE + layer, E, H, _p(w))
+    return w
+
+
+def synth_hidden(n, H=2048, seed=HIDDEN_SEED):
+    x = np.empty((n, H), np.float32)
+    _orc().orc_synth_hidden(seed, n, H, _p(x))
+    return x
+
+
+def synth_expert(layer, e, H=2048, FF=640):
+    gu = np.empty((2 * FF, H), np.float32)
+    dn = np.empty((H, FF), np.float32)
+    _orc().orc_synth_expert(layer, H, FF, e, _p(gu), _p(dn))
+    return gu, dn
+
+
+def normal_bias(E=512, seed=BIAS_SEED):
+    return synth_randn(seed, E)
+
+
+def zipf_bias(E=512, s=1.1):
+    p = (np.arange(1, E + 1, dtype=np.float64)) ** (-s)
+    return np.log(p / p.sum()).astype(np.float32)
+
+
+def normal_logits(n, E=512, seed=OVERRIDE_SEED):
+    return synth_randn(seed, n * E).reshape(n, E)
+
+
+def ref_layer_blobs(layer, typ, H=2048, FF=640, E=512, experts=None, threads=None, isa=None):
+    """Blobs [E * blob_bytes] of a synthetic layer, encoded by the reference's own quantizer (oracle/_ref:
+    ref_encode_expert, the converter's recipe) from the oracle generator's draws, experts in parallel. ``experts``:
+    only these are generated; the others get the first listed expert's two headers and a zero payload (valid blobs
+    that must not be routed to). Returns (blobs, blob_bytes)."""
+    from concurrent.futures import ThreadPoolExecutor
+    isa = isa or host_isa()
+    path = os.path.join(REF_DIR, f"libinzref_{isa}_h{H}.so")
+    if not os.path.exists(path):
+        raise FileNotFoundError(path)
+    L = ctypes.CDLL(path)
+    L.ref_blob_bytes.restype, L.ref_blob_bytes.argtypes = U64, [I]
+    L.ref_qmat_bytes.restype, L.ref_qmat_bytes.argtypes = ctypes.c_size_t, [I, I, I]
+    L.ref_encode_expert.restype, L.ref_encode_expert.argtypes = None, [P, P, I, I, P]
+    bb = int(L.ref_blob_bytes(typ))
+    gub = int(L.ref_qmat_bytes(typ, 2 * FF, H))
+    out = np.zeros(E * bb, np.uint8)
+    ex = list(range(E)) if experts is None else sorted(set(int(e) for e in experts))
+
+    def one(e):
+        gu, dn = synth_expert(layer, e, H, FF)
+        L.ref_encode_expert(_p(gu), _p(dn), typ, 1, ctypes.c_void_p(out.ctypes.data + e * bb))
+
+    with ThreadPoolExecutor(max_workers=threads or os.cpu_count() or 1) as pool:
+        list(pool.map(one, ex))
+    for e in range(E):
+        if e not in ex:
+            out[e * bb:e * bb + 64] = out[ex[0] * bb:ex[0] * bb + 64]
+            out[e * bb + gub:e * bb + gub + 64] = out[ex[0] * bb + gub:ex[0] * bb + gub + 64]
+    return out, bb
 
 
 class Oracle:

@@ -5,6 +5,7 @@
  */
 #include "moe_oracle.h"
 
+#include <immintrin.h>
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
@@ -440,4 +441,64 @@ int orc_moe_routed(int H, int FF, int E, int topk, const uint16_t *router, const
     free(qx); free(qd); free(sx); free(bx); free(sd); free(bd); free(sumx); free(sumd); free(GU); free(D);
     free(tok); free(slot); free(tw);
     return rc;
+}
+
+/* ---------------- seeded synthetic inputs (tests/test_quant.c:10-17) ---------------- */
+
+#define LCG_A 6364136223846793005ull
+#define LCG_C 1442695040888963407ull
+
+static float synth_randn(uint64_t *s) {
+    double u1, u2;
+    *s = *s * LCG_A + LCG_C;
+    u1 = ((*s >> 11) + 1.0) / 9007199254740993.0;
+    *s = *s * LCG_A + LCG_C;
+    u2 = (*s >> 11) / 9007199254740992.0;
+    return (float)(sqrt(-2 * log(u1)) * cos(2 * M_PI * u2));
+}
+
+/* the state after n steps of s -> s * A + C, composing the affine map by repeated squaring */
+uint64_t orc_synth_jump(uint64_t s, uint64_t n_normals) {
+    uint64_t n = 2 * n_normals, ma = 1, mc = 0, a = LCG_A, c = LCG_C;
+    for (; n; n >>= 1) {
+        if (n & 1) {
+            ma *= a;
+            mc = mc * a + c;
+        }
+        c = c * a + c;
+        a *= a;
+    }
+    return s * ma + mc;
+}
+
+uint64_t orc_synth_randn(uint64_t state, int64_t n, float scale, float *out) {
+    for (int64_t i = 0; i < n; i++) out[i] = synth_randn(&state) * scale;
+    return state;
+}
+
+void orc_synth_expert(uint64_t seed, int H, int FF, int e, float *gu, float *dn) {
+    const uint64_t per = (uint64_t)3 * FF * H;
+    const float sd = (float)sqrt(1.0 / H);
+    uint64_t s = orc_synth_jump(seed, per * (uint64_t)e);
+    for (size_t i = 0; i < (size_t)2 * FF * H; i++) gu[i] = synth_randn(&s) * sd;
+    for (size_t i = 0; i < (size_t)H * FF; i++) dn[i] = synth_randn(&s) * sd;
+}
+
+void orc_synth_router(uint64_t seed, int E, int H, uint16_t *w) {
+    uint64_t s = seed;
+    for (size_t i = 0; i < (size_t)E * H; i++) w[i] = _cvtss_sh(synth_randn(&s) * 0.02f, 0);
+}
+
+void orc_synth_hidden(uint64_t seed, int n, int H, float *x) {
+    uint64_t s = seed;
+    for (int t = 0; t < n; t++) {
+        float *r = x + (size_t)t * H;
+        double ss = 0;
+        for (int i = 0; i < H; i++) {
+            r[i] = synth_randn(&s);
+            ss += (double)r[i] * r[i];
+        }
+        const float k = (float)(1.0 / sqrt(ss / H + 1e-6));
+        for (int i = 0; i < H; i++) r[i] = r[i] * k;
+    }
 }

@@ -69,6 +69,18 @@ int orc_moe_routed(int H, int FF, int E, int topk, const uint16_t *router, const
                    float *logits_out, float *probs_out, int32_t *sel_out, float *w_out, int32_t *unit_expert_out,
                    float *moe_out, int q8_vnni);
 
+/* ---- seeded synthetic inputs (test infrastructure): the LCG + Box-Muller normal of the reference's tests
+ * (tests/test_quant.c:10-17), so that the CPU side of a test or of the benchmark's reference arm draws its inputs
+ * without the product library ---- */
+uint64_t orc_synth_jump(uint64_t state, uint64_t n_normals);
+uint64_t orc_synth_randn(uint64_t state, int64_t n, float scale, float *out);
+/* expert e of a layer seeded `seed`: gu [2FF][H] (gate rows, then up rows), dn [H][FF], each randn * sqrt(1/H) */
+void orc_synth_expert(uint64_t seed, int H, int FF, int e, float *gu, float *dn);
+/* router [E][H] fp16 bits from randn * 0.02, rounded to nearest even (the reference's inz_f32_to_f16) */
+void orc_synth_router(uint64_t seed, int E, int H, uint16_t *w);
+/* hidden states [n][H] from randn, each row divided by sqrt(mean(x^2) + 1e-6) */
+void orc_synth_hidden(uint64_t seed, int n, int H, float *x);
+
 #ifdef __cplusplus
 }
 #endif

@@ -2,9 +2,10 @@
 
 Run here, where the reference tree was present when oracle/_ref was built:
     python tests/golden/make_golden.py
-Inputs are not stored: they are regenerated from seeds by inferenz_b200.synth (deterministic), and the fixture keeps
-a SHA-256 of every expert blob it used so a test can prove the regenerated inputs are the same bytes. Outputs are the
-reference's: logits, probabilities, top-k, renormalised weights, first-touch unit order, y.
+Inputs are not stored: they are regenerated from seeds by the oracle's copy of the reference tests' generator (the
+streams inferenz_b200.synth draws too), the experts encoded by the reference's own quantizer (oracle.ref_layer_blobs);
+the fixture keeps a SHA-256 of every expert blob it used so a test can prove regenerated inputs are the same bytes.
+Outputs are the reference's: logits, probabilities, top-k, renormalised weights, first-touch unit order, y.
 """
 import hashlib
 import os
@@ -17,29 +18,75 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 
 import oracle  # noqa: E402
-from inferenz_b200 import synth  # noqa: E402
 
-H, FF, E, K = 2048, 640, 512, 10
+FF, E, K = 640, 512, 10
+T_Q4L, T_Q8G = oracle.T_Q4L, oracle.T_Q8G
 
-# name: (n tokens, expert type, routing hook)
+# name: (n tokens, expert type, routing hook, hidden size). The override cases put 3 experts in every token's top-10
+# (they get the prefill GEMM numerics: >= 12 tokens) next to a long tail of decode experts.
 CASES = {
-    "decode_n1_q4l": (1, synth.T_Q4L, None),
-    "decode_n4_q4l_bias": (4, synth.T_Q4L, "bias"),
-    "prefill_n48_q4l_override": (48, synth.T_Q4L, "override"),
-    "decode_n4_q8g_bias": (4, synth.T_Q8G, "bias"),
+    "decode_n1_q4l": (1, T_Q4L, None, 2048),
+    "decode_n4_q4l_bias": (4, T_Q4L, "bias", 2048),
+    "prefill_n48_q4l_override": (48, T_Q4L, "override", 2048),
+    "decode_n4_q8g_bias": (4, T_Q8G, "bias", 2048),
+    "prefill_n40_q8g_override": (40, T_Q8G, "override", 2048),
+    "prefill_n24_q4l_h2560_override": (24, T_Q4L, "override", 2560),
 }
 
 
 def case_inputs(name):
-    n, typ, hook = CASES[name]
-    R = synth.router(0, E, H)
-    x = synth.hidden(n, H)
-    bias = synth.normal_bias(E) if hook == "bias" else None
+    """(n, expert type, H, router, x, bias, logits override) of a golden case"""
+    n, typ, hook, H = CASES[name]
+    R = oracle.synth_router(0, E, H)
+    x = oracle.synth_hidden(n, H)
+    bias = oracle.normal_bias(E) if hook == "bias" else None
     ov = None
     if hook == "override":
-        ov = synth.normal_logits(n, E)
+        ov = oracle.normal_logits(n, E)
         ov[:, :3] += 6.0
+    return n, typ, H, R, x, bias, ov
+
+
+# The benchmark's timed workloads (bench.py make_inputs), as the reference computes them: name -> (n, type, hook).
+BENCH_CASES = {
+    "decode1": (1, T_Q4L, None),
+    "decode32": (32, T_Q4L, "bias"),
+    "prefill4096": (4096, T_Q4L, "zipf"),
+    "q8g2048": (2048, T_Q8G, "logits"),
+}
+BENCH_SAMPLE_ROWS = 24  # full output rows kept per large workload (evenly spaced tokens, first and last included)
+
+
+def bench_inputs(name):
+    """(n, type, router, x, bias, logits override) of a benchmark workload; layer 0, H = 2048"""
+    n, typ, hook = BENCH_CASES[name]
+    R = oracle.synth_router(0, E, 2048)
+    x = oracle.synth_hidden(n, 2048)
+    bias = oracle.normal_bias(E) if hook == "bias" else oracle.zipf_bias(E) if hook == "zipf" else None
+    ov = oracle.normal_logits(n, E) if hook == "logits" else None
     return n, typ, R, x, bias, ov
+
+
+def sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def bench_fixture(name, threads=0):
+    """Compact record of the reference's output on a benchmark workload: routing as hashes of its exact bits (logits,
+    probabilities, renormalised weights) plus top-k and unit order, per-token output norms, and full output rows of
+    sampled tokens (all rows for small n)."""
+    n, typ, R, x, bias, ov = bench_inputs(name)
+    orc = oracle.Oracle()
+    sel = oracle.routing(orc, R, x, bias=bias, override=ov)
+    blobs, bb = oracle.ref_layer_blobs(0, typ, 2048, FF, E, experts=np.unique(sel))
+    ref = oracle.Ref(2048, threads=threads, expert_type=typ)
+    d = ref.moe_routed(R, blobs, bb, x, bias=bias, override=ov)
+    isa = ref.isa
+    ref.close()
+    rows = np.arange(n) if n <= 64 else np.unique(np.linspace(0, n - 1, BENCH_SAMPLE_ROWS).round().astype(np.int64))
+    return dict(sel=d["sel"], units=d["units"], w_sha=sha(d["w"]), logits_sha=sha(d["logits"]),
+                probs_sha=sha(d["probs"]), y_norm=np.linalg.norm(d["y"].astype(np.float64), axis=1),
+                y_rows=rows, y_sample=d["y"][rows], experts=np.unique(sel), isa=np.array(isa))
 
 
 def blob_hashes(blobs, bb, experts):
@@ -51,7 +98,7 @@ def quant_fixture(ref):
     out = {}
     for i, (rows, cols, typ, rot) in enumerate([(64, 320, 102, 64), (16, 640, 102, 0), (9, 320, 103, -1),
                                                 (32, 256, 103, 128)]):
-        w = synth.randn(100 + i, rows * cols, 0.03).reshape(rows, cols)
+        w = oracle.synth_randn(100 + i, rows * cols, 0.03).reshape(rows, cols)
         out[f"q{i}_shape"] = np.array([rows, cols, typ, rot])
         out[f"q{i}_bytes"] = ref.quantize(w, typ, rot_block=rot, seed=0, threads=1)
     return out
@@ -59,21 +106,30 @@ def quant_fixture(ref):
 
 def main():
     orc = oracle.Oracle()
+    only = sys.argv[1:]
     for name in CASES:
-        n, typ, R, x, bias, ov = case_inputs(name)
+        if only and name not in only:
+            continue
+        n, typ, H, R, x, bias, ov = case_inputs(name)
         ref = oracle.Ref(H, threads=0, expert_type=typ)
         sel = oracle.routing(orc, R, x, bias=bias, override=ov)
         experts = np.unique(sel)
-        blobs, bb = synth.layer_blobs(0, typ, H, FF, E, experts=experts)
+        blobs, bb = oracle.ref_layer_blobs(0, typ, H, FF, E, experts=experts)
         d = ref.moe_routed(R, blobs, bb, x, bias=bias, override=ov)
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), logits=d["logits"], probs=d["probs"], sel=d["sel"],
                             w=d["w"], units=d["units"], y=d["y"], experts=experts,
                             blob_sha256=blob_hashes(blobs, bb, experts), isa=np.array(ref.isa))
         print(name, "units", len(d["units"]), "isa", ref.isa)
         ref.close()
-    ref = oracle.Ref(H, threads=0)
-    np.savez_compressed(os.path.join(HERE, "quantizer.npz"), **quant_fixture(ref))
-    ref.close()
+    for name in BENCH_CASES:
+        if only and f"bench_{name}" not in only:
+            continue
+        np.savez_compressed(os.path.join(HERE, f"bench_{name}.npz"), **bench_fixture(name))
+        print("bench", name)
+    if not only or "quantizer" in only:
+        ref = oracle.Ref(2048, threads=0)
+        np.savez_compressed(os.path.join(HERE, "quantizer.npz"), **quant_fixture(ref))
+        ref.close()
 
 
 if __name__ == "__main__":

@@ -37,6 +37,26 @@ def test_reference_arm_prints_one_contract_line():
     assert d["e2e"] == {"value": d["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
 
 
+def test_reference_arm_never_loads_the_product_library():
+    """the reference arm draws its inputs with the oracle's generator and encodes experts with the reference's own
+    quantizer: libinzg.so must not be mapped in its process"""
+    code = ("import sys; sys.argv = ['bench.py', '--impl', 'reference', '--steps', '2', '--warmup', '3']; "
+            "import bench; bench.main(); maps = open('/proc/self/maps').read(); "
+            "print('MAPPED' if 'libinzg' in maps else 'CLEAN')")
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")}
+    p = subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
+    assert p.returncode == 0, p.stderr[-2000:]
+    lines = [l for l in p.stdout.splitlines() if l.strip()]
+    assert lines[-1] == "CLEAN" and json.loads(lines[0])["impl"] == "reference"
+
+
+def test_arms_describe_the_same_workload():
+    sys.path.insert(0, ROOT)
+    import bench
+    src = open(os.path.join(ROOT, "bench.py")).read()
+    assert src.count('"config": {"workload": WORKLOAD') == 3  # single GPU, expert parallel, reference
+
+
 def test_reference_arm_other_ranks_exit_quietly():
     assert _bench({"RANK": "1", "WORLD_SIZE": "2"}) == []
 

@@ -99,3 +99,34 @@ def test_q8g_decode_and_gemm(orc):
 def test_reference_model_hidden_2560(orc):
     R, x, blobs, bb, want = _case(orc, 2560, 2)
     _check(_run(2560, R, x, blobs, bb, synth.T_Q4L), want, "decode n=2 Q4L H=2560")
+
+
+def test_reference_model_hidden_2560_gemm_path(orc):
+    ov = _gemm_override(24)
+    R, x, blobs, bb, want = _case(orc, 2560, 24, override=ov)
+    got = _run(2560, R, x, blobs, bb, synth.T_Q4L, override=ov)
+    assert got["stats"]["gemm_units"] >= 3
+    _check(got, want, "prefill n=24 Q4L H=2560 (GEMM path)")
+
+
+@pytest.mark.parametrize("name", ["decode_n1_q4l", "decode_n4_q4l_bias", "decode_n4_q8g_bias",
+                                  "prefill_n48_q4l_override", "prefill_n40_q8g_override",
+                                  "prefill_n24_q4l_h2560_override"])
+def test_golden_cases(name):
+    """the reference's own outputs (tests/golden, made by the compiled reference): routing bit for bit, outputs within
+    the tolerance; the blobs (host draws, GPU encoder) hash to the ones the reference encoded"""
+    import hashlib
+    import importlib.util
+    import os
+    here = os.path.dirname(os.path.abspath(__file__))
+    spec = importlib.util.spec_from_file_location("make_golden", os.path.join(here, "golden", "make_golden.py"))
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    n, typ, Hc, R, x, bias, ov = mg.case_inputs(name)
+    g = np.load(os.path.join(here, "golden", f"{name}.npz"))
+    blobs, bb = synth.layer_blobs(0, typ, Hc, 640, 512, experts=g["experts"])
+    for e, h in zip(g["experts"], g["blob_sha256"]):
+        assert hashlib.sha256(blobs[e * bb:(e + 1) * bb].tobytes()).hexdigest() == h, "encoder bytes differ"
+    got = _run(Hc, R, x, blobs, bb, typ, bias=bias, override=ov)
+    want = {k: g[k] for k in ("logits", "probs", "sel", "w", "units", "y")}
+    _check(got, want, f"golden {name}")

@@ -12,9 +12,13 @@ from inferenz_b200 import synth
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 H, FF, E, K = 2048, 640, 512, 10
-GU_BYTES = {synth.T_Q4L: 1392704, synth.T_Q8G: 2703424}
 
-GOLDEN = ["decode_n1_q4l", "decode_n4_q4l_bias", "decode_n4_q8g_bias", "prefill_n48_q4l_override"]
+GOLDEN = ["decode_n1_q4l", "decode_n4_q4l_bias", "decode_n4_q8g_bias", "prefill_n48_q4l_override",
+          "prefill_n40_q8g_override", "prefill_n24_q4l_h2560_override"]
+
+
+def gu_bytes(typ, H=H):
+    return int(synth.lib.inzg_qmat_bytes(typ, 2 * FF, H))
 
 
 def golden_inputs(name):
@@ -32,11 +36,11 @@ def bits(a):
 @pytest.mark.parametrize("name", GOLDEN)
 def test_restatement_matches_golden(orc, name):
     g = np.load(os.path.join(HERE, "golden", f"{name}.npz"))
-    n, typ, R, x, bias, ov = golden_inputs(name)
-    blobs, bb = synth.layer_blobs(0, typ, H, FF, E, experts=g["experts"])
+    n, typ, Hc, R, x, bias, ov = golden_inputs(name)
+    blobs, bb = oracle.ref_layer_blobs(0, typ, Hc, FF, E, experts=g["experts"])
     for e, h in zip(g["experts"], g["blob_sha256"]):
         assert hashlib.sha256(blobs[e * bb:(e + 1) * bb].tobytes()).hexdigest() == h, "inputs differ from golden"
-    d = orc.moe_routed(R, blobs, bb, GU_BYTES[typ], x, bias=bias, override=ov)
+    d = orc.moe_routed(R, blobs, bb, gu_bytes(typ, Hc), x, bias=bias, override=ov, H=Hc)
     for k in ("logits", "probs", "w", "y"):
         assert np.array_equal(bits(d[k]), bits(g[k])), k
     assert np.array_equal(d["sel"], g["sel"])
@@ -99,9 +103,10 @@ def test_prefill_activation_blocks_live(orc, ref, K, rot):
 
 
 @pytest.mark.slow
-@pytest.mark.parametrize("n,hook", [(2, "bias"), (20, "override")])
-def test_whole_layer_live(orc, n, hook):
-    """restated layer == compiled reference layer on fresh inputs (decode batch path and GEMM path)"""
+@pytest.mark.parametrize("n,hook,typ", [(2, "bias", synth.T_Q4L), (20, "override", synth.T_Q4L),
+                                        (20, "override", synth.T_Q8G), (3, "bias", synth.T_Q8G)])
+def test_whole_layer_live(orc, n, hook, typ):
+    """restated layer == compiled reference layer on fresh inputs (decode batch path and GEMM path, Q4L and Q8G)"""
     R = synth.router(5, E, H)
     x = synth.hidden(n, H, seed=21)
     bias = synth.normal_bias(E, seed=22) if hook == "bias" else None
@@ -110,14 +115,14 @@ def test_whole_layer_live(orc, n, hook):
         ov = synth.normal_logits(n, E, seed=23)
         ov[:, 7] += 8.0
     sel = oracle.routing(orc, R, x, bias=bias, override=ov)
-    blobs, bb = synth.layer_blobs(5, synth.T_Q4L, H, FF, E, experts=np.unique(sel))
     try:
-        ref = oracle.Ref(H, threads=0)
+        ref = oracle.Ref(H, threads=0, expert_type=typ)
     except (FileNotFoundError, OSError) as e:
         pytest.skip(str(e))
+    blobs, bb = oracle.ref_layer_blobs(5, typ, H, FF, E, experts=np.unique(sel))
     b = ref.moe_routed(R, blobs, bb, x, bias=bias, override=ov)
     ref.close()
-    a = orc.moe_routed(R, blobs, bb, GU_BYTES[synth.T_Q4L], x, bias=bias, override=ov)
+    a = orc.moe_routed(R, blobs, bb, gu_bytes(typ), x, bias=bias, override=ov)
     for k in ("logits", "probs", "w", "moe_out", "y"):
         assert np.array_equal(bits(a[k]), bits(b[k])), k
     assert np.array_equal(a["sel"], b["sel"]) and np.array_equal(a["units"], b["units"])
