@@ -527,37 +527,43 @@ static int enqueue_shared(inzg_ctx *c, int layer, int n, const float *X, float *
     const int H = cf.hidden, FF = cf.ff;
     const int gemm = n_rule >= kGemmMinT;
     int launches = 0;
+    bool bad = false;
+    auto add = [&](int r) {  // a launcher that has no kernel for the shape fails the call (no silent skip)
+        if (r < 0) bad = true;
+        else launches += r;
+    };
     if (!quantized)
-        launches += launch_act_quant_x(X, n, H, D.gu_rot, D.gu_seed, c->xq64, c->xsb64, gemm ? c->xq256 : nullptr,
-                                       c->xs256, st);
+        add(launch_act_quant_x(X, n, H, D.gu_rot, D.gu_seed, c->xq64, c->xsb64, gemm ? c->xq256 : nullptr,
+                                       c->xs256, st));
     RouteDev R{};
     R.n = n; R.topk = 1; R.E = 1; R.n_rule = n_rule; R.absent_ok = 0;
     R.cnt = c->sh_cnt; R.off = c->sh_off; R.first = c->sh_first; R.etok = c->sh_etok; R.eslot = c->sh_eslot;
     R.ew = c->sh_ew; R.units = c->sh_units; R.meta = c->sh_meta; R.dec_units = c->sh_dec; R.gemm_units = c->sh_gemm;
     R.gemm_tiles = c->sh_tiles;
-    launches += launch_shared_route(R, n, gemm, gemv_items_per_unit(D, 0, R.n), gemv_items_per_unit(D, 1, R.n), gemm_token_tile(),
-                                    c->sh_upath, c->sh_eexp, st);
+    add(launch_shared_route(R, n, gemm, gemv_items_per_unit(D, 0, R.n), gemv_items_per_unit(D, 1, R.n), gemm_token_tile(),
+                                    c->sh_upath, c->sh_eexp, st));
     const bool tc = c->have_tc && S.has_maps;
+    if (gemm && !tc) return -2;  // the prefill GEMM needs its tensor maps: no silent CUDA-core fallback
     const int max_tiles = (n + gemm_token_tile() - 1) / gemm_token_tile() + 1;
     const int grid = c->num_sms * 4;
     if (!gemm) {
-        launches += launch_gemv_decode(D, 0, R, c->xq64, c->xsb64, c->GU, 2 * FF, c->num_sms, st);
+        add(launch_gemv_decode(D, 0, R, c->xq64, c->xsb64, c->GU, 2 * FF, c->num_sms, st));
     } else if (tc) {
-        launches += launch_gather_gemm_rows(c->xq256, c->xs256, H, (H + kKB - 1) / kKB, c->sh_etok, c->sh_eexp,
-                                            c->sh_upath, n, c->xqe, c->xse, st);
-        launches += launch_gemm_tc(0, S.map_gu.bytes, c->map_xqe.bytes, D.ws_gu, 2 * FF, H, R, c->xse, c->GU, 2 * FF,
-                                   max_tiles, st);
+        add(launch_gather_gemm_rows(c->xq256, c->xs256, H, (H + kKB - 1) / kKB, c->sh_etok, c->sh_eexp,
+                                            c->sh_upath, n, c->xqe, c->xse, st));
+        add(launch_gemm_tc(0, S.map_gu.bytes, c->map_xqe.bytes, D.ws_gu, 2 * FF, H, R, c->xse, c->GU, 2 * FF,
+                                   max_tiles, st));
     } else {
-        launches += launch_gemm_v1(D, 0, R, c->xq256, c->xs256, c->GU, 2 * FF, grid, st);
+        add(launch_gemm_v1(D, 0, R, c->xq256, c->xs256, c->GU, 2 * FF, grid, st));
     }
-    launches += launch_swiglu_quant(c->GU, FF, n, c->sh_eexp, c->sh_upath, D.dn_rot, D.dn_seed, c->dq64, c->dsb64,
-                                    c->dq256, c->ds256, st);
-    if (!gemm) launches += launch_gemv_decode(D, 1, R, c->dq64, c->dsb64, c->mo, H, c->num_sms, st);
-    else if (tc) launches += launch_gemm_tc(1, S.map_dn.bytes, c->map_dq.bytes, D.ws_dn, H, FF, R, c->ds256, c->mo, H,
-                                           max_tiles, st);
-    else launches += launch_gemm_v1(D, 1, R, c->dq256, c->ds256, c->mo, H, grid, st);
-    launches += launch_shared_add(X, c->sh_gate[layer], c->mo, y, n, H, c->sh_meta, c->meta, st);
-    return launches;
+    add(launch_swiglu_quant(c->GU, FF, n, c->sh_eexp, c->sh_upath, D.dn_rot, D.dn_seed, c->dq64, c->dsb64,
+                                    c->dq256, c->ds256, st));
+    if (!gemm) add(launch_gemv_decode(D, 1, R, c->dq64, c->dsb64, c->mo, H, c->num_sms, st));
+    else if (tc) add(launch_gemm_tc(1, S.map_dn.bytes, c->map_dq.bytes, D.ws_dn, H, FF, R, c->ds256, c->mo, H,
+                                           max_tiles, st));
+    else add(launch_gemm_v1(D, 1, R, c->dq256, c->ds256, c->mo, H, grid, st));
+    add(launch_shared_add(X, c->sh_gate[layer], c->mo, y, n, H, c->sh_meta, c->meta, st));
+    return bad ? -1 : launches;
 }
 
 // Enqueue the whole layer on `st`. ev != nullptr: record ev[i] before stage i and ev[N] at the end.
@@ -569,6 +575,11 @@ static int enqueue_forward(inzg_ctx *c, int layer, const LayerSlot &L, int n, co
     const int NE = n * K;
     const LayerDev &D = L.dev;
     int launches = 0;
+    bool bad = false;
+    auto add = [&](int r) {  // a launcher that has no kernel for the shape fails the call (no silent skip)
+        if (r < 0) bad = true;
+        else launches += r;
+    };
     auto mark = [&](int i) {
         if (ev) cudaEventRecord(ev[i], st);
     };
@@ -578,8 +589,8 @@ static int enqueue_forward(inzg_ctx *c, int layer, const LayerSlot &L, int n, co
     if (branch) {
         cudaEventRecord(c->fork, st);
         cudaStreamWaitEvent(c->side, c->fork, 0);
-        launches += launch_act_quant_x(X, n, H, D.gu_rot, D.gu_seed, c->xq64, c->xsb64, any_gemm ? c->xq256 : nullptr,
-                                       c->xs256, c->side);
+        add(launch_act_quant_x(X, n, H, D.gu_rot, D.gu_seed, c->xq64, c->xsb64, any_gemm ? c->xq256 : nullptr,
+                                       c->xs256, c->side));
         cudaEventRecord(c->join, c->side);
     }
     mark(0);
@@ -587,7 +598,7 @@ static int enqueue_forward(inzg_ctx *c, int layer, const LayerSlot &L, int n, co
         if (ovr_on_device)
             cudaMemcpyAsync(c->logits, ovr, sizeof(float) * (size_t)n * E, cudaMemcpyDeviceToDevice, st);
     } else {
-        launches += launch_router_logits(L.router, L.router32, X, n, H, E, bias, c->logits, c->meta, st);
+        add(launch_router_logits(L.router, L.router32, X, n, H, E, bias, c->logits, c->meta, st));
     }
     mark(1);
     RouteDev R{};
@@ -596,60 +607,63 @@ static int enqueue_forward(inzg_ctx *c, int layer, const LayerSlot &L, int n, co
     R.ew = c->ew; R.ccnt = c->ccnt; R.cmask = c->cmask; R.units = c->units; R.meta = c->meta; R.dec_units = c->dec_units;
     R.gemm_units = c->gemm_units; R.gemm_tiles = c->gemm_tiles;
     const bool tc = !simt_gemm && c->have_tc && L.has_maps;
+    // the prefill GEMM runs on tcgen05 unless the caller asked for the CUDA-core cross-check (INZG_GEMM_SIMT); a
+    // context without tensor maps fails the call instead of falling back silently
+    if (any_gemm && !simt_gemm && !tc) return -2;
     const int fused = launch_route_fused(R, c->logits, dump ? c->probs : nullptr, gemv_items_per_unit(D, 0, R.n), gemv_items_per_unit(D, 1, R.n),
                                          gemm_token_tile(), c->upath, c->eexp, st);
     if (fused > 0) {
-        launches += fused;
+        add(fused);
         mark(2);
     } else {
-        launches += launch_softmax_topk(c->logits, n, E, K, c->sel, c->w, dump ? c->probs : nullptr, st);
+        add(launch_softmax_topk(c->logits, n, E, K, c->sel, c->w, dump ? c->probs : nullptr, st));
         mark(2);
     }
     if (!branch)
-        launches += launch_act_quant_x(X, n, H, D.gu_rot, D.gu_seed, c->xq64, c->xsb64, any_gemm ? c->xq256 : nullptr,
-                                       c->xs256, st);
+        add(launch_act_quant_x(X, n, H, D.gu_rot, D.gu_seed, c->xq64, c->xsb64, any_gemm ? c->xq256 : nullptr,
+                                       c->xs256, st));
     mark(3);
-    if (fused <= 0) launches += launch_route(R, gemv_items_per_unit(D, 0, R.n), gemv_items_per_unit(D, 1, R.n), gemm_token_tile(), c->upath, c->eexp, st);
+    if (fused <= 0) add(launch_route(R, gemv_items_per_unit(D, 0, R.n), gemv_items_per_unit(D, 1, R.n), gemm_token_tile(), c->upath, c->eexp, st));
     const int nkbH = (H + kKB - 1) / kKB;
     const int max_tiles = (NE + gemm_token_tile() - 1) / gemm_token_tile() + std::min(E, NE / kGemmMinT) + 1;
     if (branch) cudaStreamWaitEvent(st, c->join, 0);
     mark(4);
     const int grid = c->num_sms * 4;
-    const int r1 = launch_gemv_decode(D, 0, R, c->xq64, c->xsb64, c->GU, 2 * FF, c->num_sms, st);
-    if (r1 < 0) return -1;
-    launches += r1;
+    add(launch_gemv_decode(D, 0, R, c->xq64, c->xsb64, c->GU, 2 * FF, c->num_sms, st));
     mark(5);
     if (any_gemm) {
         if (tc) {
-            launches += launch_gather_gemm_rows(c->xq256, c->xs256, H, nkbH, c->etok, c->eexp, c->upath, NE, c->xqe,
-                                                c->xse, st);
-            launches += launch_gemm_tc(0, L.map_gu.bytes, c->map_xqe.bytes, D.ws_gu, 2 * FF, H, R, c->xse, c->GU,
-                                       2 * FF, max_tiles, st);
+            add(launch_gather_gemm_rows(c->xq256, c->xs256, H, nkbH, c->etok, c->eexp, c->upath, NE, c->xqe,
+                                                c->xse, st));
+            add(launch_gemm_tc(0, L.map_gu.bytes, c->map_xqe.bytes, D.ws_gu, 2 * FF, H, R, c->xse, c->GU,
+                                       2 * FF, max_tiles, st));
         } else {
-            launches += launch_gemm_v1(D, 0, R, c->xq256, c->xs256, c->GU, 2 * FF, grid, st);
+            add(launch_gemm_v1(D, 0, R, c->xq256, c->xs256, c->GU, 2 * FF, grid, st));
         }
     }
     mark(6);
-    launches += launch_swiglu_quant(c->GU, FF, NE, c->eexp, c->upath, D.dn_rot, D.dn_seed, c->dq64, c->dsb64, c->dq256,
-                                    c->ds256, st);
+    add(launch_swiglu_quant(c->GU, FF, NE, c->eexp, c->upath, D.dn_rot, D.dn_seed, c->dq64, c->dsb64, c->dq256,
+                                    c->ds256, st));
     mark(7);
-    launches += launch_gemv_decode(D, 1, R, c->dq64, c->dsb64, c->mo, H, c->num_sms, st);
+    add(launch_gemv_decode(D, 1, R, c->dq64, c->dsb64, c->mo, H, c->num_sms, st));
     mark(8);
     if (any_gemm) {
-        if (tc) launches += launch_gemm_tc(1, L.map_dn.bytes, c->map_dq.bytes, D.ws_dn, H, FF, R, c->ds256, c->mo, H,
-                                           max_tiles, st);
-        else launches += launch_gemm_v1(D, 1, R, c->dq256, c->ds256, c->mo, H, grid, st);
+        if (tc) add(launch_gemm_tc(1, L.map_dn.bytes, c->map_dq.bytes, D.ws_dn, H, FF, R, c->ds256, c->mo, H,
+                                           max_tiles, st));
+        else add(launch_gemm_v1(D, 1, R, c->dq256, c->ds256, c->mo, H, grid, st));
     }
     mark(9);
-    launches += launch_combine(c->mo, n, H, K, yd, c->num_sms, st);
+    add(launch_combine(c->mo, n, H, K, yd, c->num_sms, st));
     mark(10);
     if (c->shared[layer].has_experts) {  // y += sigmoid(gate . x) * shared(x), after the routed sum (:1141-1148)
         const LayerDev &S = c->shared[layer].dev;
         const bool same_rot = S.gu_rot == D.gu_rot && S.gu_seed == D.gu_seed;
-        launches += enqueue_shared(c, layer, n, X, yd, n, same_rot, st);
+        const int r = enqueue_shared(c, layer, n, X, yd, n, same_rot, st);
+        if (r == -2) return -2;
+        add(r);
     }
     mark(11);
-    return launches;
+    return bad ? -1 : launches;
 }
 
 inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, float *y, const inzg_moe_opts *opt) {
@@ -708,7 +722,8 @@ inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, fl
             if (e != cudaSuccess || nl < 0) {
                 if (graph) cudaGraphDestroy(graph);
                 return e != cudaSuccess ? cuda_fail(c, e, "moe_forward: capture")
-                                        : fail(c, INZG_UNSUPPORTED, "moe_forward: capture");
+                       : nl == -2       ? fail(c, INZG_UNSUPPORTED, "moe_forward: no tensor maps for the prefill GEMM")
+                                        : fail(c, INZG_UNSUPPORTED, "moe_forward: no kernel for this shape");
             }
             cudaGraphExec_t exec = nullptr;
             e = cudaGraphInstantiate(&exec, graph, 0);
@@ -730,6 +745,7 @@ inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, fl
         e = cudaGraphLaunch(g->exec, st);
         if (e != cudaSuccess) return cuda_fail(c, e, "moe_forward: graph launch");
     }
+    if (launches == -2) return fail(c, INZG_UNSUPPORTED, "moe_forward: no tensor maps for the prefill GEMM");
     if (launches < 0) return fail(c, INZG_UNSUPPORTED, "moe_forward: no kernel for this geometry");
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(c, e, "moe_forward: kernel launch");
@@ -817,23 +833,24 @@ inzg_status inzg_moe_experts(inzg_ctx *c, int layer, int m, const float *x_dev, 
     launch_route(R, gemv_items_per_unit(D, 0, R.n), gemv_items_per_unit(D, 1, R.n), gemm_token_tile(), c->upath,
                  c->eexp, st);
     const bool tc = c->have_tc && L.has_maps;
+    if (any_gemm && !tc) return fail(c, INZG_UNSUPPORTED, "moe_experts: no tensor maps for the prefill GEMM");
     const int nkbH = (H + kKB - 1) / kKB;
     const int max_tiles = (NE + gemm_token_tile() - 1) / gemm_token_tile() + std::min(E, NE / kGemmMinT) + 1;
-    const int grid = c->num_sms * 4;
     launch_gemv_decode(D, 0, R, c->xq64, c->xsb64, c->GU, 2 * FF, c->num_sms, st);
     if (any_gemm) {
         if (tc) {
             launch_gather_gemm_rows(c->xq256, c->xs256, H, nkbH, c->etok, c->eexp, c->upath, NE, c->xqe, c->xse, st);
-            launch_gemm_tc(0, L.map_gu.bytes, c->map_xqe.bytes, D.ws_gu, 2 * FF, H, R, c->xse, c->GU, 2 * FF, max_tiles, st);
-        } else {
-            launch_gemm_v1(D, 0, R, c->xq256, c->xs256, c->GU, 2 * FF, grid, st);
+            if (launch_gemm_tc(0, L.map_gu.bytes, c->map_xqe.bytes, D.ws_gu, 2 * FF, H, R, c->xse, c->GU, 2 * FF,
+                               max_tiles, st) < 0)
+                return fail(c, INZG_UNSUPPORTED, "moe_experts: no GEMM kernel for this shape");
         }
     }
     launch_swiglu_quant(c->GU, FF, NE, c->eexp, c->upath, D.dn_rot, D.dn_seed, c->dq64, c->dsb64, c->dq256, c->ds256, st);
     launch_gemv_decode(D, 1, R, c->dq64, c->dsb64, out_dev, H, c->num_sms, st);
     if (any_gemm) {
-        if (tc) launch_gemm_tc(1, L.map_dn.bytes, c->map_dq.bytes, D.ws_dn, H, FF, R, c->ds256, out_dev, H, max_tiles, st);
-        else launch_gemm_v1(D, 1, R, c->dq256, c->ds256, out_dev, H, grid, st);
+        if (launch_gemm_tc(1, L.map_dn.bytes, c->map_dq.bytes, D.ws_dn, H, FF, R, c->ds256, out_dev, H, max_tiles,
+                           st) < 0)
+            return fail(c, INZG_UNSUPPORTED, "moe_experts: no GEMM kernel for this shape");
     }
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? INZG_OK : cuda_fail(c, e, "moe_experts: kernel launch");
@@ -864,7 +881,9 @@ inzg_status inzg_shared_expert(inzg_ctx *c, int layer, int n, const float *x_dev
     if (!c->shared[layer].has_experts) return fail(c, INZG_NOT_READY, "shared_expert: layer has no shared expert");
     cudaSetDevice(cf.device);
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
-    enqueue_shared(c, layer, n, x_dev, y_dev, n_batch, false, st);
+    const int r = enqueue_shared(c, layer, n, x_dev, y_dev, n_batch, false, st);
+    if (r < 0) return fail(c, INZG_UNSUPPORTED, r == -2 ? "shared_expert: no tensor maps for the prefill GEMM"
+                                                        : "shared_expert: no kernel for this shape");
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? INZG_OK : cuda_fail(c, e, "shared_expert: kernel launch");
 }

@@ -38,6 +38,7 @@ constexpr int kEpiWarps = 8, kEpiThreads = kEpiWarps * 32, kHalfN = TBN / 2;  //
 constexpr int kThreads = 64 + kEpiThreads;
 constexpr int kMagicI = 0x4B400000;  // 1.5 * 2^23 as a float: kMagicI + x reads as 12582912 + x for |x| < 2^22
 constexpr int kStageBytes = (TBM + TBN) * TBK;  // 32 KiB
+constexpr int kMaxKB = 10;                      // 256-blocks of K: up to 2560, the reference model's width
 
 struct TcShared {
     uint64_t full[TSTAGES], empty[TSTAGES], acc_full[2], acc_empty[2], drain;
@@ -45,7 +46,7 @@ struct TcShared {
     uint64_t xs_empty[2];              // every epilogue thread has finished the item that used buffer [parity]
     uint32_t tmem_base;
     int abort, never;                  // never: drains ignore the abort flag
-    alignas(16) float xs[2][8][TBN];  // token block scales per item parity, [block][token] (K <= 2048: <= 8 blocks)
+    alignas(16) float xs[2][kMaxKB][TBN];  // token block scales per item parity, [block][token] (K <= 2560)
     int oslot[2][TBN];                 // down matrix: each token's output slot and routing weight, per item parity
     float ow[2][TBN];
 };
@@ -225,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         // An item's token scales (zero past the expert's tokens) and, for the down matrix, each token's output slot
         // and weight are staged in shared memory one item ahead: loaded into registers when the item before it
         // starts, stored after that item's first block, so the loads overlap its MMAs.
-        constexpr int kPre = 8 * TBN / kEpiThreads;  // scales per thread (nkb <= 8)
+        constexpr int kPre = (kMaxKB * TBN + kEpiThreads - 1) / kEpiThreads;  // scales per thread (nkb <= kMaxKB)
         float pre[kPre];
         int pslot = 0;
         float pw = 0.0f;
@@ -394,7 +395,7 @@ void gemm_tc_set_attributes() {
 // grid: an upper bound on (token tiles x row tiles); CTAs past the device-built tile count return at once
 int launch_gemm_tc(int kind, const void *mapA, const void *mapB, const float *wsc, int rows, int K, const RouteDev &R,
                    const float *xs_e, float *out, int out_ld, int max_tiles, cudaStream_t st) {
-    if (rows % TBM || K % TBK || K > 8 * kKB) return -1;
+    if (rows % TBM || K % TBK || K > kMaxKB * kKB) return -1;
     const int mt = kind == 0 ? kMetaGemmTilesGU : kMetaGemmTilesDN;
     static int sms[64] = {0};  // persistent grid: one CTA per SM (at most the items the call can have)
     int dev = 0;
