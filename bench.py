@@ -249,7 +249,9 @@ def stage_roofline(stage_ms, stats, n, hbm, q8g=False, i8_peak=None):
     int8 tensor-pipe fraction: ops = GEMM-path token-expert pairs x 2 x rows x K, against the measured int8 peak."""
     dec, gemm = stats["dec_units"], stats["gemm_units"]
     gu, dn = (GU_PAYLOAD_Q8G, DN_PAYLOAD_Q8G) if q8g else (GU_PAYLOAD, DN_PAYLOAD)
+    expert_bytes = EXPERT_BYTES_Q8G if q8g else EXPERT_BYTES_Q4L
     algo = {
+        "fused_decode": ROUTER_BYTES + stats["units"] * expert_bytes + 2 * n * H * 4,  # the whole layer, one launch
         "router_logits": ROUTER_BYTES + n * H * 4 + n * E * 4,
         "gate_up_gemv": dec * gu,
         "down_gemv": dec * dn,

@@ -64,9 +64,11 @@ typedef struct {
 #define INZG_PROFILE 4u     /* time every stage with CUDA events on the call's stream; the call then synchronises */
 #define INZG_NO_GRAPH 8u    /* launch the kernels one by one instead of replaying the cached CUDA graph */
 #define INZG_GEMM_SIMT 16u  /* prefill-path experts on the CUDA-core int8 GEMM instead of tcgen05 (cross-check) */
+#define INZG_NO_FUSED 32u   /* calls of 1-2 tokens through the separate kernels instead of the single fused decode
+                             * launch (cross-check; both give the same bits) */
 
 /* stages timed under INZG_PROFILE (the reference's diag stages are coarser: DG_ROUTER, DG_EXPERT_*, DG_SHARED) */
-#define INZG_N_STAGES 11
+#define INZG_N_STAGES 12
 
 typedef struct {
     unsigned flags;

@@ -81,6 +81,9 @@ INZG_API int inzg_synth_layer_blobs_device(uint64_t seed, int type, int H, int F
  * memory on every SM, `iters` x 4 per SM). *tops = int8 tera-operations per second (2 per multiply-add), *ms the
  * timed kernel's duration (optional). Returns 0, or -1 on a CUDA failure or a wait that ran out. */
 INZG_API int inzg_probe_tensor_i8(int device, int iters, double *tops, double *ms);
+/* the architecture of the library's kernels as loaded on `device` (cudaFuncGetAttributes): binaryVersion 100 for
+ * sm_100 SASS; ptxVersion the PTX ISA target. Returns 0, or -1 without a usable device. */
+INZG_API int inzg_kernel_arch(int device, int *binary_version, int *ptx_version);
 
 #ifdef __cplusplus
 }

@@ -10,8 +10,8 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libinzg.so")
 
 T_F16, T_Q4L, T_Q8G = 1, 102, 103
-IO_DEVICE, DUMP_ROUTE, PROFILE, NO_GRAPH, GEMM_SIMT = 1, 2, 4, 8, 16
-N_STAGES = 11
+IO_DEVICE, DUMP_ROUTE, PROFILE, NO_GRAPH, GEMM_SIMT, NO_FUSED = 1, 2, 4, 8, 16, 32
+N_STAGES = 12
 
 STATUS = {0: "INZG_OK", 1: "INZG_BAD_ARG", 2: "INZG_CORRUPT_BLOB", 3: "INZG_OOM", 4: "INZG_CUDA", 5: "INZG_NCCL",
           6: "INZG_TIMEOUT", 7: "INZG_DEVICE_CHECK", 8: "INZG_UNSUPPORTED", 9: "INZG_NOT_READY"}
@@ -87,6 +87,7 @@ SIGNATURES = {
     "inzg_synth_layer_blobs_device": (I, [U64, I, I, I, I, I, P, P]),
     "inzg_synth_experts_device": (I, [U64, I, I, I, I, P, P, P]),
     "inzg_probe_tensor_i8": (I, [I, I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]),
+    "inzg_kernel_arch": (I, [I, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
 }
 
 

@@ -96,6 +96,7 @@ struct inzg_ctx {
     int32_t *cnt = nullptr, *off = nullptr, *first = nullptr, *etok = nullptr, *eslot = nullptr, *ccnt = nullptr;
     int32_t *units = nullptr, *meta = nullptr, *dec_units = nullptr, *gemm_units = nullptr, *gemm_tiles = nullptr;
     int32_t *upath = nullptr, *eexp = nullptr;
+    int32_t *fused_cnt = nullptr;  // the fused decode kernel's barrier and hand-off counters
     uint64_t *cmask = nullptr;
     float *ew = nullptr, *GU = nullptr, *mo = nullptr;
     int8_t *dq64 = nullptr, *dq256 = nullptr;
@@ -141,7 +142,7 @@ struct inzg_ctx {
 
 static const char *kStageNames[INZG_N_STAGES] = {"router_logits", "softmax_topk_route", "act_quant", "route",
                                                  "gate_up_gemv", "gate_up_gemm", "swiglu_quant", "down_gemv",
-                                                 "down_gemm", "combine", "shared_expert"};
+                                                 "down_gemm", "combine", "fused_decode", "shared_expert"};
 
 static void drop_graphs(inzg_ctx *c) {
     for (auto &g : c->graphs) cudaGraphExecDestroy(g.exec);
@@ -183,7 +184,7 @@ static void free_scratch(inzg_ctx *c) {
                     c->gemm_units, c->gemm_tiles, c->upath, c->eexp, c->ew, c->GU, c->mo, c->dq64, c->dq256, c->dsb64,
                     c->ds256, c->xqe, c->xse, c->sh_cnt, c->sh_off, c->sh_first, c->sh_etok, c->sh_eslot,
                     c->sh_eexp, c->sh_upath, c->sh_units, c->sh_dec, c->sh_gemm, c->sh_tiles, c->sh_meta, c->sh_ew,
-                    c->cmask};
+                    c->cmask, c->fused_cnt};
     for (void *p : ptrs)
         if (p) cudaFree(p);
 }
@@ -275,6 +276,9 @@ inzg_ctx *inzg_create(const inzg_config *cfg, inzg_status *status) {
     c->sh_gemm = dalloc<int32_t>(1, ok);
     c->sh_tiles = dalloc<int32_t>(T / 16 + 2, ok);
     c->sh_meta = dalloc<int32_t>(16, ok);
+    c->fused_cnt = dalloc<int32_t>(fused_counter_ints((int)E, 8, (int)H), ok);
+    if (ok && cudaMemset(c->fused_cnt, 0, sizeof(int32_t) * fused_counter_ints((int)E, 8, (int)H)) != cudaSuccess)
+        ok = false;
     if (!ok) {
         free_scratch(c);
         cudaStreamDestroy(c->stream);
@@ -568,8 +572,8 @@ static int enqueue_shared(inzg_ctx *c, int layer, int n, const float *X, float *
 
 // Enqueue the whole layer on `st`. ev != nullptr: record ev[i] before stage i and ev[N] at the end.
 static int enqueue_forward(inzg_ctx *c, int layer, const LayerSlot &L, int n, const float *X, float *yd, const float *bias,
-                           const float *ovr, bool ovr_on_device, bool dump, bool simt_gemm, cudaEvent_t *ev,
-                           cudaStream_t st) {
+                           const float *ovr, bool ovr_on_device, bool dump, bool simt_gemm, bool no_fused,
+                           cudaEvent_t *ev, cudaStream_t st) {
     const inzg_config &cf = c->cfg;
     const int H = cf.hidden, E = cf.n_expert, K = cf.topk, FF = cf.ff;
     const int NE = n * K;
@@ -583,6 +587,27 @@ static int enqueue_forward(inzg_ctx *c, int layer, const LayerSlot &L, int n, co
     auto mark = [&](int i) {
         if (ev) cudaEventRecord(ev[i], st);
     };
+    auto shared_stage = [&]() -> int {  // y += sigmoid(gate . x) * shared(x), after the routed sum (:1141-1148)
+        if (!c->shared[layer].has_experts) return 0;
+        const LayerDev &S = c->shared[layer].dev;
+        const bool same_rot = S.gu_rot == D.gu_rot && S.gu_seed == D.gu_seed;
+        return enqueue_shared(c, layer, n, X, yd, n, same_rot, st);
+    };
+    // Decode calls of up to 8 tokens: the whole routed layer as one persistent launch (k_fused.cu). The logits
+    // override of a host call was copied into c->logits by the caller.
+    if (!no_fused && fused_decode_fits(D, n, K, L.has_router || ovr)) {
+        for (int i = 0; i <= 10; i++) mark(i);
+        const float *ov = ovr ? (ovr_on_device ? ovr : c->logits) : nullptr;
+        add(launch_fused_decode(D, n, K, X, ov ? nullptr : bias, ov, c->logits, dump ? c->probs : nullptr, c->sel, c->w,
+                                c->units, c->meta, c->xq64, c->xsb64, c->GU, c->dq64, c->dsb64, c->mo, yd,
+                                c->fused_cnt, c->num_sms, st));
+        mark(11);
+        const int r = shared_stage();
+        if (r == -2) return -2;
+        add(r);
+        mark(12);
+        return bad ? -1 : launches;
+    }
     const bool any_gemm = n > 8 && (int64_t)n * K >= kGemmMinT;
     // the inputs' quantization (both numeric paths) depends on x only: a side branch when not profiling
     const bool branch = ev == nullptr;
@@ -655,14 +680,11 @@ static int enqueue_forward(inzg_ctx *c, int layer, const LayerSlot &L, int n, co
     mark(9);
     add(launch_combine(c->mo, n, H, K, yd, c->num_sms, st));
     mark(10);
-    if (c->shared[layer].has_experts) {  // y += sigmoid(gate . x) * shared(x), after the routed sum (:1141-1148)
-        const LayerDev &S = c->shared[layer].dev;
-        const bool same_rot = S.gu_rot == D.gu_rot && S.gu_seed == D.gu_seed;
-        const int r = enqueue_shared(c, layer, n, X, yd, n, same_rot, st);
-        if (r == -2) return -2;
-        add(r);
-    }
     mark(11);
+    const int r = shared_stage();
+    if (r == -2) return -2;
+    add(r);
+    mark(12);
     return bad ? -1 : launches;
 }
 
@@ -706,9 +728,11 @@ inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, fl
     int launches = 0;
     if (profile || (flags & INZG_NO_GRAPH)) {
         launches = enqueue_forward(c, layer, L, n, X, yd, bias, ovr, dev_io, dump, flags & INZG_GEMM_SIMT,
+                                   flags & INZG_NO_FUSED,
                                    profile ? c->ev : nullptr, st);
     } else {
-        inzg_ctx::GraphKey key{layer, n, X, yd, bias, ovr, flags & (INZG_IO_DEVICE | INZG_DUMP_ROUTE | INZG_GEMM_SIMT)};
+        inzg_ctx::GraphKey key{layer, n, X, yd, bias, ovr,
+                               flags & (INZG_IO_DEVICE | INZG_DUMP_ROUTE | INZG_GEMM_SIMT | INZG_NO_FUSED)};
         inzg_ctx::GraphEntry *g = nullptr;
         for (auto &ge : c->graphs)
             if (ge.key == key) g = &ge;
@@ -716,7 +740,8 @@ inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, fl
             cudaStream_t cs = c->capture_stream;
             e = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
             if (e != cudaSuccess) return cuda_fail(c, e, "moe_forward: begin capture");
-            const int nl = enqueue_forward(c, layer, L, n, X, yd, bias, ovr, dev_io, dump, flags & INZG_GEMM_SIMT, nullptr, cs);
+            const int nl = enqueue_forward(c, layer, L, n, X, yd, bias, ovr, dev_io, dump, flags & INZG_GEMM_SIMT,
+                                           flags & INZG_NO_FUSED, nullptr, cs);
             cudaGraph_t graph = nullptr;
             e = cudaStreamEndCapture(cs, &graph);
             if (e != cudaSuccess || nl < 0) {

@@ -55,4 +55,13 @@ void launch_pool_requant(const uint8_t *blobs, uint64_t blob_bytes, uint64_t gu_
 void launch_pool_repack(const uint8_t *blobs, uint64_t blob_bytes, uint64_t gu_bytes, int e0, int ne,
                         const LayerDev &L, uint8_t *pool, uint8_t *luts, cudaStream_t st);
 
+// The whole routed layer in one cooperative launch for calls of 1-2 tokens (k_fused.cu); -1 when the shape has no
+// instantiation. counters: fused_counter_ints(E, 8, H) ints, all zero before the first call.
+size_t fused_counter_ints(int E, int n_max, int H);
+bool fused_decode_fits(const LayerDev &L, int n, int K, bool have_router_or_ovr);
+int launch_fused_decode(const LayerDev &L, int n, int K, const float *x, const float *bias, const float *ovr,
+                        float *logits, float *probs, int32_t *sel, float *w, int32_t *units, int32_t *meta,
+                        int8_t *xq64, float2 *xsb64, float *GU, int8_t *dq64, float2 *dsb64, float *mo, float *y,
+                        int32_t *counters, int num_sms, cudaStream_t st);
+
 }  // namespace inzg

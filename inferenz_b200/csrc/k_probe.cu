@@ -118,3 +118,24 @@ extern "C" INZG_API int inzg_probe_tensor_i8(int device, int iters, double *tops
     if (saved >= 0) cudaSetDevice(saved);
     return rc;
 }
+
+// The architecture the library's kernels were built for and run as on `device`: cudaFuncGetAttributes of one of them
+// (binaryVersion 100 = sm_100 SASS, loaded without a PTX recompilation).
+extern "C" INZG_API int inzg_kernel_arch(int device, int *binary_version, int *ptx_version) {
+    int saved = -1;
+    cudaGetDevice(&saved);
+    if (cudaSetDevice(device) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    cudaFuncAttributes fa{};
+    const cudaError_t e = cudaFuncGetAttributes(&fa, inzg::tensor_i8_probe_kernel);
+    if (saved >= 0) cudaSetDevice(saved);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    if (binary_version) *binary_version = fa.binaryVersion;
+    if (ptx_version) *ptx_version = fa.ptxVersion;
+    return 0;
+}

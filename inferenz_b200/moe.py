@@ -10,7 +10,7 @@ import ctypes
 
 import numpy as np
 
-from ._lib import (DUMP_ROUTE, GEMM_SIMT, IO_DEVICE, N_STAGES, NO_GRAPH, PROFILE, Config, InzgError, MoeOpts, Stats, T_Q4L,
+from ._lib import (DUMP_ROUTE, GEMM_SIMT, IO_DEVICE, N_STAGES, NO_FUSED, NO_GRAPH, PROFILE, Config, InzgError, MoeOpts, Stats, T_Q4L,
                    T_Q8G, lib)
 
 
@@ -105,23 +105,27 @@ class MoePool:
         self._check(lib.inzg_device_status(self._ctx, stream and ctypes.c_void_p(stream)), "device_status")
 
     # -- forward --
-    def moe_block(self, layer, xin, bias=None, logits_override=None, dump=False, y=None, graph=True, simt_gemm=False):
-        """y [n][H] = routed MoE layer of xin [n][H] (host arrays; copies in and out inside the call)."""
+    def moe_block(self, layer, xin, bias=None, logits_override=None, dump=False, y=None, graph=True, simt_gemm=False,
+                  fused=True):
+        """y [n][H] = routed MoE layer of xin [n][H] (host arrays; copies in and out inside the call). fused=False runs
+        calls of 1-2 tokens through the separate kernels instead of the single fused launch (a cross-check)."""
         x = np.ascontiguousarray(xin, dtype=np.float32)
         n = x.shape[0]
         y = np.empty_like(x) if y is None else y
         b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
         o = None if logits_override is None else np.ascontiguousarray(logits_override, dtype=np.float32)
-        flags = (DUMP_ROUTE if dump else 0) | (0 if graph else NO_GRAPH) | (GEMM_SIMT if simt_gemm else 0)
+        flags = (DUMP_ROUTE if dump else 0) | (0 if graph else NO_GRAPH) | (GEMM_SIMT if simt_gemm else 0) | \
+            (0 if fused else NO_FUSED)
         opts = MoeOpts(flags, None if b is None else b.ctypes.data,
                        None if o is None else o.ctypes.data, None)
         self._check(lib.inzg_moe_forward(self._ctx, layer, n, _ptr(x), _ptr(y), ctypes.byref(opts)), "moe_forward")
         return y
 
     def moe_block_device(self, layer, n, x_ptr, y_ptr, bias_ptr=None, override_ptr=None, stream=None, dump=False,
-                         profile=False, graph=True):
+                         profile=False, graph=True, fused=True):
         """Stream-ordered call on device pointers (ints); returns immediately (profile=True: after the call)."""
-        flags = IO_DEVICE | (DUMP_ROUTE if dump else 0) | (PROFILE if profile else 0) | (0 if graph else NO_GRAPH)
+        flags = IO_DEVICE | (DUMP_ROUTE if dump else 0) | (PROFILE if profile else 0) | (0 if graph else NO_GRAPH) | \
+            (0 if fused else NO_FUSED)
         opts = MoeOpts(flags, bias_ptr, override_ptr, stream)
         self._check(lib.inzg_moe_forward(self._ctx, layer, n, ctypes.c_void_p(x_ptr), ctypes.c_void_p(y_ptr),
                                          ctypes.byref(opts)), "moe_forward")

@@ -1,7 +1,7 @@
 /* moe_host.c -- a C host of libinzg, the way the reference engine (C11) would drive it: open the model's GGUF, create
  * a context, fill the expert pool of every layer from the file, then run one MoE forward on a small batch.
  * Built and run by tests/test_abi.py to show the public header compiles as plain C and links; the router weights
- * are zeros here (a real engine passes its L->router view).
+ * are zeros here (a real engine passes its layer's F16 router view).
  *
  *   moe_host <model.gguf> [hidden ff n_expert topk]
  *

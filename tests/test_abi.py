@@ -33,10 +33,22 @@ def test_library_exports_every_declared_symbol():
     assert declared_symbols() <= set(_lib.SIGNATURES), set(declared_symbols()) - set(_lib.SIGNATURES)
 
 
-def test_library_is_the_sm100a_build():
-    from inferenz_b200 import _lib
-    data = open(_lib.LIB_PATH, "rb").read()
-    assert b"sm_100a" in data or b"sm_100" in data
+@pytest.mark.gpu
+def test_library_kernels_run_as_sm100_code():
+    """the kernels load as sm_100 machine code (cudaFuncGetAttributes at run time), not a PTX recompilation"""
+    from inferenz_b200 import lib
+    bv, pv = ctypes.c_int(0), ctypes.c_int(0)
+    assert lib.inzg_kernel_arch(0, ctypes.byref(bv), ctypes.byref(pv)) == 0
+    assert bv.value == 100, bv.value
+
+
+def test_kernel_arch_query_fails_cleanly_without_a_device():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a device is present")
+    from inferenz_b200 import lib
+    bv = ctypes.c_int(0)
+    assert lib.inzg_kernel_arch(0, ctypes.byref(bv), None) == -1
 
 
 def test_status_strings():
