@@ -41,6 +41,10 @@ GU_PAYLOAD_Q8G = 2 * FF * (H // 64) * 66    # Q8G: 64 index bytes + fp16 scale p
 DN_PAYLOAD_Q8G = H * (FF // 64) * 66
 EXPERT_BYTES_Q8G = 4055168
 ROUTER_BYTES = E * H * 2
+# prefill-numerics experts read the requantized int8 weights and their per-(row, 256-block) fp32 scales
+GEMM_GU_BYTES = 2 * FF * H + 2 * FF * (H // 256) * 4
+GEMM_DN_BYTES = H * FF + H * (-(-FF // 256)) * 4
+GEMV_GEMM_MAX_TOKENS = 32  # calls up to this size run those experts inside the decode GEMV launches
 
 
 NVLINK_GBS = 770.0  # NVLink 5 peer copy per direction per GPU, the pool's published measurement (900 GB/s nominal)
@@ -253,8 +257,9 @@ def stage_roofline(stage_ms, stats, n, hbm, q8g=False, i8_peak=None):
     algo = {
         "fused_decode": ROUTER_BYTES + stats["units"] * expert_bytes + 2 * n * H * 4,  # the whole layer, one launch
         "router_logits": ROUTER_BYTES + n * H * 4 + n * E * 4,
-        "gate_up_gemv": dec * gu,
-        "down_gemv": dec * dn,
+        # calls of <= 32 tokens: the decode GEMV launches also run the prefill-numerics experts (GEMM items)
+        "gate_up_gemv": dec * gu + (gemm * GEMM_GU_BYTES if n <= GEMV_GEMM_MAX_TOKENS else 0),
+        "down_gemv": dec * dn + (gemm * GEMM_DN_BYTES if n <= GEMV_GEMM_MAX_TOKENS else 0),
         "gate_up_gemm": gemm * gu,
         "down_gemm": gemm * dn,
     }

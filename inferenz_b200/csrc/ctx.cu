@@ -43,6 +43,7 @@ struct LayerSlot {
     int e_first = 0;            // the pool holds experts [e_first, e_first + dev.E) of the layer's n_expert
     bool has_maps = false;
     TmaMap map_gu, map_dn;      // TMA maps over the prefill-path int8 weights
+    TmaMap map16_gu, map16_dn;  // the same weights in 16-row boxes (GEMM items of the decode GEMV)
     uint4 *router = nullptr;
     float *router32 = nullptr;  // the same router in fp32, laid out for the many-token kernel (nullptr: not used)
     uint8_t *pool = nullptr;
@@ -485,7 +486,9 @@ static inzg_status load_pool(inzg_ctx *c, LayerSlot &L, int type, const void *bl
     cudaFree(stage);
     if (err != cudaSuccess) return cuda_fail(c, err, "pool_add_layer");
     L.has_maps = make_tma_map_i8(L.map_gu.bytes, D.w8_gu, (uint64_t)E * 2 * FF, H, 128) &&
-                 make_tma_map_i8(L.map_dn.bytes, D.w8_dn, (uint64_t)E * H, FF, 128);
+                 make_tma_map_i8(L.map_dn.bytes, D.w8_dn, (uint64_t)E * H, FF, 128) &&
+                 make_tma_map_i8(L.map16_gu.bytes, D.w8_gu, (uint64_t)E * 2 * FF, H, 16) &&
+                 make_tma_map_i8(L.map16_dn.bytes, D.w8_dn, (uint64_t)E * H, FF, 16);
     err = cudaGetLastError();
     if (err != cudaSuccess) return cuda_fail(c, err, "pool_add_layer repack");
     L.has_experts = true;
@@ -635,8 +638,13 @@ static int enqueue_forward(inzg_ctx *c, int layer, const LayerSlot &L, int n, co
     // the prefill GEMM runs on tcgen05 unless the caller asked for the CUDA-core cross-check (INZG_GEMM_SIMT); a
     // context without tensor maps fails the call instead of falling back silently
     if (any_gemm && !simt_gemm && !tc) return -2;
+    // decode-sized calls: the prefill-numerics experts run inside the decode GEMV launches as 16-token GEMM items
+    const bool in_gemv = any_gemm && tc && n <= kGemvGemmMaxTokens;
+    const int gtile = in_gemv ? kGemvGemmTile : gemm_token_tile();
+    const DecGemm gm_gu{c->xq256, c->xs256, D.ws_gu, L.map16_gu.bytes}, gm_dn{c->dq256, c->ds256, D.ws_dn,
+                                                                               L.map16_dn.bytes};
     const int fused = launch_route_fused(R, c->logits, dump ? c->probs : nullptr, gemv_items_per_unit(D, 0, R.n), gemv_items_per_unit(D, 1, R.n),
-                                         gemm_token_tile(), c->upath, c->eexp, st);
+                                         gtile, c->upath, c->eexp, st);
     if (fused > 0) {
         add(fused);
         mark(2);
@@ -648,15 +656,15 @@ static int enqueue_forward(inzg_ctx *c, int layer, const LayerSlot &L, int n, co
         add(launch_act_quant_x(X, n, H, D.gu_rot, D.gu_seed, c->xq64, c->xsb64, any_gemm ? c->xq256 : nullptr,
                                        c->xs256, st));
     mark(3);
-    if (fused <= 0) add(launch_route(R, gemv_items_per_unit(D, 0, R.n), gemv_items_per_unit(D, 1, R.n), gemm_token_tile(), c->upath, c->eexp, st));
+    if (fused <= 0) add(launch_route(R, gemv_items_per_unit(D, 0, R.n), gemv_items_per_unit(D, 1, R.n), gtile, c->upath, c->eexp, st));
     const int nkbH = (H + kKB - 1) / kKB;
     const int max_tiles = (NE + gemm_token_tile() - 1) / gemm_token_tile() + std::min(E, NE / kGemmMinT) + 1;
     if (branch) cudaStreamWaitEvent(st, c->join, 0);
     mark(4);
     const int grid = c->num_sms * 4;
-    add(launch_gemv_decode(D, 0, R, c->xq64, c->xsb64, c->GU, 2 * FF, c->num_sms, st));
+    add(launch_gemv_decode(D, 0, R, c->xq64, c->xsb64, c->GU, 2 * FF, c->num_sms, st, in_gemv ? &gm_gu : nullptr));
     mark(5);
-    if (any_gemm) {
+    if (any_gemm && !in_gemv) {
         if (tc) {
             add(launch_gather_gemm_rows(c->xq256, c->xs256, H, nkbH, c->etok, c->eexp, c->upath, NE, c->xqe,
                                                 c->xse, st));
@@ -670,9 +678,9 @@ static int enqueue_forward(inzg_ctx *c, int layer, const LayerSlot &L, int n, co
     add(launch_swiglu_quant(c->GU, FF, NE, c->eexp, c->upath, D.dn_rot, D.dn_seed, c->dq64, c->dsb64, c->dq256,
                                     c->ds256, st));
     mark(7);
-    add(launch_gemv_decode(D, 1, R, c->dq64, c->dsb64, c->mo, H, c->num_sms, st));
+    add(launch_gemv_decode(D, 1, R, c->dq64, c->dsb64, c->mo, H, c->num_sms, st, in_gemv ? &gm_dn : nullptr));
     mark(8);
-    if (any_gemm) {
+    if (any_gemm && !in_gemv) {
         if (tc) add(launch_gemm_tc(1, L.map_dn.bytes, c->map_dq.bytes, D.ws_dn, H, FF, R, c->ds256, c->mo, H,
                                            max_tiles, st));
         else add(launch_gemm_v1(D, 1, R, c->dq256, c->ds256, c->mo, H, grid, st));
@@ -855,14 +863,18 @@ inzg_status inzg_moe_experts(inzg_ctx *c, int layer, int m, const float *x_dev, 
     R.cnt = c->cnt; R.off = c->off; R.first = c->first; R.etok = c->etok; R.eslot = c->eslot;
     R.ew = c->ew; R.ccnt = c->ccnt; R.cmask = c->cmask; R.units = c->units; R.meta = c->meta; R.dec_units = c->dec_units;
     R.gemm_units = c->gemm_units; R.gemm_tiles = c->gemm_tiles;
-    launch_route(R, gemv_items_per_unit(D, 0, R.n), gemv_items_per_unit(D, 1, R.n), gemm_token_tile(), c->upath,
-                 c->eexp, st);
     const bool tc = c->have_tc && L.has_maps;
     if (any_gemm && !tc) return fail(c, INZG_UNSUPPORTED, "moe_experts: no tensor maps for the prefill GEMM");
+    const bool in_gemv = any_gemm && m <= kGemvGemmMaxTokens;  // GEMM items inside the decode GEMV launches
+    launch_route(R, gemv_items_per_unit(D, 0, R.n), gemv_items_per_unit(D, 1, R.n),
+                 in_gemv ? kGemvGemmTile : gemm_token_tile(), c->upath, c->eexp, st);
+    const DecGemm gm_gu{c->xq256, c->xs256, D.ws_gu, L.map16_gu.bytes}, gm_dn{c->dq256, c->ds256, D.ws_dn,
+                                                                               L.map16_dn.bytes};
     const int nkbH = (H + kKB - 1) / kKB;
     const int max_tiles = (NE + gemm_token_tile() - 1) / gemm_token_tile() + std::min(E, NE / kGemmMinT) + 1;
-    launch_gemv_decode(D, 0, R, c->xq64, c->xsb64, c->GU, 2 * FF, c->num_sms, st);
-    if (any_gemm) {
+    if (launch_gemv_decode(D, 0, R, c->xq64, c->xsb64, c->GU, 2 * FF, c->num_sms, st, in_gemv ? &gm_gu : nullptr) < 0)
+        return fail(c, INZG_UNSUPPORTED, "moe_experts: no decode kernel for this call");
+    if (any_gemm && !in_gemv) {
         if (tc) {
             launch_gather_gemm_rows(c->xq256, c->xs256, H, nkbH, c->etok, c->eexp, c->upath, NE, c->xqe, c->xse, st);
             if (launch_gemm_tc(0, L.map_gu.bytes, c->map_xqe.bytes, D.ws_gu, 2 * FF, H, R, c->xse, c->GU, 2 * FF,
@@ -871,8 +883,9 @@ inzg_status inzg_moe_experts(inzg_ctx *c, int layer, int m, const float *x_dev, 
         }
     }
     launch_swiglu_quant(c->GU, FF, NE, c->eexp, c->upath, D.dn_rot, D.dn_seed, c->dq64, c->dsb64, c->dq256, c->ds256, st);
-    launch_gemv_decode(D, 1, R, c->dq64, c->dsb64, out_dev, H, c->num_sms, st);
-    if (any_gemm) {
+    if (launch_gemv_decode(D, 1, R, c->dq64, c->dsb64, out_dev, H, c->num_sms, st, in_gemv ? &gm_dn : nullptr) < 0)
+        return fail(c, INZG_UNSUPPORTED, "moe_experts: no decode kernel for this call");
+    if (any_gemm && !in_gemv) {
         if (launch_gemm_tc(1, L.map_dn.bytes, c->map_dq.bytes, D.ws_dn, H, FF, R, c->ds256, out_dev, H, max_tiles,
                            st) < 0)
             return fail(c, INZG_UNSUPPORTED, "moe_experts: no GEMM kernel for this shape");

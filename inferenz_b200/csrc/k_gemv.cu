@@ -26,6 +26,13 @@
 // weight fragment, then two MMAs and the reference's fma per token. The bias chains need only the
 // scales and bsum, so they run once per item in the epilogue. Every wait is bounded; a CTA that gives up records
 // INZG_TIMEOUT and drains its copies before it leaves.
+//
+// GEMM items (calls of 9-32 tokens): the experts such a call sends down the reference's prefill numerics (>= 12 tokens)
+// run in the same launch instead of a separate gather + GEMM. Their items -- up to 15 row tiles of one expert with all
+// its tokens -- lead the work queue; a stage then carries 128 bytes of K of the requantized int8 row tiles (tensor
+// copies) and of the token rows (bulk copies), and each warp runs ldmatrix + s8 x s8 MMAs with the per-256-block fp32
+// fold (gemm_item). The kernel instantiation with GEMM items takes them in a loop of their own before the decode loop;
+// calls without them run the decode-only instantiation.
 #include "inzg_internal.h"
 #include "k_async.cuh"
 #include "k_launch.h"
@@ -36,7 +43,7 @@
 
 namespace inzg {
 
-template <bool Q8, int NG, int KIND, int W = 8>
+template <bool Q8, int NG, int KIND, int W = 8, bool HG = false>
 struct DecGeo {
     // Consumer warps, one 16-row tile each: an item is up to W row tiles of one expert matrix (the last item of a
     // matrix holds the remaining tiles). W = 8: 9 warps per CTA, items of 128 rows, for calls of a few tokens whose
@@ -50,7 +57,10 @@ struct DecGeo {
     static constexpr int WB = Q8 ? 32 : 16;          // weight bytes per lane per group
     static constexpr int GD = (NG + 3) / 4;
     static constexpr int WQ = KC * 32 * WB;          // weight bytes of one row tile in one stage
-    static constexpr int STAGE = WARPS * WQ;
+    // GEMM items (wide geometry only) also bring, per stage, the 128-byte K chunk of each of their <= 32 token rows,
+    // after the weights at a padded stride (the 8 rows an ldmatrix reads fall in 8 different bank quads)
+    static constexpr int TSTR = 144, TOK = HG ? 32 * TSTR : 0;
+    static constexpr int STAGE = (WARPS * WQ + TOK + 1023) / 1024 * 1024;
     static constexpr int K = NG * kGroup;
     static constexpr int MT = 12;                    // most tokens of a decode expert: 11 (8 when n <= 8)
     // item buffer: token activations [MT][K], their (s, bsum) [MT][NG], the row tiles' scales [WARPS][GD][8][4][2]
@@ -64,11 +74,13 @@ struct DecGeo {
 // Item descriptor written by the producer warp, read by the consumers after the item's buffer has landed
 // (e == kDecEnd: the work queue is empty).
 constexpr int kDecEnd = -3;
+constexpr int kGemmEnd = -4;  // the CTA's GEMM items are over: decode items follow
 struct DecItem {
     int e, base, ntok, rb, ntiles;
     uint4 lut;
-    int oslot[16];
-    float ow[16];
+    int oslot[32];  // down matrix: each token's output slot and routing weight (decode items <= 12 tokens, GEMM
+    float ow[32];   // items <= 32)
+    int trow[32];   // GEMM items: activation row of each token (gate|up: the token, down: the entry)
 };
 
 struct DecShared {
@@ -78,10 +90,10 @@ struct DecShared {
 };
 
 // Consumer: the item's TC >= ntok tokens on this warp's 16-row tile. q: running stage counter (advanced by NCH).
-template <bool Q8, int NG, int KIND, int W, int TC>
+template <bool Q8, int NG, int KIND, int W, bool HG, int TC>
 __device__ __forceinline__ bool dec_item(DecShared &S, const uint8_t *stages, const uint8_t *ib, const DecItem &it,
                                          int &q, float *__restrict__ out, int out_ld, uint32_t one) {
-    using G = DecGeo<Q8, NG, KIND, W>;
+    using G = DecGeo<Q8, NG, KIND, W, HG>;
     volatile int *abort = &S.abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gr = lane >> 2, t = lane & 3;
     // Tokens go through the MMAs in pairs (A = 2p, B = 2p + 1). Column n = gr of the activation operand carries token
@@ -242,20 +254,260 @@ __device__ __forceinline__ bool dec_item(DecShared &S, const uint8_t *stages, co
     return true;
 }
 
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t &r0, uint32_t &r1) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+__device__ __forceinline__ void mma_s8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Consumer of a GEMM item: up to 8 * NTG tokens of a prefill-numerics expert on this warp's 16-row tile, with the
+// reference's prefill arithmetic (inz_gemm_rows, src/quant.c:1615-1668) -- per 256-block the exact int32 dot of the
+// requantized int8 weights and the token's int8 block, then f = fma((float)dot_b, ws_b * xs_b, f) over the blocks in
+// order (the tcgen05 GEMM's float sequence, k_gemm_tc.cu). A stage holds 128 bytes of K of the tile's 16 rows as the
+// tensor copy left them (128-byte swizzle: 16-byte chunk c of row r at chunk c ^ (r & 7)) and the same 128 bytes of
+// every token row; ldmatrix gives the MMA's A fragments from the first, its B fragments from the second. The accumulators start at the bits of 1.5 * 2^23, so
+// one add of -12582912 gives (float)dot exactly (|dot| <= 256 * 127 * 127 < 2^22).
+template <bool Q8, int NG, int KIND, int W, int NTG>
+__device__ __forceinline__ bool gemm_item(DecShared &S, const uint8_t *stages, const DecItem &it,
+                                          int &q, float *__restrict__ out, int out_ld, const float *__restrict__ as,
+                                          const float *__restrict__ wsc, int mrows) {
+    using G = DecGeo<Q8, NG, KIND, W, true>;
+    constexpr int K = G::K, NCHG = K / 128, NKB = (K + 255) / 256;
+    volatile int *abort = &S.abort;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gr = lane >> 2, t = lane & 3;
+    const bool valid = it.e >= 0 && warp < it.ntiles;
+    const int ntok = it.ntok;
+    const int row0 = (it.rb * G::WARPS + warp) * 16 + gr;  // this thread's rows row0 and row0 + 8
+    const float *ws0 = wsc + ((size_t)(it.e < 0 ? 0 : it.e) * mrows + row0) * NKB, *ws1 = ws0 + 8 * NKB;
+    // the block-scale rows of this thread's accumulator columns (tokens 8 tg + 2t, 8 tg + 2t + 1); a column past the
+    // item's tokens reads token 0's (its outputs are not written)
+    int xsr[NTG][2];
+#pragma unroll
+    for (int tg = 0; tg < NTG; tg++)
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int j = tg * 8 + 2 * t + h;
+            xsr[tg][h] = it.trow[j < ntok ? j : 0] * NKB;
+        }
+    // ldmatrix lane addresses: A matrix lane >> 3 = (rows 0-7 | 8-15) x (first | second 16 bytes of a 32-byte K step);
+    // B matrix (lane >> 3) & 1 = first | second 16 bytes of the step for token rows lane & 7
+    const int ar = lane & 15;
+    const uint32_t a_row = (uint32_t)ar * 128, a_sw = (uint32_t)(ar & 7), a_hi = (uint32_t)(lane >> 4);
+    const uint32_t b_lane = (uint32_t)(G::WARPS * G::WQ + (lane & 7) * G::TSTR + 16 * ((lane >> 3) & 1));
+    int D[NTG][4];
+    float2 f[NTG][2];
+#pragma unroll
+    for (int tg = 0; tg < NTG; tg++) f[tg][0] = f[tg][1] = make_float2(0.0f, 0.0f);
+    const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
+    float w0 = 0.0f, w1 = 0.0f, xv[NTG][2];
+#pragma unroll 1
+    for (int c = 0; c < NCHG; c++, q++) {
+        const int s = q % G::STAGES;
+        if (!(c & 1) && valid) {  // a block begins: its scales load while its MMAs run
+            const int b = c >> 1;
+            w0 = __ldg(ws0 + b);
+            w1 = __ldg(ws1 + b);
+#pragma unroll
+            for (int tg = 0; tg < NTG; tg++) {
+                xv[tg][0] = __ldg(as + xsr[tg][0] + b);
+                xv[tg][1] = __ldg(as + xsr[tg][1] + b);
+#pragma unroll
+                for (int i = 0; i < 4; i++) D[tg][i] = 0x4B400000;
+            }
+        }
+        if (!mbar_wait(&S.full[s], (q / G::STAGES) & 1, abort)) return false;
+        if (valid) {
+            const uint32_t sb = smem_u32(stages + (size_t)s * G::STAGE), wt = sb + (uint32_t)(warp * G::WQ) + a_row;
+#pragma unroll
+            for (int ks = 0; ks < 4; ks++) {
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4(wt + ((((uint32_t)(2 * ks) + a_hi) ^ a_sw) << 4), a0, a1, a2, a3);
+#pragma unroll
+                for (int tg = 0; tg < NTG; tg++) {
+                    uint32_t b0, b1;
+                    ldsm_x2(sb + b_lane + (uint32_t)(tg * 8 * G::TSTR + 32 * ks), b0, b1);
+                    mma_s8s8(D[tg], a0, a1, a2, a3, b0, b1);
+                }
+            }
+            if ((c & 1) || c == NCHG - 1) {  // the block's dot is complete: fold it
+                const float2 wp0 = make_float2(w0, w0), wp1 = make_float2(w1, w1);
+#pragma unroll
+                for (int tg = 0; tg < NTG; tg++) {
+                    const float2 xp = make_float2(xv[tg][0], xv[tg][1]);
+                    const float2 p0 = __fmul2_rn(wp0, xp), p1 = __fmul2_rn(wp1, xp);
+                    const float2 d01 = __fadd2_rn(make_float2(__int_as_float(D[tg][0]), __int_as_float(D[tg][1])),
+                                                  neg_magic);
+                    const float2 d23 = __fadd2_rn(make_float2(__int_as_float(D[tg][2]), __int_as_float(D[tg][3])),
+                                                  neg_magic);
+                    f[tg][0] = __ffma2_rn(d01, p0, f[tg][0]);
+                    f[tg][1] = __ffma2_rn(d23, p1, f[tg][1]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.empty[s]);
+    }
+    if (!valid) return true;
+#pragma unroll
+    for (int tg = 0; tg < NTG; tg++)
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int j = tg * 8 + 2 * t + h;
+            if (j >= ntok) continue;
+#pragma unroll
+            for (int r = 0; r < 2; r++) {
+                const float v = h ? f[tg][r].y : f[tg][r].x;
+                const int row = row0 + 8 * r;
+                if (KIND == 0) out[(size_t)(it.base + j) * out_ld + row] = v;
+                else out[(size_t)it.oslot[j] * out_ld + row] = __fmul_rn(it.ow[j], v);
+            }
+        }
+    return true;
+}
+
+// GEMM phase of the producer warp (kernels with GEMM items): takes items from the queue while they are GEMM items
+// (they precede every decode item) and issues, per item, its stages of 128 bytes of K: the row tiles by tensor copies
+// (16 rows, 128-byte swizzle) and the token rows' chunks by bulk copies; then publishes the kGemmEnd marker and hands
+// the first non-GEMM item back in `pending`. A loop of its own ahead of the decode loop (and the GEMM items a kernel
+// instantiation of their own), so the decode loop compiles as in the decode-only kernel. Returns false when a wait ran
+// out.
 template <bool Q8, int NG, int KIND, int W>
-__global__ void __launch_bounds__(DecGeo<Q8, NG, KIND, W>::THREADS, 1)
+__device__ __forceinline__ bool gemm_produce(DecShared &S, uint8_t *stages, const MatLayout &M, int E, const RouteDev &R,
+                                          const CUtensorMap *wmap, const int8_t *__restrict__ gaq, int meta_work,
+                                          int ngi, int per, int &q, int &li, int &na, int &pending) {
+    using G = DecGeo<Q8, NG, KIND, W, true>;
+    volatile int *abort = &S.abort;
+    const int lane = threadIdx.x & 31, tiles = M.rows / 16;
+    for (;; li++) {
+        const int ab = li & 1;
+        if (li >= 2 && !mbar_wait(&S.aempty[ab], ((li >> 1) + 1) & 1, abort)) return false;
+        DecItem &D = S.item[ab];
+        int item = 0;
+        if (lane == 0) item = atomicAdd(R.meta + meta_work, 1);
+        item = __shfl_sync(0xffffffffu, item, 0);
+        if (item >= ngi) {
+            if (lane == 0) {
+                D.e = kGemmEnd;
+                mbar_arrive(&S.afull[ab]);
+            }
+            pending = item;
+            na++;
+            li++;
+            return true;
+        }
+        int e = 0, base = 0, ntok = 0;
+        if (lane == 0) {  // (unit << 16 | token tile) of a prefill-numerics expert
+            const int tl = __ldg(R.gemm_tiles + item / per), u = tl >> 16, tt = tl & 0xFFFF;
+            e = u < E ? __ldg(R.gemm_units + u) : -1;
+            if (e < 0 || e >= E) { set_error(R.meta, kErrBadExpert); e = -1; }
+            else {
+                base = __ldg(R.off + e) + tt * kGemvGemmTile;
+                ntok = __ldg(R.cnt + e) - tt * kGemvGemmTile;
+                ntok = ntok < kGemvGemmTile ? ntok : kGemvGemmTile;  // the ring's token rows hold 32
+                if (ntok <= 0) { set_error(R.meta, kErrOverflow); e = -1; ntok = 0; }
+            }
+        }
+        e = __shfl_sync(0xffffffffu, e, 0);
+        base = __shfl_sync(0xffffffffu, base, 0);
+        ntok = __shfl_sync(0xffffffffu, ntok, 0);
+        int row = 0;
+        if (lane < ntok) {
+            row = KIND == 0 ? __ldg(R.etok + base + lane) : base + lane;
+            if (KIND == 1) { D.oslot[lane] = __ldg(R.eslot + base + lane); D.ow[lane] = __ldg(R.ew + base + lane); }
+            D.trow[lane] = row;
+        }
+        const int rb = item % per, rt0 = rb * G::WARPS, nt = tiles - rt0 < G::WARPS ? tiles - rt0 : G::WARPS;
+        if (lane == 0) {
+            D.e = e; D.base = base; D.ntok = ntok; D.rb = rb; D.ntiles = nt;
+            D.lut = make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();  // every lane's trow / oslot / ow before the release
+        if (lane == 0) mbar_arrive(&S.afull[ab]);  // nothing in the item buffer: every operand comes with the stages
+        na++;
+        for (int c = 0; c < G::K / 128; c++, q++) {
+            const int s = q % G::STAGES;
+            if (q >= G::STAGES && !mbar_wait(&S.empty[s], ((q / G::STAGES) + 1) & 1, abort)) return false;
+            uint8_t *sp = stages + (size_t)s * G::STAGE;
+            if (lane == 0) {
+                if (e >= 0) mbar_expect_tx(&S.full[s], (uint32_t)(nt * 2048 + ntok * 128));
+                else mbar_arrive(&S.full[s]);
+            }
+            __syncwarp();
+            if (e >= 0 && lane < nt)
+                tma_load_2d(sp + (size_t)lane * G::WQ, wmap, c * 128, e * M.rows + (rt0 + lane) * 16, &S.full[s]);
+            if (e >= 0 && lane < ntok)
+                bulk_g2s(sp + G::WARPS * G::WQ + lane * G::TSTR, gaq + (size_t)row * G::K + c * 128, 128, &S.full[s]);
+        }
+    }
+}
+
+// GEMM phase of a consumer warp: GEMM items up to the kGemmEnd marker. Returns 0 (decode items follow), 1 (the queue
+// is over) or -1 (a wait ran out).
+template <bool Q8, int NG, int KIND, int W>
+__device__ __forceinline__ int gemm_consume(DecShared &S, const uint8_t *stages, int &q, int &li, float *__restrict__ out,
+                                         int out_ld, const float *__restrict__ gas, const float *__restrict__ gws,
+                                         int mrows) {
+    volatile int *abort = &S.abort;
+    const int lane = threadIdx.x & 31;
+    for (;; li++) {
+        const int ab = li & 1;
+        if (!mbar_wait(&S.afull[ab], (li >> 1) & 1, abort)) return -1;
+        const DecItem &it = S.item[ab];
+        if (it.e == kDecEnd) return 1;
+        const bool end = it.e == kGemmEnd;
+        if (!end) {
+            // prefill-numerics experts have at least 12 tokens: 2-4 groups of 8 MMA columns
+            const int nt = it.ntok;
+            bool ok;
+            if (nt <= 16) ok = gemm_item<Q8, NG, KIND, W, 2>(S, stages, it, q, out, out_ld, gas, gws, mrows);
+            else if (nt <= 24) ok = gemm_item<Q8, NG, KIND, W, 3>(S, stages, it, q, out, out_ld, gas, gws, mrows);
+            else ok = gemm_item<Q8, NG, KIND, W, 4>(S, stages, it, q, out, out_ld, gas, gws, mrows);
+            if (!ok) return -1;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.aempty[ab]);
+        if (end) {
+            li++;
+            return 0;
+        }
+    }
+}
+
+template <bool Q8, int NG, int KIND, int W, bool HG>
+__global__ void __launch_bounds__(DecGeo<Q8, NG, KIND, W, HG>::THREADS, 1)
     gemv_decode_kernel(const uint8_t *__restrict__ pool, uint64_t slab_bytes, MatLayout M, const uint8_t *__restrict__ luts,
                        int lut_off, int E, RouteDev R, const int8_t *__restrict__ aq, const float2 *__restrict__ asb,
-                       float *__restrict__ out, int out_ld, int meta_items, int meta_work, uint32_t one) {
-    using G = DecGeo<Q8, NG, KIND, W>;
+                       float *__restrict__ out, int out_ld, int meta_items, int meta_work, uint32_t one,
+                       const __grid_constant__ CUtensorMap wmap, const int8_t *__restrict__ gaq,
+                       const float *__restrict__ gas, const float *__restrict__ gws, int meta_gtiles) {
+    using G = DecGeo<Q8, NG, KIND, W, HG>;
     extern __shared__ __align__(1024) uint8_t smem[];
     DecShared &S = *reinterpret_cast<DecShared *>(smem);
+    // the stage ring starts on a 1024-byte boundary (the 128-byte swizzle of the GEMM items' tensor copies): HDR and
+    // STAGE are multiples of 1024 and the dynamic shared memory starts on one (checked: a CTA that finds otherwise
+    // fails the call)
     uint8_t *stages = smem + G::HDR;
     uint8_t *ibufs = stages + (size_t)G::STAGES * G::STAGE;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nitems = R.meta[meta_items];
     const int tiles = M.rows / 16, per = (tiles + G::WARPS - 1) / G::WARPS;  // items per matrix
+    // HG: the call's GEMM items (prefill-numerics experts, the heaviest work) come first in the queue, then the decode
+    // items
+    const int ngi = HG ? R.meta[meta_gtiles] * per : 0;
+    const int nitems = R.meta[meta_items] + ngi;
     if ((int)blockIdx.x >= nitems) return;
+    if (HG && (smem_u32(smem) & 1023u)) {
+        if (threadIdx.x == 0) set_error(R.meta, kErrBadSlot);
+        return;
+    }
     if (threadIdx.x == 0) {
         for (int i = 0; i < G::STAGES; i++) { mbar_init(&S.full[i], 1); mbar_init(&S.empty[i], G::WARPS); }
         for (int i = 0; i < 2; i++) { mbar_init(&S.afull[i], 1); mbar_init(&S.aempty[i], G::WARPS); }
@@ -271,13 +523,20 @@ __global__ void __launch_bounds__(DecGeo<Q8, NG, KIND, W>::THREADS, 1)
         // items come from the call's work queue (the route kernel lists experts heaviest first and clears the counter)
         int q = 0, li = 0, na = 0;  // stages issued, items begun, items whose buffers were issued
         bool ok = true;
-        for (;; li++) {
+        // HG: the GEMM phase first; its kGemmEnd marker tells the consumers that decode items follow
+        int pending = -1;
+        if constexpr (HG)
+            ok = gemm_produce<Q8, NG, KIND, W>(S, stages, M, E, R, &wmap, gaq, meta_work, ngi, per, q, li, na, pending);
+        for (; ok; li++) {
             const int ab = li & 1;
             if (li >= 2 && !mbar_wait(&S.aempty[ab], ((li >> 1) + 1) & 1, abort)) { ok = false; break; }
             DecItem &D = S.item[ab];
-            int item = 0;
-            if (lane == 0) item = atomicAdd(R.meta + meta_work, 1);
-            item = __shfl_sync(0xffffffffu, item, 0);
+            int item = pending;
+            if (!HG || item < 0) {
+                if (lane == 0) item = atomicAdd(R.meta + meta_work, 1);
+                item = __shfl_sync(0xffffffffu, item, 0);
+            }
+            pending = -1;
             if (item >= nitems) {
                 if (lane == 0) {
                     D.e = kDecEnd;
@@ -285,9 +544,10 @@ __global__ void __launch_bounds__(DecGeo<Q8, NG, KIND, W>::THREADS, 1)
                 }
                 break;
             }
+            const int unit_item = item - ngi, rb = unit_item % per;
             int e = 0, base = 0, ntok = 0;
             if (lane == 0) {
-                e = __ldg(R.dec_units + item / per);
+                e = __ldg(R.dec_units + unit_item / per);
                 if (e < 0 || e >= E) { set_error(R.meta, kErrBadExpert); e = -1; }
                 else {
                     base = __ldg(R.off + e);
@@ -303,10 +563,10 @@ __global__ void __launch_bounds__(DecGeo<Q8, NG, KIND, W>::THREADS, 1)
                 row = KIND == 0 ? __ldg(R.etok + base + lane) : base + lane;
                 if (KIND == 1) { D.oslot[lane] = __ldg(R.eslot + base + lane); D.ow[lane] = __ldg(R.ew + base + lane); }
             }
-            const int rt0 = (item % per) * G::WARPS, nt = tiles - rt0 < G::WARPS ? tiles - rt0 : G::WARPS;
+            const int rt0 = rb * G::WARPS, nt = tiles - rt0 < G::WARPS ? tiles - rt0 : G::WARPS;
             const uint8_t *slab = pool + (size_t)(e < 0 ? 0 : e) * slab_bytes;
             if (lane == 0) {
-                D.e = e; D.base = base; D.ntok = ntok; D.rb = item % per; D.ntiles = nt;
+                D.e = e; D.base = base; D.ntok = ntok; D.rb = rb; D.ntiles = nt;
                 D.lut = (!Q8 && e >= 0) ? __ldg(reinterpret_cast<const uint4 *>(luts + (size_t)e * 32 + lut_off))
                                         : make_uint4(0, 0, 0, 0);
             }
@@ -359,8 +619,14 @@ __global__ void __launch_bounds__(DecGeo<Q8, NG, KIND, W>::THREADS, 1)
     }
 
     // ---------------- consumer warps ----------------
-    int q = 0;
-    for (int li = 0;; li++) {
+    int q = 0, li = 0;
+    bool fail = false;
+    if constexpr (HG) {
+        const int r = gemm_consume<Q8, NG, KIND, W>(S, stages, q, li, out, out_ld, gas, gws, M.rows);
+        if (r == 1) return;
+        fail = r < 0;
+    }
+    for (; !fail; li++) {
         const int ab = li & 1;
         if (!mbar_wait(&S.afull[ab], (li >> 1) & 1, abort)) break;
         const DecItem &it = S.item[ab];
@@ -368,13 +634,13 @@ __global__ void __launch_bounds__(DecGeo<Q8, NG, KIND, W>::THREADS, 1)
         const uint8_t *ib = ibufs + (size_t)ab * G::IBUF;
         const int nt = it.ntok;
         bool ok;
-        if (nt <= 1) ok = dec_item<Q8, NG, KIND, W, 1>(S, stages, ib, it, q, out, out_ld, one);
-        else if (nt <= 2) ok = dec_item<Q8, NG, KIND, W, 2>(S, stages, ib, it, q, out, out_ld, one);
-        else if (nt <= 3) ok = dec_item<Q8, NG, KIND, W, 3>(S, stages, ib, it, q, out, out_ld, one);
-        else if (nt <= 4) ok = dec_item<Q8, NG, KIND, W, 4>(S, stages, ib, it, q, out, out_ld, one);
-        else if (nt <= 6) ok = dec_item<Q8, NG, KIND, W, 6>(S, stages, ib, it, q, out, out_ld, one);
-        else if (nt <= 8) ok = dec_item<Q8, NG, KIND, W, 8>(S, stages, ib, it, q, out, out_ld, one);
-        else ok = dec_item<Q8, NG, KIND, W, 12>(S, stages, ib, it, q, out, out_ld, one);
+        if (nt <= 1) ok = dec_item<Q8, NG, KIND, W, HG, 1>(S, stages, ib, it, q, out, out_ld, one);
+        else if (nt <= 2) ok = dec_item<Q8, NG, KIND, W, HG, 2>(S, stages, ib, it, q, out, out_ld, one);
+        else if (nt <= 3) ok = dec_item<Q8, NG, KIND, W, HG, 3>(S, stages, ib, it, q, out, out_ld, one);
+        else if (nt <= 4) ok = dec_item<Q8, NG, KIND, W, HG, 4>(S, stages, ib, it, q, out, out_ld, one);
+        else if (nt <= 6) ok = dec_item<Q8, NG, KIND, W, HG, 6>(S, stages, ib, it, q, out, out_ld, one);
+        else if (nt <= 8) ok = dec_item<Q8, NG, KIND, W, HG, 8>(S, stages, ib, it, q, out, out_ld, one);
+        else ok = dec_item<Q8, NG, KIND, W, HG, 12>(S, stages, ib, it, q, out, out_ld, one);
         if (!ok) break;
         __syncwarp();
         if (lane == 0) mbar_arrive(&S.aempty[ab]);
@@ -384,17 +650,27 @@ __global__ void __launch_bounds__(DecGeo<Q8, NG, KIND, W>::THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-template <bool Q8, int NG, int KIND, int W>
+template <bool Q8, int NG, int KIND, int W, bool HG>
 static void launch_one(const LayerDev &L, const MatLayout &M, const RouteDev &R, const int8_t *aq, const float2 *asb,
-                       float *out, int out_ld, int meta_items, int num_sms, cudaStream_t st) {
-    using G = DecGeo<Q8, NG, KIND, W>;
+                       float *out, int out_ld, int meta_items, int num_sms, cudaStream_t st, const DecGemm *gm) {
+    using G = DecGeo<Q8, NG, KIND, W, HG>;
     static_assert(G::SMEM <= 227 * 1024, "decode GEMV shared memory");
     static_assert(sizeof(DecShared) <= G::HDR, "decode GEMV header");
     static_assert(G::WARPS < 32, "one producer lane per row tile");
-    cudaFuncSetAttribute(gemv_decode_kernel<Q8, NG, KIND, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
-    gemv_decode_kernel<Q8, NG, KIND, W><<<num_sms, G::THREADS, G::SMEM, st>>>(
+    // GEMM items: a stage holds 128 bytes of K of every row tile (16 rows), the item buffer 16 token rows
+    static_assert(!HG || (G::WARPS == 15 && G::WQ == 2048), "GEMM item stage geometry");
+    static_assert(!HG || kGemvGemmTile <= 32, "GEMM item token rows");
+    static_assert(G::HDR % 1024 == 0 && G::STAGE % 1024 == 0, "stage ring alignment");
+    static_assert(G::K % 128 == 0, "GEMM item K chunks");
+    cudaFuncSetAttribute(gemv_decode_kernel<Q8, NG, KIND, W, HG>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
+    CUtensorMap none;
+    memset(&none, 0, sizeof(none));
+    const bool g = HG && gm != nullptr;
+    gemv_decode_kernel<Q8, NG, KIND, W, HG><<<num_sms, G::THREADS, G::SMEM, st>>>(
         L.pool, L.slab_bytes, M, L.luts, KIND == 0 ? 0 : 16, L.E, R, aq, asb, out, out_ld, meta_items,
-        KIND == 0 ? kMetaWorkGU : kMetaWorkDN, 1u);
+        KIND == 0 ? kMetaWorkGU : kMetaWorkDN, 1u, g ? *reinterpret_cast<const CUtensorMap *>(gm->wmap) : none,
+        g ? gm->aq : nullptr, g ? gm->as : nullptr, g ? gm->ws : nullptr,
+        g ? (KIND == 0 ? kMetaGemmTilesGU : kMetaGemmTilesDN) : -1);
 }
 
 // Row tiles per item for a call of n token rows: wide items (15 tiles, 16 warps per CTA) once the call has enough
@@ -411,7 +687,7 @@ int gemv_items_per_unit(const LayerDev &L, int kind, int n) {
 // Returns the number of kernels launched, 0 for a geometry probe (kind 2/3), or -1 if the geometry has no
 // instantiation. asb: per activation row and 64-group, (scale, scale * sum of q) as the reference keeps them.
 int launch_gemv_decode(const LayerDev &L, int kind, const RouteDev &R, const int8_t *aq, const float2 *asb, float *out,
-                       int out_ld, int num_sms, cudaStream_t st) {
+                       int out_ld, int num_sms, cudaStream_t st, const DecGemm *gm) {
     if (kind < 0)  // geometry probe: both matrices must have an instantiation
         return launch_gemv_decode(L, 2, R, aq, asb, out, out_ld, num_sms, st) < 0 ||
                        launch_gemv_decode(L, 3, R, aq, asb, out, out_ld, num_sms, st) < 0 ? -1 : 0;
@@ -422,15 +698,18 @@ int launch_gemv_decode(const LayerDev &L, int kind, const RouteDev &R, const int
     const bool q8 = L.type == INZG_T_Q8G;
     if (M.rows % 16) return -1;
     const bool wide = tiles_per_item(R.n) == 15;
+    if (gm && !probe && (!wide || !gm->wmap || !gm->aq || !gm->as || !gm->ws)) return -1;  // GEMM items: wide only
 #define INZG_GEMV_CASE(Q, N)                                                                                     \
     if (q8 == Q && M.ng == N) {                                                                                  \
         if (probe) return 0;                                                                                     \
         if (kind == 0) {                                                                                         \
-            if (wide) launch_one<Q, N, 0, 15>(L, M, R, aq, asb, out, out_ld, mi, num_sms, st);                  \
-            else launch_one<Q, N, 0, 8>(L, M, R, aq, asb, out, out_ld, mi, num_sms, st);                        \
+            if (gm) launch_one<Q, N, 0, 15, true>(L, M, R, aq, asb, out, out_ld, mi, num_sms, st, gm);          \
+            else if (wide) launch_one<Q, N, 0, 15, false>(L, M, R, aq, asb, out, out_ld, mi, num_sms, st, gm);  \
+            else launch_one<Q, N, 0, 8, false>(L, M, R, aq, asb, out, out_ld, mi, num_sms, st, nullptr);        \
         } else {                                                                                                 \
-            if (wide) launch_one<Q, N, 1, 15>(L, M, R, aq, asb, out, out_ld, mi, num_sms, st);                  \
-            else launch_one<Q, N, 1, 8>(L, M, R, aq, asb, out, out_ld, mi, num_sms, st);                        \
+            if (gm) launch_one<Q, N, 1, 15, true>(L, M, R, aq, asb, out, out_ld, mi, num_sms, st, gm);          \
+            else if (wide) launch_one<Q, N, 1, 15, false>(L, M, R, aq, asb, out, out_ld, mi, num_sms, st, gm);  \
+            else launch_one<Q, N, 1, 8, false>(L, M, R, aq, asb, out, out_ld, mi, num_sms, st, nullptr);        \
         }                                                                                                        \
         return 1;                                                                                                \
     }

@@ -34,8 +34,19 @@ int launch_shared_route(const RouteDev &R, int n, int gemm, int gu_items_per_uni
                         int32_t *upath, int32_t *eexp, cudaStream_t st);
 
 void gemv_set_attributes();
+// Prefill-numerics experts of a decode-sized call (at most kGemvGemmMaxTokens tokens), run by the decode GEMV kernel
+// itself as GEMM items (the call's R.gemm_tiles, built with a token tile of kGemvGemmTile: one tile per expert): int8
+// activations per 256-block by token (gate|up) or by entry (down), their block scales, the layer's per-(row,
+// 256-block) weight scales and a TMA map over the requantized int8 weights with 16-row boxes (make_tma_map_i8(..., 16)).
+constexpr int kGemvGemmTile = 32, kGemvGemmMaxTokens = 32;
+struct DecGemm {
+    const int8_t *aq;
+    const float *as;
+    const float *ws;
+    const void *wmap;
+};
 int launch_gemv_decode(const LayerDev &L, int kind, const RouteDev &R, const int8_t *aq, const float2 *asb, float *out,
-                       int out_ld, int num_sms, cudaStream_t st);
+                       int out_ld, int num_sms, cudaStream_t st, const DecGemm *gm = nullptr);
 int gemv_items_per_unit(const LayerDev &L, int kind, int n);  // n: token rows of the call (R.n)
 int launch_gemm_v1(const LayerDev &L, int kind, const RouteDev &R, const int8_t *aq, const float *as, float *out,
                    int out_ld, int grid, cudaStream_t st);
