@@ -75,7 +75,8 @@ typedef struct {
     const float *logit_bias;       /* optional [n_expert], added to the router logits before the softmax (test hook,
                                       no counterpart in the reference) */
     const float *logits_override;  /* optional [n][n_expert], replaces the router logits (test hook) */
-    void *stream;                  /* cudaStream_t to run on; NULL = the context's own stream */
+    void *stream;                  /* cudaStream_t to run on; NULL = the context's own (non-blocking) stream, so
+                                      pass cudaStreamLegacy to order a call on CUDA's legacy default stream */
 } inzg_moe_opts;
 
 typedef struct {
@@ -209,8 +210,38 @@ INZG_EXPORT inzg_status inzg_shared_expert(inzg_ctx *ctx, int layer, int n, cons
                                            int n_batch, void *stream);
 
 /* Waits for `stream` and reports the device-side checks of the calls since the last routing step
- * (INZG_TIMEOUT / INZG_DEVICE_CHECK). */
+ * (INZG_TIMEOUT / INZG_DEVICE_CHECK), including a timed-out expert-parallel exchange. */
 INZG_EXPORT inzg_status inzg_device_status(inzg_ctx *ctx, void *stream);
+
+/* ---- Expert parallelism with the exchange in the library: peer memory over NVLink / NVSwitch, no collective library.
+ * One context per GPU (one rank per GPU: a connect that finds two ranks on one device fails), rank r of `world`
+ * (<= 8) holding experts [r * n_expert / world, (r + 1) * n_expert / world) of every layer it runs
+ * (inzg_pool_add_layer_range) and the router. Each rank exposes one device buffer to the others; a step ships every
+ * (token, owning rank) row once and every owned output slot once, directly into the peer's memory, with device-side
+ * epoch flags instead of host synchronisation, and ends with the rank-order combine -- the single-GPU bits.
+ *
+ * Between processes: inzg_ep_attach on every rank, exchange the INZG_EP_HANDLE_BYTES handles (any host channel),
+ * inzg_ep_connect with all of them in rank order. In one process: inzg_ep_attach on every context, then
+ * inzg_ep_connect_local with the contexts in rank order (peer access is enabled between their devices).
+ * `capacity`: the most tokens a rank passes to one inzg_ep_forward; the context's max_tokens must be at least
+ * world * capacity (the rows a rank can receive). */
+#define INZG_EP_HANDLE_BYTES 128
+INZG_EXPORT inzg_status inzg_ep_attach(inzg_ctx *ctx, int rank, int world, int capacity, void *handle_out);
+INZG_EXPORT inzg_status inzg_ep_connect(inzg_ctx *ctx, const void *handles);
+INZG_EXPORT inzg_status inzg_ep_connect_local(inzg_ctx *const *ctxs, int world);
+
+/* One expert-parallel MoE layer on this rank's n <= capacity tokens x_dev [n][hidden] -> y_dev [n][hidden] (device
+ * pointers, 16-byte aligned): route, dispatch, the owned experts, return, combine, and the layer's shared expert if
+ * set. Every rank calls it for the same layers in the same order (n may differ per rank, n_batch is the sum). Ordered
+ * on `stream` (NULL = the context's stream), captured in a CUDA graph per (layer, n, pointers); returns without
+ * synchronising. A peer that never arrives makes the step's waits run out after about a second: the outputs are then
+ * incomplete and inzg_device_status reports INZG_TIMEOUT. */
+INZG_EXPORT inzg_status inzg_ep_forward(inzg_ctx *ctx, int layer, int n, const float *x_dev, const float *logit_bias_dev,
+                                        float *y_dev, int n_batch, void *stream);
+
+/* Leaves the exchange (after every rank's last inzg_ep_forward has completed): closes the peers' mappings and frees
+ * this rank's buffer. inzg_destroy does it too. */
+INZG_EXPORT inzg_status inzg_ep_detach(inzg_ctx *ctx);
 
 #ifdef __cplusplus
 }

@@ -11,6 +11,7 @@ LIB_PATH = os.path.join(_HERE, "libinzg.so")
 
 T_F16, T_Q4L, T_Q8G = 1, 102, 103
 IO_DEVICE, DUMP_ROUTE, PROFILE, NO_GRAPH, GEMM_SIMT, NO_FUSED = 1, 2, 4, 8, 16, 32
+EP_HANDLE_BYTES = 128  # INZG_EP_HANDLE_BYTES
 N_STAGES = 12
 
 STATUS = {0: "INZG_OK", 1: "INZG_BAD_ARG", 2: "INZG_CORRUPT_BLOB", 3: "INZG_OOM", 4: "INZG_CUDA", 5: "INZG_NCCL",
@@ -63,6 +64,11 @@ SIGNATURES = {
     "inzg_device_status": (I, [P, P]),
     "inzg_set_shared": (I, [P, I, I, P, U64, P]),
     "inzg_shared_expert": (I, [P, I, I, P, P, I, P]),
+    "inzg_ep_attach": (I, [P, I, I, I, P]),
+    "inzg_ep_connect": (I, [P, P]),
+    "inzg_ep_connect_local": (I, [P, I]),
+    "inzg_ep_forward": (I, [P, I, I, P, P, P, I, P]),
+    "inzg_ep_detach": (I, [P]),
     "inzg_gguf_open": (P, [ctypes.c_char_p, ctypes.POINTER(GgufInfo), ctypes.c_char_p, ctypes.c_size_t]),
     "inzg_gguf_get_info": (I, [P, ctypes.POINTER(GgufInfo)]),
     "inzg_gguf_experts": (I, [P, I, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(U64), ctypes.POINTER(U64)]),

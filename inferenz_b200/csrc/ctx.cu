@@ -78,8 +78,25 @@ uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
 
 }  // namespace
 
+// This rank's part of the expert-parallel exchange (k_ep.cu): its exposed buffer, the peers' mappings, the step
+// counter and the local scratch of a step.
+struct EpState {
+    int rank = 0, world = 0, cap = 0;
+    uint8_t *base = nullptr;            // exposed: rsel | rw | rx | slot | flags
+    size_t bytes = 0;
+    size_t o_rsel = 0, o_rw = 0, o_rx = 0, o_slot = 0, o_flags = 0;
+    std::vector<void *> opened;          // peers' buffers opened through IPC (closed at detach)
+    EpPeers P{};
+    bool connected = false;
+    uint8_t *local = nullptr;            // epoch | tickets[2] | err | sel [cap][K] | w [cap][K] | out [world*cap][K][H]
+    uint32_t *epoch = nullptr;
+    int32_t *tickets = nullptr, *err = nullptr, *sel = nullptr;
+    float *w = nullptr, *out = nullptr;
+};
+
 struct inzg_ctx {
     inzg_config cfg{};
+    EpState *ep = nullptr;
     int num_sms = 0;
     cudaStream_t stream = nullptr;
     std::vector<LayerSlot> layers;
@@ -123,9 +140,10 @@ struct inzg_ctx {
         int layer, n;
         const void *x, *y, *bias, *ovr;
         unsigned flags;
+        int aux;  // expert-parallel steps: the batch size of the numeric-path rule (forward calls: 0)
         bool operator==(const GraphKey &o) const {
             return layer == o.layer && n == o.n && x == o.x && y == o.y && bias == o.bias && ovr == o.ovr &&
-                   flags == o.flags;
+                   flags == o.flags && aux == o.aux;
         }
     };
     struct GraphEntry {
@@ -305,6 +323,7 @@ void inzg_destroy(inzg_ctx *c) {
     if (!c) return;
     cudaSetDevice(c->cfg.device);
     cudaStreamSynchronize(c->stream);
+    inzg_ep_detach(c);
     for (auto *v : {&c->layers, &c->shared})
         for (auto &L : *v) {
             if (L.router) cudaFree(L.router);
@@ -740,7 +759,7 @@ inzg_status inzg_moe_forward(inzg_ctx *c, int layer, int n, const float *xin, fl
                                    profile ? c->ev : nullptr, st);
     } else {
         inzg_ctx::GraphKey key{layer, n, X, yd, bias, ovr,
-                               flags & (INZG_IO_DEVICE | INZG_DUMP_ROUTE | INZG_GEMM_SIMT | INZG_NO_FUSED)};
+                               flags & (INZG_IO_DEVICE | INZG_DUMP_ROUTE | INZG_GEMM_SIMT | INZG_NO_FUSED), 0};
         inzg_ctx::GraphEntry *g = nullptr;
         for (auto &ge : c->graphs)
             if (ge.key == key) g = &ge;
@@ -837,6 +856,52 @@ inzg_status inzg_route(inzg_ctx *c, int layer, int n, const float *x_dev, const 
     return e == cudaSuccess ? INZG_OK : cuda_fail(c, e, "route: kernel launch");
 }
 
+// The experts of the context's pool on m token rows (the body of inzg_moe_experts and of an expert-parallel step):
+// launches, or -1 (a launcher has no kernel for the shape) / -2 (the prefill GEMM has no tensor maps).
+static int enqueue_experts(inzg_ctx *c, LayerSlot &L, int m, const float *x_dev, const int32_t *sel_dev,
+                           const float *w_dev, int n_batch, float *out_dev, cudaStream_t st) {
+    const inzg_config &cf = c->cfg;
+    const LayerDev &D = L.dev;
+    const int H = cf.hidden, K = cf.topk, FF = cf.ff, E = D.E;
+    const int NE = m * K;
+    const bool any_gemm = n_batch > 8 && NE >= kGemmMinT;
+    const bool tc = c->have_tc && L.has_maps;
+    if (any_gemm && !tc) return -2;
+    int launches = 0;
+    bool bad = false;
+    auto add = [&](int r) {
+        if (r < 0) bad = true;
+        else launches += r;
+    };
+    add(launch_act_quant_x(x_dev, m, H, D.gu_rot, D.gu_seed, c->xq64, c->xsb64, any_gemm ? c->xq256 : nullptr,
+                           c->xs256, st));
+    RouteDev R{};
+    R.n = m; R.topk = K; R.E = E; R.n_rule = n_batch; R.absent_ok = 1;
+    R.sel = const_cast<int32_t *>(sel_dev); R.w = const_cast<float *>(w_dev);
+    R.cnt = c->cnt; R.off = c->off; R.first = c->first; R.etok = c->etok; R.eslot = c->eslot;
+    R.ew = c->ew; R.ccnt = c->ccnt; R.cmask = c->cmask; R.units = c->units; R.meta = c->meta; R.dec_units = c->dec_units;
+    R.gemm_units = c->gemm_units; R.gemm_tiles = c->gemm_tiles;
+    const bool in_gemv = any_gemm && m <= kGemvGemmMaxTokens;  // GEMM items inside the decode GEMV launches
+    add(launch_route(R, gemv_items_per_unit(D, 0, R.n), gemv_items_per_unit(D, 1, R.n),
+                     in_gemv ? kGemvGemmTile : gemm_token_tile(), c->upath, c->eexp, st));
+    const DecGemm gm_gu{c->xq256, c->xs256, D.ws_gu, L.map16_gu.bytes}, gm_dn{c->dq256, c->ds256, D.ws_dn,
+                                                                               L.map16_dn.bytes};
+    const int nkbH = (H + kKB - 1) / kKB;
+    const int max_tiles = (NE + gemm_token_tile() - 1) / gemm_token_tile() + std::min(E, NE / kGemmMinT) + 1;
+    add(launch_gemv_decode(D, 0, R, c->xq64, c->xsb64, c->GU, 2 * FF, c->num_sms, st, in_gemv ? &gm_gu : nullptr));
+    if (any_gemm && !in_gemv) {
+        add(launch_gather_gemm_rows(c->xq256, c->xs256, H, nkbH, c->etok, c->eexp, c->upath, NE, c->xqe, c->xse, st));
+        add(launch_gemm_tc(0, L.map_gu.bytes, c->map_xqe.bytes, D.ws_gu, 2 * FF, H, R, c->xse, c->GU, 2 * FF,
+                           max_tiles, st));
+    }
+    add(launch_swiglu_quant(c->GU, FF, NE, c->eexp, c->upath, D.dn_rot, D.dn_seed, c->dq64, c->dsb64, c->dq256,
+                            c->ds256, st));
+    add(launch_gemv_decode(D, 1, R, c->dq64, c->dsb64, out_dev, H, c->num_sms, st, in_gemv ? &gm_dn : nullptr));
+    if (any_gemm && !in_gemv)
+        add(launch_gemm_tc(1, L.map_dn.bytes, c->map_dq.bytes, D.ws_dn, H, FF, R, c->ds256, out_dev, H, max_tiles, st));
+    return bad ? -1 : launches;
+}
+
 inzg_status inzg_moe_experts(inzg_ctx *c, int layer, int m, const float *x_dev, const int32_t *sel_dev,
                              const float *w_dev, int n_batch, float *out_dev, void *stream) {
     if (!c) return INZG_BAD_ARG;
@@ -848,48 +913,13 @@ inzg_status inzg_moe_experts(inzg_ctx *c, int layer, int m, const float *x_dev, 
         return fail(c, INZG_BAD_ARG, "moe_experts: x and out must be 16-byte aligned");
     LayerSlot &L = c->layers[layer];
     if (!L.has_experts) return fail(c, INZG_NOT_READY, "moe_experts: layer has no experts");
-    const LayerDev &D = L.dev;
     cudaSetDevice(cf.device);
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
-    if (launch_gemv_decode(D, -1, RouteDev{}, nullptr, nullptr, nullptr, 0, 0, st) < 0)
+    if (launch_gemv_decode(L.dev, -1, RouteDev{}, nullptr, nullptr, nullptr, 0, 0, st) < 0)
         return fail(c, INZG_UNSUPPORTED, "moe_experts: no decode kernel for this geometry");
-    const int H = cf.hidden, K = cf.topk, FF = cf.ff, E = D.E;
-    const int NE = m * K;
-    const bool any_gemm = n_batch > 8 && NE >= kGemmMinT;
-    launch_act_quant_x(x_dev, m, H, D.gu_rot, D.gu_seed, c->xq64, c->xsb64, any_gemm ? c->xq256 : nullptr, c->xs256, st);
-    RouteDev R{};
-    R.n = m; R.topk = K; R.E = E; R.n_rule = n_batch; R.absent_ok = 1;
-    R.sel = const_cast<int32_t *>(sel_dev); R.w = const_cast<float *>(w_dev);
-    R.cnt = c->cnt; R.off = c->off; R.first = c->first; R.etok = c->etok; R.eslot = c->eslot;
-    R.ew = c->ew; R.ccnt = c->ccnt; R.cmask = c->cmask; R.units = c->units; R.meta = c->meta; R.dec_units = c->dec_units;
-    R.gemm_units = c->gemm_units; R.gemm_tiles = c->gemm_tiles;
-    const bool tc = c->have_tc && L.has_maps;
-    if (any_gemm && !tc) return fail(c, INZG_UNSUPPORTED, "moe_experts: no tensor maps for the prefill GEMM");
-    const bool in_gemv = any_gemm && m <= kGemvGemmMaxTokens;  // GEMM items inside the decode GEMV launches
-    launch_route(R, gemv_items_per_unit(D, 0, R.n), gemv_items_per_unit(D, 1, R.n),
-                 in_gemv ? kGemvGemmTile : gemm_token_tile(), c->upath, c->eexp, st);
-    const DecGemm gm_gu{c->xq256, c->xs256, D.ws_gu, L.map16_gu.bytes}, gm_dn{c->dq256, c->ds256, D.ws_dn,
-                                                                               L.map16_dn.bytes};
-    const int nkbH = (H + kKB - 1) / kKB;
-    const int max_tiles = (NE + gemm_token_tile() - 1) / gemm_token_tile() + std::min(E, NE / kGemmMinT) + 1;
-    if (launch_gemv_decode(D, 0, R, c->xq64, c->xsb64, c->GU, 2 * FF, c->num_sms, st, in_gemv ? &gm_gu : nullptr) < 0)
-        return fail(c, INZG_UNSUPPORTED, "moe_experts: no decode kernel for this call");
-    if (any_gemm && !in_gemv) {
-        if (tc) {
-            launch_gather_gemm_rows(c->xq256, c->xs256, H, nkbH, c->etok, c->eexp, c->upath, NE, c->xqe, c->xse, st);
-            if (launch_gemm_tc(0, L.map_gu.bytes, c->map_xqe.bytes, D.ws_gu, 2 * FF, H, R, c->xse, c->GU, 2 * FF,
-                               max_tiles, st) < 0)
-                return fail(c, INZG_UNSUPPORTED, "moe_experts: no GEMM kernel for this shape");
-        }
-    }
-    launch_swiglu_quant(c->GU, FF, NE, c->eexp, c->upath, D.dn_rot, D.dn_seed, c->dq64, c->dsb64, c->dq256, c->ds256, st);
-    if (launch_gemv_decode(D, 1, R, c->dq64, c->dsb64, out_dev, H, c->num_sms, st, in_gemv ? &gm_dn : nullptr) < 0)
-        return fail(c, INZG_UNSUPPORTED, "moe_experts: no decode kernel for this call");
-    if (any_gemm && !in_gemv) {
-        if (launch_gemm_tc(1, L.map_dn.bytes, c->map_dq.bytes, D.ws_dn, H, FF, R, c->ds256, out_dev, H, max_tiles,
-                           st) < 0)
-            return fail(c, INZG_UNSUPPORTED, "moe_experts: no GEMM kernel for this shape");
-    }
+    const int r = enqueue_experts(c, L, m, x_dev, sel_dev, w_dev, n_batch, out_dev, st);
+    if (r == -2) return fail(c, INZG_UNSUPPORTED, "moe_experts: no tensor maps for the prefill GEMM");
+    if (r < 0) return fail(c, INZG_UNSUPPORTED, "moe_experts: no kernel for this shape");
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? INZG_OK : cuda_fail(c, e, "moe_experts: kernel launch");
 }
@@ -940,6 +970,273 @@ inzg_status inzg_device_status(inzg_ctx *c, void *stream) {
         snprintf(msg, sizeof(msg), "device check failed (code %d)", code);
         return fail(c, code == kErrTimeout ? INZG_TIMEOUT : INZG_DEVICE_CHECK, msg);
     }
+    if (c->ep && c->ep->err) {  // the exchange's own error word (sticky until read here)
+        int32_t ep_err = 0;
+        e = cudaMemcpy(&ep_err, c->ep->err, sizeof(ep_err), cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess && ep_err != kErrNone) e = cudaMemset(c->ep->err, 0, sizeof(int32_t));
+        if (e != cudaSuccess) return cuda_fail(c, e, "device_status");
+        if (ep_err != kErrNone) return fail(c, INZG_TIMEOUT, "expert-parallel exchange: a peer did not arrive in time");
+    }
+    return INZG_OK;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Expert parallelism over peer memory (k_ep.cu)
+// ---------------------------------------------------------------------------------------------------------------
+namespace {
+
+// the exported handle: the IPC handle of the rank's buffer, the device's UUID and the exchange's shape
+struct EpHandle {
+    cudaIpcMemHandle_t ipc;
+    unsigned char uuid[16];
+    int32_t rank, world, cap, hidden, topk, n_expert;
+    unsigned char pad[INZG_EP_HANDLE_BYTES - sizeof(cudaIpcMemHandle_t) - 16 - 6 * sizeof(int32_t)];
+};
+static_assert(sizeof(EpHandle) == INZG_EP_HANDLE_BYTES, "EP handle size");
+
+void ep_free(EpState *ep) {
+    for (void *p : ep->opened)
+        if (p) cudaIpcCloseMemHandle(p);
+    ep->opened.clear();
+    if (ep->base) cudaFree(ep->base);
+    if (ep->local) cudaFree(ep->local);
+    delete ep;
+}
+
+// every peer's regions from its base (all ranks share the layout)
+void ep_bind(EpState *ep, int d, uint8_t *b) {
+    ep->P.rsel[d] = reinterpret_cast<int32_t *>(b + ep->o_rsel);
+    ep->P.rw[d] = reinterpret_cast<float *>(b + ep->o_rw);
+    ep->P.rx[d] = reinterpret_cast<float *>(b + ep->o_rx);
+    ep->P.slot[d] = reinterpret_cast<float *>(b + ep->o_slot);
+    ep->P.flags[d] = reinterpret_cast<uint32_t *>(b + ep->o_flags);
+}
+
+}  // namespace
+
+inzg_status inzg_ep_attach(inzg_ctx *c, int rank, int world, int capacity, void *handle_out) {
+    if (!c) return INZG_BAD_ARG;
+    const inzg_config &cf = c->cfg;
+    if (world < 1 || world > kEpMaxRanks || rank < 0 || rank >= world || capacity < 1 || !handle_out)
+        return fail(c, INZG_BAD_ARG, "ep_attach: bad rank, world (1..8), capacity or handle");
+    if (cf.n_expert % world) return fail(c, INZG_BAD_ARG, "ep_attach: n_expert must be a multiple of world");
+    if ((int64_t)world * capacity > cf.max_tokens)
+        return fail(c, INZG_BAD_ARG, "ep_attach: max_tokens must be at least world * capacity");
+    if (c->ep) return fail(c, INZG_BAD_ARG, "ep_attach: already attached");
+    cudaSetDevice(cf.device);
+    const size_t G = world, C = capacity, K = cf.topk, H = cf.hidden;
+    EpState *ep = new EpState();
+    ep->rank = rank;
+    ep->world = world;
+    ep->cap = capacity;
+    size_t o = 0;
+    ep->o_rsel = o; o = align_up(o + G * C * K * 4, 256);
+    ep->o_rw = o; o = align_up(o + G * C * K * 4, 256);
+    ep->o_rx = o; o = align_up(o + G * C * H * 4, 256);
+    ep->o_slot = o; o = align_up(o + C * K * H * 4, 256);
+    ep->o_flags = o; o = align_up(o + 2 * G * 4, 256);
+    ep->bytes = o;
+    const size_t lb = 256 + align_up(C * K * 4, 256) * 2 + G * C * K * H * 4;
+    cudaError_t e = cudaMalloc(&ep->base, ep->bytes);
+    if (e == cudaSuccess) e = cudaMemset(ep->base, 0, ep->bytes);
+    if (e == cudaSuccess) e = cudaMemset(ep->base + ep->o_rsel, 0xFF, G * C * K * 4);  // no slot owned yet
+    if (e == cudaSuccess) e = cudaMalloc(&ep->local, lb);
+    if (e == cudaSuccess) e = cudaMemset(ep->local, 0, 256);
+    EpHandle h{};
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h.ipc, ep->base);
+    cudaDeviceProp prop{};
+    if (e == cudaSuccess) e = cudaGetDeviceProperties(&prop, cf.device);
+    if (e != cudaSuccess) {
+        ep_free(ep);
+        return cuda_fail(c, e, "ep_attach");
+    }
+    ep->epoch = reinterpret_cast<uint32_t *>(ep->local);
+    ep->tickets = reinterpret_cast<int32_t *>(ep->local + 16);
+    ep->err = reinterpret_cast<int32_t *>(ep->local + 32);
+    ep->sel = reinterpret_cast<int32_t *>(ep->local + 256);
+    ep->w = reinterpret_cast<float *>(ep->local + 256 + align_up(C * K * 4, 256));
+    ep->out = reinterpret_cast<float *>(ep->local + 256 + 2 * align_up(C * K * 4, 256));
+    ep->P.rank = rank;
+    ep->P.world = world;
+    ep->P.cap = capacity;
+    ep->P.topk = cf.topk;
+    ep->P.hidden = cf.hidden;
+    ep->P.e_per = cf.n_expert / world;
+    ep_bind(ep, rank, ep->base);
+    memcpy(h.uuid, &prop.uuid, 16);
+    h.rank = rank; h.world = world; h.cap = capacity; h.hidden = cf.hidden; h.topk = cf.topk; h.n_expert = cf.n_expert;
+    memcpy(handle_out, &h, sizeof(h));
+    c->ep = ep;
+    return INZG_OK;
+}
+
+inzg_status inzg_ep_connect(inzg_ctx *c, const void *handles) {
+    if (!c) return INZG_BAD_ARG;
+    EpState *ep = c->ep;
+    if (!ep || !handles) return fail(c, INZG_BAD_ARG, "ep_connect: attach first; handles missing");
+    if (ep->connected) return fail(c, INZG_BAD_ARG, "ep_connect: already connected");
+    cudaSetDevice(c->cfg.device);
+    const EpHandle *hs = static_cast<const EpHandle *>(handles);
+    for (int d = 0; d < ep->world; d++) {
+        const EpHandle &h = hs[d];
+        if (h.rank != d || h.world != ep->world || h.cap != ep->cap || h.hidden != c->cfg.hidden ||
+            h.topk != c->cfg.topk || h.n_expert != c->cfg.n_expert)
+            return fail(c, INZG_BAD_ARG, "ep_connect: handles disagree on rank order or the exchange's shape");
+        for (int j = 0; j < d; j++)
+            if (!memcmp(hs[j].uuid, h.uuid, 16))
+                return fail(c, INZG_BAD_ARG, "ep_connect: two ranks on one GPU (one rank per device)");
+    }
+    ep->opened.assign(ep->world, nullptr);
+    for (int d = 0; d < ep->world; d++) {
+        if (d == ep->rank) continue;
+        void *p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, hs[d].ipc, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (void *q : ep->opened)
+                if (q) cudaIpcCloseMemHandle(q);
+            ep->opened.clear();
+            return cuda_fail(c, e, "ep_connect: open a peer's buffer");
+        }
+        ep->opened[d] = p;
+        ep_bind(ep, d, static_cast<uint8_t *>(p));
+    }
+    ep->connected = true;
+    return INZG_OK;
+}
+
+inzg_status inzg_ep_connect_local(inzg_ctx *const *ctxs, int world) {
+    if (!ctxs || world < 1 || world > kEpMaxRanks) return INZG_BAD_ARG;
+    for (int d = 0; d < world; d++) {
+        inzg_ctx *c = ctxs[d];
+        if (!c || !c->ep || c->ep->connected || c->ep->world != world || c->ep->rank != d) {
+            if (c) fail(c, INZG_BAD_ARG, "ep_connect_local: every context attached once, in rank order");
+            return INZG_BAD_ARG;
+        }
+        for (int j = 0; j < d; j++)
+            if (ctxs[j]->cfg.device == c->cfg.device)
+                return fail(c, INZG_BAD_ARG, "ep_connect_local: two ranks on one GPU (one rank per device)");
+    }
+    for (int d = 0; d < world; d++) {
+        inzg_ctx *c = ctxs[d];
+        cudaSetDevice(c->cfg.device);
+        for (int j = 0; j < world; j++) {
+            if (j == d) continue;
+            cudaError_t e = cudaDeviceEnablePeerAccess(ctxs[j]->cfg.device, 0);
+            if (e == cudaErrorPeerAccessAlreadyEnabled) {
+                cudaGetLastError();
+                e = cudaSuccess;
+            }
+            if (e != cudaSuccess) return cuda_fail(c, e, "ep_connect_local: peer access");
+            ep_bind(c->ep, j, ctxs[j]->ep->base);
+        }
+    }
+    for (int d = 0; d < world; d++) ctxs[d]->ep->connected = true;
+    return INZG_OK;
+}
+
+inzg_status inzg_ep_detach(inzg_ctx *c) {
+    if (!c) return INZG_BAD_ARG;
+    if (!c->ep) return INZG_OK;
+    cudaSetDevice(c->cfg.device);
+    cudaDeviceSynchronize();
+    drop_graphs(c);  // graphs of expert-parallel steps hold the peers' pointers
+    ep_free(c->ep);
+    c->ep = nullptr;
+    return INZG_OK;
+}
+
+// One expert-parallel step of this rank (k_ep.cu): launches, or -1 / -2 as enqueue_experts.
+static int enqueue_ep(inzg_ctx *c, int layer, int n, const float *x, const float *bias, float *y, int n_batch,
+                      cudaStream_t st) {
+    const inzg_config &cf = c->cfg;
+    EpState *ep = c->ep;
+    LayerSlot &L = c->layers[layer];
+    const int H = cf.hidden, E = cf.n_expert, K = cf.topk;
+    int launches = 0;
+    bool bad = false;
+    auto add = [&](int r) {
+        if (r < 0) bad = true;
+        else launches += r;
+    };
+    add(launch_router_logits(L.router, L.router32, x, n, H, E, bias, c->logits, c->meta, st));
+    add(launch_softmax_topk(c->logits, n, E, K, ep->sel, ep->w, nullptr, st));
+    add(launch_ep_dispatch(x, n, ep->sel, ep->w, ep->P, ep->epoch, ep->tickets, c->num_sms, st));
+    add(launch_ep_wait(ep->P.flags[ep->rank], ep->world, 0, ep->epoch, false, ep->err, st));
+    const int r = enqueue_experts(c, L, ep->world * ep->cap, ep->P.rx[ep->rank], ep->P.rsel[ep->rank],
+                                  ep->P.rw[ep->rank], n_batch, ep->out, st);
+    if (r == -2) return -2;
+    add(r);
+    add(launch_ep_return(ep->out, ep->P, ep->epoch, ep->tickets + 1, c->num_sms, st));
+    add(launch_ep_wait(ep->P.flags[ep->rank], ep->world, 1, ep->epoch, true, ep->err, st));
+    add(launch_combine(ep->P.slot[ep->rank], n, H, K, y, c->num_sms, st));
+    if (c->shared[layer].has_experts) {
+        const int rs = enqueue_shared(c, layer, n, x, y, n_batch, false, st);
+        if (rs == -2) return -2;
+        add(rs);
+    }
+    return bad ? -1 : launches;
+}
+
+inzg_status inzg_ep_forward(inzg_ctx *c, int layer, int n, const float *x_dev, const float *logit_bias_dev,
+                            float *y_dev, int n_batch, void *stream) {
+    if (!c) return INZG_BAD_ARG;
+    const inzg_config &cf = c->cfg;
+    EpState *ep = c->ep;
+    if (!ep || !ep->connected) return fail(c, INZG_NOT_READY, "ep_forward: attach and connect first");
+    if (layer < 0 || layer >= cf.n_layers) return fail(c, INZG_BAD_ARG, "ep_forward: bad layer");
+    if (n < 1 || n > ep->cap || n_batch < n || !x_dev || !y_dev)
+        return fail(c, INZG_BAD_ARG, "ep_forward: bad n (1..capacity), n_batch or pointer");
+    if ((reinterpret_cast<uintptr_t>(x_dev) | reinterpret_cast<uintptr_t>(y_dev)) & 15)
+        return fail(c, INZG_BAD_ARG, "ep_forward: x and y must be 16-byte aligned");
+    LayerSlot &L = c->layers[layer];
+    if (!L.has_router || !L.has_experts) return fail(c, INZG_NOT_READY, "ep_forward: layer not loaded");
+    if (L.e_first != ep->rank * ep->P.e_per || L.dev.E != ep->P.e_per)
+        return fail(c, INZG_NOT_READY, "ep_forward: the pool must hold exactly this rank's experts");
+    cudaSetDevice(cf.device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    if (launch_gemv_decode(L.dev, -1, RouteDev{}, nullptr, nullptr, nullptr, 0, 0, st) < 0)
+        return fail(c, INZG_UNSUPPORTED, "ep_forward: no decode kernel for this geometry");
+    inzg_ctx::GraphKey key{layer, n, x_dev, y_dev, logit_bias_dev, nullptr, 0x80000000u, n_batch};
+    inzg_ctx::GraphEntry *g = nullptr;
+    for (auto &ge : c->graphs)
+        if (ge.key == key) g = &ge;
+    cudaError_t e = cudaSuccess;
+    if (!g) {
+        cudaStream_t cs = c->capture_stream;
+        e = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
+        if (e != cudaSuccess) return cuda_fail(c, e, "ep_forward: begin capture");
+        const int nl = enqueue_ep(c, layer, n, x_dev, logit_bias_dev, y_dev, n_batch, cs);
+        cudaGraph_t graph = nullptr;
+        e = cudaStreamEndCapture(cs, &graph);
+        if (e != cudaSuccess || nl < 0) {
+            if (graph) cudaGraphDestroy(graph);
+            return e != cudaSuccess ? cuda_fail(c, e, "ep_forward: capture")
+                   : nl == -2       ? fail(c, INZG_UNSUPPORTED, "ep_forward: no tensor maps for the prefill GEMM")
+                                    : fail(c, INZG_UNSUPPORTED, "ep_forward: no kernel for this shape");
+        }
+        cudaGraphExec_t exec = nullptr;
+        e = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess) return cuda_fail(c, e, "ep_forward: graph instantiate");
+        if (c->graphs.size() >= 64) {
+            auto it = std::min_element(c->graphs.begin(), c->graphs.end(),
+                                       [](const inzg_ctx::GraphEntry &a, const inzg_ctx::GraphEntry &b) {
+                                           return a.last_use < b.last_use;
+                                       });
+            cudaGraphExecDestroy(it->exec);
+            c->graphs.erase(it);
+        }
+        c->graphs.push_back({key, exec, nl, 0});
+        g = &c->graphs.back();
+    }
+    g->last_use = ++c->use_clock;
+    e = cudaGraphLaunch(g->exec, st);
+    if (e != cudaSuccess) return cuda_fail(c, e, "ep_forward: graph launch");
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(c, e, "ep_forward: kernel launch");
+    c->stats.calls++;
+    c->stats.tokens += n;
+    c->stats.last_launches = g->launches;
     return INZG_OK;
 }
 

@@ -48,6 +48,17 @@ struct LayerDev {
     float *ws_gu, *ws_dn;     // [E][2FF][H/256], [E][H][ceil(FF/256)]
 };
 
+// The expert-parallel exchange (k_ep.cu): every rank's exposed buffer, as seen from this rank (peer pointers).
+constexpr int kEpMaxRanks = 8;
+struct EpPeers {
+    int rank, world, cap, topk, hidden, e_per;
+    int32_t *rsel[kEpMaxRanks];  // [world][cap][topk] local expert of each received slot, -1 if not owned there
+    float *rw[kEpMaxRanks];      // [world][cap][topk] routing weights
+    float *rx[kEpMaxRanks];      // [world][cap][hidden] received rows
+    float *slot[kEpMaxRanks];    // [cap][topk][hidden] the rank's own tokens' slot outputs
+    uint32_t *flags[kEpMaxRanks];  // [2][world] dispatch / return epochs written by each peer
+};
+
 // Routing products of one forward call (device).
 struct RouteDev {
     int n, topk, E;

@@ -66,6 +66,14 @@ void launch_pool_requant(const uint8_t *blobs, uint64_t blob_bytes, uint64_t gu_
 void launch_pool_repack(const uint8_t *blobs, uint64_t blob_bytes, uint64_t gu_bytes, int e0, int ne,
                         const LayerDev &L, uint8_t *pool, uint8_t *luts, cudaStream_t st);
 
+// Expert-parallel exchange over peer memory (k_ep.cu). epoch_dev: the rank's step counter; tickets: one int per kernel.
+int launch_ep_dispatch(const float *x, int n, const int32_t *sel, const float *w, const EpPeers &P,
+                       const uint32_t *epoch_dev, int32_t *ticket, int num_sms, cudaStream_t st);
+int launch_ep_return(const float *out, const EpPeers &P, const uint32_t *epoch_dev, int32_t *ticket, int num_sms,
+                     cudaStream_t st);
+int launch_ep_wait(const uint32_t *flags, int world, int which, uint32_t *epoch_dev, bool advance, int32_t *err,
+                   cudaStream_t st);
+
 // The whole routed layer in one cooperative launch for calls of 1-2 tokens (k_fused.cu); -1 when the shape has no
 // instantiation. counters: fused_counter_ints(E, 8, H) ints, all zero before the first call.
 size_t fused_counter_ints(int E, int n_max, int H);

@@ -17,6 +17,15 @@ logic). The per-rank compute is a backend: :class:`DeviceBackend` drives libinzg
 import torch
 import torch.distributed as dist
 
+CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy
+
+
+def stream_handle(s):
+    """The CUDA stream handle libinzg should order a call on for torch stream ``s``: torch's default stream has handle
+    0, which libinzg reads as "the context's own stream", so it is passed as cudaStreamLegacy (what handle 0 means to
+    CUDA) to keep the call ordered with torch's work on that stream."""
+    return s.cuda_stream or CUDA_STREAM_LEGACY
+
 
 class DeviceBackend:
     """libinzg on this rank's GPU: a MoePool holding experts [e_first, e_first + n_local) of every layer used."""
@@ -27,7 +36,7 @@ class DeviceBackend:
 
     def _st(self):
         s = self.stream if self.stream is not None else torch.cuda.current_stream(self.pool.device)
-        return s.cuda_stream
+        return stream_handle(s)
 
     def route(self, layer, x, bias=None):
         n = x.shape[0]
@@ -173,4 +182,39 @@ class ExpertParallelMoE:
         return y
 
 
-__all__ = ["DeviceBackend", "ExpertParallelMoE"]
+class PeerExchangeMoE:
+    """The expert-parallel layer with the exchange inside libinzg (``inzg_ep_*``): each rank's pool holds its
+    ``n_expert / world`` experts; every (token, owning rank) row and every owned output slot crosses NVLink once,
+    written by the library's kernels straight into the peer's memory, with device-side epoch flags instead of host
+    synchronisation or a collective. The step (route, dispatch, owned experts, return, rank-order combine, shared
+    expert) runs as one CUDA graph per shape; outputs equal the single-GPU call bit for bit.
+
+    The handles are exchanged once over ``group`` (any backend: ``all_gather_object``)."""
+
+    def __init__(self, pool, capacity, group=None, rank=None, world=None):
+        self.pool = pool
+        self.group = group
+        self.rank = dist.get_rank(group) if rank is None else rank
+        self.world = dist.get_world_size(group) if world is None else world
+        self.capacity = capacity
+        handle = pool.ep_attach(self.rank, self.world, capacity)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        pool.ep_connect(handles)
+
+    def moe_block(self, layer, x, bias=None, n_batch=None, y=None, stream=None):
+        """y [n][H] for this rank's n <= capacity tokens x [n][H] (fp32, on the pool's device). n_batch: the whole
+        batch's token count (default: n on every rank)."""
+        n = x.shape[0]
+        if y is None:
+            y = torch.empty_like(x)
+        s = stream if stream is not None else torch.cuda.current_stream(x.device)
+        self.pool.ep_forward_device(layer, n, x.data_ptr(), y.data_ptr(), n * self.world if n_batch is None else n_batch,
+                                    None if bias is None else bias.data_ptr(), stream_handle(s))
+        return y
+
+    def close(self):
+        self.pool.ep_detach()
+
+
+__all__ = ["DeviceBackend", "ExpertParallelMoE", "PeerExchangeMoE", "stream_handle"]

@@ -10,7 +10,7 @@ import ctypes
 
 import numpy as np
 
-from ._lib import (DUMP_ROUTE, GEMM_SIMT, IO_DEVICE, N_STAGES, NO_FUSED, NO_GRAPH, PROFILE, Config, InzgError, MoeOpts, Stats, T_Q4L,
+from ._lib import (DUMP_ROUTE, EP_HANDLE_BYTES, GEMM_SIMT, IO_DEVICE, N_STAGES, NO_FUSED, NO_GRAPH, PROFILE, Config, InzgError, MoeOpts, Stats, T_Q4L,
                    T_Q8G, lib)
 
 
@@ -100,6 +100,25 @@ class MoePool:
     def shared_device(self, layer, n, x_ptr, y_ptr, n_batch, stream=None):
         self._check(lib.inzg_shared_expert(self._ctx, layer, n, ctypes.c_void_p(x_ptr), ctypes.c_void_p(y_ptr), n_batch,
                                            stream and ctypes.c_void_p(stream)), "shared_expert")
+
+    # expert parallelism with the exchange in the library (peer memory; include/inzg.h inzg_ep_*)
+    def ep_attach(self, rank, world, capacity):
+        """This rank's exchange buffer; returns its handle (bytes) for the other ranks."""
+        h = ctypes.create_string_buffer(EP_HANDLE_BYTES)
+        self._check(lib.inzg_ep_attach(self._ctx, rank, world, capacity, h), "ep_attach")
+        return h.raw
+
+    def ep_connect(self, handles):
+        """handles: every rank's ep_attach bytes, in rank order."""
+        buf = ctypes.create_string_buffer(b"".join(handles), EP_HANDLE_BYTES * len(handles))
+        self._check(lib.inzg_ep_connect(self._ctx, buf), "ep_connect")
+
+    def ep_forward_device(self, layer, n, x_ptr, y_ptr, n_batch, bias_ptr=None, stream=None):
+        self._check(lib.inzg_ep_forward(self._ctx, layer, n, ctypes.c_void_p(x_ptr), bias_ptr and ctypes.c_void_p(bias_ptr),
+                                        ctypes.c_void_p(y_ptr), n_batch, stream and ctypes.c_void_p(stream)), "ep_forward")
+
+    def ep_detach(self):
+        self._check(lib.inzg_ep_detach(self._ctx), "ep_detach")
 
     def device_status(self, stream=None):
         self._check(lib.inzg_device_status(self._ctx, stream and ctypes.c_void_p(stream)), "device_status")

@@ -129,3 +129,109 @@ def test_expert_parallel_building_blocks_single_rank():
     p.join(timeout=120)
     assert p.exitcode == 0
     assert np.array_equal(y.view(np.uint32), y_one.view(np.uint32))
+
+
+# ---- the exchange inside libinzg (inzg_ep_*: peer memory, device-side epoch flags) ----
+
+def _peer_worker(rank, world, port, n_total, steps, q, absent_rank=-1):
+    import datetime
+
+    import torch.distributed as dist
+
+    from inferenz_b200 import InzgError, MoePool, synth
+    from inferenz_b200.ep import PeerExchangeMoE
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    # the handles travel over gloo: no collective library touches the exchange
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    try:
+        x_all = synth.hidden(n_total, H)
+        bias = np.zeros(E, np.float32)
+        bias[[3, 200, 300, 511]] = 9.0  # four experts take every token: both numeric paths run
+        e0, nl = rank * (E // world), E // world
+        blobs, bb = synth.layer_blobs_range(0, synth.T_Q4L, H, FF, e0, e0 + nl)
+        R = synth.router(0, E, H)
+        per = n_total // world
+        dev = torch.device("cuda", rank)
+        with MoePool(H, FF, E, K, max_tokens=per * world, n_layers=1, device=rank) as pool:
+            pool.set_router(0, R)
+            pool.add_layer_range(0, synth.T_Q4L, blobs, bb, e0, nl)
+            ep = PeerExchangeMoE(pool, capacity=per)
+            x = torch.from_numpy(x_all[rank * per:(rank + 1) * per]).to(dev)
+            bd = torch.from_numpy(bias).to(dev)
+            status = "ok"
+            ys = []
+            if rank != absent_rank:
+                for _ in range(steps):
+                    ys.append(ep.moe_block(0, x, bias=bd, n_batch=n_total).clone())
+                torch.cuda.synchronize(dev)
+                try:
+                    pool.device_status()
+                except InzgError as err:
+                    status = str(err)
+                    pool.device_status()  # reported once: the context is usable again
+            dist.barrier()  # the absent rank keeps its memory mapped until the others are done
+            ep.close()
+            out = [y.cpu().numpy() for y in ys]
+        q.put((rank, status, out))
+        if rank == 0 and absent_rank < 0:
+            full, _ = synth.layer_blobs(0, synth.T_Q4L, H, FF, E)
+            with MoePool(H, FF, E, K, max_tokens=n_total, n_layers=1, device=0) as one:
+                one.set_router(0, R)
+                one.add_layer(0, synth.T_Q4L, full, bb)
+                q.put(("one", one.moe_block(0, x_all, bias=bias)))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_peer(world, n_total, steps, absent_rank=-1):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, n_total, steps, q, absent_rank))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(world + (1 if absent_rank < 0 else 0)):
+        item = q.get(timeout=600)
+        got[item[0]] = item[1:]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return got
+
+
+def test_peer_exchange_single_rank():
+    """One rank: the whole step (route, dispatch into its own buffer, experts, return, combine) through the exchange's
+    kernels and flags equals inzg_moe_forward bit for bit, at every step (the epochs advance)."""
+    got = _run_peer(1, 20, 3)
+    status, ys = got[0]
+    (y_one,) = got["one"]
+    assert status == "ok"
+    for step, y in enumerate(ys):
+        same = (y.view(np.uint32) == y_one.view(np.uint32)).mean(axis=1)
+        print(f"step {step}: bit-identical fraction per token {np.round(same, 3).tolist()}")
+        assert np.array_equal(y.view(np.uint32), y_one.view(np.uint32)), f"step {step}"
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_peer_exchange_two_gpus_equals_single_gpu():
+    got = _run_peer(2, 48, 3)
+    (y_one,) = got["one"]
+    for step in range(3):
+        y_ep = np.concatenate([got[r][1][step] for r in range(2)])
+        assert got[0][0] == "ok" and got[1][0] == "ok"
+        assert np.array_equal(y_ep.view(np.uint32), y_one.view(np.uint32)), f"step {step}"
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_peer_exchange_absent_peer_times_out():
+    """Rank 1 connects and then never runs a step (it stays out between steps, nothing in flight): rank 0's waits run
+    out after about a second each, inzg_device_status reports INZG_TIMEOUT once, and the next status check is clean."""
+    got = _run_peer(2, 16, 1, absent_rank=1)
+    status, _ = got[0]
+    assert "INZG_TIMEOUT" in status, status
