@@ -14,10 +14,11 @@ e2e    = the same through the public host API (MoePool.moe_block on pinned host 
 --impl reference: the reference's own CPU implementation of the layer (oracle/_ref, all host cores), on inputs drawn by
          the oracle's generator and experts encoded by the reference's quantizer: this arm never loads libinzg.
 Multi-GPU (--gpus N under torchrun, one process per GPU): expert parallelism. Rank g holds
-experts [g*512/N, (g+1)*512/N) and decodes its own 32 tokens (weak scaling: 32*N tokens per step); a step routes
-the rank's tokens, sends each token row once to every GPU owning one of its experts (NCCL all-to-all), runs the local
-experts, returns every (token, rank-k) output (NCCL all-to-all) and combines in rank order. value = all ranks'
-tokens / the max over ranks of the summed per-step CUDA-event times.
+experts [g*512/N, (g+1)*512/N) and decodes its own 32 tokens (weak scaling: 32*N tokens per step); a step
+(inzg_ep_forward) routes the rank's tokens, writes each token row once into every GPU owning one of its experts, runs
+the local experts, writes each owned (token, rank-k) output back into the token's GPU and combines in rank order -- the
+library's own kernels over peer memory (NVLink), no collective library. value = all ranks' tokens / the max over ranks
+of the summed per-step CUDA-event times.
 """
 import argparse
 import json
@@ -44,7 +45,7 @@ ROUTER_BYTES = E * H * 2
 # prefill-numerics experts read the requantized int8 weights and their per-(row, 256-block) fp32 scales
 GEMM_GU_BYTES = 2 * FF * H + 2 * FF * (H // 256) * 4
 GEMM_DN_BYTES = H * FF + H * (-(-FF // 256)) * 4
-GEMV_GEMM_MAX_TOKENS = 32  # calls up to this size run those experts inside the decode GEMV launches
+GEMV_GEMM_MAX_TOKENS = 256  # calls up to this size run those experts inside the decode GEMV launches
 
 
 NVLINK_GBS = 770.0  # NVLink 5 peer copy per direction per GPU, the pool's published measurement (900 GB/s nominal)
@@ -54,11 +55,17 @@ WORKLOAD = ("BASELINE configs[1]: MoE layer, decode batch of 32 tokens per GPU (
             "top-10, FF 640, Q4L experts, F16 router, N(0,1) per-expert logit bias")
 
 
-def ep_fixed_exchange_bytes(world, capacity, hidden=H, topk=K):
-    """Bytes one GPU sends -- and receives -- over NVLink per step of ExpertParallelMoE.moe_block_fixed: to each of
-    the world-1 other ranks a block of `capacity` fp32 token rows with their (local expert, weight) pairs, and the
-    capacity x topk fp32 result rows back. The block a rank keeps for itself crosses no link."""
-    return (world - 1) * capacity * (4 * hidden + 8 * topk + 4 * topk * hidden)
+def ep_exchange_bytes(sel_all, rank, world, n_expert=E, hidden=H, topk=K):
+    """(bytes rank `rank` writes into its peers per expert-parallel step, rows sent, slots returned) for the step's
+    selections sel_all [world][n_loc][topk]: each of its tokens' fp32 rows once to every other rank owning one of the
+    token's experts, the (local expert, weight) metadata of all n_loc rows to every peer, and every slot it owns of a
+    token living on another rank (fp32 [hidden]) back to that rank. What a rank keeps for itself crosses no link."""
+    sel_all = np.asarray(sel_all)
+    owner = sel_all // (n_expert // world)
+    n_loc = sel_all.shape[1]
+    rows = int(sum(len(set(owner[rank, t].tolist()) - {rank}) for t in range(n_loc)))
+    slots = int(sum((owner[s] == rank).sum() for s in range(world) if s != rank))
+    return rows * hidden * 4 + (world - 1) * n_loc * topk * 8 + slots * hidden * 4, rows, slots
 
 
 def peaks():
@@ -409,7 +416,11 @@ def probe_i8(device):
 
 
 def run_ep(args):
-    """--gpus N > 1: the expert-parallel decode step (see the module docstring)."""
+    """--gpus N > 1: the expert-parallel decode step with the exchange in libinzg (inzg_ep_forward): each rank routes
+    its 32 tokens, writes every (token, owning rank) row straight into the owner's buffer, runs its 512/N experts on
+    what it received, writes each owned slot straight back into the token's home and combines in rank order -- peer
+    memory over NVLink, device-side epoch flags, one CUDA graph per step. torch.distributed (gloo) only carries the
+    buffer handles, barriers and the per-rank timings."""
     import datetime
 
     # the ranks share the host's cores for the synthetic layer's generation: give each its share (torchrun sets
@@ -420,63 +431,54 @@ def run_ep(args):
     import torch.distributed as dist
 
     from inferenz_b200 import MoePool, synth
-    from inferenz_b200.ep import DeviceBackend, ExpertParallelMoE
+    from inferenz_b200.ep import PeerExchangeMoE
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
-    # host-side bookkeeping (barriers, per-rank timings) on gloo, apart from the communicator the graph captures
-    host = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=300))
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
     dev = torch.device("cuda", local)
     hbm, _, peak_kind = peaks()
     n_loc = 32
+    nb = n_loc * world
     e0, nl = rank * E // world, E // world
     t0 = time.time()
     blobs, bb = synth.layer_blobs_range(0, synth.T_Q4L, H, FF, e0, e0 + nl)
     gen_s = time.time() - t0
-    pool = MoePool(H, FF, E, K, max_tokens=n_loc * world, n_layers=1, device=local)
+    pool = MoePool(H, FF, E, K, max_tokens=nb, n_layers=1, device=local)
     pool.set_router(0, synth.router(0, E, H))
     pool.add_layer_range(0, synth.T_Q4L, blobs, bb, e0, nl)
+    del blobs
     stream = torch.cuda.Stream(dev)
-    ep = ExpertParallelMoE(DeviceBackend(pool, stream), E, K, H)
-    x_all = synth.hidden(n_loc * world, H)
+    x_all = synth.hidden(nb, H)
+    bias = synth.normal_bias(E)
     xd = torch.from_numpy(x_all[rank * n_loc:(rank + 1) * n_loc].copy()).to(dev)
-    bd = torch.from_numpy(synth.normal_bias(E)).to(dev)
+    yd = torch.empty_like(xd)
+    bd = torch.from_numpy(bias).to(dev)
     flush = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
-    nb = n_loc * world
+    ep = PeerExchangeMoE(pool, capacity=n_loc)
+    # the step's routing on every rank (for the byte counts): this rank's selections, gathered over gloo
+    sel = torch.empty((n_loc, K), dtype=torch.int32, device=dev)
+    wts = torch.empty((n_loc, K), dtype=torch.float32, device=dev)
+    pool.route_device(0, n_loc, xd.data_ptr(), sel.data_ptr(), wts.data_ptr(), bd.data_ptr(), stream.cuda_stream)
+    stream.synchronize()
+    sels = [torch.zeros((n_loc, K), dtype=torch.int32) for _ in range(world)]
+    dist.all_gather(sels, sel.cpu())
+    sel_all = torch.stack(sels).numpy()                      # [world][n_loc][K]
+    local_units = int(np.unique(sel_all[sel_all // (E // world) == rank]).size)
+    xb, rows_out, slots_back = ep_exchange_bytes(sel_all, rank, world)
 
-    def ep_step():  # fixed-size exchanges: no host synchronisation inside the step
-        return ep.moe_block_fixed(0, xd, bd, n_batch=nb, capacity=n_loc)
+    def step():
+        ep.moe_block(0, xd, bias=bd, n_batch=nb, y=yd, stream=stream)
 
-    graph, graph_err, y_graph = None, None, None
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             flush.zero_()
-            ep_step()
-        ep.moe_block(0, xd, bd, n_batch=nb, stats=True)
-        local_units = ep.last["local_units"]
-        stream.synchronize()
-        dist.barrier(group=host)
-        try:  # the whole step, NCCL exchanges included, as one CUDA graph
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
-                y_graph = ep_step()
-            graph.replay()
-            stream.synchronize()
-        except Exception as exc:  # every rank falls back together below
-            graph, graph_err = None, f"{type(exc).__name__}: {exc}"[:200]
-        ok = torch.tensor([1 if graph is not None else 0])
-        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=host)
-        if int(ok.item()) == 0:
-            graph = None
-        step = graph.replay if graph is not None else ep_step
-        for _ in range(3):
-            flush.zero_()
             step()
         stream.synchronize()
-        dist.barrier(group=host)
+        pool.device_status(stream.cuda_stream)
+        dist.barrier()
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
         with Clocks(local) as ck:
             for a, b in evs:
@@ -487,34 +489,35 @@ def run_ep(args):
             stream.synchronize()
         pool.device_status(stream.cuda_stream)
         my_total = sum(a.elapsed_time(b) for a, b in evs)
+        launches = pool.stats()["last_launches"]
         # end to end: the step's tokens from pinned host memory and its output back to the host, wall clock
         xp = torch.from_numpy(x_all[rank * n_loc:(rank + 1) * n_loc].copy()).pin_memory()
         yp = torch.empty((n_loc, H), dtype=torch.float32).pin_memory()
         e2e_steps = max(args.steps // 4, 5)
-        dist.barrier(group=host)
+        dist.barrier()
         ts = []
         for _ in range(e2e_steps):
             flush.zero_()
             stream.synchronize()
             t1 = time.perf_counter()
             xd.copy_(xp, non_blocking=True)
-            y = step()
-            yp.copy_(y_graph if graph is not None else y, non_blocking=True)
+            step()
+            yp.copy_(yd, non_blocking=True)
             stream.synchronize()
             ts.append(time.perf_counter() - t1)
+        pool.device_status(stream.cuda_stream)
     # per rank: device ms over the timed steps, end-to-end seconds, local experts touched
     mine = torch.tensor([my_total, sum(ts), float(local_units)], dtype=torch.float64)
     every = [torch.zeros(3, dtype=torch.float64) for _ in range(world)]
-    dist.all_gather(every, mine, group=host)
+    dist.all_gather(every, mine)
     per_rank = [[round(float(v), 4) for v in t.tolist()] for t in every]
     total_ms = max(r[0] for r in per_rank)
     e2e_s = max(r[1] for r in per_rank)
     ms_step = total_ms / args.steps
     value = nb * args.steps / (total_ms * 1e-3)
     units_all = int(sum(r[2] for r in per_rank))
-    # per GPU: router + its experts' weights + its tokens in and out
+    # per GPU: router + its experts' weights + the rows it received and returned
     bytes_gpu = ROUTER_BYTES + local_units * EXPERT_BYTES_Q4L + 2 * n_loc * H * 4
-    xb = ep_fixed_exchange_bytes(world, n_loc)  # the step's NVLink bytes per GPU and direction
     if rank == 0:
         ach = bytes_gpu / (ms_step * 1e-3) / 1e9
         line = {
@@ -522,32 +525,30 @@ def run_ep(args):
             "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8 x Q4L (fp32 accumulate)", "data": "synthetic (seeded; no dataset)",
             "config": {"workload": WORKLOAD, "global_batch": nb, "seq_len": 1},
-            "arm": {"parallelism": f"ep{world}: 512/N experts per GPU, NCCL all-to-all dispatch and combine",
+            "arm": {"parallelism": f"ep{world}: 512/N experts per GPU; dispatch and return written by the library's "
+                                   "kernels straight into the peers' memory (NVLink), device-side epoch flags",
                     "l2": "flushed (512 MB write) before every step"},
-            "roofline": {"bound": "hbm", "kernel": "layer step per GPU (router + local experts, incl. NCCL exchange)",
+            "roofline": {"bound": "hbm", "kernel": "layer step per GPU (router + local experts, incl. the exchange)",
                          "algorithmic_bytes": bytes_gpu, "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(ach / hbm, 4), "peak_kind": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)",
                          "traffic": None},
-            "nvlink": {"bytes_out_per_gpu": xb, "achieved": round(xb / (ms_step * 1e-3) / 1e9, 1),
+            "nvlink": {"bytes_out_rank0": xb, "achieved": round(xb / (ms_step * 1e-3) / 1e9, 1),
                        "peak": NVLINK_GBS, "unit": "GB/s", "frac": round(xb / (ms_step * 1e-3) / 1e9 / NVLINK_GBS, 4),
                        "peak_kind": "measured peer copy per direction (900 nominal)"},
             "cpu_baseline": None,
             "e2e": {"value": round(nb * e2e_steps / e2e_s, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": n_loc * H * 4 * world, "d2h_bytes_per_step": n_loc * H * 4 * world},
             "clocks": ck.summary(),
-            "gpu_launches": 11 * args.steps,
+            "gpu_launches": launches * args.steps,
             "detail": {"experts_touched_all_gpus": units_all, "experts_touched_rank0": local_units,
-                       "layer_gen_s_rank0": round(gen_s, 1), "exchange": "fixed-size all-to-all (32 rows per rank pair)",
-                       "cuda_graph": graph is not None, "graph_error": graph_err,
+                       "rows_sent_rank0": rows_out, "slots_returned_rank0": slots_back,
+                       "launches_per_step": launches, "layer_gen_s_rank0": round(gen_s, 1),
                        "per_rank_device_ms_e2e_s_units": per_rank},
         }
         print(json.dumps(line))
-    dist.barrier(group=host)
-    # a graph holding NCCL calls must be released before the process group: drop every reference to it
-    step = y_graph = graph = None
-    import gc
-    gc.collect()
+    dist.barrier()
     torch.cuda.synchronize(dev)
+    ep.close()
     pool.close()
     dist.destroy_process_group()
 

@@ -1159,8 +1159,7 @@ static int enqueue_ep(inzg_ctx *c, int layer, int n, const float *x, const float
         else launches += r;
     };
     add(launch_router_logits(L.router, L.router32, x, n, H, E, bias, c->logits, c->meta, st));
-    add(launch_softmax_topk(c->logits, n, E, K, ep->sel, ep->w, nullptr, st));
-    add(launch_ep_dispatch(x, n, ep->sel, ep->w, ep->P, ep->epoch, ep->tickets, c->num_sms, st));
+    add(launch_ep_dispatch(c->logits, x, n, E, ep->P, ep->epoch, ep->tickets, st));
     add(launch_ep_wait(ep->P.flags[ep->rank], ep->world, 0, ep->epoch, false, ep->err, st));
     const int r = enqueue_experts(c, L, ep->world * ep->cap, ep->P.rx[ep->rank], ep->P.rsel[ep->rank],
                                   ep->P.rw[ep->rank], n_batch, ep->out, st);

@@ -8,8 +8,9 @@
 //   rx   [G][C][H] f32    the rows sources sent here (a row only when the token has an expert here)
 //   slot [C][K][H] f32    this rank's tokens' expert outputs, written by the owner of each slot
 //   flags [2][G] u32      dispatch / return epochs written by each peer
-// One step on every rank: route -> ep_dispatch (each (token, owner) row and its slot metadata straight into the
-// owner's buffer, then a release of the owner's dispatch flag) -> ep_wait (acquire every peer's dispatch flag) ->
+// One step on every rank: router logits -> ep_dispatch (per token the reference's softmax and top-k, then its row and
+// slot metadata straight into each owner's buffer, then a release of the owners' dispatch flags) -> ep_wait (acquire
+// every peer's dispatch flag) ->
 // the owned experts on all received rows (the single-GPU experts path; its numeric-path rule uses the whole batch) ->
 // ep_return (each owned slot straight into its home's slot buffer, then a release of the home's return flag) ->
 // ep_wait (every peer's return flag) -> the rank-order combine of the K slots (src/model_fwd.c:1134-1140). Slots are
@@ -27,6 +28,7 @@
 
 #include "inzg_internal.h"
 #include "k_launch.h"
+#include "k_softmax.cuh"
 
 namespace inzg {
 
@@ -49,51 +51,73 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
 __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
-// the last block of a grid to finish releases `epoch` into flag[me] of every peer's flag array `which`
+// the last block of a grid to finish releases `epoch` into flag[me] of every peer's flag array `which`: the block's
+// stores are ordered before thread 0's system-scope release fence by the barrier, the fence before the ticket (the
+// grid-wide barrier pattern), and the last block's acquire-release fence before its release stores of the flags
 __device__ void release_peers(const EpPeers &P, int which, uint32_t epoch, int32_t *ticket) {
-    __threadfence_system();  // this block's peer stores before its ticket
     __syncthreads();
     if (threadIdx.x == 0) {
+        fence_acq_rel_sys();
         const int t = atomicAdd(ticket, 1);
         if (t == (int)gridDim.x - 1) {
-            __threadfence_system();  // every block's stores (their fences preceded their tickets) before the flags
+            fence_acq_rel_sys();
             for (int d = 0; d < P.world; d++) st_release_sys(P.flags[d] + which * P.world + P.rank, epoch);
             *ticket = 0;  // the next step's kernels start after this one ends
         }
     }
 }
 
-// dispatch: pair (row t, destination d) per warp; t < n carries a token (its K selections), t >= n only clears
-// its metadata. A row is sent once to every rank owning at least one of its experts.
-__global__ void __launch_bounds__(256) ep_dispatch_kernel(const float *__restrict__ x, int n, const int32_t *__restrict__ sel,
-                                                          const float *__restrict__ w, EpPeers P, const uint32_t *epoch_dev,
+// copy of one row of H floats by the calling group of `nthr` threads (index `tid`): all loads of a pass are in flight
+// before its stores
+__device__ __forceinline__ void copy_row(float4 *__restrict__ dst, const float4 *__restrict__ src, int n4, int tid,
+                                         int nthr) {
+    constexpr int U = 8;
+    for (int i0 = tid; i0 < n4; i0 += U * nthr) {
+        float4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; u++)
+            if (i0 + u * nthr < n4) v[u] = __ldg(src + i0 + u * nthr);
+#pragma unroll
+        for (int u = 0; u < U; u++)
+            if (i0 + u * nthr < n4) dst[i0 + u * nthr] = v[u];
+    }
+}
+
+// route + dispatch, one block per row t of the rank's capacity: warp 0 runs the reference's softmax and top-k of token
+// t on its router logits (t < n), then the block writes the row's slot metadata into every rank (-1 where that rank
+// owns none of the token's experts; rows t >= n only clear theirs) and the token's fp32 row once into every rank owning
+// at least one of its experts.
+__global__ void __launch_bounds__(256) ep_dispatch_kernel(const float *__restrict__ logits, const float *__restrict__ x,
+                                                          int n, int E, EpPeers P, const uint32_t *epoch_dev,
                                                           int32_t *ticket) {
+    extern __shared__ float ex[];  // [E] softmax scratch of warp 0
+    __shared__ int32_t ssel[kMaxTopK];
+    __shared__ float sw[kMaxTopK];
     const uint32_t epoch = *epoch_dev + 1;
-    const int K = P.topk, H = P.hidden, C = P.cap, G = P.world;
-    const int lane = threadIdx.x & 31;
-    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), nw = gridDim.x * (blockDim.x >> 5);
-    for (int p = gw; p < C * G; p += nw) {
-        const int t = p / G, d = p % G;
-        int loc = -1;
-        float wk = 0.0f;
-        if (lane < K && t < n) {
-            const int e = sel[(size_t)t * K + lane];
-            if (e >= d * P.e_per && e < (d + 1) * P.e_per) {
-                loc = e - d * P.e_per;
-                wk = w[(size_t)t * K + lane];
-            }
+    const int K = P.topk, H = P.hidden, C = P.cap, G = P.world, t = blockIdx.x, tid = threadIdx.x;
+    if (t < n) {
+        if (tid < 32) softmax_topk_warp(logits + (size_t)t * E, E, K, ex, nullptr, ssel, sw);
+    } else if (tid < K) {
+        ssel[tid] = -1;
+        sw[tid] = 0.0f;
+    }
+    __syncthreads();
+    const size_t row = (size_t)P.rank * C + t;
+    for (int d = 0; d < G; d++) {
+        const int lo = d * P.e_per;
+        bool here = false;
+        for (int k = 0; k < K; k++) here |= ssel[k] >= lo && ssel[k] < lo + P.e_per;
+        if (tid < K) {
+            const int e = ssel[tid];
+            const bool own = e >= lo && e < lo + P.e_per;
+            P.rsel[d][row * K + tid] = own ? e - lo : -1;
+            P.rw[d][row * K + tid] = own ? sw[tid] : 0.0f;
         }
-        const size_t row = (size_t)P.rank * C + t;
-        if (lane < K) {
-            P.rsel[d][row * K + lane] = loc;
-            P.rw[d][row * K + lane] = wk;
-        }
-        if (__any_sync(0xffffffffu, loc >= 0)) {
-            const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)t * H);
-            float4 *dst = reinterpret_cast<float4 *>(P.rx[d] + row * H);
-            for (int i = lane; i < H / 4; i += 32) dst[i] = __ldg(src + i);
-        }
+        if (here)
+            copy_row(reinterpret_cast<float4 *>(P.rx[d] + row * H), reinterpret_cast<const float4 *>(x + (size_t)t * H),
+                     H / 4, tid, blockDim.x);
     }
     release_peers(P, 0, epoch, ticket);
 }
@@ -109,9 +133,8 @@ __global__ void __launch_bounds__(256) ep_return_kernel(const float *__restrict_
     for (int p = gw; p < G * C * K; p += nw) {
         if (mine[p] < 0) continue;  // uniform over the warp
         const int r = p / K, k = p % K, s = r / C, t = r % C;
-        const float4 *src = reinterpret_cast<const float4 *>(out + (size_t)p * H);
-        float4 *dst = reinterpret_cast<float4 *>(P.slot[s] + ((size_t)t * K + k) * H);
-        for (int i = lane; i < H / 4; i += 32) dst[i] = src[i];
+        copy_row(reinterpret_cast<float4 *>(P.slot[s] + ((size_t)t * K + k) * H),
+                 reinterpret_cast<const float4 *>(out + (size_t)p * H), H / 4, lane, 32);
     }
     release_peers(P, 1, epoch, ticket);
 }
@@ -142,10 +165,10 @@ __global__ void ep_wait_kernel(const uint32_t *flags, int world, int which, uint
 
 }  // namespace
 
-int launch_ep_dispatch(const float *x, int n, const int32_t *sel, const float *w, const EpPeers &P,
-                       const uint32_t *epoch_dev, int32_t *ticket, int num_sms, cudaStream_t st) {
-    const int pairs = P.cap * P.world, blocks = std::min((pairs + 7) / 8, num_sms * 4);
-    ep_dispatch_kernel<<<blocks, 256, 0, st>>>(x, n, sel, w, P, epoch_dev, ticket);
+int launch_ep_dispatch(const float *logits, const float *x, int n, int E, const EpPeers &P, const uint32_t *epoch_dev,
+                       int32_t *ticket, cudaStream_t st) {
+    if (E % 32 || E > 32 * kMaxPerLane || P.topk > kMaxTopK) return -1;
+    ep_dispatch_kernel<<<P.cap, 256, (size_t)E * sizeof(float), st>>>(logits, x, n, E, P, epoch_dev, ticket);
     return 1;
 }
 

@@ -34,11 +34,12 @@ int launch_shared_route(const RouteDev &R, int n, int gemm, int gu_items_per_uni
                         int32_t *upath, int32_t *eexp, cudaStream_t st);
 
 void gemv_set_attributes();
-// Prefill-numerics experts of a decode-sized call (at most kGemvGemmMaxTokens tokens), run by the decode GEMV kernel
-// itself as GEMM items (the call's R.gemm_tiles, built with a token tile of kGemvGemmTile: one tile per expert): int8
-// activations per 256-block by token (gate|up) or by entry (down), their block scales, the layer's per-(row,
-// 256-block) weight scales and a TMA map over the requantized int8 weights with 16-row boxes (make_tma_map_i8(..., 16)).
-constexpr int kGemvGemmTile = 32, kGemvGemmMaxTokens = 32;
+// Prefill-numerics experts of a decode-sized call (at most kGemvGemmMaxTokens token rows), run by the decode GEMV
+// kernel itself as GEMM items (the call's R.gemm_tiles, built with a token tile of kGemvGemmTile: an expert with more
+// tokens takes one item per tile and row block): int8 activations per 256-block by token (gate|up) or by entry
+// (down), their block scales, the layer's per-(row, 256-block) weight scales and a TMA map over the requantized int8
+// weights with 16-row boxes (make_tma_map_i8(..., 16)).
+constexpr int kGemvGemmTile = 32, kGemvGemmMaxTokens = 256;
 struct DecGemm {
     const int8_t *aq;
     const float *as;
@@ -67,8 +68,9 @@ void launch_pool_repack(const uint8_t *blobs, uint64_t blob_bytes, uint64_t gu_b
                         const LayerDev &L, uint8_t *pool, uint8_t *luts, cudaStream_t st);
 
 // Expert-parallel exchange over peer memory (k_ep.cu). epoch_dev: the rank's step counter; tickets: one int per kernel.
-int launch_ep_dispatch(const float *x, int n, const int32_t *sel, const float *w, const EpPeers &P,
-                       const uint32_t *epoch_dev, int32_t *ticket, int num_sms, cudaStream_t st);
+// route + dispatch from the router logits [n][E] (softmax and top-k per token inside)
+int launch_ep_dispatch(const float *logits, const float *x, int n, int E, const EpPeers &P, const uint32_t *epoch_dev,
+                       int32_t *ticket, cudaStream_t st);
 int launch_ep_return(const float *out, const EpPeers &P, const uint32_t *epoch_dev, int32_t *ticket, int num_sms,
                      cudaStream_t st);
 int launch_ep_wait(const uint32_t *flags, int world, int which, uint32_t *epoch_dev, bool advance, int32_t *err,

@@ -183,75 +183,6 @@ __global__ void __launch_bounds__(256) route_scatter_kernel(const int32_t *__res
     }
 }
 
-// Small calls (n <= 64): the whole dispatch in one block of E threads, thread e = expert e. Counting, the
-// first-touch key and the token-ordered scatter read the call's n * topk selections from shared memory.
-constexpr int kSmallRouteMax = 64;
-__global__ void __launch_bounds__(1024) route_small_kernel(const int32_t *__restrict__ sel, const float *__restrict__ w,
-                                                           int n, int topk, int E, int gu_items_per_unit,
-                                                           int dn_items_per_unit, int gemm_tn, RouteDev R,
-                                                           int32_t *__restrict__ upath, int32_t *__restrict__ eexp) {
-    __shared__ int32_t ss[kSmallRouteMax * kMaxTopK];
-    __shared__ int32_t sc[1024], su[1024], sd[1024], sg[1024], st[1024], bins[32];
-    const int e = threadIdx.x, nk = n * topk;
-    for (int i = e; i < nk; i += blockDim.x) ss[i] = sel[i];
-    if (e == 0) begin_call_errors(R.meta);  // this call's sticky error code starts with the router's
-    __syncthreads();
-    int c = 0, first = 0x7F7F7F7F;
-    if (e < E)
-        for (int i = 0; i < nk; i++)
-            if (ss[i] == e) { c++; first = min(first, i); }
-    if (e == 0)
-        for (int i = 0; i < nk; i++)
-            if ((ss[i] < 0 && !R.absent_ok) || ss[i] >= E) set_error(R.meta, kErrBadExpert);
-    const int is_unit = c > 0;
-    const int is_dec = is_unit && (R.n_rule <= 8 || c < kGemmMinT);
-    const int is_gemm = is_unit && !is_dec;
-    const int tiles = is_gemm ? (c + gemm_tn - 1) / gemm_tn : 0;
-    sc[e] = c; su[e] = is_unit; sd[e] = is_dec; sg[e] = is_gemm; st[e] = tiles;
-    __syncthreads();
-    for (int o = 1; o < blockDim.x; o <<= 1) {
-        int a = 0, b = 0, d = 0, g = 0, h = 0;
-        if (e >= o) { a = sc[e - o]; b = su[e - o]; d = sd[e - o]; g = sg[e - o]; h = st[e - o]; }
-        __syncthreads();
-        if (e >= o) { sc[e] += a; su[e] += b; sd[e] += d; sg[e] += g; st[e] += h; }
-        __syncthreads();
-    }
-    if (e < E) {
-        const int off = sc[e] - c;
-        R.cnt[e] = c;
-        R.off[e] = off;
-        R.first[e] = first;
-        if (e == E - 1) R.off[E] = sc[e];
-        upath[e] = is_gemm;
-        if (is_unit) R.units[su[e] - 1] = e;
-        if (is_gemm) {
-            R.gemm_units[sg[e] - 1] = e;
-            const int base = st[e] - tiles;
-            for (int i = 0; i < tiles; i++) R.gemm_tiles[base + i] = ((sg[e] - 1) << 16) | i;
-        }
-        int pos = off;  // scan in (token, k) order: tokens ascending inside the expert's list
-        for (int i = 0; i < nk && pos < off + c; i++)
-            if (ss[i] == e) {
-                R.etok[pos] = i / topk;
-                R.eslot[pos] = i;
-                R.ew[pos] = w[i];
-                eexp[pos] = e;
-                pos++;
-            }
-    }
-    order_dec_units(is_dec, c, e, R.dec_units, R.meta, bins);
-    if (e == blockDim.x - 1) {
-        R.meta[kMetaNUnits] = su[e];
-        R.meta[kMetaNDec] = sd[e];
-        R.meta[kMetaNGemm] = sg[e];
-        R.meta[kMetaDecItemsGU] = sd[e] * gu_items_per_unit;
-        R.meta[kMetaDecItemsDN] = sd[e] * dn_items_per_unit;
-        R.meta[kMetaGemmTilesGU] = st[e];
-        R.meta[kMetaGemmTilesDN] = st[e];
-        if (R.absent_ok ? sc[e] > nk : sc[e] != nk) set_error(R.meta, kErrOverflow);
-    }
-}
-
 // inclusive scan of v over the block (blockDim.x <= 1024); ws: 32 ints of shared scratch
 __device__ __forceinline__ int block_scan_incl(int v, int *ws) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
@@ -275,6 +206,89 @@ __device__ __forceinline__ int block_scan_incl(int v, int *ws) {
     if (w > 0) v += ws[w - 1];
     __syncthreads();
     return v;
+}
+
+// Calls of up to 256 token rows: the whole dispatch in one block of E threads (thread e = expert e). Every selection
+// sets bit t of its expert's 256-bit token mask, so an expert's count is a popcount, its first-touch key the first
+// token's slot, and an entry's place in the expert's token-ordered list the popcount of the lower tokens -- the
+// reference's order without any scan over the selections.
+constexpr int kSmallRouteMax = 256, kSmallRouteWords = kSmallRouteMax / 64;
+__global__ void __launch_bounds__(1024) route_small_kernel(const int32_t *__restrict__ sel, const float *__restrict__ w,
+                                                           int n, int topk, int E, int gu_items_per_unit,
+                                                           int dn_items_per_unit, int gemm_tn, RouteDev R,
+                                                           int32_t *__restrict__ upath, int32_t *__restrict__ eexp) {
+    __shared__ unsigned long long em[kSmallRouteWords][1024];
+    __shared__ int32_t soff[1024], ws[32], bins[32];
+    const int e = threadIdx.x, nk = n * topk, nw = (n + 63) / 64;
+    for (int j = 0; j < nw; j++)
+        if (e < E) em[j][e] = 0ull;
+    if (e == 0) begin_call_errors(R.meta);  // this call's sticky error code starts with the router's
+    __syncthreads();
+    for (int i = e; i < nk; i += blockDim.x) {
+        const int x = sel[i], t = i / topk;
+        if (x >= 0 && x < E) {
+            const unsigned long long bit = 1ull << (t & 63);
+            if (atomicOr(&em[t >> 6][x], bit) & bit) set_error(R.meta, kErrBadExpert);  // one expert named twice
+        } else if (x >= E || !R.absent_ok) {
+            set_error(R.meta, kErrBadExpert);
+        }
+    }
+    __syncthreads();
+    int c = 0, first = 0x7F7F7F7F;
+    if (e < E) {
+        int t0 = -1;
+        for (int j = nw - 1; j >= 0; j--) {
+            const unsigned long long m = em[j][e];
+            c += __popcll(m);
+            if (m) t0 = j * 64 + __ffsll((long long)m) - 1;
+        }
+        if (t0 >= 0)
+            for (int k = 0; k < topk; k++)
+                if (sel[t0 * topk + k] == e) first = t0 * topk + k;
+    }
+    const int is_unit = c > 0, is_dec = is_unit && (R.n_rule <= 8 || c < kGemmMinT), is_gemm = is_unit && !is_dec;
+    const int tiles = is_gemm ? (c + gemm_tn - 1) / gemm_tn : 0;
+    // two scans: counts (12 bits: at most 256 x 16 entries) | tiles, units | decode | prefill counts (10 bits each)
+    const int sa = block_scan_incl(c | (tiles << 12), ws);
+    const int sb = block_scan_incl(is_unit | (is_dec << 10) | (is_gemm << 20), ws);
+    const int c_incl = sa & 4095, t_incl = sa >> 12;
+    const int u_incl = sb & 1023, d_incl = (sb >> 10) & 1023, g_incl = sb >> 20;
+    if (e < E) {
+        const int off = c_incl - c;
+        soff[e] = off;
+        R.cnt[e] = c;
+        R.off[e] = off;
+        R.first[e] = first;
+        if (e == E - 1) R.off[E] = c_incl;
+        upath[e] = is_gemm;
+        if (is_unit) R.units[u_incl - 1] = e;
+        if (is_gemm) {
+            R.gemm_units[g_incl - 1] = e;
+            for (int i = 0; i < tiles; i++) R.gemm_tiles[t_incl - tiles + i] = ((g_incl - 1) << 16) | i;
+        }
+    }
+    order_dec_units(is_dec, c, e, R.dec_units, R.meta, bins);
+    if (e == blockDim.x - 1) {
+        R.meta[kMetaNUnits] = u_incl;
+        R.meta[kMetaNDec] = d_incl;
+        R.meta[kMetaNGemm] = g_incl;
+        R.meta[kMetaDecItemsGU] = d_incl * gu_items_per_unit;
+        R.meta[kMetaDecItemsDN] = d_incl * dn_items_per_unit;
+        R.meta[kMetaGemmTilesGU] = t_incl;
+        R.meta[kMetaGemmTilesDN] = t_incl;
+        if (R.absent_ok ? c_incl > nk : c_incl != nk) set_error(R.meta, kErrOverflow);
+    }
+    __syncthreads();
+    for (int i = e; i < nk; i += blockDim.x) {
+        const int x = sel[i], t = i / topk;
+        if (x < 0 || x >= E) continue;
+        int pos = soff[x] + __popcll(em[t >> 6][x] & ((1ull << (t & 63)) - 1ull));
+        for (int j = 0; j < (t >> 6); j++) pos += __popcll(em[j][x]);
+        R.etok[pos] = t;
+        R.eslot[pos] = i;
+        R.ew[pos] = w[i];
+        eexp[pos] = x;
+    }
 }
 
 // Small calls (n <= 64) in one cluster of kRouteCluster blocks of 1024 threads. Softmax + top-k run one warp per
@@ -425,7 +439,7 @@ void route_set_attributes(int E) {
 int launch_route(const RouteDev &R, int gu_items_per_unit, int dn_items_per_unit, int gemm_tn,
                  int32_t *upath, int32_t *eexp, cudaStream_t st) {
     const int n = R.n, topk = R.topk, E = R.E;
-    if (n <= kSmallRouteMax) {
+    if (n <= kSmallRouteMax && n * topk < 4096 && E < 1024) {  // the packed scans' field widths
         const int threads = (E + 31) / 32 * 32;
         route_small_kernel<<<1, threads, 0, st>>>(R.sel, R.w, n, topk, E, gu_items_per_unit, dn_items_per_unit, gemm_tn,
                                                   R, upath, eexp);

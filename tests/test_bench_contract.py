@@ -63,7 +63,15 @@ def test_reference_arm_other_ranks_exit_quietly():
 
 def test_ep_exchange_bytes():
     sys.path.insert(0, ROOT)
+    import numpy as np
     import bench
-    assert bench.ep_fixed_exchange_bytes(1, 32) == 0  # one GPU: nothing crosses a link
-    # 8 GPUs, 32 rows per rank pair: 7 peers x 32 x (8192 B row + 80 B (expert, weight) pairs + 81920 B of results)
-    assert bench.ep_fixed_exchange_bytes(8, 32) == 7 * 32 * (8192 + 80 + 81920) == 20203008
+    rng = np.random.default_rng(0)
+    sel = np.stack([rng.permutation(512)[:10] for _ in range(32)])[None]  # one rank, 32 tokens
+    assert bench.ep_exchange_bytes(sel, 0, 1) == (0, 0, 0)  # one GPU: nothing crosses a link
+    # 2 ranks, one token each: rank 0's token picks experts 0 (own) and 300 (rank 1's); rank 1's token picks 1 and 2
+    # (both rank 0's) -> rank 0 sends its row once to rank 1 with the row's (expert, weight) metadata and returns
+    # both slots of rank 1's token
+    sel2 = np.array([[[0, 300]], [[1, 2]]])
+    assert bench.ep_exchange_bytes(sel2, 0, 2, topk=2) == (8192 + 1 * 1 * 2 * 8 + 2 * 8192, 1, 2)
+    # rank 1 sends its row to rank 0 (both its experts live there) and returns the one slot of rank 0's token it owns
+    assert bench.ep_exchange_bytes(sel2, 1, 2, topk=2) == (8192 + 16 + 8192, 1, 1)

@@ -44,11 +44,12 @@ def test_tcgen05_gemm_equals_simt_gemm_and_oracle(orc, expert_type):
 
 
 @pytest.mark.parametrize("expert_type", [synth.T_Q4L, synth.T_Q8G])
-@pytest.mark.parametrize("n", [12, 20, 32])
+@pytest.mark.parametrize("n", [12, 20, 32, 70])
 def test_decode_gemv_gemm_items_equal_simt_gemm(orc, expert_type, n):
-    """Calls of 9-32 tokens run their prefill-numerics experts (>= 12 tokens) inside the decode GEMV launches as GEMM
-    items (ldmatrix + s8 x s8 MMA over tensor-copied int8 tiles): bit-identical to the CUDA-core int8 GEMM, within the
-    north-star tolerance of the oracle, and without the separate gather / GEMM launches."""
+    """Calls of 9-256 tokens run their prefill-numerics experts (>= 12 tokens) inside the decode GEMV launches as GEMM
+    items (ldmatrix + s8 x s8 MMA over tensor-copied int8 tiles, 32 tokens per item: at 70 tokens the busiest experts
+    take three token tiles, the last one partial): bit-identical to the CUDA-core int8 GEMM, within the north-star
+    tolerance of the oracle, and without the separate gather / GEMM launches."""
     ov = synth.normal_logits(n, E, seed=50 + n)
     ov[:, :3] += 9.0           # experts 0-2 take every token
     ov[:12, 300:302] += 12.0   # experts 300-301 take exactly the first 12 (the smallest prefill-numerics expert)
@@ -60,7 +61,7 @@ def test_decode_gemv_gemm_items_equal_simt_gemm(orc, expert_type, n):
     blobs, bb = synth.layer_blobs(0, expert_type, H, FF, E, experts=np.unique(sel))
     gu_bytes = int(synth.lib.inzg_qmat_bytes(expert_type, 2 * FF, H))
     want = orc.moe_routed(R, blobs, bb, gu_bytes, x, override=ov, dumps=False)["y"]
-    with MoePool(H, FF, E, K, max_tokens=64, n_layers=1, device=0) as pool:
+    with MoePool(H, FF, E, K, max_tokens=max(n, 64), n_layers=1, device=0) as pool:
         pool.add_layer(0, expert_type, blobs, bb)
         y = pool.moe_block(0, x, logits_override=ov, dump=True)
         pool.route_dump(n)
