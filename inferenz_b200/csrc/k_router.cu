@@ -145,56 +145,71 @@ __global__ void __launch_bounds__(WPB * 32) router_small_kernel(const uint4 *__r
 // Many tokens: FMA-bound (4.3 G FMA at 4096 tokens). Thread = (lane l, 2 experts from two quads, 8 tokens): each
 // 16-byte shared load of x (4 chain steps of one token) feeds 8 FMAs; the next chunk's weights load during the FMAs.
 // Block = 8 warps = 16 expert quads = 64 experts; grid = (E / 64, n / 8).
+// LT tokens per block: 8 for many tokens (8 FMAs per x load); 2 or 4 for decode-sized calls, where the grid needs
+// more blocks than tokens / 8 to put several warps of chains on every SM (the weights then come from L2 once per
+// token block).
 constexpr int kLT = 8;
+template <int LT, int EPT = 2>
 __global__ void __launch_bounds__(256) router_large_kernel(const uint4 *__restrict__ Wr, const float *__restrict__ X,
                                                            int n, int H, int E, const float *__restrict__ bias,
                                                            float *__restrict__ logits) {
     extern __shared__ __align__(16) float xs[];
     const int S = H / 8, SC = S / 8, SP = S + 4;
-    const int t0 = blockIdx.y * kLT, nt = min(kLT, n - t0);
+    const int t0 = blockIdx.y * LT, nt = min(LT, n - t0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, l = lane & 7;
-    const int qa = blockIdx.x * 16 + warp * 2, qb = qa + 1;  // the warp's two expert quads
+    // the warp's expert quads: qa, and qb = qa + 1 when a thread runs two experts
+    const int qa = blockIdx.x * 8 * EPT + warp * EPT, qb = qa + 1;
     const int ea = qa * 4 + (lane >> 3), eb = qb * 4 + (lane >> 3);
-    const bool live = qb * 4 < E + 4 && qa * 4 < E;
+    const bool live = qa * 4 < E;
     const uint4 *wa = Wr + (size_t)qa * SC * 32 + lane, *wb = Wr + (size_t)qb * SC * 32 + lane;
-    const bool hasb = qb * 4 < E;
-    uint4 ca = live ? __ldg(wa) : make_uint4(0, 0, 0, 0), cb = hasb ? __ldg(wb) : make_uint4(0, 0, 0, 0);
-    stage_x<kLT>(xs, X, t0, nt, H);
+    const bool hasb = EPT == 2 && qb * 4 < E;
+    // the weights stream from L2 through an 8-chunk register ring
+    constexpr int PF = 8;
+    uint4 ra[PF], rb[PF];
+#pragma unroll
+    for (int u = 0; u < PF; u++) {
+        ra[u] = live ? __ldg(wa + (size_t)u * 32) : make_uint4(0, 0, 0, 0);
+        rb[u] = hasb ? __ldg(wb + (size_t)u * 32) : make_uint4(0, 0, 0, 0);
+    }
+    stage_x<LT>(xs, X, t0, nt, H);
     __syncthreads();
     if (!live) return;
-    float A[kLT], B[kLT];
+    float A[LT], B[LT];
 #pragma unroll
-    for (int tt = 0; tt < kLT; tt++) { A[tt] = 0.0f; B[tt] = 0.0f; }
-    for (int jc = 0; jc < SC; jc++) {
-        uint4 na = make_uint4(0, 0, 0, 0), nb = make_uint4(0, 0, 0, 0);
-        if (jc + 1 < SC) {
-            na = __ldg(wa + (size_t)(jc + 1) * 32);
-            if (hasb) nb = __ldg(wb + (size_t)(jc + 1) * 32);
-        }
-        float w1[8], w2[8];
-        h8(ca, w1);
-        h8(cb, w2);
+    for (int tt = 0; tt < LT; tt++) { A[tt] = 0.0f; B[tt] = 0.0f; }
+    for (int jc0 = 0; jc0 < SC; jc0 += PF) {
 #pragma unroll
-        for (int tt = 0; tt < kLT; tt++) {
-            const float *xp = xs + (size_t)tt * 8 * SP + l * SP + jc * 8;
-            const float4 a = reinterpret_cast<const float4 *>(xp)[0], b = reinterpret_cast<const float4 *>(xp)[1];
-            float r = A[tt], q = B[tt];
-            r = __fmaf_rn(w1[0], a.x, r); q = __fmaf_rn(w2[0], a.x, q);
-            r = __fmaf_rn(w1[1], a.y, r); q = __fmaf_rn(w2[1], a.y, q);
-            r = __fmaf_rn(w1[2], a.z, r); q = __fmaf_rn(w2[2], a.z, q);
-            r = __fmaf_rn(w1[3], a.w, r); q = __fmaf_rn(w2[3], a.w, q);
-            r = __fmaf_rn(w1[4], b.x, r); q = __fmaf_rn(w2[4], b.x, q);
-            r = __fmaf_rn(w1[5], b.y, r); q = __fmaf_rn(w2[5], b.y, q);
-            r = __fmaf_rn(w1[6], b.z, r); q = __fmaf_rn(w2[6], b.z, q);
-            r = __fmaf_rn(w1[7], b.w, r); q = __fmaf_rn(w2[7], b.w, q);
-            A[tt] = r;
-            B[tt] = q;
+        for (int u = 0; u < PF; u++) {
+            const int jc = jc0 + u;
+            if (jc >= SC) break;  // H % 512 != 0: the last pass is partial
+            float w1[8], w2[8];
+            h8(ra[u], w1);
+            if (EPT == 2) h8(rb[u], w2);
+            if (jc + PF < SC) {
+                ra[u] = __ldg(wa + (size_t)(jc + PF) * 32);
+                if (hasb) rb[u] = __ldg(wb + (size_t)(jc + PF) * 32);
+            }
+#pragma unroll
+            for (int tt = 0; tt < LT; tt++) {
+                const float *xp = xs + (size_t)tt * 8 * SP + l * SP + jc * 8;
+                const float4 a = reinterpret_cast<const float4 *>(xp)[0], b = reinterpret_cast<const float4 *>(xp)[1];
+                float r = A[tt];
+                r = __fmaf_rn(w1[0], a.x, r); r = __fmaf_rn(w1[1], a.y, r); r = __fmaf_rn(w1[2], a.z, r);
+                r = __fmaf_rn(w1[3], a.w, r); r = __fmaf_rn(w1[4], b.x, r); r = __fmaf_rn(w1[5], b.y, r);
+                r = __fmaf_rn(w1[6], b.z, r); r = __fmaf_rn(w1[7], b.w, r);
+                A[tt] = r;
+                if (EPT == 2) {
+                    float q = B[tt];
+                    q = __fmaf_rn(w2[0], a.x, q); q = __fmaf_rn(w2[1], a.y, q); q = __fmaf_rn(w2[2], a.z, q);
+                    q = __fmaf_rn(w2[3], a.w, q); q = __fmaf_rn(w2[4], b.x, q); q = __fmaf_rn(w2[5], b.y, q);
+                    q = __fmaf_rn(w2[6], b.z, q); q = __fmaf_rn(w2[7], b.w, q);
+                    B[tt] = q;
+                }
+            }
         }
-        ca = na;
-        cb = nb;
     }
 #pragma unroll
-    for (int tt = 0; tt < kLT; tt++) {
+    for (int tt = 0; tt < LT; tt++) {
         write_logit(A[tt], l, tt, nt, t0, ea, E, bias, logits);
         if (hasb) write_logit(B[tt], l, tt, nt, t0, eb, E, bias, logits);
     }
@@ -366,34 +381,34 @@ static size_t router_smem(int TT, int H) { return (size_t)TT * 8 * (H / 8 + 4) *
 static size_t router_small_smem(int TT, int WPB, int H) { return 128 + (size_t)2 * WPB * H * 8 + (size_t)TT * H * 4; }
 
 void router_set_attributes(int H) {
-    cudaFuncSetAttribute(router_large_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_smem(kLT, H));
+    cudaFuncSetAttribute(router_large_kernel<kLT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_smem(kLT, H));
+    cudaFuncSetAttribute(router_large_kernel<4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_smem(4, H));
+    cudaFuncSetAttribute(router_large_kernel<2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_smem(2, H));
     cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_gemm_smem());
     cudaFuncSetAttribute(router_small_kernel<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_small_smem(1, 1, H));
     cudaFuncSetAttribute(router_small_kernel<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_small_smem(2, 1, H));
-    cudaFuncSetAttribute(router_small_kernel<4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_small_smem(4, 1, H));
-    cudaFuncSetAttribute(router_small_kernel<8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_small_smem(8, 1, H));
 }
 
 int launch_router_logits(const uint4 *Wr, const float *Wf, const float *X, int n, int H, int E, const float *bias,
                          float *logits, int32_t *meta, cudaStream_t st) {
     CUtensorMap mapX;
-    // few tokens: every block pulls its experts' weights and the token tile in one go; one warp (4 experts) per block
-    // up to 8 tokens so the 2 MB router spreads over every SM. Many tokens: 64 experts x 8 tokens per block, FMA-bound.
+    // 1-2 tokens: every block pulls its experts' weights and the token tile in one go, one warp (8 experts) per block so
+    // the 2 MB router spreads over every SM. 3-64 tokens: 64 experts x 2-4 tokens per block of 8 warps, weights
+    // streamed from L2. Many tokens: 64 experts x 8 tokens per block (or the TMA-tiled kernel), FMA-bound.
     if (n <= 1) {
         router_small_kernel<1, 1><<<dim3((E / 4 + 1) / 2, n), 32, router_small_smem(1, 1, H), st>>>(Wr, X, n, H, E, bias, logits, meta);
     } else if (n <= 2) {
         router_small_kernel<2, 1><<<dim3((E / 4 + 1) / 2, 1), 32, router_small_smem(2, 1, H), st>>>(Wr, X, n, H, E, bias, logits, meta);
-    } else if (n <= 4) {
-        router_small_kernel<4, 1><<<dim3((E / 4 + 1) / 2, 1), 32, router_small_smem(4, 1, H), st>>>(Wr, X, n, H, E, bias, logits, meta);
+    } else if (n <= 32) {  // ROUTER_SMALL_CALL
+        router_large_kernel<2, 2><<<dim3((E + 63) / 64, (n + 1) / 2), 256, router_smem(2, H), st>>>(Wr, X, n, H, E, bias, logits);
     } else if (n <= 64) {
-        router_small_kernel<8, 1><<<dim3((E / 4 + 1) / 2, (n + 7) / 8), 32, router_small_smem(8, 1, H), st>>>(Wr, X, n, H, E, bias,
-                                                                                                  logits, meta);
+        router_large_kernel<4, 2><<<dim3((E + 63) / 64, (n + 3) / 4), 256, router_smem(4, H), st>>>(Wr, X, n, H, E, bias, logits);
     } else if (Wf && n >= kRouterGemmMinTokens && router_gemm_fits(E, H) && make_tma_map_f32(&mapX, X, n, H, kRT)) {
         router_gemm_kernel<<<dim3(E / kRE, (n + kRT - 1) / kRT), 256, router_gemm_smem(), st>>>(mapX, Wf, n, H, E, bias,
                                                                                               logits, meta);
     } else {
         dim3 grid((E + 63) / 64, (n + kLT - 1) / kLT);
-        router_large_kernel<<<grid, 256, router_smem(kLT, H), st>>>(Wr, X, n, H, E, bias, logits);
+        router_large_kernel<kLT><<<grid, 256, router_smem(kLT, H), st>>>(Wr, X, n, H, E, bias, logits);
     }
     return 1;
 }

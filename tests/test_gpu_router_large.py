@@ -1,4 +1,4 @@
-"""Router logits on the many-token kernel (fp32 router copy, eight per-lane SIMT sub-GEMMs, 64-token tiles).
+"""Router logits on the many-token kernels (fp32 router copy in 64-token tiles; 64 experts x 2-8 tokens per block).
 
 600 tokens = 9 full tiles and a ragged one of 24. The logits must be the oracle's bits (the reference's 8-lane FMA
 chains and add tree, then the per-expert bias), and the top-k the oracle's selection.
@@ -14,8 +14,10 @@ pytestmark = pytest.mark.gpu
 H, FF, E, K = 2048, 640, 512, 10
 
 
-def test_many_token_router_bit_exact(orc):
-    n = 600
+@pytest.mark.parametrize("n", [600, 3, 17, 32, 33, 64])
+def test_many_token_router_bit_exact(orc, n):
+    """600: the fp32-copy tiles; 3-64 (decode-sized calls): 64 experts x 2 or 4 tokens per block, odd counts leaving a
+    partial token block"""
     R = synth.router(0, E, H)
     x = synth.hidden(n, H, seed=61)
     bias = synth.zipf_bias(E)  # concentrates the selection (the layer then needs few experts' blobs)
