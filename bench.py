@@ -475,6 +475,7 @@ def run_ep(args):
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             flush.zero_()
+            ep.barrier(stream)
             step()
         stream.synchronize()
         pool.device_status(stream.cuda_stream)
@@ -483,6 +484,7 @@ def run_ep(args):
         with Clocks(local) as ck:
             for a, b in evs:
                 flush.zero_()
+                ep.barrier(stream)  # every rank's timed step starts together (device-side rendezvous)
                 a.record(stream)
                 step()
                 b.record(stream)
@@ -498,6 +500,7 @@ def run_ep(args):
         ts = []
         for _ in range(e2e_steps):
             flush.zero_()
+            ep.barrier(stream)
             stream.synchronize()
             t1 = time.perf_counter()
             xd.copy_(xp, non_blocking=True)

@@ -239,6 +239,11 @@ INZG_EXPORT inzg_status inzg_ep_connect_local(inzg_ctx *const *ctxs, int world);
 INZG_EXPORT inzg_status inzg_ep_forward(inzg_ctx *ctx, int layer, int n, const float *x_dev, const float *logit_bias_dev,
                                         float *y_dev, int n_batch, void *stream);
 
+/* Device-side rendezvous of all ranks on `stream`, outside any step (every rank calls it the same number of times):
+ * the stream continues once every rank's stream has reached its own call. For timing steps from a common start; a peer
+ * that never arrives makes it give up after about a second (INZG_TIMEOUT at inzg_device_status). */
+INZG_EXPORT inzg_status inzg_ep_barrier(inzg_ctx *ctx, void *stream);
+
 /* Leaves the exchange (after every rank's last inzg_ep_forward has completed): closes the peers' mappings and frees
  * this rank's buffer. inzg_destroy does it too. */
 INZG_EXPORT inzg_status inzg_ep_detach(inzg_ctx *ctx);

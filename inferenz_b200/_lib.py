@@ -69,6 +69,7 @@ SIGNATURES = {
     "inzg_ep_connect_local": (I, [P, I]),
     "inzg_ep_forward": (I, [P, I, I, P, P, P, I, P]),
     "inzg_ep_detach": (I, [P]),
+    "inzg_ep_barrier": (I, [P, P]),
     "inzg_gguf_open": (P, [ctypes.c_char_p, ctypes.POINTER(GgufInfo), ctypes.c_char_p, ctypes.c_size_t]),
     "inzg_gguf_get_info": (I, [P, ctypes.POINTER(GgufInfo)]),
     "inzg_gguf_experts": (I, [P, I, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(U64), ctypes.POINTER(U64)]),

@@ -82,16 +82,15 @@ uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
 // counter and the local scratch of a step.
 struct EpState {
     int rank = 0, world = 0, cap = 0;
-    uint8_t *base = nullptr;            // exposed: rsel | rw | rx | slot | flags
+    uint8_t *base = nullptr;            // exposed: rsel | rw | rx | out | flags
     size_t bytes = 0;
-    size_t o_rsel = 0, o_rw = 0, o_rx = 0, o_slot = 0, o_flags = 0;
+    size_t o_rsel = 0, o_rw = 0, o_rx = 0, o_out = 0, o_flags = 0;
     std::vector<void *> opened;          // peers' buffers opened through IPC (closed at detach)
     EpPeers P{};
     bool connected = false;
-    uint8_t *local = nullptr;            // epoch | tickets[2] | err | sel [cap][K] | w [cap][K] | out [world*cap][K][H]
-    uint32_t *epoch = nullptr;
+    uint8_t *local = nullptr;            // epoch | tickets[2] | err | rendezvous epoch | sel [cap][K] (own selections)
+    uint32_t *epoch = nullptr, *bar_epoch = nullptr;
     int32_t *tickets = nullptr, *err = nullptr, *sel = nullptr;
-    float *w = nullptr, *out = nullptr;
 };
 
 struct inzg_ctx {
@@ -1008,7 +1007,7 @@ void ep_bind(EpState *ep, int d, uint8_t *b) {
     ep->P.rsel[d] = reinterpret_cast<int32_t *>(b + ep->o_rsel);
     ep->P.rw[d] = reinterpret_cast<float *>(b + ep->o_rw);
     ep->P.rx[d] = reinterpret_cast<float *>(b + ep->o_rx);
-    ep->P.slot[d] = reinterpret_cast<float *>(b + ep->o_slot);
+    ep->P.out[d] = reinterpret_cast<float *>(b + ep->o_out);
     ep->P.flags[d] = reinterpret_cast<uint32_t *>(b + ep->o_flags);
 }
 
@@ -1033,10 +1032,10 @@ inzg_status inzg_ep_attach(inzg_ctx *c, int rank, int world, int capacity, void 
     ep->o_rsel = o; o = align_up(o + G * C * K * 4, 256);
     ep->o_rw = o; o = align_up(o + G * C * K * 4, 256);
     ep->o_rx = o; o = align_up(o + G * C * H * 4, 256);
-    ep->o_slot = o; o = align_up(o + C * K * H * 4, 256);
-    ep->o_flags = o; o = align_up(o + 2 * G * 4, 256);
+    ep->o_out = o; o = align_up(o + G * C * K * H * 4, 256);
+    ep->o_flags = o; o = align_up(o + 3 * G * 4, 256);
     ep->bytes = o;
-    const size_t lb = 256 + align_up(C * K * 4, 256) * 2 + G * C * K * H * 4;
+    const size_t lb = 256 + align_up(C * K * 4, 256);
     cudaError_t e = cudaMalloc(&ep->base, ep->bytes);
     if (e == cudaSuccess) e = cudaMemset(ep->base, 0, ep->bytes);
     if (e == cudaSuccess) e = cudaMemset(ep->base + ep->o_rsel, 0xFF, G * C * K * 4);  // no slot owned yet
@@ -1053,9 +1052,8 @@ inzg_status inzg_ep_attach(inzg_ctx *c, int rank, int world, int capacity, void 
     ep->epoch = reinterpret_cast<uint32_t *>(ep->local);
     ep->tickets = reinterpret_cast<int32_t *>(ep->local + 16);
     ep->err = reinterpret_cast<int32_t *>(ep->local + 32);
+    ep->bar_epoch = reinterpret_cast<uint32_t *>(ep->local + 48);
     ep->sel = reinterpret_cast<int32_t *>(ep->local + 256);
-    ep->w = reinterpret_cast<float *>(ep->local + 256 + align_up(C * K * 4, 256));
-    ep->out = reinterpret_cast<float *>(ep->local + 256 + 2 * align_up(C * K * 4, 256));
     ep->P.rank = rank;
     ep->P.world = world;
     ep->P.cap = capacity;
@@ -1134,6 +1132,17 @@ inzg_status inzg_ep_connect_local(inzg_ctx *const *ctxs, int world) {
     return INZG_OK;
 }
 
+inzg_status inzg_ep_barrier(inzg_ctx *c, void *stream) {
+    if (!c) return INZG_BAD_ARG;
+    EpState *ep = c->ep;
+    if (!ep || !ep->connected) return fail(c, INZG_NOT_READY, "ep_barrier: attach and connect first");
+    cudaSetDevice(c->cfg.device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    launch_ep_barrier(ep->P, ep->bar_epoch, ep->err, st);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? INZG_OK : cuda_fail(c, e, "ep_barrier: kernel launch");
+}
+
 inzg_status inzg_ep_detach(inzg_ctx *c) {
     if (!c) return INZG_BAD_ARG;
     if (!c->ep) return INZG_OK;
@@ -1151,7 +1160,7 @@ static int enqueue_ep(inzg_ctx *c, int layer, int n, const float *x, const float
     const inzg_config &cf = c->cfg;
     EpState *ep = c->ep;
     LayerSlot &L = c->layers[layer];
-    const int H = cf.hidden, E = cf.n_expert, K = cf.topk;
+    const int H = cf.hidden, E = cf.n_expert;
     int launches = 0;
     bool bad = false;
     auto add = [&](int r) {
@@ -1159,15 +1168,15 @@ static int enqueue_ep(inzg_ctx *c, int layer, int n, const float *x, const float
         else launches += r;
     };
     add(launch_router_logits(L.router, L.router32, x, n, H, E, bias, c->logits, c->meta, st));
-    add(launch_ep_dispatch(c->logits, x, n, E, ep->P, ep->epoch, ep->tickets, st));
+    add(launch_ep_dispatch(c->logits, x, n, E, ep->P, ep->sel, ep->epoch, ep->tickets, st));
     add(launch_ep_wait(ep->P.flags[ep->rank], ep->world, 0, ep->epoch, false, ep->err, st));
     const int r = enqueue_experts(c, L, ep->world * ep->cap, ep->P.rx[ep->rank], ep->P.rsel[ep->rank],
-                                  ep->P.rw[ep->rank], n_batch, ep->out, st);
+                                  ep->P.rw[ep->rank], n_batch, ep->P.out[ep->rank], st);
     if (r == -2) return -2;
     add(r);
-    add(launch_ep_return(ep->out, ep->P, ep->epoch, ep->tickets + 1, c->num_sms, st));
+    add(launch_ep_signal(ep->P, ep->epoch, st));
     add(launch_ep_wait(ep->P.flags[ep->rank], ep->world, 1, ep->epoch, true, ep->err, st));
-    add(launch_combine(ep->P.slot[ep->rank], n, H, K, y, c->num_sms, st));
+    add(launch_ep_combine(ep->sel, n, ep->P, y, c->num_sms, st));
     if (c->shared[layer].has_experts) {
         const int rs = enqueue_shared(c, layer, n, x, y, n_batch, false, st);
         if (rs == -2) return -2;

@@ -55,8 +55,8 @@ struct EpPeers {
     int32_t *rsel[kEpMaxRanks];  // [world][cap][topk] local expert of each received slot, -1 if not owned there
     float *rw[kEpMaxRanks];      // [world][cap][topk] routing weights
     float *rx[kEpMaxRanks];      // [world][cap][hidden] received rows
-    float *slot[kEpMaxRanks];    // [cap][topk][hidden] the rank's own tokens' slot outputs
-    uint32_t *flags[kEpMaxRanks];  // [2][world] dispatch / return epochs written by each peer
+    float *out[kEpMaxRanks];     // [world * cap][topk][hidden] the rank's expert outputs for every row it received
+    uint32_t *flags[kEpMaxRanks];  // [3][world] dispatch / outputs-ready / rendezvous epochs written by each peer
 };
 
 // Routing products of one forward call (device).

@@ -68,11 +68,13 @@ void launch_pool_repack(const uint8_t *blobs, uint64_t blob_bytes, uint64_t gu_b
                         const LayerDev &L, uint8_t *pool, uint8_t *luts, cudaStream_t st);
 
 // Expert-parallel exchange over peer memory (k_ep.cu). epoch_dev: the rank's step counter; tickets: one int per kernel.
-// route + dispatch from the router logits [n][E] (softmax and top-k per token inside)
-int launch_ep_dispatch(const float *logits, const float *x, int n, int E, const EpPeers &P, const uint32_t *epoch_dev,
-                       int32_t *ticket, cudaStream_t st);
-int launch_ep_return(const float *out, const EpPeers &P, const uint32_t *epoch_dev, int32_t *ticket, int num_sms,
-                     cudaStream_t st);
+// route + dispatch from the router logits [n][E] (softmax and top-k per token inside; sel_out [n][topk] kept for the
+// combine)
+int launch_ep_dispatch(const float *logits, const float *x, int n, int E, const EpPeers &P, int32_t *sel_out,
+                       const uint32_t *epoch_dev, int32_t *ticket, cudaStream_t st);
+int launch_ep_signal(const EpPeers &P, const uint32_t *epoch_dev, cudaStream_t st);
+int launch_ep_barrier(const EpPeers &P, uint32_t *bar_epoch, int32_t *err, cudaStream_t st);
+int launch_ep_combine(const int32_t *sel, int n, const EpPeers &P, float *y, int num_sms, cudaStream_t st);
 int launch_ep_wait(const uint32_t *flags, int world, int which, uint32_t *epoch_dev, bool advance, int32_t *err,
                    cudaStream_t st);
 

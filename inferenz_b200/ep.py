@@ -213,6 +213,11 @@ class PeerExchangeMoE:
                                     None if bias is None else bias.data_ptr(), stream_handle(s))
         return y
 
+    def barrier(self, stream=None):
+        """Device-side rendezvous of all ranks on ``stream`` (outside any step)."""
+        s = stream if stream is not None else torch.cuda.current_stream(self.pool.device)
+        self.pool.ep_barrier(stream_handle(s))
+
     def close(self):
         self.pool.ep_detach()
 

@@ -117,6 +117,9 @@ class MoePool:
         self._check(lib.inzg_ep_forward(self._ctx, layer, n, ctypes.c_void_p(x_ptr), bias_ptr and ctypes.c_void_p(bias_ptr),
                                         ctypes.c_void_p(y_ptr), n_batch, stream and ctypes.c_void_p(stream)), "ep_forward")
 
+    def ep_barrier(self, stream=None):
+        self._check(lib.inzg_ep_barrier(self._ctx, stream and ctypes.c_void_p(stream)), "ep_barrier")
+
     def ep_detach(self):
         self._check(lib.inzg_ep_detach(self._ctx), "ep_detach")
 

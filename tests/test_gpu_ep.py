@@ -164,6 +164,8 @@ def _peer_worker(rank, world, port, n_total, steps, q, absent_rank=-1):
             ys = []
             if rank != absent_rank:
                 for _ in range(steps):
+                    if absent_rank < 0:
+                        ep.barrier()  # device-side rendezvous between steps
                     ys.append(ep.moe_block(0, x, bias=bd, n_batch=n_total).clone())
                 torch.cuda.synchronize(dev)
                 try:
