@@ -556,6 +556,121 @@ def run_ep(args):
     dist.destroy_process_group()
 
 
+STACK_WORKLOAD = ("BASELINE configs[4]: stack of 48 MoE layers (random Q4L experts and F16 router per layer, d=2048, "
+                  "512 experts, top-10, FF 640), 16384 tokens N(0,1) RMS-normalised per step, expert parallel over N GPUs")
+
+
+def run_stack(args):
+    """--stack: BASELINE configs[4]. Every rank draws and encodes its experts of each layer on its GPU (512/N per layer)
+    and loads them without a host round trip; one step is the 48 layers on the batch's 16384 tokens (each layer on the
+    same input: the benchmark measures the layer, not a model), on one GPU through inzg_moe_forward, on N GPUs through
+    inzg_ep_forward with 16384/N tokens per rank. The pool (about 3.1 GB per layer on one GPU with the prefill copy)
+    exceeds the L2 by far, so no flush is needed between steps."""
+    import datetime
+
+    import torch
+
+    from inferenz_b200 import MoePool, synth
+    from inferenz_b200.ep import PeerExchangeMoE
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    dev = torch.device("cuda", local)
+    hbm, _, peak_kind = peaks()
+    i8_peak = probe_i8(local)
+    layers, n_total = args.stack_layers, args.stack_tokens
+    n_loc = n_total // world
+    e0, nl = rank * E // world, E // world
+    bb = synth.blob_bytes(synth.T_Q4L, H, FF)
+    t0 = time.time()
+    pool = MoePool(H, FF, E, K, max_tokens=n_total, n_layers=layers, device=local)
+    buf = torch.empty(nl * bb, dtype=torch.uint8, device=dev)
+    for l in range(layers):
+        synth.layer_blobs_device(l, synth.T_Q4L, H, FF, e0, e0 + nl, buf.data_ptr())
+        pool.add_layer_device(l, synth.T_Q4L, buf.data_ptr(), bb, e0, nl)
+        pool.set_router(l, synth.router(l, E, H))
+    del buf
+    setup_s = time.time() - t0
+    x_all = synth.hidden(n_total, H)
+    xd = torch.from_numpy(x_all[rank * n_loc:(rank + 1) * n_loc].copy()).to(dev)
+    yd = torch.empty_like(xd)
+    stream = torch.cuda.Stream(dev)
+    ep = PeerExchangeMoE(pool, capacity=n_loc) if world > 1 else None
+
+    def step():
+        for l in range(layers):
+            if ep is None:
+                pool.moe_block_device(l, n_loc, xd.data_ptr(), yd.data_ptr(), stream=stream.cuda_stream)
+            else:
+                ep.moe_block(l, xd, n_batch=n_total, y=yd, stream=stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            if ep is not None:
+                ep.barrier(stream)
+            step()
+        stream.synchronize()
+        pool.device_status(stream.cuda_stream)
+        if dist is not None:
+            dist.barrier()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        with Clocks(local) as ck:
+            for a, b in evs:
+                if ep is not None:
+                    ep.barrier(stream)
+                a.record(stream)
+                step()
+                b.record(stream)
+            stream.synchronize()
+        pool.device_status(stream.cuda_stream)
+    my_ms = sum(a.elapsed_time(b) for a, b in evs)
+    total_ms = my_ms
+    if dist is not None:
+        every = [torch.zeros(1, dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(every, torch.tensor([my_ms], dtype=torch.float64))
+        total_ms = max(float(t.item()) for t in every)
+    ms_step = total_ms / args.steps
+    # every expert of every layer is routed at 16384 tokens: the whole router and pool per layer, over all ranks
+    bytes_step = layers * (ROUTER_BYTES * world + E * EXPERT_BYTES_Q4L + 2 * n_total * H * 4)
+    ops_step = layers * n_total * (2 * E * H + K * 2 * (2 * FF * H + H * FF))
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(n_total * args.steps / (total_ms * 1e-3), 1), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8 x Q4L (fp32 accumulate)", "data": "synthetic (seeded; no dataset)",
+            "config": {"workload": STACK_WORKLOAD, "layers": layers, "global_batch": n_total, "seq_len": 1},
+            "arm": {"parallelism": "single GPU" if world == 1 else f"ep{world}: 512/N experts per GPU, in-library "
+                                                                   "exchange over peer memory",
+                    "l2": "inputs larger than L2 (the pool)"},
+            "roofline": {"bound": "hbm", "kernel": "whole stack step, all GPUs", "algorithmic_bytes": bytes_step,
+                         "achieved": round(bytes_step / (ms_step * 1e-3) / 1e9, 1), "peak": hbm * world,
+                         "unit": "GB/s", "frac": round(bytes_step / (ms_step * 1e-3) / 1e9 / (hbm * world), 4),
+                         "peak_kind": peak_kind + " (MEASURED_PEAKS.json hbm_gbs) x GPUs", "traffic": None},
+            "tensor_roofline": {"ops": ops_step, "achieved_tops": round(ops_step / (ms_step * 1e-3) / 1e12, 1),
+                                "peak_tops": round(i8_peak * world, 1) if i8_peak else None,
+                                "frac": round(ops_step / (ms_step * 1e-3) / 1e12 / (i8_peak * world), 4) if i8_peak
+                                else None},
+            "clocks": ck.summary(), "gpu_launches": pool.stats()["last_launches"] * layers * args.steps,
+            "detail": {"setup_s_rank0": round(setup_s, 1), "pool_bytes_rank0": pool.stats()["pool_bytes"]},
+        }
+        print(json.dumps(line))
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    if ep is not None:
+        ep.close()
+    pool.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 def oracle_inputs(cfg, n):
     """The same workload inputs as make_inputs, drawn by the oracle's generator (no product library)"""
     import oracle
@@ -637,11 +752,16 @@ def main():
                     help="time a single workload (profiling runs); the JSON line then reports that workload")
     ap.add_argument("--prefill-tokens", type=int, default=4096,
                     help="tokens of the prefill workload (smaller only for profiler captures; parity is then skipped)")
+    ap.add_argument("--stack", action="store_true", help="BASELINE configs[4]: the 48-layer stack, 16384 tokens")
+    ap.add_argument("--stack-layers", type=int, default=48)
+    ap.add_argument("--stack-tokens", type=int, default=16384)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.stack:
+        run_stack(args)
     elif int(os.environ.get("WORLD_SIZE", "1")) > 1:
         run_ep(args)
     else:

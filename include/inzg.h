@@ -188,6 +188,11 @@ INZG_EXPORT inzg_status inzg_route_topk_noalloc(inzg_ctx *ctx, int layer, int n,
 INZG_EXPORT inzg_status inzg_pool_add_layer_range(inzg_ctx *ctx, int layer, int expert_type, const void *blobs,
                                                   uint64_t blob_bytes, int e_first, int n_local);
 
+/* The same from blobs already in this context's device memory (e.g. encoded there by inzg_synth_layer_blobs_device):
+ * the headers are checked after a small copy to the host, the blobs re-laid out on the device without a host trip. */
+INZG_EXPORT inzg_status inzg_pool_add_layer_device(inzg_ctx *ctx, int layer, int expert_type, const void *blobs_dev,
+                                                   uint64_t blob_bytes, int e_first, int n_local);
+
 /* Router, softmax and top-k of n tokens (the routing stage of inzg_moe_forward): sel_dev [n][topk] (expert ids),
  * w_dev [n][topk] (renormalised weights). logit_bias_dev: the test hook, optional. */
 INZG_EXPORT inzg_status inzg_route(inzg_ctx *ctx, int layer, int n, const float *x_dev, const float *logit_bias_dev,

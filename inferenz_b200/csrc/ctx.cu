@@ -407,7 +407,7 @@ inzg_status inzg_pool_add_layer(inzg_ctx *c, int layer, int type, const void *bl
 // Validate, upload and re-lay out experts [e_first, e_first + n_local) into slot L (a layer's routed pool, or a
 // layer's shared expert as a one-expert pool).
 static inzg_status load_pool(inzg_ctx *c, LayerSlot &L, int type, const void *blobs, uint64_t blob_bytes, int e_first,
-                             int n_local) {
+                             int n_local, bool dev_src = false) {
     const inzg_config &cf = c->cfg;
     if (e_first < 0 || n_local < 1 || e_first + n_local > cf.n_expert)
         return fail(c, INZG_BAD_ARG, "pool_add_layer: expert range outside the layer's experts");
@@ -418,13 +418,29 @@ static inzg_status load_pool(inzg_ctx *c, LayerSlot &L, int type, const void *bl
     if (blob_bytes < gu_bytes + dn_bytes) return fail(c, INZG_BAD_ARG, "pool_add_layer: blob smaller than its matrices");
     // validate every blob the way q_bind_lin does (src/model_fwd.c:87-96, 853-855): magic, type, rows, cols
     const uint8_t *b = static_cast<const uint8_t *>(blobs);
+    std::vector<QHeader> dev_hdr;  // device blobs: their two headers copied to the host first
+    if (dev_src) {
+        cudaSetDevice(cf.device);
+        dev_hdr.resize((size_t)2 * E);
+        if (cudaMemcpy2D(dev_hdr.data(), 2 * sizeof(QHeader), b, blob_bytes, 64, E, cudaMemcpyDeviceToHost) !=
+                cudaSuccess ||
+            cudaMemcpy2D(dev_hdr.data() + 1, 2 * sizeof(QHeader), b + gu_bytes, blob_bytes, 64, E,
+                         cudaMemcpyDeviceToHost) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(c, INZG_BAD_ARG, "pool_add_layer_device: blobs are not readable device memory");
+        }
+    }
+    auto header = [&](int e, bool down, QHeader &h) {
+        if (dev_src) h = dev_hdr[(size_t)2 * e + (down ? 1 : 0)];
+        else memcpy(&h, b + (size_t)e * blob_bytes + (down ? gu_bytes : 0), 64);
+    };
     QHeader h0g, h0d;
-    memcpy(&h0g, b, 64);
-    memcpy(&h0d, b + gu_bytes, 64);
+    header(0, false, h0g);
+    header(0, true, h0d);
     for (int e = 0; e < E; e++) {
         QHeader hg, hd;
-        memcpy(&hg, b + (size_t)e * blob_bytes, 64);
-        memcpy(&hd, b + (size_t)e * blob_bytes + gu_bytes, 64);
+        header(e, false, hg);
+        header(e, true, hd);
         if (hg.magic != kMagic || hd.magic != kMagic || hg.type != type || hd.type != type || hg.rows != (uint32_t)(2 * FF) ||
             hg.cols != (uint32_t)H || hd.rows != (uint32_t)H || hd.cols != (uint32_t)FF) {
             char msg[128];
@@ -485,23 +501,26 @@ static inzg_status load_pool(inzg_ctx *c, LayerSlot &L, int type, const void *bl
     }
     cudaMemsetAsync(L.pool, 0, D.slab_bytes * E, c->stream);  // scale padding past ng stays zero
     // stage blobs through a device buffer in chunks of experts and re-lay them out on the device
+    // device blobs: re-laid out in place of the source; host blobs: staged through a device buffer in chunks
     const int chunk = std::min(E, 32);
     uint8_t *stage = nullptr;
-    if (cudaMalloc(&stage, blob_bytes * chunk) != cudaSuccess) {
+    if (!dev_src && cudaMalloc(&stage, blob_bytes * chunk) != cudaSuccess) {
         cudaGetLastError();
         return fail(c, INZG_OOM, "pool_add_layer: staging buffer");
     }
     cudaError_t err = cudaSuccess;
     for (int e0 = 0; e0 < E && err == cudaSuccess; e0 += chunk) {
         const int ne = std::min(chunk, E - e0);
-        err = cudaMemcpyAsync(stage, b + (size_t)e0 * blob_bytes, blob_bytes * ne, cudaMemcpyHostToDevice, c->stream);
+        const uint8_t *src = dev_src ? b + (size_t)e0 * blob_bytes : stage;
+        if (!dev_src)
+            err = cudaMemcpyAsync(stage, b + (size_t)e0 * blob_bytes, blob_bytes * ne, cudaMemcpyHostToDevice, c->stream);
         if (err == cudaSuccess) {
-            launch_pool_repack(stage, blob_bytes, gu_bytes, e0, ne, D, L.pool, L.luts, c->stream);
-            launch_pool_requant(stage, blob_bytes, gu_bytes, e0, ne, D, c->stream);
+            launch_pool_repack(src, blob_bytes, gu_bytes, e0, ne, D, L.pool, L.luts, c->stream);
+            launch_pool_requant(src, blob_bytes, gu_bytes, e0, ne, D, c->stream);
         }
         if (err == cudaSuccess) err = cudaStreamSynchronize(c->stream);
     }
-    cudaFree(stage);
+    if (stage) cudaFree(stage);
     if (err != cudaSuccess) return cuda_fail(c, err, "pool_add_layer");
     L.has_maps = make_tma_map_i8(L.map_gu.bytes, D.w8_gu, (uint64_t)E * 2 * FF, H, 128) &&
                  make_tma_map_i8(L.map_dn.bytes, D.w8_dn, (uint64_t)E * H, FF, 128) &&
@@ -522,6 +541,14 @@ inzg_status inzg_pool_add_layer_range(inzg_ctx *c, int layer, int type, const vo
     if (!c) return INZG_BAD_ARG;
     if (layer < 0 || layer >= c->cfg.n_layers || !blobs) return fail(c, INZG_BAD_ARG, "pool_add_layer: bad layer or pointer");
     return load_pool(c, c->layers[layer], type, blobs, blob_bytes, e_first, n_local);
+}
+
+inzg_status inzg_pool_add_layer_device(inzg_ctx *c, int layer, int type, const void *blobs_dev, uint64_t blob_bytes,
+                                       int e_first, int n_local) {
+    if (!c) return INZG_BAD_ARG;
+    if (layer < 0 || layer >= c->cfg.n_layers || !blobs_dev)
+        return fail(c, INZG_BAD_ARG, "pool_add_layer_device: bad layer or pointer");
+    return load_pool(c, c->layers[layer], type, blobs_dev, blob_bytes, e_first, n_local, true);
 }
 
 inzg_status inzg_set_shared(inzg_ctx *c, int layer, int type, const void *blob, uint64_t blob_bytes, const float *gate) {

@@ -512,7 +512,8 @@ struct DevBuf {
     }
 };
 
-constexpr int kExpertBatch = 16;  // experts per device batch of the layer generators
+constexpr int kExpertBatch = 16;   // experts per device batch of the host-drawn layer generators
+constexpr int kDeviceBatch = 128;  // experts per batch when drawn on the device too (one level-learning CTA each)
 
 }  // namespace
 
@@ -591,7 +592,7 @@ INZG_API int inzg_synth_layer_blobs_device(uint64_t seed, int type, int H, int F
     if (e1 <= e0 || e0 < 0 || !blobs_dev || (type != INZG_T_Q4L && type != INZG_T_Q8G) || H % kGroup || FF % kGroup)
         return -1;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const int nb = std::min(kExpertBatch, e1 - e0);
+    const int nb = std::min(kDeviceBatch, e1 - e0);
     const size_t per = (size_t)3 * FF * H;
     DevBuf wbuf, scratch;
     if (!wbuf.alloc(sizeof(float) * per * nb) || !scratch.alloc(sizeof(float) * encode_scratch_floats(nb, H, FF)))

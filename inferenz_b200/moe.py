@@ -75,6 +75,11 @@ class MoePool:
         self._check(lib.inzg_pool_add_layer_range(self._ctx, layer, expert_type, _ptr(b), blob_bytes, e_first, n_local),
                     "pool_add_layer_range")
 
+    def add_layer_device(self, layer, expert_type, blobs_ptr, blob_bytes, e_first, n_local):
+        """Experts [e_first, e_first + n_local) from blobs already in this pool's device memory (a device pointer)."""
+        self._check(lib.inzg_pool_add_layer_device(self._ctx, layer, expert_type, ctypes.c_void_p(blobs_ptr), blob_bytes,
+                                                   e_first, n_local), "pool_add_layer_device")
+
     def set_shared(self, layer, expert_type, blob, blob_bytes, gate):
         """The layer's shared expert: blob = gate|up then down (one expert blob's layout), gate [H] float32."""
         b = np.ascontiguousarray(blob, dtype=np.uint8)

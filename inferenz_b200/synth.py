@@ -91,5 +91,13 @@ def layer_blobs_range(layer, expert_type, H, FF, e0, e1):
     return out, bb
 
 
+def layer_blobs_device(layer, expert_type, H, FF, e0, e1, blobs_ptr, stream=None):
+    """Experts [e0, e1) of a synthetic layer drawn and encoded on the current GPU into device memory at blobs_ptr
+    ([(e1 - e0) * blob_bytes] bytes): the same stream as layer_blobs up to CUDA's double log/cos/sqrt in Box-Muller."""
+    if lib.inzg_synth_layer_blobs_device(layer, expert_type, H, FF, e0, e1, ctypes.c_void_p(blobs_ptr),
+                                         stream and ctypes.c_void_p(stream)) != 0:
+        raise RuntimeError("inzg_synth_layer_blobs_device failed")
+
+
 __all__ = ["router", "hidden", "normal_bias", "zipf_bias", "normal_logits", "layer_blobs", "layer_blobs_range",
-           "blob_bytes", "expert_fp32", "T_Q4L", "T_Q8G"]
+           "layer_blobs_device", "blob_bytes", "expert_fp32", "T_Q4L", "T_Q8G"]
