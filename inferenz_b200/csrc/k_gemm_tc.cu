@@ -12,8 +12,9 @@
 // the next item's loads and MMAs overlap the previous item's epilogue.
 //   warp 0      TMA producer: A (weights, [E*rows][K] int8) and B (tokens, [entries][K] int8) boxes of 128 x 128 bytes,
 //               128-byte swizzle, into a 4-stage ring (no multicast)
-//   warp 1      allocates 256 TMEM columns once (two 128-column int32 accumulators), one lane issues 4 MMAs (K = 32)
-//               per half; tcgen05.commit frees the smem stage and, after a block's 8 MMAs, hands the accumulator over
+//   warp 1      allocates all 512 TMEM columns once (four 128-column int32 accumulators, so the MMAs can run up to
+//               three 256-blocks ahead of the epilogue's per-block fold), one lane issues 4 MMAs (K = 32) per half;
+//               tcgen05.commit frees the smem stage and, after a block's 8 MMAs, hands the accumulator over
 //   warps 2-9   epilogue: thread = (weight row = TMEM lane, half of the tile's tokens); per block tcgen05.ld of its 64
 //               int32 dots, the per-block FMA into 64 fp32 registers (packed f32x2 add / mul / fma, two tokens per
 //               instruction), then the accumulator is refilled and released; at the item's end its outputs are
@@ -38,10 +39,12 @@ constexpr int kEpiWarps = 8, kEpiThreads = kEpiWarps * 32, kHalfN = TBN / 2;  //
 constexpr int kThreads = 64 + kEpiThreads;
 constexpr int kMagicI = 0x4B400000;  // 1.5 * 2^23 as a float: kMagicI + x reads as 12582912 + x for |x| < 2^22
 constexpr int kStageBytes = (TBM + TBN) * TBK;  // 32 KiB
+// more than half of an SM's shared memory per CTA, so a CTA is alone on its SM with all 512 TMEM columns
+static_assert(TSTAGES * kStageBytes > 116 * 1024, "one gemm_tc CTA per SM");
 constexpr int kMaxKB = 10;                      // 256-blocks of K: up to 2560, the reference model's width
 
 struct TcShared {
-    uint64_t full[TSTAGES], empty[TSTAGES], acc_full[2], acc_empty[2], drain;
+    uint64_t full[TSTAGES], empty[TSTAGES], acc_full[4], acc_empty[4], drain;
     uint64_t xs_full[2];               // every epilogue thread has written the item's xs / oslot / ow [parity]
     uint64_t xs_empty[2];              // every epilogue thread has finished the item that used buffer [parity]
     uint32_t tmem_base;
@@ -117,7 +120,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
             mbar_init(&S.full[s], 1);
             mbar_init(&S.empty[s], 1);
         }
-        for (int b = 0; b < 2; b++) {
+        for (int b = 0; b < 4; b++) {
             mbar_init(&S.acc_full[b], 1);
             mbar_init(&S.acc_empty[b], kEpiThreads);
         }
@@ -131,7 +134,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(&S.tmem_base)));
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&S.tmem_base)));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -140,7 +143,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     const uint32_t tmem = S.tmem_base;
     if (warp >= 2) {  // both accumulators start at the bits of 1.5 * 2^23 (the epilogue's int -> float step)
         const uint32_t q = tmem + ((uint32_t)((warp & 3) * 32) << 16) + ((warp - 2) >> 2) * kHalfN;
-        for (int b = 0; b < 2; b++)
+        for (int b = 0; b < 4; b++)
             for (int c = 0; c < kHalfN; c += 32) tmem_fill32(q + b * TBN + c, kMagicI);
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     }
@@ -181,9 +184,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
             int kg = 0, bg = 0;  // stages consumed, blocks accumulated by this CTA
             for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
                 for (int kh = 0; kh < nkh; kh++, kg++) {
-                    const int s = kg % TSTAGES, buf = bg & 1;
+                    const int s = kg % TSTAGES, buf = bg & 3;
                     const bool first_half = (kh & 1) == 0;
-                    if (first_half && bg >= 2 && !mbar_wait(&S.acc_empty[buf], ((bg / 2) - 1) & 1, abort)) { ok = false; break; }
+                    if (first_half && bg >= 4 && !mbar_wait(&S.acc_empty[buf], ((bg / 4) - 1) & 1, abort)) { ok = false; break; }
                     if (!mbar_wait(&S.full[s], (kg / TSTAGES) & 1, abort)) { ok = false; break; }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const uint8_t *stage = ring + s * kStageBytes;
@@ -281,9 +284,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
             for (int j = 0; j < kHalfN / 2; j++) f[j] = make_float2(0.0f, 0.0f);
             const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
             for (int b = 0; b < nkb; b++, bg++) {
-                const int buf = bg & 1;
+                const int buf = bg & 3;
                 const float wsb = __ldg(wsr + b);  // in flight while the block's MMAs finish
-                if (!mbar_wait(&S.acc_full[buf], (bg / 2) & 1, abort)) {
+                if (!mbar_wait(&S.acc_full[buf], (bg / 4) & 1, abort)) {
                     ok = false;
                     S.abort = 1;
                     break;
@@ -341,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     if (S.abort && threadIdx.x == 0) atomicCAS(&R.meta[kMetaError], 0, kErrTimeout);
     if (warp == 1) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
     }
 }
 
