@@ -2,7 +2,8 @@
 
 The tensor-core GEMM and the CUDA-core int8 GEMM compute the same exact int32 block dots and the reference's
 per-256-block FMA sequence, so their layer outputs must be identical bit for bit; both must match the CPU oracle
-within the north-star tolerance. Token counts span several 128-token tiles and a partial tile.
+within the north-star tolerance. Token counts span several 128-token tiles and a partial tile (calls above 256 rows: smaller ones run the same
+numerics as GEMM items inside the decode GEMV, tested below).
 """
 import numpy as np
 import pytest
@@ -17,9 +18,9 @@ H, FF, E, K = 2048, 640, 512, 10
 
 @pytest.mark.parametrize("expert_type", [synth.T_Q4L, synth.T_Q8G])
 def test_tcgen05_gemm_equals_simt_gemm_and_oracle(orc, expert_type):
-    n = 160
+    n = 300  # above 256 rows: the prefill-numerics experts take the tcgen05 GEMM (smaller calls run them as GEMM items)
     ov = synth.normal_logits(n, E, seed=41)
-    ov[:, :4] += 9.0          # experts 0-3 take nearly every token: 160 tokens = one full and one partial tile
+    ov[:, :4] += 9.0          # experts 0-3 take nearly every token: 300 tokens = two full tiles and a partial one
     ov[:40, 100:104] += 12.0  # experts 100-103 get 40 tokens: one partial tile
     R = synth.router(0, E, H)
     x = synth.hidden(n, H, seed=42)
