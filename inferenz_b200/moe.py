@@ -118,6 +118,15 @@ class MoePool:
         buf = ctypes.create_string_buffer(b"".join(handles), EP_HANDLE_BYTES * len(handles))
         self._check(lib.inzg_ep_connect(self._ctx, buf), "ep_connect")
 
+    @staticmethod
+    def ep_connect_local(pools):
+        """Connects the exchange of pools living in this process (one per GPU, each attached, in rank order) through
+        peer access between their devices."""
+        arr = (ctypes.c_void_p * len(pools))(*[p._ctx for p in pools])
+        st = lib.inzg_ep_connect_local(arr, len(pools))
+        if st != 0:
+            pools[0]._check(st, "ep_connect_local")
+
     def ep_forward_device(self, layer, n, x_ptr, y_ptr, n_batch, bias_ptr=None, stream=None):
         self._check(lib.inzg_ep_forward(self._ctx, layer, n, ctypes.c_void_p(x_ptr), bias_ptr and ctypes.c_void_p(bias_ptr),
                                         ctypes.c_void_p(y_ptr), n_batch, stream and ctypes.c_void_p(stream)), "ep_forward")
