@@ -214,6 +214,35 @@ INZG_EXPORT inzg_status inzg_combine(inzg_ctx *ctx, int n, const float *slots_de
 INZG_EXPORT inzg_status inzg_shared_expert(inzg_ctx *ctx, int layer, int n, const float *x_dev, float *y_dev,
                                            int n_batch, void *stream);
 
+/* ---- Hyper-connections around the layer: the steps either side of moe_block in q_forward (src/model_fwd.c:1264-1267).
+ * The residual X [n][4*hidden] holds four streams of `hidden` floats per token. */
+#define INZG_HC_RANK 320  /* Q_HC_RANK, src/model.h:14 */
+
+/* The hyper-connection weights of `layer` (the reference's hcw L->mhc, src/engine_internal.h:27-32, bound by
+ * src/engine.c:152-153): norm [4*hidden] fp32 (1 + w, folded), down [320][4*hidden] and up [4*hidden][320] as fp16
+ * bits (the converter's hc type, src/convert.c:148, 251-252), inject [4][4*hidden] fp32 or NULL (the final mixer has
+ * none). Host pointers, copied to the device. */
+INZG_EXPORT inzg_status inzg_set_hc(inzg_ctx *ctx, int layer, const float *norm, const uint16_t *down_f16,
+                                    const uint16_t *up_f16, const float *inject);
+
+/* hc_in (src/model_fwd.c:432-439), which makes the layer's input: X_dev [n][4*hidden] -> xin_dev [n][hidden] and
+ * inj_dev [n][4] (NULL: not computed). Device pointers, 16-byte aligned; stream NULL = the context's stream. The
+ * first call with more tokens than before allocates the step's scratch (call it once at full size before any stream
+ * capture). Bit-exact with the reference except the SiLU of the 320-wide bottleneck and the inject sigmoid, whose
+ * glibc expf is evaluated in double and rounded once (one ulp apart on ~1e-4 of inputs). */
+INZG_EXPORT inzg_status inzg_hc_in(inzg_ctx *ctx, int layer, int n, const float *X_dev, float *xin_dev, float *inj_dev,
+                                   void *stream);
+
+/* hc_out (src/model_fwd.c:442-450), which consumes the layer's output: X[t][s][:] += inj[t][s] * y[t][:] for the four
+ * streams s, one fma per element as in the reference build. Device pointers (X_dev and y_dev 16-byte aligned). */
+INZG_EXPORT inzg_status inzg_hc_out(inzg_ctx *ctx, int n, float *X_dev, const float *inj_dev, const float *y_dev,
+                                    void *stream);
+
+/* q_forward's MoE step for one layer (src/model_fwd.c:1264-1267) on the device: hc_in with the layer's weights,
+ * inzg_moe_forward (INZG_IO_DEVICE implied; INZG_DUMP_ROUTE and INZG_PROFILE refused), hc_out; X_dev [n][4*hidden]
+ * is updated in place. */
+INZG_EXPORT inzg_status inzg_moe_block_hc(inzg_ctx *ctx, int layer, int n, float *X_dev, const inzg_moe_opts *opt);
+
 /* Waits for `stream` and reports the device-side checks of the calls since the last routing step
  * (INZG_TIMEOUT / INZG_DEVICE_CHECK), including a timed-out expert-parallel exchange. */
 INZG_EXPORT inzg_status inzg_device_status(inzg_ctx *ctx, void *stream);

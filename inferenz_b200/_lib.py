@@ -71,6 +71,10 @@ SIGNATURES = {
     "inzg_ep_detach": (I, [P]),
     "inzg_ep_barrier": (I, [P, P]),
     "inzg_pool_add_layer_device": (I, [P, I, I, P, U64, I, I]),
+    "inzg_set_hc": (I, [P, I, P, P, P, P]),
+    "inzg_hc_in": (I, [P, I, I, P, P, P, P]),
+    "inzg_hc_out": (I, [P, I, P, P, P, P]),
+    "inzg_moe_block_hc": (I, [P, I, I, P, ctypes.POINTER(MoeOpts)]),
     "inzg_gguf_open": (P, [ctypes.c_char_p, ctypes.POINTER(GgufInfo), ctypes.c_char_p, ctypes.c_size_t]),
     "inzg_gguf_get_info": (I, [P, ctypes.POINTER(GgufInfo)]),
     "inzg_gguf_experts": (I, [P, I, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(U64), ctypes.POINTER(U64)]),

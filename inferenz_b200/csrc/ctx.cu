@@ -52,6 +52,12 @@ struct LayerSlot {
     LayerDev dev{};
 };
 
+// hyper-connection weights of one layer (inzg_set_hc): one allocation, norm | inject | down32 | down | up
+struct HcSlot {
+    uint8_t *mem = nullptr;
+    HcDev dev{};
+};
+
 template <class T>
 T *dalloc(size_t count, bool &ok) {
     void *p = nullptr;
@@ -101,6 +107,9 @@ struct inzg_ctx {
     std::vector<LayerSlot> layers;
     std::vector<LayerSlot> shared;           // per layer: the shared expert as a one-expert pool (inzg_set_shared)
     std::vector<float *> sh_gate;            // per layer: the shared expert's gate vector [hidden]
+    std::vector<HcSlot> hc;                  // per layer: the hyper-connection weights around the MoE (inzg_set_hc)
+    float *hc_Xn = nullptr, *hc_d = nullptr, *hc_m = nullptr, *hc_inj = nullptr;  // hc_in scratch, hc_cap tokens
+    int hc_cap = 0;
     std::string err;
     inzg_stats stats{};
     // scratch
@@ -230,6 +239,7 @@ inzg_ctx *inzg_create(const inzg_config *cfg, inzg_status *status) {
     c->cfg = *cfg;
     c->layers.resize(cfg->n_layers);
     c->shared.resize(cfg->n_layers);
+    c->hc.resize(cfg->n_layers);
     c->sh_gate.assign(cfg->n_layers, nullptr);
     cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, cfg->device);
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
@@ -333,6 +343,10 @@ void inzg_destroy(inzg_ctx *c) {
         }
     for (float *g : c->sh_gate)
         if (g) cudaFree(g);
+    for (auto &h : c->hc)
+        if (h.mem) cudaFree(h.mem);
+    for (float *p : {c->hc_Xn, c->hc_d, c->hc_m, c->hc_inj})
+        if (p) cudaFree(p);
     drop_graphs(c);
     for (int i = 0; i <= INZG_N_STAGES; i++)
         if (c->ev[i]) cudaEventDestroy(c->ev[i]);
@@ -1343,6 +1357,135 @@ inzg_status inzg_get_stats(const inzg_ctx *c, inzg_stats *out) {
     if (!c || !out) return INZG_BAD_ARG;
     *out = c->stats;
     return INZG_OK;
+}
+
+// ---- hyper-connections around the layer (src/model_fwd.c:404-450, 1264-1267) ----
+
+inzg_status inzg_set_hc(inzg_ctx *c, int layer, const float *norm, const uint16_t *down, const uint16_t *up,
+                        const float *inject) {
+    if (!c) return INZG_BAD_ARG;
+    const inzg_config &cf = c->cfg;
+    if (layer < 0 || layer >= cf.n_layers || !norm || !down || !up) return fail(c, INZG_BAD_ARG, "set_hc: bad layer or pointer");
+    cudaSetDevice(cf.device);
+    const int W = 4 * cf.hidden, R = INZG_HC_RANK;
+    const size_t f16 = (size_t)R * W * 2;
+    const size_t o_inj = (size_t)W * 4, o_d32 = o_inj + (size_t)4 * W * 4, o_dn = o_d32 + (size_t)R * W * 4,
+                 o_up = o_dn + f16, total = o_up + f16;
+    HcSlot &h = c->hc[layer];
+    if (!h.mem && cudaMalloc(&h.mem, total) != cudaSuccess) {
+        cudaGetLastError();
+        h.mem = nullptr;
+        return fail(c, INZG_OOM, "set_hc: weight buffer");
+    }
+    uint16_t *tmp = nullptr;
+    if (cudaMalloc(&tmp, 2 * f16) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(c, INZG_OOM, "set_hc: staging buffer");
+    }
+    cudaStream_t st = c->stream;
+    cudaError_t e = cudaMemcpyAsync(h.mem, norm, (size_t)W * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess && inject) e = cudaMemcpyAsync(h.mem + o_inj, inject, (size_t)4 * W * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(tmp, down, f16, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(tmp + (size_t)R * W, up, f16, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) {
+        launch_router_repack(tmp, reinterpret_cast<uint4 *>(h.mem + o_dn), R, W, st);
+        launch_router_repack32(tmp, reinterpret_cast<float *>(h.mem + o_d32), R, W, st);
+        launch_router_repack(tmp + (size_t)R * W, reinterpret_cast<uint4 *>(h.mem + o_up), W, R, st);
+        e = cudaStreamSynchronize(st);
+    }
+    cudaFree(tmp);
+    if (e != cudaSuccess) return cuda_fail(c, e, "set_hc");
+    hc_set_attributes(cf.hidden);
+    HcDev &d = h.dev;
+    d.norm = reinterpret_cast<const float *>(h.mem);
+    d.inject = inject ? reinterpret_cast<const float *>(h.mem + o_inj) : nullptr;
+    d.down32 = router_gemm_fits(R, W) ? reinterpret_cast<const float *>(h.mem + o_d32) : nullptr;
+    d.down = reinterpret_cast<const uint4 *>(h.mem + o_dn);
+    d.up = reinterpret_cast<const uint4 *>(h.mem + o_up);
+    d.rank = R;
+    return INZG_OK;
+}
+
+// hc_in's scratch for n tokens (grown, never shrunk; allocated outside any stream capture by the first call that
+// needs it)
+static inzg_status hc_scratch(inzg_ctx *c, int n) {
+    if (n <= c->hc_cap) return INZG_OK;
+    for (float **p : {&c->hc_Xn, &c->hc_d, &c->hc_m, &c->hc_inj})
+        if (*p) {
+            cudaFree(*p);
+            *p = nullptr;
+        }
+    c->hc_cap = 0;
+    const size_t W = 4 * (size_t)c->cfg.hidden;
+    bool ok = true;
+    c->hc_Xn = dalloc<float>((size_t)n * W, ok);
+    c->hc_m = dalloc<float>((size_t)n * W, ok);
+    c->hc_d = dalloc<float>((size_t)n * INZG_HC_RANK, ok);
+    c->hc_inj = dalloc<float>((size_t)n * 4, ok);
+    if (!ok) return fail(c, INZG_OOM, "hc_in: scratch");
+    c->hc_cap = n;
+    return INZG_OK;
+}
+
+// validates and enqueues hc_in; inj_dev nullptr: the inject weights are not computed
+static inzg_status hc_in_enqueue(inzg_ctx *c, int layer, int n, const float *X_dev, float *xin_dev, float *inj_dev,
+                                 cudaStream_t st) {
+    const inzg_config &cf = c->cfg;
+    if ((reinterpret_cast<uintptr_t>(X_dev) | reinterpret_cast<uintptr_t>(xin_dev) | reinterpret_cast<uintptr_t>(inj_dev)) & 15)
+        return fail(c, INZG_BAD_ARG, "hc_in: pointers must be 16-byte aligned");
+    const HcSlot &h = c->hc[layer];
+    if (!h.mem) return fail(c, INZG_NOT_READY, "hc_in: layer has no hyper-connection weights (inzg_set_hc)");
+    if (launch_hc_in(h.dev, n, cf.hidden, X_dev, c->hc_Xn, c->hc_d, c->hc_m, xin_dev, inj_dev, c->meta, c->num_sms, st) < 0)
+        return fail(c, INZG_UNSUPPORTED, "hc_in: no kernel for this width");
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? INZG_OK : cuda_fail(c, e, "hc_in: kernel launch");
+}
+
+inzg_status inzg_hc_in(inzg_ctx *c, int layer, int n, const float *X_dev, float *xin_dev, float *inj_dev, void *stream) {
+    if (!c) return INZG_BAD_ARG;
+    const inzg_config &cf = c->cfg;
+    if (layer < 0 || layer >= cf.n_layers || n <= 0 || n > cf.max_tokens || !X_dev || !xin_dev)
+        return fail(c, INZG_BAD_ARG, "hc_in: bad layer, n or pointer");
+    cudaSetDevice(cf.device);
+    const inzg_status s = hc_scratch(c, n);
+    if (s != INZG_OK) return s;
+    return hc_in_enqueue(c, layer, n, X_dev, xin_dev, inj_dev, stream ? static_cast<cudaStream_t>(stream) : c->stream);
+}
+
+inzg_status inzg_hc_out(inzg_ctx *c, int n, float *X_dev, const float *inj_dev, const float *y_dev, void *stream) {
+    if (!c) return INZG_BAD_ARG;
+    const inzg_config &cf = c->cfg;
+    if (n <= 0 || n > cf.max_tokens || !X_dev || !inj_dev || !y_dev) return fail(c, INZG_BAD_ARG, "hc_out: bad n or pointer");
+    if ((reinterpret_cast<uintptr_t>(X_dev) | reinterpret_cast<uintptr_t>(y_dev)) & 15)
+        return fail(c, INZG_BAD_ARG, "hc_out: X and y must be 16-byte aligned");
+    cudaSetDevice(cf.device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    launch_hc_out(X_dev, inj_dev, y_dev, n, cf.hidden, c->num_sms, st);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? INZG_OK : cuda_fail(c, e, "hc_out: kernel launch");
+}
+
+inzg_status inzg_moe_block_hc(inzg_ctx *c, int layer, int n, float *X_dev, const inzg_moe_opts *opt) {
+    if (!c) return INZG_BAD_ARG;
+    const inzg_config &cf = c->cfg;
+    if (layer < 0 || layer >= cf.n_layers || n <= 0 || n > cf.max_tokens || !X_dev)
+        return fail(c, INZG_BAD_ARG, "moe_block_hc: bad layer, n or pointer");
+    if (opt && (opt->flags & (INZG_DUMP_ROUTE | INZG_PROFILE)))
+        return fail(c, INZG_BAD_ARG, "moe_block_hc: route dumps and profiling are for inzg_moe_forward");
+    if (c->hc[layer].mem && !c->hc[layer].dev.inject)
+        return fail(c, INZG_BAD_ARG, "moe_block_hc: the layer's hyper-connection has no inject vectors");
+    inzg_moe_opts o = opt ? *opt : inzg_moe_opts{};
+    o.flags |= INZG_IO_DEVICE;
+    cudaSetDevice(cf.device);
+    inzg_status s = hc_scratch(c, n);
+    if (s != INZG_OK) return s;
+    cudaStream_t st = o.stream ? static_cast<cudaStream_t>(o.stream) : c->stream;
+    // X -> (xin, inj) -> the layer (y) -> X += inj * y, with the context's own device buffers in between
+    s = hc_in_enqueue(c, layer, n, X_dev, c->xin, c->hc_inj, st);
+    if (s != INZG_OK) return s;
+    s = inzg_moe_forward(c, layer, n, c->xin, c->y, &o);
+    if (s != INZG_OK) return s;
+    return inzg_hc_out(c, n, X_dev, c->hc_inj, c->y, o.stream);
 }
 
 }  // extern "C"

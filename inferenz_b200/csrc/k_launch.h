@@ -13,6 +13,9 @@ bool router_gemm_fits(int E, int H);
 // Wf: the fp32 copy (nullptr: the f16 kernels only)
 int launch_router_logits(const uint4 *Wr, const float *Wf, const float *X, int n, int H, int E, const float *bias,
                          float *logits, int32_t *meta, cudaStream_t st);
+// lin_mm's F16 path for any rows % 4 == 0, K % 64 == 0 (W in the router layout, Wf its fp32 copy or nullptr)
+int launch_f16_rows(const uint4 *Wr, const float *Wf, const float *X, int n, int K, int rows, float *Y, int32_t *meta,
+                    cudaStream_t st);
 int launch_softmax_topk(const float *logits, int n, int E, int topk, int32_t *sel, float *w, float *probs,
                         cudaStream_t st);
 
@@ -66,6 +69,22 @@ void launch_pool_requant(const uint8_t *blobs, uint64_t blob_bytes, uint64_t gu_
                          cudaStream_t st);
 void launch_pool_repack(const uint8_t *blobs, uint64_t blob_bytes, uint64_t gu_bytes, int e0, int ne,
                         const LayerDev &L, uint8_t *pool, uint8_t *luts, cudaStream_t st);
+
+// Hyper-connections around the layer (k_hc.cu, src/model_fwd.c:404-450). Weights of one block on the device.
+struct HcDev {
+    const float *norm = nullptr;    // [4H], the folded 1 + w
+    const uint4 *down = nullptr;    // [rank][4H] f16 in the router layout
+    const float *down32 = nullptr;  // its fp32 copy for the many-token kernel (nullptr: not used)
+    const uint4 *up = nullptr;      // [4H][rank] f16 in the router layout
+    const float *inject = nullptr;  // [4][4H] (nullptr: no inject, as the final mixer)
+    int rank = 0;
+};
+void hc_set_attributes(int H);
+// X [n][4H] -> xin [n][H], inj [n][4] (skipped when w.inject or inj is null); scratch Xn [n][4H], d [n][rank],
+// m [n][4H]. Returns the number of kernels launched, -1 when a matrix shape has no kernel.
+int launch_hc_in(const HcDev &w, int n, int H, const float *X, float *Xn, float *d, float *m, float *xin, float *inj,
+                 int32_t *meta, int num_sms, cudaStream_t st);
+int launch_hc_out(float *X, const float *inj, const float *y, int n, int H, int num_sms, cudaStream_t st);
 
 // Expert-parallel exchange over peer memory (k_ep.cu). epoch_dev: the rank's step counter; tickets: one int per kernel.
 // route + dispatch from the router logits [n][E] (softmax and top-k per token inside; sel_out [n][topk] kept for the

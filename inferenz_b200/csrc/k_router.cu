@@ -167,9 +167,9 @@ __global__ void __launch_bounds__(256) router_large_kernel(const uint4 *__restri
     constexpr int PF = 8;
     uint4 ra[PF], rb[PF];
 #pragma unroll
-    for (int u = 0; u < PF; u++) {
-        ra[u] = live ? __ldg(wa + (size_t)u * 32) : make_uint4(0, 0, 0, 0);
-        rb[u] = hasb ? __ldg(wb + (size_t)u * 32) : make_uint4(0, 0, 0, 0);
+    for (int u = 0; u < PF; u++) {  // u < SC: a matrix narrower than 8 chunks (K < 512) has fewer to fetch
+        ra[u] = live && u < SC ? __ldg(wa + (size_t)u * 32) : make_uint4(0, 0, 0, 0);
+        rb[u] = hasb && u < SC ? __ldg(wb + (size_t)u * 32) : make_uint4(0, 0, 0, 0);
     }
     stage_x<LT>(xs, X, t0, nt, H);
     __syncthreads();
@@ -380,13 +380,32 @@ bool router_gemm_fits(int E, int H) { return E % kRE == 0 && H % (8 * kRJ) == 0;
 static size_t router_smem(int TT, int H) { return (size_t)TT * 8 * (H / 8 + 4) * sizeof(float); }
 static size_t router_small_smem(int TT, int WPB, int H) { return 128 + (size_t)2 * WPB * H * 8 + (size_t)TT * H * 4; }
 
+// the opt-in shared memory per block of the current device
+static size_t smem_optin() {
+    int dev = 0, v = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    return (size_t)v;
+}
+
+// Raises a kernel's dynamic shared memory limit to `bytes` (never lowers it: contexts of different widths share the
+// kernels); sizes above the device's limit are skipped -- launch_f16_rows does not pick those kernels.
+template <class F>
+static void raise_smem(F *fn, int slot, size_t bytes, size_t cap) {
+    static size_t cur[8] = {};
+    if (bytes > cap || bytes <= cur[slot]) return;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) == cudaSuccess) cur[slot] = bytes;
+    else cudaGetLastError();
+}
+
 void router_set_attributes(int H) {
-    cudaFuncSetAttribute(router_large_kernel<kLT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_smem(kLT, H));
-    cudaFuncSetAttribute(router_large_kernel<4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_smem(4, H));
-    cudaFuncSetAttribute(router_large_kernel<2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_smem(2, H));
-    cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_gemm_smem());
-    cudaFuncSetAttribute(router_small_kernel<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_small_smem(1, 1, H));
-    cudaFuncSetAttribute(router_small_kernel<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_small_smem(2, 1, H));
+    const size_t cap = smem_optin();
+    raise_smem(router_large_kernel<kLT>, 0, router_smem(kLT, H), cap);
+    raise_smem(router_large_kernel<4, 2>, 1, router_smem(4, H), cap);
+    raise_smem(router_large_kernel<2, 2>, 2, router_smem(2, H), cap);
+    raise_smem(router_gemm_kernel, 3, router_gemm_smem(), cap);
+    raise_smem(router_small_kernel<1, 1>, 4, router_small_smem(1, 1, H), cap);
+    raise_smem(router_small_kernel<2, 1>, 5, router_small_smem(2, 1, H), cap);
 }
 
 int launch_router_logits(const uint4 *Wr, const float *Wf, const float *X, int n, int H, int E, const float *bias,
@@ -409,6 +428,36 @@ int launch_router_logits(const uint4 *Wr, const float *Wf, const float *X, int n
     } else {
         dim3 grid((E + 63) / 64, (n + kLT - 1) / kLT);
         router_large_kernel<kLT><<<grid, 256, router_smem(kLT, H), st>>>(Wr, X, n, H, E, bias, logits);
+    }
+    return 1;
+}
+
+// Y[t][r] = sum_k f16(W[r][k]) x[t][k] in the router's chain order for any rows % 4 == 0 and K % 64 == 0 -- lin_mm's
+// F16 path (src/model_fwd.c:104-121), used for the hyper-connection matrices (320 x 4H and 4H x 320): the router's
+// kernels, each picked only when its shared memory at this K fits the device (router_set_attributes(K) first).
+// Returns the number of kernels launched, -1 when no kernel fits.
+int launch_f16_rows(const uint4 *Wr, const float *Wf, const float *X, int n, int K, int rows, float *Y, int32_t *meta,
+                    cudaStream_t st) {
+    if (n <= 0 || rows % 4 || K % 64) return -1;
+    const size_t cap = smem_optin();
+    CUtensorMap mapX;
+    if (n == 1 && router_small_smem(1, 1, K) <= cap) {
+        router_small_kernel<1, 1><<<dim3((rows / 4 + 1) / 2, 1), 32, router_small_smem(1, 1, K), st>>>(Wr, X, n, K, rows, nullptr, Y, meta);
+    } else if (n == 2 && router_small_smem(2, 1, K) <= cap) {
+        router_small_kernel<2, 1><<<dim3((rows / 4 + 1) / 2, 1), 32, router_small_smem(2, 1, K), st>>>(Wr, X, n, K, rows, nullptr, Y, meta);
+    } else if (n <= 32 && router_smem(2, K) <= cap) {
+        router_large_kernel<2, 2><<<dim3((rows + 63) / 64, (n + 1) / 2), 256, router_smem(2, K), st>>>(Wr, X, n, K, rows, nullptr, Y);
+    } else if (n <= 64 && router_smem(4, K) <= cap) {
+        router_large_kernel<4, 2><<<dim3((rows + 63) / 64, (n + 3) / 4), 256, router_smem(4, K), st>>>(Wr, X, n, K, rows, nullptr, Y);
+    } else if (Wf && n >= kRouterGemmMinTokens && router_gemm_fits(rows, K) && make_tma_map_f32(&mapX, X, n, K, kRT)) {
+        router_gemm_kernel<<<dim3(rows / kRE, (n + kRT - 1) / kRT), 256, router_gemm_smem(), st>>>(mapX, Wf, n, K, rows,
+                                                                                                 nullptr, Y, meta);
+    } else if (router_smem(kLT, K) <= cap) {
+        router_large_kernel<kLT><<<dim3((rows + 63) / 64, (n + kLT - 1) / kLT), 256, router_smem(kLT, K), st>>>(Wr, X, n, K, rows, nullptr, Y);
+    } else if (router_smem(4, K) <= cap) {
+        router_large_kernel<4, 2><<<dim3((rows + 63) / 64, (n + 3) / 4), 256, router_smem(4, K), st>>>(Wr, X, n, K, rows, nullptr, Y);
+    } else {
+        return -1;
     }
     return 1;
 }

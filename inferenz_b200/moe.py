@@ -14,6 +14,9 @@ from ._lib import (DUMP_ROUTE, EP_HANDLE_BYTES, GEMM_SIMT, IO_DEVICE, N_STAGES, 
                    T_Q8G, lib)
 
 
+HC_RANK = 320  # INZG_HC_RANK: the hyper-connection bottleneck (src/model.h:14)
+
+
 def _ptr(a):
     return None if a is None else ctypes.c_void_p(a.ctypes.data)
 
@@ -86,6 +89,33 @@ class MoePool:
         g = np.ascontiguousarray(gate, dtype=np.float32)
         assert g.shape == (self.hidden,) and b.size >= blob_bytes
         self._check(lib.inzg_set_shared(self._ctx, layer, expert_type, _ptr(b), blob_bytes, _ptr(g)), "set_shared")
+
+    # -- hyper-connections around the layer (src/model_fwd.c:404-450, 1264-1267) --
+    def set_hc(self, layer, norm, down, up, inject=None):
+        """The layer's hyper-connection weights: norm [4H] f32, down [320][4H] and up [4H][320] as f16 bits (uint16),
+        inject [4][4H] f32 or None."""
+        W = 4 * self.hidden
+        nm = np.ascontiguousarray(norm, dtype=np.float32)
+        dn = np.ascontiguousarray(down, dtype=np.uint16)
+        upm = np.ascontiguousarray(up, dtype=np.uint16)
+        ij = None if inject is None else np.ascontiguousarray(inject, dtype=np.float32)
+        assert nm.shape == (W,) and dn.shape == (HC_RANK, W) and upm.shape == (W, HC_RANK)
+        assert ij is None or ij.shape == (4, W)
+        self._check(lib.inzg_set_hc(self._ctx, layer, _ptr(nm), _ptr(dn), _ptr(upm), _ptr(ij)), "set_hc")
+
+    def hc_in_device(self, layer, n, X_ptr, xin_ptr, inj_ptr=None, stream=None):
+        self._check(lib.inzg_hc_in(self._ctx, layer, n, ctypes.c_void_p(X_ptr), ctypes.c_void_p(xin_ptr),
+                                   inj_ptr and ctypes.c_void_p(inj_ptr), stream and ctypes.c_void_p(stream)), "hc_in")
+
+    def hc_out_device(self, n, X_ptr, inj_ptr, y_ptr, stream=None):
+        self._check(lib.inzg_hc_out(self._ctx, n, ctypes.c_void_p(X_ptr), ctypes.c_void_p(inj_ptr),
+                                    ctypes.c_void_p(y_ptr), stream and ctypes.c_void_p(stream)), "hc_out")
+
+    def moe_block_hc_device(self, layer, n, X_ptr, bias_ptr=None, override_ptr=None, stream=None, graph=True):
+        """q_forward's MoE step on device pointers: X [n][4H] updated in place (hc_in, the layer, hc_out)."""
+        opts = MoeOpts(IO_DEVICE | (0 if graph else NO_GRAPH), bias_ptr, override_ptr, stream)
+        self._check(lib.inzg_moe_block_hc(self._ctx, layer, n, ctypes.c_void_p(X_ptr), ctypes.byref(opts)),
+                    "moe_block_hc")
 
     # -- expert-parallel building blocks (device pointers as ints; stream-ordered, no synchronisation) --
     def route_device(self, layer, n, x_ptr, sel_ptr, w_ptr, bias_ptr=None, stream=None):

@@ -96,6 +96,28 @@ def synth_expert(layer, e, H=2048, FF=640):
     return gu, dn
 
 
+def synth_hc(layer, H=2048, rank=320, seed=0x4843):
+    """Hyper-connection weights of one block (the hcw of src/engine_internal.h:27-32) with magnitudes like a trained
+    model's: norm = 1 + w (folded, small w), down [rank][4H] and up [4H][rank] as f16 bits, inject [4][4H]."""
+    W = 4 * H
+    st = seed * 1000003 + layer
+    norm = 1.0 + 0.1 * synth_randn(st, W)
+    down = _f16_bits(synth_randn(st + 1, rank * W, (1.0 / W) ** 0.5).reshape(rank, W))
+    up = _f16_bits(synth_randn(st + 2, W * rank, (1.0 / rank) ** 0.5).reshape(W, rank))
+    inject = synth_randn(st + 3, 4 * W, (1.0 / W) ** 0.5).reshape(4, W)
+    return {"norm": np.ascontiguousarray(norm, np.float32), "down": down, "up": up,
+            "inject": np.ascontiguousarray(inject, np.float32)}
+
+
+def synth_residual(n, H=2048, seed=0x5245):
+    """The residual stream X [n][4H] entering hc_in: four streams of hidden-state scale."""
+    return np.ascontiguousarray(synth_randn(seed, n * 4 * H).reshape(n, 4 * H), np.float32)
+
+
+def _f16_bits(a):
+    return np.ascontiguousarray(np.asarray(a, np.float32).astype(np.float16).view(np.uint16))
+
+
 def normal_bias(E=512, seed=BIAS_SEED):
     return synth_randn(seed, E)
 
@@ -160,6 +182,8 @@ class Oracle:
             ("orc_act_quantize", None, [P, I, I, U32, P, P, P]),
             ("orc_xq", None, [P, I, I, U32, P, P, P]),
             ("orc_moe_routed", I, [I, I, I, I, P, P, U64, U64, I, P, P, P, P, P, P, P, P, P, P, I]),
+            ("orc_hc_in", None, [I, I, P, P, P, P, I, P, P, P]),
+            ("orc_hc_out", None, [I, I, P, P, P]),
         ]:
             fn = getattr(L, name)
             fn.restype = res
@@ -201,6 +225,25 @@ class Oracle:
         sm = np.zeros(nkb, np.int32)
         self.lib.orc_xq(_p(x), K, rot, seed, _p(q), _p(s), _p(sm))
         return q, s, sm
+
+    def hc_in(self, hc, X):
+        """hc_in (src/model_fwd.c:404-439): X [n][4H] -> (xin [n][H], inj [n][4]); hc: dict from synth_hc."""
+        n, W = X.shape
+        H, rank = W // 4, hc["down"].shape[0]
+        xin = np.zeros((n, H), np.float32)
+        inj = np.zeros((n, 4), np.float32)
+        inject = hc.get("inject")
+        self.lib.orc_hc_in(H, rank, _p(hc["norm"]), _p(hc["down"]), _p(hc["up"]), _p(inject), n,
+                           _p(np.ascontiguousarray(X, np.float32)), _p(xin), _p(inj if inject is not None else None))
+        return xin, inj
+
+    def hc_out(self, X, inj, y):
+        """hc_out (src/model_fwd.c:442-450): returns X + inj_s * y per stream (one fma per element)."""
+        n, W = X.shape
+        Xo = np.ascontiguousarray(X, np.float32).copy()
+        self.lib.orc_hc_out(W // 4, n, _p(Xo), _p(np.ascontiguousarray(inj, np.float32)),
+                            _p(np.ascontiguousarray(y, np.float32)))
+        return Xo
 
     def moe_routed(self, router, blobs, blob_bytes, gu_bytes, xin, bias=None, override=None, H=2048, FF=640, E=512,
                    topk=10, dumps=True):
@@ -246,6 +289,7 @@ class Ref:
             ("ref_matmul_gemm", None, [P, I, P, P]), ("ref_xq", None, [P, I, I, I, U32, P, P, P]),
             ("ref_moe_routed", I, [P, P, P, U64, I, P, P, P, P, P, P, P, P, P, P]),
             ("ref_shared", I, [P, P, U64, I, P, I, P, P, P]),
+            ("ref_hc_rank", I, []), ("ref_hc_in", I, [P, P, P, P, P, I, P, P, P]), ("ref_hc_out", None, [I, P, P, P]),
         ]:
             fn = getattr(L, name)
             fn.restype = res
@@ -300,6 +344,29 @@ class Ref:
         if rc != 0:
             raise RuntimeError("reference: shared expert matrices do not match")
         return yo, D
+
+
+    def hc_in(self, hc, X):
+        """The reference's own hc_in; same arguments and results as Oracle.hc_in."""
+        n, W = X.shape
+        assert W == 4 * self.H and hc["down"].shape == (self.lib.ref_hc_rank(), W)
+        xin = np.zeros((n, self.H), np.float32)
+        inj = np.zeros((n, 4), np.float32)
+        inject = hc.get("inject")
+        rc = self.lib.ref_hc_in(self.ctx, _p(hc["norm"]), _p(hc["down"]), _p(hc["up"]), _p(inject), n,
+                                _p(np.ascontiguousarray(X, np.float32)), _p(xin),
+                                _p(inj if inject is not None else None))
+        if rc != 0:
+            raise RuntimeError("reference: bad hc_in call")
+        return xin, inj
+
+    def hc_out(self, X, inj, y):
+        """The reference's own hc_out; returns the updated copy of X."""
+        n = X.shape[0]
+        Xo = np.ascontiguousarray(X, np.float32).copy()
+        self.lib.ref_hc_out(n, _p(Xo), _p(np.ascontiguousarray(inj, np.float32)),
+                            _p(np.ascontiguousarray(y, np.float32)))
+        return Xo
 
 
 class RefGguf:

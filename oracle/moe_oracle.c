@@ -443,6 +443,67 @@ int orc_moe_routed(int H, int FF, int E, int topk, const uint16_t *router, const
     return rc;
 }
 
+/* ---------------- hyper-connections around the layer ---------------- */
+
+/* dot_f32, src/model_fwd.c:24-34: two 8-lane fma accumulators over 16-element blocks (s0: elements 16i + l, s1:
+ * 16i + 8 + l), added lane-wise, then hsum256_ps. n % 16 == 0 here (4H and H), so the scalar tail never runs. */
+static float dot_f32(const float *a, const float *b, int n) {
+    float s0[8] = {0, 0, 0, 0, 0, 0, 0, 0}, s1[8] = {0, 0, 0, 0, 0, 0, 0, 0}, v[8];
+    for (int i = 0; i + 16 <= n; i += 16)
+        for (int l = 0; l < 8; l++) {
+            s0[l] = fmaf(a[i + l], b[i + l], s0[l]);
+            s1[l] = fmaf(a[i + 8 + l], b[i + 8 + l], s1[l]);
+        }
+    for (int l = 0; l < 8; l++) v[l] = s0[l] + s1[l];
+    return hsum8(v);
+}
+
+/* sigmoidf, src/model_fwd.c:42 (glibc expf) */
+static float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+/* sigmoid256, src/model_fwd.c:397-400, one lane: 1 / (1 + exp256_ps(0 - x)) */
+static float sigmoid_cephes(float x) { return 1.0f / (1.0f + cephes_exp(0.0f - x)); }
+
+/* hc_in, src/model_fwd.c:404-439 with rmsnorm 37-40 (eps 1e-6f, src/model.h:18) and lin_mm's F16 path (the
+ * router's numerics, inz_matvec_f16_rows / inz_matmul_f16_rows). W = 4H; rank = 320 (Q_HC_RANK). */
+void orc_hc_in(int H, int rank, const float *norm, const uint16_t *down, const uint16_t *up, const float *inject,
+               int n, const float *X, float *xin, float *inj) {
+    const int W = 4 * H;
+    float *Xn = calloc((size_t)n * W, sizeof(float)), *d = malloc(sizeof(float) * (size_t)n * rank);
+    float *m = malloc(sizeof(float) * (size_t)n * W);
+    for (int t = 0; t < n; t++)
+        for (int s = 0; s < 4; s++) {
+            const float *x = X + (size_t)t * W + (size_t)s * H;
+            float *o = Xn + (size_t)t * W + (size_t)s * H;
+            const float r = 1.0f / sqrtf(dot_f32(x, x, H) / (float)H + 1e-6f);
+            for (int i = 0; i < H; i++) o[i] = x[i] * r * norm[s * H + i];
+        }
+    orc_router_logits(down, rank, W, Xn, n, d);
+    for (size_t i = 0; i < (size_t)n * rank; i++) d[i] = siluf(d[i] / 4.0f);
+    orc_router_logits(up, W, rank, d, n, m);
+    for (int t = 0; t < n; t++) {
+        const float *mt = m + (size_t)t * W, *xt = Xn + (size_t)t * W;
+        for (int i = 0; i < H; i++) {
+            float acc = 0.0f;
+            for (int s = 0; s < 4; s++) acc = fmaf(sigmoid_cephes(mt[s * H + i]), xt[s * H + i], acc);
+            xin[(size_t)t * H + i] = acc * 0.25f;
+        }
+        if (inj)
+            for (int s = 0; s < 4; s++) inj[t * 4 + s] = 2.0f * sigmoidf_(dot_f32(inject + (size_t)s * W, xt, W) / 4.0f);
+    }
+    free(Xn); free(d); free(m);
+}
+
+/* hc_out, src/model_fwd.c:442-450: X_s += inj_s * y, one fma per element (the reference build contracts it) */
+void orc_hc_out(int H, int n, float *X, const float *inj, const float *y) {
+    for (int t = 0; t < n; t++)
+        for (int s = 0; s < 4; s++) {
+            float *x = X + (size_t)t * 4 * H + (size_t)s * H;
+            const float w = inj[t * 4 + s];
+            for (int i = 0; i < H; i++) x[i] = fmaf(w, y[(size_t)t * H + i], x[i]);
+        }
+}
+
 /* ---------------- seeded synthetic inputs (tests/test_quant.c:10-17) ---------------- */
 
 #define LCG_A 6364136223846793005ull

@@ -69,6 +69,12 @@ int orc_moe_routed(int H, int FF, int E, int topk, const uint16_t *router, const
                    float *logits_out, float *probs_out, int32_t *sel_out, float *w_out, int32_t *unit_expert_out,
                    float *moe_out, int q8_vnni);
 
+/* hyper-connections (src/model_fwd.c:404-450): hc_in X [n][4H] -> xin [n][H], inj [n][4] (inj NULL: not computed);
+ * norm [4H], down [rank][4H] f16, up [4H][rank] f16, inject [4][4H]. hc_out: X [n][4H] += inj * y in place. */
+void orc_hc_in(int H, int rank, const float *norm, const uint16_t *down, const uint16_t *up, const float *inject,
+               int n, const float *X, float *xin, float *inj);
+void orc_hc_out(int H, int n, float *X, const float *inj, const float *y);
+
 /* ---- seeded synthetic inputs (test infrastructure): the LCG + Box-Muller normal of the reference's tests
  * (tests/test_quant.c:10-17), so that the CPU side of a test or of the benchmark's reference arm draws its inputs
  * without the product library ---- */

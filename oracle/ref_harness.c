@@ -22,6 +22,8 @@
  *   ref_shared                        -- the shared expert of moe_block (src/model_fwd.c:1041-1069 without the
  *                                        lookahead, and :1141-1148) around the reference's lin_mm, siluf,
  *                                        sigmoidf and dot_f32.
+ *   ref_hc_in / ref_hc_out            -- the hyper-connection steps either side of the layer (src/model_fwd.c:
+ *                                        404-450), the reference's own functions.
  */
 #include "model.h"
 #undef Q_H
@@ -318,3 +320,34 @@ API int ref_shared(void *ctx, const uint8_t *blob, uint64_t gu_bytes, int type, 
     if (D_out) memcpy(D_out, D, sizeof(float) * (size_t)n * Q_H);
     return 0;
 }
+
+/* ---- hyper-connections around the MoE layer ----
+ * hc_in (src/model_fwd.c:432-439) and hc_out (:442-450) themselves, with F16 down/up matrices (the converter's
+ * default hc type, src/convert.c:148) bound by q_bind_lin. norm [4H], down [320][4H] f16 bits, up [4H][320] f16 bits,
+ * inject [4][4H] (NULL: no inj, as the final mixer); X [n][4H] -> xin [n][H], inj [n][4]. hc_in's scratch (e->Xn,
+ * e->tmp, e->big) is allocated for this call's n only. Returns 0, or -1 on a bad n. */
+API int ref_hc_rank(void) { return Q_HC_RANK; }
+
+API int ref_hc_in(void *ctx, const float *norm, const uint16_t *down, const uint16_t *up, const float *inject, int n,
+                  const float *X, float *xin, float *inj) {
+    ref_ctx *c = ctx;
+    inz_engine *e = c->e;
+    if (n <= 0 || n > Q_MAX_T) return -1;
+    hcw w;
+    memset(&w, 0, sizeof(w));
+    w.norm = norm;
+    w.inject = inject;
+    if (!q_bind_lin(&w.down, INZ_T_F16, Q_HC_RANK, Q_HCW, (const uint8_t *)down) ||
+        !q_bind_lin(&w.up, INZ_T_F16, Q_HCW, Q_HC_RANK, (const uint8_t *)up))
+        return -1;
+    float *sXn = e->Xn, *stmp = e->tmp, *sbig = e->big;
+    e->Xn = inz_aligned(64, sizeof(float) * (size_t)n * Q_HCW);
+    e->tmp = inz_aligned(64, sizeof(float) * (size_t)n * Q_HC_RANK);
+    e->big = inz_aligned(64, sizeof(float) * (size_t)n * Q_HCW);
+    hc_in(e, &w, n, X, xin, inject ? inj : NULL);
+    free(e->Xn); free(e->tmp); free(e->big);
+    e->Xn = sXn; e->tmp = stmp; e->big = sbig;
+    return 0;
+}
+
+API void ref_hc_out(int n, float *X, const float *inj, const float *y) { hc_out(n, X, inj, y); }
