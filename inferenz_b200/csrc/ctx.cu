@@ -52,7 +52,7 @@ struct LayerSlot {
     LayerDev dev{};
 };
 
-// hyper-connection weights of one layer (inzg_set_hc): one allocation, norm | inject | down32 | down | up
+// hyper-connection weights of one layer (inzg_set_hc): one allocation, norm | inject | down32 | up32 | down | up
 struct HcSlot {
     uint8_t *mem = nullptr;
     HcDev dev{};
@@ -375,7 +375,8 @@ inzg_status inzg_set_router(inzg_ctx *c, int layer, const uint16_t *w, int rows,
         cudaFree(tmp);
         return fail(c, INZG_OOM, "set_router: router buffer");
     }
-    if (router_gemm_fits(rows, cols) && !L.router32 && cudaMalloc(&L.router32, bytes * 2) != cudaSuccess) {
+    if (router_gemm_fits(rows, cols) && !L.router32 &&
+        cudaMalloc(&L.router32, sizeof(float) * router32_floats(rows, cols)) != cudaSuccess) {
         cudaFree(tmp);
         return fail(c, INZG_OOM, "set_router: router buffer");
     }
@@ -1369,8 +1370,8 @@ inzg_status inzg_set_hc(inzg_ctx *c, int layer, const float *norm, const uint16_
     cudaSetDevice(cf.device);
     const int W = 4 * cf.hidden, R = INZG_HC_RANK;
     const size_t f16 = (size_t)R * W * 2;
-    const size_t o_inj = (size_t)W * 4, o_d32 = o_inj + (size_t)4 * W * 4, o_dn = o_d32 + (size_t)R * W * 4,
-                 o_up = o_dn + f16, total = o_up + f16;
+    const size_t o_inj = (size_t)W * 4, o_d32 = o_inj + (size_t)4 * W * 4, o_u32 = o_d32 + router32_floats(R, W) * 4,
+                 o_dn = o_u32 + router32_floats(W, R) * 4, o_up = o_dn + f16, total = o_up + f16;
     HcSlot &h = c->hc[layer];
     if (!h.mem && cudaMalloc(&h.mem, total) != cudaSuccess) {
         cudaGetLastError();
@@ -1391,6 +1392,7 @@ inzg_status inzg_set_hc(inzg_ctx *c, int layer, const float *norm, const uint16_
         launch_router_repack(tmp, reinterpret_cast<uint4 *>(h.mem + o_dn), R, W, st);
         launch_router_repack32(tmp, reinterpret_cast<float *>(h.mem + o_d32), R, W, st);
         launch_router_repack(tmp + (size_t)R * W, reinterpret_cast<uint4 *>(h.mem + o_up), W, R, st);
+        launch_router_repack32(tmp + (size_t)R * W, reinterpret_cast<float *>(h.mem + o_u32), W, R, st);
         e = cudaStreamSynchronize(st);
     }
     cudaFree(tmp);
@@ -1402,6 +1404,7 @@ inzg_status inzg_set_hc(inzg_ctx *c, int layer, const float *norm, const uint16_
     d.down32 = router_gemm_fits(R, W) ? reinterpret_cast<const float *>(h.mem + o_d32) : nullptr;
     d.down = reinterpret_cast<const uint4 *>(h.mem + o_dn);
     d.up = reinterpret_cast<const uint4 *>(h.mem + o_up);
+    d.up32 = router_gemm_fits(W, R) ? reinterpret_cast<const float *>(h.mem + o_u32) : nullptr;
     d.rank = R;
     return INZG_OK;
 }

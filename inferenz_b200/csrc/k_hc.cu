@@ -135,7 +135,7 @@ int launch_hc_in(const HcDev &w, int n, int H, const float *X, float *Xn, float 
     launches += k;
     hc_silu_kernel<<<grid_for((int64_t)n * w.rank, 256, num_sms), 256, 0, st>>>(d, n * w.rank);
     launches++;
-    k = launch_f16_rows(w.up, nullptr, d, n, w.rank, W, m, meta, st);
+    k = launch_f16_rows(w.up, w.up32, d, n, w.rank, W, m, meta, st);
     if (k < 0) return -1;
     launches += k;
     hc_mix_kernel<<<grid_for((int64_t)n * H, 256, num_sms), 256, 0, st>>>(m, Xn, n, H, xin);

@@ -10,6 +10,7 @@ void router_set_attributes(int H);
 void launch_router_repack(const uint16_t *W, uint4 *Wr, int E, int H, cudaStream_t st);
 void launch_router_repack32(const uint16_t *W, float *Wf, int E, int H, cudaStream_t st);
 bool router_gemm_fits(int E, int H);
+size_t router32_floats(int E, int H);  // floats of the fp32 copy (launch_router_repack32), whole 128-column chunks
 // Wf: the fp32 copy (nullptr: the f16 kernels only)
 int launch_router_logits(const uint4 *Wr, const float *Wf, const float *X, int n, int H, int E, const float *bias,
                          float *logits, int32_t *meta, cudaStream_t st);
@@ -76,6 +77,7 @@ struct HcDev {
     const uint4 *down = nullptr;    // [rank][4H] f16 in the router layout
     const float *down32 = nullptr;  // its fp32 copy for the many-token kernel (nullptr: not used)
     const uint4 *up = nullptr;      // [4H][rank] f16 in the router layout
+    const float *up32 = nullptr;    // its fp32 copy (nullptr: not used)
     const float *inject = nullptr;  // [4][4H] (nullptr: no inject, as the final mixer)
     int rank = 0;
 };

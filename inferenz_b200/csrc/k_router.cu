@@ -235,14 +235,22 @@ size_t router_gemm_smem() {
     return 1024 + (red > stages ? red : stages);
 }
 
-// W [E][H] f16 -> Wf [E/32][H/128][8][16][32] fp32 (see above). One thread per output float.
+// 128-column chunks of an H-wide matrix; a last partial chunk is padded with zero weights, and the tensor copies of x
+// read zeros past column H, so each padded step is fma(0, 0, acc) = acc: the chains stay exact (acc is never -0, as
+// every chain starts at +0)
+__host__ __device__ __forceinline__ int router_chunks(int H) { return (H + 8 * kRJ - 1) / (8 * kRJ); }
+
+size_t router32_floats(int E, int H) { return (size_t)E * router_chunks(H) * 8 * kRJ; }
+
+// W [E][H] f16 -> Wf [E/32][chunks][8][16][32] fp32 (see above). One thread per output float.
 __global__ void router_repack32_kernel(const uint16_t *__restrict__ W, float *__restrict__ Wf, int E, int H) {
-    const int nch = H / (8 * kRJ);
-    const int64_t total = (int64_t)E * H;
+    const int nch = router_chunks(H);
+    const int64_t total = (int64_t)E * nch * 8 * kRJ;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int e_ = (int)(i % kRE), j_ = (int)((i / kRE) % kRJ), l = (int)((i / (kRE * kRJ)) % 8);
         const int c = (int)((i / (kRE * kRJ * 8)) % nch), eb = (int)(i / ((int64_t)kRE * kRJ * 8 * nch));
-        Wf[i] = h2f(W[(size_t)(eb * kRE + e_) * H + 8 * (c * kRJ + j_) + l]);
+        const int k = 8 * (c * kRJ + j_) + l;
+        Wf[i] = k < H ? h2f(W[(size_t)(eb * kRE + e_) * H + k]) : 0.0f;
     }
 }
 
@@ -254,7 +262,7 @@ __global__ void __launch_bounds__(256, 2) router_gemm_kernel(const __grid_consta
     __shared__ uint64_t bar[kRStages];
     uint8_t *stage0 = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(rgs_raw) + 1023) & ~uintptr_t(1023));
     const int eb = blockIdx.x, t0 = blockIdx.y * kRT, nt = min(kRT, n - t0);
-    const int nch = H / (8 * kRJ);
+    const int nch = router_chunks(H);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tg = lane & 7, eg = lane >> 3;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kRStages; s++) mbar_init(&bar[s], 1);
@@ -371,11 +379,11 @@ void launch_router_repack(const uint16_t *W, uint4 *Wr, int E, int H, cudaStream
 }
 
 void launch_router_repack32(const uint16_t *W, float *Wf, int E, int H, cudaStream_t st) {
-    const int64_t total = (int64_t)E * H;
+    const int64_t total = (int64_t)router32_floats(E, H);
     router_repack32_kernel<<<(int)std::min<int64_t>((total + 255) / 256, 65535), 256, 0, st>>>(W, Wf, E, H);
 }
 
-bool router_gemm_fits(int E, int H) { return E % kRE == 0 && H % (8 * kRJ) == 0; }
+bool router_gemm_fits(int E, int H) { return E % kRE == 0 && H % 64 == 0; }
 
 static size_t router_smem(int TT, int H) { return (size_t)TT * 8 * (H / 8 + 4) * sizeof(float); }
 static size_t router_small_smem(int TT, int WPB, int H) { return 128 + (size_t)2 * WPB * H * 8 + (size_t)TT * H * 4; }

@@ -105,3 +105,33 @@ def test_moe_block_with_hyper_connections(orc, n):
     exact = np.mean(got.view(np.uint32) == want.view(np.uint32))
     print(f"moe_block_hc n={n}: rel_l2 of the update max {err.max():.2e}; bit-identical residual {exact:.4f}")
     assert err.max() <= LAYER_TOL
+
+
+def test_hc_in_timing():
+    """Device time of hc_in at the benchmark's token counts (printed, not asserted): L2 flushed before every call,
+    CUDA events on the launching stream. Algorithmic bytes: both F16 matrices, norm and inject once, X read, xin
+    written; FMAs: the two 320 x 4H products."""
+    H, W, R = 2048, 8192, 320
+    hc = oracle.synth_hc(4, H=H)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")  # 256 MB > L2
+    with MoePool(H, 640, 512, 10, max_tokens=4096, n_layers=1, device=0) as pool:
+        pool.set_hc(0, hc["norm"], hc["down"], hc["up"], hc["inject"])
+        for n in (1, 32, 4096):
+            Xd = torch.randn(n, W, device="cuda")
+            xin = torch.empty((n, H), device="cuda")
+            inj = torch.empty((n, 4), device="cuda")
+            ts = []
+            for it in range(13):
+                flush.fill_(float(it))
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                pool.hc_in_device(0, n, Xd.data_ptr(), xin.data_ptr(), inj.data_ptr(), stream=_st())
+                b.record()
+                torch.cuda.synchronize()
+                if it >= 3:
+                    ts.append(a.elapsed_time(b) * 1e3)
+            pool.device_status(_st())
+            us = float(np.median(ts))
+            byts = 2 * R * W * 2 + W * 4 + 4 * W * 4 + n * W * 4 + n * H * 4
+            print(f"hc_in timing H={H} n={n}: {us:.1f} us median of {len(ts)}; {byts / us / 1e3:.0f} GB/s algorithmic; "
+                  f"{2 * 2 * n * R * W / us / 1e6:.2f} TFLOP/s (fp32 FMA chains)")
