@@ -1368,6 +1368,7 @@ inzg_status inzg_set_hc(inzg_ctx *c, int layer, const float *norm, const uint16_
     const inzg_config &cf = c->cfg;
     if (layer < 0 || layer >= cf.n_layers || !norm || !down || !up) return fail(c, INZG_BAD_ARG, "set_hc: bad layer or pointer");
     cudaSetDevice(cf.device);
+    drop_graphs(c);
     const int W = 4 * cf.hidden, R = INZG_HC_RANK;
     const size_t f16 = (size_t)R * W * 2;
     const size_t o_inj = (size_t)W * 4, o_d32 = o_inj + (size_t)4 * W * 4, o_u32 = o_d32 + router32_floats(R, W) * 4,
@@ -1413,6 +1414,7 @@ inzg_status inzg_set_hc(inzg_ctx *c, int layer, const float *norm, const uint16_
 // needs it)
 static inzg_status hc_scratch(inzg_ctx *c, int n) {
     if (n <= c->hc_cap) return INZG_OK;
+    drop_graphs(c);  // captured hc_in steps name the old scratch
     for (float **p : {&c->hc_Xn, &c->hc_d, &c->hc_m, &c->hc_inj})
         if (*p) {
             cudaFree(*p);
@@ -1438,9 +1440,43 @@ static inzg_status hc_in_enqueue(inzg_ctx *c, int layer, int n, const float *X_d
         return fail(c, INZG_BAD_ARG, "hc_in: pointers must be 16-byte aligned");
     const HcSlot &h = c->hc[layer];
     if (!h.mem) return fail(c, INZG_NOT_READY, "hc_in: layer has no hyper-connection weights (inzg_set_hc)");
-    if (launch_hc_in(h.dev, n, cf.hidden, X_dev, c->hc_Xn, c->hc_d, c->hc_m, xin_dev, inj_dev, c->meta, c->num_sms, st) < 0)
-        return fail(c, INZG_UNSUPPORTED, "hc_in: no kernel for this width");
-    const cudaError_t e = cudaGetLastError();
+    // the step's kernels are captured once per (layer, n, buffers) into a CUDA graph and replayed, as the layer's
+    const inzg_ctx::GraphKey key{layer, n, X_dev, xin_dev, inj_dev, nullptr, 0x40000000u, 0};
+    inzg_ctx::GraphEntry *g = nullptr;
+    for (auto &ge : c->graphs)
+        if (ge.key == key) g = &ge;
+    cudaError_t e = cudaSuccess;
+    if (!g) {
+        cudaStream_t cs = c->capture_stream;
+        e = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
+        if (e != cudaSuccess) return cuda_fail(c, e, "hc_in: begin capture");
+        const int nl = launch_hc_in(h.dev, n, cf.hidden, X_dev, c->hc_Xn, c->hc_d, c->hc_m, xin_dev, inj_dev, c->meta,
+                                    c->num_sms, cs);
+        cudaGraph_t graph = nullptr;
+        e = cudaStreamEndCapture(cs, &graph);
+        if (e != cudaSuccess || nl < 0) {
+            if (graph) cudaGraphDestroy(graph);
+            return e != cudaSuccess ? cuda_fail(c, e, "hc_in: capture") : fail(c, INZG_UNSUPPORTED, "hc_in: no kernel for this width");
+        }
+        cudaGraphExec_t exec = nullptr;
+        e = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess) return cuda_fail(c, e, "hc_in: graph instantiate");
+        if (c->graphs.size() >= 64) {  // evict the least recently used
+            auto it = std::min_element(c->graphs.begin(), c->graphs.end(),
+                                       [](const inzg_ctx::GraphEntry &a, const inzg_ctx::GraphEntry &b) {
+                                           return a.last_use < b.last_use;
+                                       });
+            cudaGraphExecDestroy(it->exec);
+            c->graphs.erase(it);
+        }
+        c->graphs.push_back({key, exec, nl, 0});
+        g = &c->graphs.back();
+    }
+    g->last_use = ++c->use_clock;
+    e = cudaGraphLaunch(g->exec, st);
+    if (e != cudaSuccess) return cuda_fail(c, e, "hc_in: graph launch");
+    e = cudaGetLastError();
     return e == cudaSuccess ? INZG_OK : cuda_fail(c, e, "hc_in: kernel launch");
 }
 
