@@ -396,14 +396,20 @@ static size_t smem_optin() {
     return (size_t)v;
 }
 
-// Raises a kernel's dynamic shared memory limit to `bytes` (never lowers it: contexts of different widths share the
-// kernels); sizes above the device's limit are skipped -- launch_f16_rows does not pick those kernels.
+// Raises a kernel's dynamic shared memory limit on the current device to `bytes` (never lowers it: contexts of
+// different widths share the kernels); sizes above the device's limit are skipped -- launch_f16_rows does not pick
+// those kernels. The limit is a per-device setting, so it is tracked per device.
 template <class F>
 static void raise_smem(F *fn, int slot, size_t bytes, size_t cap) {
-    static size_t cur[8] = {};
-    if (bytes > cap || bytes <= cur[slot]) return;
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) == cudaSuccess) cur[slot] = bytes;
-    else cudaGetLastError();
+    constexpr int kMaxDevices = 64;
+    static size_t cur[kMaxDevices][8] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = 0;
+    if (bytes > cap || bytes <= cur[dev][slot]) return;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) == cudaSuccess)
+        cur[dev][slot] = bytes;
+    else
+        cudaGetLastError();
 }
 
 void router_set_attributes(int H) {
