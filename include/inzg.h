@@ -226,7 +226,7 @@ INZG_EXPORT inzg_status inzg_set_hc(inzg_ctx *ctx, int layer, const float *norm,
                                     const uint16_t *up_f16, const float *inject);
 
 /* hc_in (src/model_fwd.c:432-439), which makes the layer's input: X_dev [n][4*hidden] -> xin_dev [n][hidden] and
- * inj_dev [n][4] (NULL: not computed). Device pointers, 16-byte aligned; stream NULL = the context's stream. The
+ * inj_dev [n][4] (NULL: not computed; INZG_BAD_ARG when the layer was set without inject vectors). Device pointers, 16-byte aligned; stream NULL = the context's stream. The
  * first call with more tokens than before allocates the step's scratch (call it once at full size before any stream
  * capture). Bit-exact with the reference except the SiLU of the 320-wide bottleneck and the inject sigmoid, whose
  * glibc expf is evaluated in double and rounded once (one ulp apart on ~1e-4 of inputs). */

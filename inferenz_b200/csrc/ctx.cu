@@ -1440,6 +1440,7 @@ static inzg_status hc_in_enqueue(inzg_ctx *c, int layer, int n, const float *X_d
         return fail(c, INZG_BAD_ARG, "hc_in: pointers must be 16-byte aligned");
     const HcSlot &h = c->hc[layer];
     if (!h.mem) return fail(c, INZG_NOT_READY, "hc_in: layer has no hyper-connection weights (inzg_set_hc)");
+    if (inj_dev && !h.dev.inject) return fail(c, INZG_BAD_ARG, "hc_in: the layer's hyper-connection has no inject vectors");
     // the step's kernels are captured once per (layer, n, buffers) into a CUDA graph and replayed, as the layer's
     const inzg_ctx::GraphKey key{layer, n, X_dev, xin_dev, inj_dev, nullptr, 0x40000000u, 0};
     inzg_ctx::GraphEntry *g = nullptr;
@@ -1511,8 +1512,6 @@ inzg_status inzg_moe_block_hc(inzg_ctx *c, int layer, int n, float *X_dev, const
         return fail(c, INZG_BAD_ARG, "moe_block_hc: bad layer, n or pointer");
     if (opt && (opt->flags & (INZG_DUMP_ROUTE | INZG_PROFILE)))
         return fail(c, INZG_BAD_ARG, "moe_block_hc: route dumps and profiling are for inzg_moe_forward");
-    if (c->hc[layer].mem && !c->hc[layer].dev.inject)
-        return fail(c, INZG_BAD_ARG, "moe_block_hc: the layer's hyper-connection has no inject vectors");
     inzg_moe_opts o = opt ? *opt : inzg_moe_opts{};
     o.flags |= INZG_IO_DEVICE;
     cudaSetDevice(cf.device);
