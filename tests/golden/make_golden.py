@@ -5,7 +5,8 @@ Run here, where the reference tree was present when oracle/_ref was built:
 Inputs are not stored: they are regenerated from seeds by the oracle's copy of the reference tests' generator (the
 streams inferenz_b200.synth draws too), the experts encoded by the reference's own quantizer (oracle.ref_layer_blobs);
 the fixture keeps a SHA-256 of every expert blob it used so a test can prove regenerated inputs are the same bytes.
-Outputs are the reference's: logits, probabilities, top-k, renormalised weights, first-touch unit order, y.
+Outputs are the reference's: logits, probabilities, top-k, renormalised weights, first-touch unit order, y; and for the
+hyper-connection steps around the layer (hc.npz), hc_in's xin and inj and hc_out's updated residual.
 """
 import hashlib
 import os
@@ -104,6 +105,30 @@ def quant_fixture(ref):
     return out
 
 
+HC_CASES = {2048: 2, 2560: 2}  # hidden size -> tokens of the hyper-connection fixture
+
+
+def hc_inputs(H):
+    """(hc weights, X, y) of the hyper-connection fixture at hidden size H"""
+    n = HC_CASES[H]
+    return oracle.synth_hc(1, H=H), oracle.synth_residual(n, H=H, seed=300), oracle.synth_hidden(n, H=H, seed=301)
+
+
+def hc_fixture():
+    """The reference's own hc_in (xin, inj) and hc_out (the updated residual) on seeded inputs, both widths; the
+    inputs' SHA-256 so a test can prove the regenerated inputs are the same bytes."""
+    out = {}
+    for H in HC_CASES:
+        hc, X, y = hc_inputs(H)
+        ref = oracle.Ref(H, threads=0)
+        xin, inj = ref.hc_in(hc, X)
+        out[f"h{H}_xin"], out[f"h{H}_inj"] = xin, inj
+        out[f"h{H}_xout"] = ref.hc_out(X, inj, y)
+        out[f"h{H}_sha"] = np.array([sha(hc[k]) for k in ("norm", "down", "up", "inject")] + [sha(X), sha(y)])
+        ref.close()
+    return out
+
+
 def main():
     orc = oracle.Oracle()
     only = sys.argv[1:]
@@ -126,6 +151,9 @@ def main():
             continue
         np.savez_compressed(os.path.join(HERE, f"bench_{name}.npz"), **bench_fixture(name))
         print("bench", name)
+    if not only or "hc" in only:
+        np.savez_compressed(os.path.join(HERE, "hc.npz"), **hc_fixture())
+        print("hc")
     if not only or "quantizer" in only:
         ref = oracle.Ref(2048, threads=0)
         np.savez_compressed(os.path.join(HERE, "quantizer.npz"), **quant_fixture(ref))

@@ -44,3 +44,27 @@ def test_hc_out_is_one_fma_per_element(orc):
     y = oracle.synth_hidden(n, H=H, seed=10)
     unfused = (X.reshape(n, 4, H) + (inj[:, :, None] * y[:, None, :]).astype(np.float32)).reshape(n, 4 * H)
     assert not np.array_equal(orc.hc_out(X, inj, y), unfused)
+
+
+def _golden():
+    import importlib.util
+    import os
+    here = os.path.dirname(os.path.abspath(__file__))
+    spec = importlib.util.spec_from_file_location("make_golden", os.path.join(here, "golden", "make_golden.py"))
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    return mg, np.load(os.path.join(here, "golden", "hc.npz"))
+
+
+@pytest.mark.parametrize("H", [2048, 2560])
+def test_hc_restatement_matches_golden(orc, H):
+    """The restatement against the reference's outputs stored in tests/golden/hc.npz (no compiled reference needed)."""
+    mg, g = _golden()
+    hc, X, y = mg.hc_inputs(H)
+    want_sha = list(g[f"h{H}_sha"])
+    assert [mg.sha(hc[k]) for k in ("norm", "down", "up", "inject")] + [mg.sha(X), mg.sha(y)] == want_sha, \
+        "regenerated inputs differ from the fixture's"
+    xin, inj = orc.hc_in(hc, X)
+    assert np.array_equal(xin.view(np.uint32), g[f"h{H}_xin"].view(np.uint32))
+    assert np.array_equal(inj.view(np.uint32), g[f"h{H}_inj"].view(np.uint32))
+    assert np.array_equal(orc.hc_out(X, inj, y).view(np.uint32), g[f"h{H}_xout"].view(np.uint32))
