@@ -398,28 +398,25 @@ static size_t smem_optin() {
 
 // Raises a kernel's dynamic shared memory limit on the current device to `bytes` (never lowers it: contexts of
 // different widths share the kernels); sizes above the device's limit are skipped -- launch_f16_rows does not pick
-// those kernels. The limit is a per-device setting, so it is tracked per device.
+// those kernels. The current limit is read back from the device, so each device (and a re-created context) is set
+// on its own.
 template <class F>
-static void raise_smem(F *fn, int slot, size_t bytes, size_t cap) {
-    constexpr int kMaxDevices = 64;
-    static size_t cur[kMaxDevices][8] = {};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = 0;
-    if (bytes > cap || bytes <= cur[dev][slot]) return;
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) == cudaSuccess)
-        cur[dev][slot] = bytes;
-    else
+static void raise_smem(F *fn, size_t bytes, size_t cap) {
+    cudaFuncAttributes fa{};
+    if (bytes > cap) return;
+    if (cudaFuncGetAttributes(&fa, fn) == cudaSuccess && (size_t)fa.maxDynamicSharedSizeBytes >= bytes) return;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess)
         cudaGetLastError();
 }
 
 void router_set_attributes(int H) {
     const size_t cap = smem_optin();
-    raise_smem(router_large_kernel<kLT>, 0, router_smem(kLT, H), cap);
-    raise_smem(router_large_kernel<4, 2>, 1, router_smem(4, H), cap);
-    raise_smem(router_large_kernel<2, 2>, 2, router_smem(2, H), cap);
-    raise_smem(router_gemm_kernel, 3, router_gemm_smem(), cap);
-    raise_smem(router_small_kernel<1, 1>, 4, router_small_smem(1, 1, H), cap);
-    raise_smem(router_small_kernel<2, 1>, 5, router_small_smem(2, 1, H), cap);
+    raise_smem(router_large_kernel<kLT>, router_smem(kLT, H), cap);
+    raise_smem(router_large_kernel<4, 2>, router_smem(4, H), cap);
+    raise_smem(router_large_kernel<2, 2>, router_smem(2, H), cap);
+    raise_smem(router_gemm_kernel, router_gemm_smem(), cap);
+    raise_smem(router_small_kernel<1, 1>, router_small_smem(1, 1, H), cap);
+    raise_smem(router_small_kernel<2, 1>, router_small_smem(2, 1, H), cap);
 }
 
 int launch_router_logits(const uint4 *Wr, const float *Wf, const float *X, int n, int H, int E, const float *bias,
