@@ -22,7 +22,7 @@ REFERENCE_TREE = os.environ.get("INZ_REFERENCE_TREE",
                                 os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 
 P, I, U32, U64, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_float
-T_Q4L, T_Q8G = 102, 103
+T_Q4L, T_Q8G, T_Q4N = 102, 103, 107
 
 
 def _p(a):
@@ -183,6 +183,7 @@ class Oracle:
             ("orc_xq", None, [P, I, I, U32, P, P, P]),
             ("orc_moe_routed", I, [I, I, I, I, P, P, U64, U64, I, P, P, P, P, P, P, P, P, P, P, I]),
             ("orc_hc_in", None, [I, I, P, P, P, P, I, P, P, P]),
+            ("orc_matmul_payload", I, [P, I, P, P, I, I]),
             ("orc_hc_out", None, [I, I, P, P, P]),
         ]:
             fn = getattr(L, name)
@@ -225,6 +226,18 @@ class Oracle:
         sm = np.zeros(nkb, np.int32)
         self.lib.orc_xq(_p(x), K, rot, seed, _p(q), _p(s), _p(sm))
         return q, s, sm
+
+    def matmul(self, payload, X, gemm=False):
+        """Y [n][rows] = one quantized matrix (any of Q4L / Q8G / Q4N) times n tokens with lin_mm's numerics: decode
+        (gemm=False) or prefill GEMM (gemm=True)."""
+        X = np.ascontiguousarray(X, np.float32)
+        n = X.shape[0]
+        rows = int(np.frombuffer(np.ascontiguousarray(payload, np.uint8)[8:12].tobytes(), np.uint32)[0])
+        Y = np.zeros((n, rows), np.float32)
+        if self.lib.orc_matmul_payload(_p(np.ascontiguousarray(payload, np.uint8)), n, _p(X), _p(Y), int(gemm),
+                                       self.q8_vnni) != 0:
+            raise ValueError("oracle: payload or shape not covered")
+        return Y
 
     def hc_in(self, hc, X):
         """hc_in (src/model_fwd.c:404-439): X [n][4H] -> (xin [n][H], inj [n][4]); hc: dict from synth_hc."""
@@ -345,6 +358,17 @@ class Ref:
             raise RuntimeError("reference: shared expert matrices do not match")
         return yo, D
 
+
+    def matmul(self, payload, X, gemm=False):
+        """The reference's own lin_mm numerics for one quantized matrix: inz_matvec_rows / inz_matmul_rows after
+        per-token activation quantization (gemm=False), or inz_gemm_rows (gemm=True)."""
+        X = np.ascontiguousarray(X, np.float32)
+        n = X.shape[0]
+        pl = np.ascontiguousarray(payload, np.uint8)
+        rows = int(np.frombuffer(pl[8:12].tobytes(), np.uint32)[0])
+        Y = np.zeros((n, rows), np.float32)
+        (self.lib.ref_matmul_gemm if gemm else self.lib.ref_matmul_decode)(_p(pl), n, _p(X), _p(Y))
+        return Y
 
     def hc_in(self, hc, X):
         """The reference's own hc_in; same arguments and results as Oracle.hc_in."""

@@ -15,12 +15,15 @@
 /* ---------------- formats ---------------- */
 
 /* index bytes per 64-weight group: bits * 64 / 8 (src/quant.c:25) */
-static size_t group_bytes(int type) { return type == ORC_T_Q4L ? 32 : type == ORC_T_Q8G ? 64 : 0; }
+static size_t group_bytes(int type) {
+    return type == ORC_T_Q4L || type == ORC_T_Q4N ? 32 : type == ORC_T_Q8G ? 64 : 0;
+}
 
-/* src/quant.c:30-36 (Q4L / Q8G only) */
+/* src/quant.c:30-36 (Q4L / Q8G / Q4N: four e4m3 scales per group in place of one fp16) */
 size_t orc_qmat_bytes(int type, int rows, int cols) {
     size_t ng = (size_t)cols / ORC_GROUP;
     size_t n = 64 + (size_t)rows * ng * group_bytes(type) + (size_t)rows * ng * 2;
+    if (type == ORC_T_Q4N) n += (size_t)rows * ng * 2;
     return (n + 63) / 64 * 64;
 }
 
@@ -48,7 +51,22 @@ int orc_qmat_view(orc_qmat *m, const void *payload) {
     m->gb = group_bytes(type);
     m->q = h + 64;
     m->d = (const uint16_t *)(m->q + (size_t)m->rows * m->ng * m->gb);
+    if (type == ORC_T_Q4N) {  /* src/quant.c:85-89: scales where the fp16 ones would be, gscale in pad2 */
+        m->s8 = (const uint8_t *)m->d;
+        m->d = NULL;
+        memcpy(&m->gscale, h + 56, 4);
+    }
     return m->gb != 0;
+}
+
+/* inz_e4m3_to_f32, src/util.c:119-126 */
+static float e4m3_to_f32(uint8_t x) {
+    const uint32_t sg = x >> 7, e = (x >> 3) & 0xF, mt = x & 7;
+    float v;
+    if (e == 0) v = (float)mt / 8.0f / 64.0f;
+    else if (e == 15 && mt == 7) v = NAN;
+    else v = (1.0f + (float)mt / 8.0f) * ldexpf(1.0f, (int)e - 7);
+    return sg ? -v : v;
 }
 
 /* IEEE half -> float, exact (src/util.c:116 _cvtsh_ss) */
@@ -259,6 +277,59 @@ void orc_matvec_decode(const orc_qmat *m, const int8_t *q, const float *s, const
     }
 }
 
+/* Q4N lane partials of one group (src/quant.c:1089-1104, 1150-1157): VPDPBUSD from the activation's LUT bias
+ * -64 * sum4 (nb4) over the biased codes, i.e. lane k of the low half = sum over weights 4k..4k+3 of (lut - 64) * x,
+ * lane k of the high half = the same over weights 32+4k..32+4k+3 (code = high nibble of byte 4k+i). Exact. */
+static void q4n_partials(const orc_qmat *m, const uint8_t *w, const int8_t *x, int32_t i0[8], int32_t i1[8]) {
+    for (int k = 0; k < 8; k++) {
+        int32_t a = 0, b = 0;
+        for (int i = 0; i < 4; i++) {
+            const int j = 4 * k + i;
+            a += ((int)m->lut[w[j] & 15] - ORC_LUT_BIAS) * x[j];
+            b += ((int)m->lut[w[j] >> 4] - ORC_LUT_BIAS) * x[32 + j];
+        }
+        i0[k] = a;
+        i1[k] = b;
+    }
+}
+
+/* mv_q4n, src/quant.c:1065-1105 (row pairs, even group count: the expert shapes): per group and lane,
+ * acc = fma(i0, scale_block * xs, acc) then fma(i1, scale_block' * xs, acc), block = k / 4 (low half) or 2 + k / 4;
+ * y = hsum8(acc) * gscale. */
+static void q4n_mv(const orc_qmat *m, const int8_t *q, const float *s, float *y) {
+    const int ng = m->ng;
+    for (int r = 0; r < m->rows; r++) {
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int g = 0; g < ng; g++) {
+            int32_t i0[8], i1[8];
+            q4n_partials(m, m->q + ((size_t)r * ng + g) * 32, q + (size_t)g * ORC_GROUP, i0, i1);
+            const uint8_t *sc = m->s8 + ((size_t)r * ng + g) * 4;
+            for (int k = 0; k < 8; k++) acc[k] = fmaf((float)i0[k], e4m3_to_f32(sc[k / 4]) * s[g], acc[k]);
+            for (int k = 0; k < 8; k++) acc[k] = fmaf((float)i1[k], e4m3_to_f32(sc[2 + k / 4]) * s[g], acc[k]);
+        }
+        y[r] = hsum8(acc) * m->gscale;
+    }
+}
+
+/* mm_q4n, src/quant.c:1139-1163: per group and lane part = fma(i1, S1, i0 * S0), acc = fma(part, xs, acc);
+ * y = hsum8(acc) * gscale (a different rounding order from mv_q4n: one token through mm differs from mv). */
+static void q4n_mm_token(const orc_qmat *m, const int8_t *q, const float *s, float *y) {
+    const int ng = m->ng;
+    for (int r = 0; r < m->rows; r++) {
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int g = 0; g < ng; g++) {
+            int32_t i0[8], i1[8];
+            q4n_partials(m, m->q + ((size_t)r * ng + g) * 32, q + (size_t)g * ORC_GROUP, i0, i1);
+            const uint8_t *sc = m->s8 + ((size_t)r * ng + g) * 4;
+            for (int k = 0; k < 8; k++) {
+                const float part = fmaf((float)i1[k], e4m3_to_f32(sc[2 + k / 4]), (float)i0[k] * e4m3_to_f32(sc[k / 4]));
+                acc[k] = fmaf(part, s[g], acc[k]);
+            }
+        }
+        y[r] = hsum8(acc) * m->gscale;
+    }
+}
+
 /* ---------------- prefill-path (GEMM) products ---------------- */
 
 /* _mm256_mulhrs_epi16 on one lane: bits 16..1 of ((a*b >> 14) + 1) */
@@ -271,7 +342,45 @@ static int sat_u8(int v) { return v < 0 ? 0 : v > 255 ? 255 : v; }
 
 /* gemm_decode_tile, src/quant.c:1532-1613, for one row: per 256-block scale ws = dmax * maxlev / 127 and
  * per-group factor F = lrint(512 * d / ws), int8 weight = sat_u8(mulhrs(level * 64, F) + 128) - 128. */
+/* gemm_decode_tile_q4n, src/quant.c:1479-1530, for one row: per 256-block sc = max e4m3 scale * maxlev / 127,
+ * ws = sc * gscale; per 16-weight block F = lrint(e4m3 * 512 / sc); int8 weight = sat_u8(mulhrs(level * 64, F) + 128)
+ * - 128 with the block's F (weights 0-15, 16-31 of a group from the low nibbles, 32-47, 48-63 from the high ones). */
+static void q4n_requant_row(const orc_qmat *m, int row, int8_t *w8, float *ws) {
+    const int K = m->cols, ng = m->ng, nkb = (K + ORC_KB - 1) / ORC_KB, nsb = ng * 4, spb = ORC_KB / 16;
+    int maxlev = 1;
+    int16_t lv[16];
+    for (int c = 0; c < 16; c++) {
+        lv[c] = (int16_t)(((int)m->lut[c] - ORC_LUT_BIAS) * 64);
+        if (abs((int)m->lut[c] - ORC_LUT_BIAS) > maxlev) maxlev = abs((int)m->lut[c] - ORC_LUT_BIAS);
+    }
+    int16_t *F = malloc(sizeof(int16_t) * (size_t)nsb);
+    const uint8_t *sr = m->s8 + (size_t)row * nsb;
+    for (int b = 0; b < nkb; b++) {
+        const int k0 = b * spb, k1 = k0 + spb < nsb ? k0 + spb : nsb;
+        float smax = 0;
+        for (int k = k0; k < k1; k++) smax = fmaxf(smax, e4m3_to_f32(sr[k]));
+        const float sc = smax * (float)maxlev / 127.0f;
+        ws[b] = sc * m->gscale;
+        const float inv = sc > 0 ? 512.0f / sc : 0;
+        for (int k = k0; k < k1; k++) F[k] = (int16_t)lrintf(e4m3_to_f32(sr[k]) * inv);
+    }
+    for (int g = 0; g < ng; g++) {
+        const uint8_t *qg = m->q + ((size_t)row * ng + g) * 32;
+        int8_t *o = w8 + (size_t)g * ORC_GROUP;
+        for (int j = 0; j < 32; j++) {
+            const int16_t f0 = F[g * 4 + j / 16], f1 = F[g * 4 + 2 + j / 16];
+            o[j] = (int8_t)(sat_u8((int16_t)(mulhrs(lv[qg[j] & 15], f0) + 128)) - 128);
+            o[32 + j] = (int8_t)(sat_u8((int16_t)(mulhrs(lv[qg[j] >> 4], f1) + 128)) - 128);
+        }
+    }
+    free(F);
+}
+
 void orc_gemm_requant_row(const orc_qmat *m, int row, int8_t *w8, float *ws) {
+    if (m->type == ORC_T_Q4N) {
+        q4n_requant_row(m, row, w8, ws);
+        return;
+    }
     const int K = m->cols, ng = m->ng, nkb = (K + ORC_KB - 1) / ORC_KB, gpb = ORC_KB / ORC_GROUP;
     const int q8 = m->type == ORC_T_Q8G;
     const int bias = q8 ? 128 : ORC_LUT_BIAS;
@@ -338,6 +447,33 @@ void orc_matmul_gemm(const orc_qmat *m, int n, const int8_t *q, const float *s, 
     }
     free(w8);
     free(ws);
+}
+
+int orc_matmul_payload(const void *payload, int n, const float *X, float *Y, int gemm, int q8_vnni) {
+    orc_qmat m;
+    if (n <= 0 || !orc_qmat_view(&m, payload)) return -1;
+    if (m.type == ORC_T_Q4N && ((m.rows & 1) || (m.ng & 1))) return -1;  /* the scalar tails are not restated */
+    const int K = m.cols, nkb = (K + ORC_KB - 1) / ORC_KB;
+    int8_t *q = malloc((size_t)n * K);
+    float *s = malloc(sizeof(float) * (size_t)n * (K / ORC_GROUP + nkb)), *b = malloc(sizeof(float) * (size_t)K);
+    int32_t *sum = malloc(sizeof(int32_t) * (size_t)n * nkb);
+    if (gemm) {
+        for (int t = 0; t < n; t++)
+            orc_xq(X + (size_t)t * K, K, m.rot_block, m.rot_seed, q + (size_t)t * K, s + (size_t)t * nkb, sum + (size_t)t * nkb);
+        orc_matmul_gemm(&m, n, q, s, sum, Y);
+    } else {
+        for (int t = 0; t < n; t++) {
+            int8_t *qt = q + (size_t)t * K;
+            float *st = s + (size_t)t * (K / ORC_GROUP);
+            orc_act_quantize(X + (size_t)t * K, K, m.rot_block, m.rot_seed, qt, st, b);
+            float *yt = Y + (size_t)t * m.rows;
+            if (m.type != ORC_T_Q4N) orc_matvec_decode(&m, qt, st, b, yt, q8_vnni);
+            else if (n == 1) q4n_mv(&m, qt, st, yt);
+            else q4n_mm_token(&m, qt, st, yt);
+        }
+    }
+    free(q); free(s); free(b); free(sum);
+    return 0;
 }
 
 /* ---------------- the routed layer ---------------- */

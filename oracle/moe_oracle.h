@@ -21,6 +21,7 @@
 #define ORC_T_F16 1
 #define ORC_T_Q4L 102
 #define ORC_T_Q8G 103
+#define ORC_T_Q4N 107         /* src/quant.h:34 INZ_T_Q4N (NVFP4 repacked: e2m1 codes, e4m3 scale per 16, global) */
 
 #ifdef __cplusplus
 extern "C" {
@@ -35,6 +36,8 @@ typedef struct {
     const uint8_t *q;
     const uint16_t *d;
     size_t gb;
+    const uint8_t *s8;  /* Q4N: e4m3 scales [rows][ng][4], one per 16 weights (d is NULL) */
+    float gscale;       /* Q4N: weight = (lut[code] - 64) * e4m3 * gscale */
 } orc_qmat;
 
 int orc_qmat_view(orc_qmat *m, const void *payload);
@@ -74,6 +77,11 @@ int orc_moe_routed(int H, int FF, int E, int topk, const uint16_t *router, const
 void orc_hc_in(int H, int rank, const float *norm, const uint16_t *down, const uint16_t *up, const float *inject,
                int n, const float *X, float *xin, float *inj);
 void orc_hc_out(int H, int n, float *X, const float *inj, const float *y);
+
+/* one matrix payload times n tokens, activations quantized here as the reference's lin_mm does: decode numerics
+ * (gemm = 0: one activation per token, mv for n == 1, mm otherwise) or prefill GEMM numerics (gemm = 1).
+ * Y [n][rows]. Returns 0, or -1 on a payload or shape this restatement does not cover. */
+int orc_matmul_payload(const void *payload, int n, const float *X, float *Y, int gemm, int q8_vnni);
 
 /* ---- seeded synthetic inputs (test infrastructure): the LCG + Box-Muller normal of the reference's tests
  * (tests/test_quant.c:10-17), so that the CPU side of a test or of the benchmark's reference arm draws its inputs
