@@ -6,7 +6,8 @@ Inputs are not stored: they are regenerated from seeds by the oracle's copy of t
 streams inferenz_b200.synth draws too), the experts encoded by the reference's own quantizer (oracle.ref_layer_blobs);
 the fixture keeps a SHA-256 of every expert blob it used so a test can prove regenerated inputs are the same bytes.
 Outputs are the reference's: logits, probabilities, top-k, renormalised weights, first-touch unit order, y; and for the
-hyper-connection steps around the layer (hc.npz), hc_in's xin and inj and hc_out's updated residual.
+hyper-connection steps around the layer (hc.npz), hc_in's xin and inj and hc_out's updated residual; and Q4N payloads
+with their products (q4n.npz).
 """
 import hashlib
 import os
@@ -129,6 +130,25 @@ def hc_fixture():
     return out
 
 
+Q4N_SHAPES = [(64, 2048), (96, 640)]
+Q4N_CALLS = [(1, False), (5, False), (12, True)]  # (tokens, GEMM numerics): mv_q4n, mm_q4n, the Q4N GEMM tile
+
+
+def q4n_fixture():
+    """Q4N payloads written by the reference quantizer (bytes kept whole: the oracle has no Q4N quantizer) and the
+    reference's products through lin_mm's three numeric paths on seeded tokens."""
+    out = {}
+    ref = oracle.Ref(2048, threads=0)
+    for i, (rows, cols) in enumerate(Q4N_SHAPES):
+        W = oracle.synth_randn(700 + rows, rows * cols, (1.0 / cols) ** 0.5).reshape(rows, cols)
+        pl = ref.quantize(W, oracle.T_Q4N)
+        out[f"m{i}_payload"] = pl
+        for n, gemm in Q4N_CALLS:
+            out[f"m{i}_n{n}"] = ref.matmul(pl, oracle.synth_hidden(n, cols, seed=800 + n), gemm=gemm)
+    ref.close()
+    return out
+
+
 def main():
     orc = oracle.Oracle()
     only = sys.argv[1:]
@@ -154,6 +174,9 @@ def main():
     if not only or "hc" in only:
         np.savez_compressed(os.path.join(HERE, "hc.npz"), **hc_fixture())
         print("hc")
+    if not only or "q4n" in only:
+        np.savez_compressed(os.path.join(HERE, "q4n.npz"), **q4n_fixture())
+        print("q4n")
     if not only or "quantizer" in only:
         ref = oracle.Ref(2048, threads=0)
         np.savez_compressed(os.path.join(HERE, "quantizer.npz"), **quant_fixture(ref))

@@ -52,3 +52,20 @@ def test_q4n_one_token_paths_round_differently(orc):
     mm = orc.matmul(payload, np.concatenate([x, x]))[0]
     assert not np.array_equal(mv, mm)
     assert np.abs(mv - mm).max() <= 1e-5 * np.abs(mv).max()
+
+
+def test_q4n_restatement_matches_golden(orc):
+    """The restatement against the reference's Q4N products stored in tests/golden/q4n.npz (no compiled reference
+    needed)."""
+    import importlib.util
+    import os
+    here = os.path.dirname(os.path.abspath(__file__))
+    spec = importlib.util.spec_from_file_location("make_golden", os.path.join(here, "golden", "make_golden.py"))
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    g = np.load(os.path.join(here, "golden", "q4n.npz"))
+    for i, (rows, cols) in enumerate(mg.Q4N_SHAPES):
+        pl = g[f"m{i}_payload"]
+        for n, gemm in mg.Q4N_CALLS:
+            got = orc.matmul(pl, oracle.synth_hidden(n, cols, seed=800 + n), gemm=gemm)
+            assert np.array_equal(got.view(np.uint32), g[f"m{i}_n{n}"].view(np.uint32)), f"{rows}x{cols} n={n}"
